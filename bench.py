@@ -1,0 +1,308 @@
+"""bs=1 greedy decode throughput of Llama-2-7B Q4_K_M on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+A step is one decode token (all 32 layers + LM head + argmax) of a random-init
+Llama-2-7B Q4_K_M GGUF (seeded; weights 4.07 GB/token >> 126 MB L2, so no L2
+flush is needed between steps), after a 128-token uniform-random prompt.
+N > 1 is tensor parallel over NCCL (strong scaling: one token stream per job).
+
+value   = tokens/s of the job, device-timed with CUDA events on the engine's
+          stream over K device-fed graph launches (max over ranks).
+e2e     = the same through the public per-step API (af_engine_step): each step
+          copies the token id host->device and reads the next id back.
+roofline: dominant kernel = the dequant GEMVs; algorithmic bytes (weights +
+          x + y) per launch / event-bracketed launch time, vs measured HBM peak.
+cpu_baseline: the reference's own CPU decode (oracle/_ref, compiled from the
+          unmodified sources), production Q8_0 path, all host threads, on a
+          bounded sample of decode steps.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PROMPT_LEN = 128
+SEED = 0
+
+
+def env_int(k, d):
+    try:
+        return int(os.environ.get(k, d))
+    except ValueError:
+        return d
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        j = json.load(open(p))
+        return float(j["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+
+    def stop(self) -> dict:
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except Exception:
+            self.p.kill()
+        self.f.flush()
+        rows = []
+        for ln in open(self.f.name).read().splitlines():
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) >= 8:
+                rows.append(parts)
+        os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[4 + i].lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def model_file(preset: str, rank: int, dist) -> str:
+    from llm_core_b200 import gguf
+    d = os.environ.get("AF_BENCH_DIR", "/dev/shm" if os.path.isdir("/dev/shm") else tempfile.gettempdir())
+    path = os.path.join(d, f"af_bench_{preset}_s{SEED}.gguf")
+    if rank == 0 and not os.path.exists(path):
+        gguf.write_random_model(path, preset, SEED)
+    if dist is not None:
+        dist.barrier()
+    return path
+
+
+def cpu_baseline_sample(path: str, steps: int, threads: int) -> dict | None:
+    """The reference CPU decode (production Q8_0 path), `steps` tokens from position 0."""
+    from oracle import RefLib
+    if not RefLib.available():
+        return None
+    ref = RefLib().open(path, threads=threads, f32_mode=False, max_ctx=4096)
+    ref.set_n_past(0)
+    ref.time_decode(1, 2)  # warm the r8 weight cache / page in
+    ref.set_n_past(0)
+    secs = ref.time_decode(1, steps)
+    ref.close()
+    return {"value": steps / secs, "unit": "tok/s", "cores": threads, "kind": "reference",
+            "sample": f"{steps} decode steps of the reference's own CPU path (Q8_0 activations, r8 repack, "
+                      f"oracle/_ref built from the unmodified sources) at context 1..{steps}, "
+                      f"{threads} threads, random-init Llama-2-7B Q4_K_M"}
+
+
+def run_reference(args):
+    rank = env_int("RANK", 0)
+    if rank != 0:
+        return 0
+    from llm_core_b200 import gguf
+    path = model_file(args.model, 0, None)
+    threads = os.cpu_count() or 1
+    from oracle import RefLib
+    if not RefLib.available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libaxref.so was not built "
+                          "(reference sources absent when the repo was built)"}))
+        return 0
+    ref = RefLib().open(path, threads=threads, f32_mode=False, max_ctx=4096)
+    ref.set_n_past(0)
+    ref.time_decode(1, max(1, args.warmup))
+    # each timed step: one reference decode token (context grows from W)
+    secs = ref.time_decode(1, args.steps)
+    ref.close()
+    val = args.steps / secs
+    cfg = gguf.PRESETS[args.model]
+    line = {
+        "impl": "reference", "metric": "bs=1 decode tok/s", "value": round(val, 3), "unit": "tok/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1000 * secs / args.steps, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "q8_0-int8 dot + f32", "data": "synthetic (seeded random-init GGUF)",
+        "config": {"workload": f"{cfg.name} Q4_K_M bs=1 greedy decode", "global_batch": 1,
+                   "seq_len": PROMPT_LEN, "parallelism": "cpu threads"},
+        "cpu_baseline": {"value": round(val, 3), "unit": "tok/s", "cores": threads, "kind": "reference",
+                         "sample": f"{args.steps} decode steps at context {args.warmup}..{args.warmup + args.steps} "
+                                   "(production Q8_0 path, all host threads)"},
+        "e2e": {"value": round(val, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+    return 0
+
+
+def run_b200(args):
+    import torch
+    rank, world = env_int("RANK", 0), env_int("WORLD_SIZE", 1)
+    local = env_int("LOCAL_RANK", 0)
+    if world != args.gpus:
+        world = args.gpus if world == 1 and args.gpus == 1 else world
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    from llm_core_b200 import gguf
+    from llm_core_b200.engine import LlamaCudaModel, nccl_unique_id
+    path = model_file(args.model, rank, dist)
+    nid = None
+    if world > 1:
+        obj = [nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        nid = obj[0]
+    t_load = time.time()
+    m = LlamaCudaModel(path, device=local, tp_rank=rank, tp_size=world, nccl_id=nid)
+    t_load = time.time() - t_load
+    cfg = gguf.PRESETS[args.model]
+    rng = np.random.default_rng(1234)
+    prompt = [1] + rng.integers(0, cfg.vocab, PROMPT_LEN).tolist()
+    nxt, _ = m.prefill(prompt, 0, want_logits=False)
+    pos = len(prompt)
+    stream = torch.cuda.ExternalStream(m.stream)
+    # warm-up
+    ids = m.decode_greedy(nxt, pos, args.warmup)
+    tok = int(ids[-1]) if len(ids) else nxt
+    pos += args.warmup
+    clocks = ClockSampler(local)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.3)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    from llm_core_b200._lib import check
+    check(m.lib.af_engine_decode_greedy(m.h, tok, pos, args.steps, None), "decode")
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1)
+    if dist is not None:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    pos += args.steps
+    ms_step = ms / args.steps
+    value = 1000.0 / ms_step
+    # e2e through the per-step public API (host token in, host id out)
+    n_e2e = min(args.steps, 4096 - pos - 8)
+    if dist is not None:
+        dist.barrier()
+    t0 = time.perf_counter()
+    t = tok
+    for i in range(n_e2e):
+        t, _ = m.step(t, pos + i, want_logits=False)
+    e2e_s = time.perf_counter() - t0
+    if dist is not None:
+        tt = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_s = float(tt.item())
+    pos += n_e2e
+    e2e = n_e2e / e2e_s
+    # per-kernel roofline (event-bracketed eager launches, after the timed region)
+    prof = m.profile(t, pos, 4)
+    pos += 4
+    gem = [k for k in prof if k.startswith("gemv")]
+    g_ms = sum(prof[k]["ms"] for k in gem)
+    g_bytes = sum(prof[k]["bytes"] for k in gem)
+    g_n = sum(prof[k]["launches"] for k in gem)
+    peak, kind = peaks()
+    achieved = g_bytes / (g_ms / 1e3) / 1e9 if g_ms > 0 else 0.0
+    wb = m.weight_bytes
+    step_gbs = wb / (ms_step / 1e3) / 1e9
+    if rank != 0:
+        return 0
+    traffic = None
+    tp_file = os.path.join(ROOT, "profiles", "gemv_traffic.json")
+    if os.path.exists(tp_file):
+        try:
+            traffic = json.load(open(tp_file)).get(args.model, {}).get(str(world))
+        except Exception:
+            traffic = None
+    threads = os.cpu_count() or 1
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_sample(path, args.cpu_steps, threads)
+    line = {
+        "metric": "bs=1 decode tok/s", "value": round(value, 2), "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "q4_k/q6_k weights, int32 dp4a dot + f32 accumulate",
+        "data": "synthetic (seeded random-init GGUF; uniform-random prompt ids)",
+        "config": {"workload": f"{cfg.name} Q4_K_M bs=1 greedy decode (BASELINE config 3)",
+                   "model": cfg.name, "global_batch": 1, "seq_len": PROMPT_LEN,
+                   "context": f"{PROMPT_LEN + 1 + args.warmup}..{PROMPT_LEN + 1 + args.warmup + args.steps}",
+                   "parallelism": f"tp{world}" if world > 1 else "single",
+                   "l2": "inputs larger than L2 (4.07 GB weights per step)"},
+        "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "kernel": f"gemv_kernel ({g_n // 4} launches/step; {kind} peak)",
+                     "bytes_per_launch": round(g_bytes / max(g_n, 1)),
+                     "avg_launch_us": round(1000 * g_ms / max(g_n, 1), 3)},
+        "step_roofline": {"weight_bytes_per_step_per_rank": wb, "achieved_gbs": round(step_gbs, 1),
+                          "frac_of_peak": round(step_gbs / peak, 4)},
+        "kernel_ms_per_step": {k: round(v["ms"] / 4, 4) for k, v in prof.items() if v["launches"]},
+        "gpu_launches": m.kernels_per_step * args.steps,
+        "clocks": clk,
+        "load_s": round(t_load, 1),
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line))
+    m.close()
+    if dist is not None:
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--model", default="llama2-7b")
+    ap.add_argument("--cpu-steps", type=int, default=12)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_b200(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,168 @@
+/*
+ * af_b200.h — C ABI of the B200 (sm_100a) decode path for AxonForge
+ * (songqiuyu/llm_core).
+ *
+ * Plain pointers, sizes and a cudaStream_t; no C++ or torch types cross this
+ * boundary.  Every function returns cudaSuccess (0) or an error code and never
+ * throws.  Device pointers are marked `d_`; host pointers `h_`.
+ *
+ * Two layers:
+ *   1. Kernel launchers — the op set of the reference CUDA backend
+ *      (src/backend/cuda/cuda_kernels.hpp:8-19) plus the Q6_K GEMV it lacks.
+ *   2. The decode engine — the GPU-resident replacement of
+ *      llama_cuda_generate (include/axonforge/models/llama_cuda.hpp:25-28):
+ *      weights uploaded byte-for-byte, fp32 KV cache on the device, one CUDA
+ *      graph per decode step, optional tensor parallelism over NCCL.
+ *
+ * Weight layouts on the device: Q4_K rows are the GGUF bytes unchanged
+ * (144-byte super-blocks, row stride = cols/256*144).  Q6_K rows are the GGUF
+ * super-blocks regrouped once at upload by af_q6k_repack: groups of 8 blocks,
+ * each [8 x (ql[128] qh[64] scales[16])][8 x f16 d], so every group starts on a
+ * 16-byte boundary (af_q6k_row_stride gives the stride).
+ */
+#ifndef AF_B200_H
+#define AF_B200_H
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ggml tensor type ids used on this path (include/axonforge/dtype.hpp:80-96). */
+#define AF_GGML_F32 0
+#define AF_GGML_Q4_K 12
+#define AF_GGML_Q6_K 14
+
+/* ------------------------------------------------------------------ status */
+
+/* Text of the last host-side error on this thread ("" if none). */
+const char* af_last_error(void);
+
+/* Device error word (0 = none).  Kernels never trap: a bounded wait that runs
+ * out writes a code here and returns.  `clear` != 0 resets it. */
+cudaError_t af_device_error(int* h_code, int clear);
+
+/* ---------------------------------------------------------- weight layout */
+
+/* Bytes of one device row of `cols` values for `ggml_type` (Q4_K: GGUF row;
+ * Q6_K: regrouped row, >= the GGUF row by at most 14 bytes). */
+size_t af_row_stride(int ggml_type, int cols);
+
+/* Regroup `rows` GGUF Q6_K rows (d_src, stride cols/256*210) into the device
+ * layout at d_dst (stride af_row_stride(AF_GGML_Q6_K, cols)).  Byte-preserving
+ * permutation; af_q6k_unpack inverts it. */
+cudaError_t af_q6k_repack(void* d_dst, const void* d_src, int rows, int cols, cudaStream_t stream);
+cudaError_t af_q6k_unpack(void* d_dst, const void* d_src, int rows, int cols, cudaStream_t stream);
+
+/* ------------------------------------------------------- kernel launchers */
+
+/* y[rows] = W · x with W in the device layout above and f32 x[cols]: the fused
+ * dequant GEMV (fp32 accumulation).  Replaces q4km_gemv_f32
+ * (src/backend/cuda/cuda_kernels.hpp:13-19, numerically wrong in the
+ * reference) and adds Q6_K.  Parity target: gemv_q4k_avx2_range /
+ * gemv_q6k_avx2_range (src/backend/cpu_x86/kernels/gemv_q4k_avx2.cpp:230-238,
+ * gemv_q6k_avx2.cpp:235-243).  cols % 256 == 0. */
+cudaError_t af_gemv_f32(float* d_y, const void* d_w, int ggml_type, const float* d_x, int rows,
+                        int cols, cudaStream_t stream);
+
+/* y = w ⊙ x / sqrt(mean(x²) + eps): rms_norm_f32 (cuda_kernels.hpp:8). */
+cudaError_t af_rms_norm_f32(float* d_y, const float* d_x, const float* d_w, int n, float eps,
+                            cudaStream_t stream);
+/* y = x / (1 + e^-x): silu_f32 (cuda_kernels.hpp:9). */
+cudaError_t af_silu_f32(float* d_y, const float* d_x, int n, cudaStream_t stream);
+/* y = a ⊙ b: mul_f32 (cuda_kernels.hpp:10). */
+cudaError_t af_mul_f32(float* d_y, const float* d_a, const float* d_b, int n, cudaStream_t stream);
+/* In-place half-split RoPE of n_heads heads at position pos with base theta:
+ * rope_f32 (cuda_kernels.hpp:11), same rotation as apply_rope
+ * (src/models/llama_model.cpp:1046-1060). */
+cudaError_t af_rope_f32(float* d_q, int n_heads, int head_dim, int pos, float theta,
+                        cudaStream_t stream);
+
+/* --------------------------------------------------------- decode engine */
+
+typedef struct af_engine af_engine;
+
+typedef struct {
+    int n_layer, n_embd, n_head, n_kv_head, ffn, vocab;
+    int n_ctx;            /* KV slots: min(context_length, max_context_len) */
+    float eps, theta;
+    int qk_norm_order;    /* 0 none, 1 before RoPE (qwen3), 2 after RoPE (hunyuan) */
+    int bos_id, eos_id;
+} af_model_config;
+
+/* Write a fresh 128-byte ncclUniqueId to h_id (rank 0 calls this and sends the
+ * bytes to the other ranks). */
+cudaError_t af_nccl_unique_id(void* h_id);
+
+/* Create an engine on `device`.  Tensor parallel when tp_size > 1: this process
+ * is rank tp_rank and `nccl_id` points at the 128-byte ncclUniqueId that every
+ * rank received from rank 0 (NULL when tp_size == 1). */
+cudaError_t af_engine_create(const af_model_config* cfg, int device, int tp_rank, int tp_size,
+                             const void* nccl_id, af_engine** out);
+cudaError_t af_engine_destroy(af_engine* e);
+
+/* Hand one GGUF tensor (host bytes, exact GGUF size) to the engine, which
+ * copies this rank's shard to the device byte-for-byte (Q6_K then regrouped
+ * on the device).  Names follow build_weights (src/models/llama_model.cpp:973-1004).
+ * dims are in GGML order (dims[0] = columns). */
+cudaError_t af_engine_load_tensor(af_engine* e, const char* name, int ggml_type,
+                                  const int64_t* dims, int n_dims, const void* h_data,
+                                  size_t nbytes);
+/* Parse a GGUF file (mmap) and load every tensor; fills *cfg_out if non-NULL. */
+cudaError_t af_gguf_read_config(const char* path, int max_context_len, af_model_config* cfg_out);
+cudaError_t af_engine_load_gguf(af_engine* e, const char* path);
+/* Allocate activations/KV, check every required tensor, capture the step graph. */
+cudaError_t af_engine_finalize(af_engine* e);
+
+/* One decode step at position pos for token: logits (optional, host, vocab
+ * floats; all ranks' shards gathered) and the greedy next id.  Host-driven:
+ * token/pos go host->device and the id comes back every call. */
+cudaError_t af_engine_step(af_engine* e, int32_t token, int32_t pos, float* h_logits,
+                           int32_t* h_next);
+/* Prefill tokens[0..n) at positions pos0.. (KV filled); last-token logits and
+ * greedy id as in af_engine_step. */
+cudaError_t af_engine_prefill(af_engine* e, const int32_t* h_tokens, int n, int32_t pos0,
+                              float* h_logits, int32_t* h_next);
+/* Device-fed greedy decode: n_steps graph launches, each feeding its argmax to
+ * the next; ids written to h_out (may be NULL).  No host round trip per step. */
+cudaError_t af_engine_decode_greedy(af_engine* e, int32_t first_token, int32_t pos0, int n_steps,
+                                    int32_t* h_out);
+/* Greedy generation with llama_generate's decode-loop semantics
+ * (src/models/llama_model.cpp:1562-1624): BOS prepended unless present, stop at
+ * EOS or the context cap.  Returns the ids in h_out, count in *n_out. */
+cudaError_t af_engine_generate(af_engine* e, const int32_t* h_prompt, int n_prompt, int max_new,
+                               int32_t* h_out, int* n_out);
+/* Copy the current residual stream (n_embd floats) to the host. */
+cudaError_t af_engine_hidden(af_engine* e, float* h_out);
+/* Copy layer l's fp32 K or V cache rows [0, n_pos) (local heads) to the host. */
+cudaError_t af_engine_kv(af_engine* e, int layer, int which_v, int n_pos, float* h_out);
+/* Launch kinds reported by af_engine_profile. */
+#define AF_PROF_EMBED 0
+#define AF_PROF_QKV 1
+#define AF_PROF_ATTN 2
+#define AF_PROF_O 3
+#define AF_PROF_GATEUP 4
+#define AF_PROF_DOWN 5
+#define AF_PROF_LMHEAD 6
+#define AF_PROF_FINAL 7
+#define AF_PROF_COMM 8
+#define AF_PROF_KINDS 9
+/* Run n_steps decode steps eagerly (no graph) with a CUDA event after every
+ * launch; per kind: total device ms, total algorithmic bytes and launch count
+ * (arrays of AF_PROF_KINDS).  Positions pos0.. are written like a real step. */
+cudaError_t af_engine_profile(af_engine* e, int32_t token, int32_t pos0, int n_steps, double* h_ms,
+                              double* h_bytes, int* h_count);
+/* Stream the step runs on (for event timing by the caller). */
+cudaStream_t af_engine_stream(af_engine* e);
+/* Kernel launches one decode step issues (graph nodes that are this library's). */
+int af_engine_kernels_per_step(af_engine* e);
+/* Per-step weight bytes this rank streams. */
+size_t af_engine_weight_bytes(af_engine* e);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* AF_B200_H */

@@ -1,0 +1,94 @@
+"""ctypes binding of libaf_b200.so (the C ABI declared in include/af_b200.h).
+
+The library is built in-tree (llm_core_b200/libaf_b200.so, see build.py).  There
+is no fallback: if it is missing or fails to load, every entry point raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+LIB_PATH = os.path.join(HERE, "libaf_b200.so")
+HEADER = os.path.join(ROOT, "include", "af_b200.h")
+
+_lib = None
+
+
+class AfError(RuntimeError):
+    pass
+
+
+class ModelConfig(C.Structure):
+    """af_model_config (include/af_b200.h)."""
+    _fields_ = [(n, C.c_int) for n in ("n_layer", "n_embd", "n_head", "n_kv_head", "ffn", "vocab", "n_ctx")] + \
+               [("eps", C.c_float), ("theta", C.c_float), ("qk_norm_order", C.c_int),
+                ("bos_id", C.c_int), ("eos_id", C.c_int)]
+
+
+def header_symbols() -> list[str]:
+    """Every function the public header declares."""
+    txt = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?[\w\s\*]+?\b(af_\w+)\s*\(", txt, re.M)))
+
+
+def load() -> C.CDLL:
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise AfError(f"{LIB_PATH} is missing: build it with `python -m llm_core_b200.build`")
+    # Load NCCL's soname from the same place torch does when torch is around,
+    # so a process never maps two NCCL copies.
+    try:
+        import torch  # noqa: F401
+    except Exception:
+        pass
+    lib = C.CDLL(LIB_PATH)
+    vp, i, f, sz = C.c_void_p, C.c_int, C.c_float, C.c_size_t
+    fp, ip = C.POINTER(C.c_float), C.POINTER(C.c_int32)
+    sig = {
+        "af_last_error": (C.c_char_p, []),
+        "af_device_error": (i, [C.POINTER(C.c_int), i]),
+        "af_row_stride": (sz, [i, i]),
+        "af_q6k_repack": (i, [vp, vp, i, i, vp]),
+        "af_q6k_unpack": (i, [vp, vp, i, i, vp]),
+        "af_gemv_f32": (i, [vp, vp, i, vp, i, i, vp]),
+        "af_rms_norm_f32": (i, [vp, vp, vp, i, f, vp]),
+        "af_silu_f32": (i, [vp, vp, i, vp]),
+        "af_mul_f32": (i, [vp, vp, vp, i, vp]),
+        "af_rope_f32": (i, [vp, i, i, i, f, vp]),
+        "af_nccl_unique_id": (i, [vp]),
+        "af_engine_create": (i, [C.POINTER(ModelConfig), i, i, i, vp, C.POINTER(vp)]),
+        "af_engine_destroy": (i, [vp]),
+        "af_engine_load_tensor": (i, [vp, C.c_char_p, i, C.POINTER(C.c_int64), i, vp, sz]),
+        "af_gguf_read_config": (i, [C.c_char_p, i, C.POINTER(ModelConfig)]),
+        "af_engine_load_gguf": (i, [vp, C.c_char_p]),
+        "af_engine_finalize": (i, [vp]),
+        "af_engine_step": (i, [vp, C.c_int32, C.c_int32, fp, ip]),
+        "af_engine_prefill": (i, [vp, ip, i, C.c_int32, fp, ip]),
+        "af_engine_decode_greedy": (i, [vp, C.c_int32, C.c_int32, i, ip]),
+        "af_engine_generate": (i, [vp, ip, i, i, ip, C.POINTER(C.c_int)]),
+        "af_engine_hidden": (i, [vp, fp]),
+        "af_engine_kv": (i, [vp, i, i, i, fp]),
+        "af_engine_profile": (i, [vp, C.c_int32, C.c_int32, i, C.POINTER(C.c_double), C.POINTER(C.c_double),
+                                  C.POINTER(C.c_int)]),
+        "af_engine_stream": (vp, [vp]),
+        "af_engine_kernels_per_step": (i, [vp]),
+        "af_engine_weight_bytes": (sz, [vp]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def check(rc: int, what: str = ""):
+    """Raise AfError for a non-zero cudaError_t, with the library's message."""
+    if rc != 0:
+        msg = load().af_last_error().decode(errors="replace")
+        raise AfError(f"{what}: cudaError {rc}" + (f" ({msg})" if msg else ""))

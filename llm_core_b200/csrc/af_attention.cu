@@ -1,0 +1,256 @@
+// af_attention.cu — GQA decode attention over the fp32 KV cache, fused with
+// RoPE, optional per-head Q/K RMSNorm and the KV-cache store of the new token.
+//
+// Reference: llama_forward_token (src/models/llama_model.cpp:1236-1272) —
+// RoPE (half-split, apply_rope / rope_and_store_k, :1046-1080), V copy into the
+// cache, then per head: scores = q·k_t / sqrt(hd), max-subtracted softmax
+// (:445-451), o = Σ p_t v_t, with kv head h / (H / KVH).  The reference runs
+// this serially on one thread; here it is split over (kv head, position chunk)
+// CTAs ("flash decoding"): each CTA produces an un-normalised partial
+// (o, running max, sum) and the last CTA of a kv head merges the partials with
+// the usual exp(m_s − M) rescaling.  Cache layout is the reference's:
+// [n_ctx][n_kv_heads * head_dim] per layer, fp32.
+#include "af_ops.cuh"
+
+namespace af {
+namespace {
+
+constexpr int kAttnThreads = 128;
+
+__device__ __forceinline__ void rms_norm_head(float* x, const float* w, int hd, float eps, float* red) {
+    // one warp (warp 0) normalises one head in shared memory
+    const int lane = threadIdx.x & 31;
+    float ss = 0.f;
+    for (int i = lane; i < hd; i += 32) ss += x[i] * x[i];
+    ss = warp_sum(ss);
+    const float s = 1.f / sqrtf(ss / (float)hd + eps);
+    __syncwarp();
+    for (int i = lane; i < hd; i += 32) x[i] = w[i] * (x[i] * s);
+    __syncwarp();
+    (void)red;
+}
+
+__global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_constant__ AttnParams p) {
+    extern __shared__ __align__(16) float sm[];
+    const int hd = p.head_dim, half = hd / 2;
+    const int G = p.n_heads / p.n_kv_heads;
+    const int kvh = blockIdx.x, split = blockIdx.y;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int kvd = p.n_kv_heads * hd;
+    const int chunk_max = (p.n_ctx + p.nsplit - 1) / p.nsplit;
+
+    float* qs = sm;                 // [G][hd]
+    float* ks = qs + G * hd;        // [hd]
+    float* vs = ks + hd;            // [hd]
+    float* sc = vs + hd;            // [G][chunk_max]
+    float* red = sc + G * chunk_max;  // [64]
+
+    pdl_launch_dependents();
+    pdl_wait();
+    const int pos = *p.pos;
+    const int seq = pos + 1;
+    const float* cr = p.cos_t + (size_t)pos * half;
+    const float* sr = p.sin_t + (size_t)pos * half;
+
+    // ---- load q (G heads), k, v of the new token
+    for (int i = tid; i < G * hd; i += kAttnThreads) qs[i] = p.q[(size_t)kvh * G * hd + i];
+    for (int i = tid; i < hd; i += kAttnThreads) {
+        ks[i] = p.k[(size_t)kvh * hd + i];
+        vs[i] = p.v[(size_t)kvh * hd + i];
+    }
+    __syncthreads();
+    if (p.qk_norm_order == 1 && warp == 0) {  // qwen3: per-head norm before RoPE
+        if (p.q_norm) for (int g = 0; g < G; ++g) rms_norm_head(qs + g * hd, p.q_norm, hd, p.eps, red);
+        if (p.k_norm) rms_norm_head(ks, p.k_norm, hd, p.eps, red);
+    }
+    __syncthreads();
+    // RoPE: pairs (i, i + hd/2)
+    for (int idx = tid; idx < (G + 1) * half; idx += kAttnThreads) {
+        const int g = idx / half, i = idx % half;
+        float* hp = g < G ? qs + g * hd : ks;
+        const float x0 = hp[i], x1 = hp[i + half];
+        hp[i] = x0 * cr[i] - x1 * sr[i];
+        hp[i + half] = x0 * sr[i] + x1 * cr[i];
+    }
+    __syncthreads();
+    if (p.qk_norm_order == 2 && warp == 0) {  // hunyuan: per-head norm after RoPE
+        if (p.q_norm) for (int g = 0; g < G; ++g) rms_norm_head(qs + g * hd, p.q_norm, hd, p.eps, red);
+        if (p.k_norm) rms_norm_head(ks, p.k_norm, hd, p.eps, red);
+    }
+    __syncthreads();
+    if (split == 0) {
+        for (int i = tid; i < hd; i += kAttnThreads) {
+            p.kc[(size_t)pos * kvd + (size_t)kvh * hd + i] = ks[i];
+            p.vc[(size_t)pos * kvd + (size_t)kvh * hd + i] = vs[i];
+        }
+    }
+
+    // ---- this CTA's positions
+    const int chunk = (seq + p.nsplit - 1) / p.nsplit;
+    const int t0 = split * chunk;
+    const int t1 = min(seq, t0 + chunk);
+    const int nt = max(0, t1 - t0);
+
+    // scores: one warp per position, lanes over the head dims
+    for (int j = warp; j < nt; j += kAttnThreads / 32) {
+        const int t = t0 + j;
+        const float* kr = (t == pos) ? ks : p.kc + (size_t)t * kvd + (size_t)kvh * hd;
+        float kv[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) kv[k] = (lane + 32 * k < hd) ? kr[lane + 32 * k] : 0.f;
+        for (int g = 0; g < G; ++g) {
+            float s = 0.f;
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                if (lane + 32 * k < hd) s += qs[g * hd + lane + 32 * k] * kv[k];
+            s = warp_sum(s);
+            if (lane == 0) sc[g * chunk_max + j] = s * p.scale;
+        }
+    }
+    __syncthreads();
+    // softmax pieces per head: warp w handles heads w, w+4, ...
+    float* mrow = red;       // [G] (G <= 32)
+    float* lrow = red + 32;  // [G]
+    for (int g = warp; g < G; g += kAttnThreads / 32) {
+        float m = -INFINITY;
+        for (int j = lane; j < nt; j += 32) m = fmaxf(m, sc[g * chunk_max + j]);
+        m = warp_max(m);
+        float l = 0.f;
+        for (int j = lane; j < nt; j += 32) {
+            const float e = expf(sc[g * chunk_max + j] - m);
+            sc[g * chunk_max + j] = e;
+            l += e;
+        }
+        l = warp_sum(l);
+        if (lane == 0) { mrow[g] = m; lrow[g] = l; }
+    }
+    __syncthreads();
+    // o_g[d] = Σ_t e_t v_t[d]; threads over (d, position parity)
+    const int lanes_per_pos = hd;  // hd <= 128
+    const int npar = kAttnThreads / lanes_per_pos;  // 1 (hd=128) or 2 (hd=64)
+    const int d = tid % lanes_per_pos, par = tid / lanes_per_pos;
+    float acc[16];
+#pragma unroll
+    for (int g = 0; g < 16; ++g) acc[g] = 0.f;
+    if (par < npar) {
+        for (int j = par; j < nt; j += npar) {
+            const int t = t0 + j;
+            const float vv = (t == pos) ? vs[d] : p.vc[(size_t)t * kvd + (size_t)kvh * hd + d];
+#pragma unroll
+            for (int g = 0; g < 16; ++g)
+                if (g < G) acc[g] = fmaf(sc[g * chunk_max + j], vv, acc[g]);
+        }
+    }
+    __syncthreads();
+    // reduce the parities through shared memory (reuse the score area)
+    if (npar > 1) {  // the q area ([G][hd]) is free again and holds the second parity
+        if (par == 1) {
+#pragma unroll
+            for (int g = 0; g < 16; ++g)
+                if (g < G) qs[g * hd + d] = acc[g];
+        }
+        __syncthreads();
+        if (par == 0) {
+#pragma unroll
+            for (int g = 0; g < 16; ++g)
+                if (g < G) acc[g] += qs[g * hd + d];
+        }
+    }
+    if (par == 0) {
+#pragma unroll
+        for (int g = 0; g < 16; ++g) {
+            if (g >= G) break;
+            const int h = kvh * G + g;
+            float* dst = p.part + ((size_t)h * p.nsplit + split) * (hd + 2);
+            dst[d] = acc[g];
+            if (d == 0) {
+                dst[hd] = nt > 0 ? mrow[g] : -INFINITY;
+                dst[hd + 1] = nt > 0 ? lrow[g] : 0.f;
+            }
+        }
+    }
+    // ---- last CTA of this kv head merges the splits
+    __threadfence();
+    __syncthreads();
+    __shared__ unsigned int last;
+    if (tid == 0) last = (atomicAdd(&p.counter[kvh], 1u) == (unsigned)(p.nsplit - 1)) ? 1u : 0u;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    for (int idx = tid; idx < G * hd; idx += kAttnThreads) {
+        const int g = idx / hd, dd = idx % hd;
+        const int h = kvh * G + g;
+        const float* base = p.part + (size_t)h * p.nsplit * (hd + 2);
+        float M = -INFINITY;
+        for (int s = 0; s < p.nsplit; ++s) M = fmaxf(M, base[s * (hd + 2) + hd]);
+        float L = 0.f, O = 0.f;
+        for (int s = 0; s < p.nsplit; ++s) {
+            const float ms = base[s * (hd + 2) + hd];
+            if (ms == -INFINITY) continue;
+            const float w = expf(ms - M);
+            L += base[s * (hd + 2) + hd + 1] * w;
+            O += base[s * (hd + 2) + dd] * w;
+        }
+        p.out[(size_t)h * hd + dd] = O / L;
+    }
+    if (tid == 0) p.counter[kvh] = 0u;
+}
+
+__global__ void finalize_kernel(const unsigned long long* key, int* token, int* pos, int* hist) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const unsigned long long k = *key;
+    const int id = (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
+    const int ps = *pos;
+    *token = id;
+    if (hist) hist[ps] = id;
+    *pos = ps + 1;
+}
+
+}  // namespace
+
+cudaError_t attention_init() {
+    return cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+}
+
+int attention_smem_bytes(const AttnParams& p) {
+    const int G = p.n_heads / p.n_kv_heads;
+    const int chunk_max = (p.n_ctx + p.nsplit - 1) / p.nsplit;
+    return (G * p.head_dim + 2 * p.head_dim + G * chunk_max + 64) * (int)sizeof(float);
+}
+
+cudaError_t attention_launch(const AttnParams& p, cudaStream_t st, bool pdl) {
+    const int G = p.n_heads / p.n_kv_heads;
+    if (G > 16 || p.head_dim > 128 || (p.head_dim != 64 && p.head_dim != 128) || p.n_heads % p.n_kv_heads) {
+        set_last_error("attention: need head_dim in {64,128} and n_heads/n_kv_heads <= 16");
+        return cudaErrorInvalidValue;
+    }
+    const int smem = attention_smem_bytes(p);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.n_kv_heads, p.nsplit);
+    cfg.blockDim = dim3(kAttnThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, attention_kernel, p);
+}
+
+cudaError_t finalize_launch(const unsigned long long* key, int* token, int* pos, int* hist, cudaStream_t st,
+                            bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(32);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, finalize_kernel, key, token, pos, hist);
+}
+
+}  // namespace af

@@ -1,0 +1,792 @@
+// af_engine.cu — GPU-resident LLaMA-family decode engine behind the C ABI.
+//
+// Replaces llama_cuda_generate (include/axonforge/models/llama_cuda.hpp:25-28,
+// whose reference body falls back to the CPU, src/models/llama_cuda_model.cpp:7-17)
+// with the forward of llama_forward_token (src/models/llama_model.cpp:1207-1333)
+// on the device:
+//
+//   embed ─┬─ per layer: [RMSNorm→QKV GEMV(+bias)] → [RoPE+KV store+attention]
+//          │             → [O GEMV + residual] → [RMSNorm→gate/up GEMV→SwiGLU]
+//          │             → [down GEMV + residual]
+//          └─ [final RMSNorm→LM head GEMV→argmax] → [id → next step's input]
+//
+// 5·L + 3 kernels per token, launched with programmatic dependent launch and
+// captured once into a CUDA graph; the token id and position live in device
+// memory, so consecutive steps chain on the device without a host round trip.
+//
+// Tensor parallelism (tp_size > 1, one process per GPU): attention heads and
+// FFN rows are column-parallel, attn_output / ffn_down are row-parallel over
+// whole 256-value super-blocks, the LM head is split over the vocabulary.
+// attn_output and ffn_down write partial sums that one NCCL all-reduce (fp32
+// sum) combines; the next GEMV's prologue adds them to the replicated residual.
+// The argmax is one all-reduce (max) of a packed (value, ~index) key.
+#include <nccl.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "af_gemv.cuh"
+#include "af_gguf.h"
+#include "af_ops.cuh"
+
+using namespace af;
+
+namespace {
+
+struct DevMat {
+    uint8_t* w = nullptr;
+    int type = -1;
+    int rows = 0, cols = 0;  // local shard shape
+    int stride = 0;
+    bool present() const { return w != nullptr; }
+};
+
+struct LayerW {
+    float *attn_norm = nullptr, *ffn_norm = nullptr, *bq = nullptr, *bk = nullptr, *bv = nullptr;
+    float *q_norm = nullptr, *k_norm = nullptr;
+    DevMat wq, wk, wv, wo, wg, wu, wd;
+};
+
+// [lo, hi) of `n` super-blocks for rank r of t, remainder to the low ranks
+// (ffn_down K = 11008 = 43 blocks splits 22/21, 11/11/11/10, 6,6,6,5,5,5,5,5).
+void block_split(int n, int r, int t, int& lo, int& hi) {
+    const int base = n / t, rem = n % t;
+    lo = r * base + (r < rem ? r : rem);
+    hi = lo + base + (r < rem ? 1 : 0);
+}
+
+}  // namespace
+
+struct af_engine {
+    af_model_config cfg{};
+    int device = 0, rank = 0, tp = 1;
+    ncclComm_t comm = nullptr;
+    cudaStream_t stream = nullptr;
+    int sms = 148;
+
+    // local shard geometry
+    int hd = 0, Hl = 0, KVl = 0, F0 = 0, F1 = 0, Fl = 0, V0 = 0, V1 = 0, Vl = 0, Vmax = 0;
+
+    // weights
+    DevMat tok_embd, output;
+    float* out_norm = nullptr;
+    std::vector<LayerW> layers;
+    std::vector<void*> allocs;
+    size_t weight_bytes = 0;
+
+    // activations / state
+    float* x[2] = {nullptr, nullptr};
+    float *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr, *h = nullptr, *ypart = nullptr;
+    float *logits = nullptr, *logits_all = nullptr;
+    float *kcache = nullptr, *vcache = nullptr, *cos_t = nullptr, *sin_t = nullptr, *apart = nullptr;
+    unsigned int* acount = nullptr;
+    unsigned long long* key = nullptr;
+    int* tokpos = nullptr;  // [0] token, [1] pos
+    int* hist = nullptr;
+    int* h_tokpos = nullptr;  // pinned host mirror
+    int nsplit = 1;
+
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t gexec = nullptr;
+    bool finalized = false;
+    int kernels_per_step = 0;
+
+    void* dalloc(size_t bytes) {
+        void* p = nullptr;
+        if (cudaMalloc(&p, bytes ? bytes : 16) != cudaSuccess) throw std::runtime_error("cudaMalloc failed");
+        allocs.push_back(p);
+        return p;
+    }
+};
+
+namespace {
+
+cudaError_t fail(const std::string& msg, cudaError_t code = cudaErrorInvalidValue) {
+    set_last_error(msg);
+    return code;
+}
+
+#define ENG_TRY(x)                                                                          \
+    do {                                                                                    \
+        cudaError_t e_ = (x);                                                               \
+        if (e_ != cudaSuccess) return fail(std::string(#x) + ": " + cudaGetErrorString(e_), e_); \
+    } while (0)
+
+#define NCCL_TRY(x)                                                                         \
+    do {                                                                                    \
+        ncclResult_t r_ = (x);                                                              \
+        if (r_ != ncclSuccess) return fail(std::string(#x) + ": " + ncclGetErrorString(r_), cudaErrorUnknown); \
+    } while (0)
+
+// Upload rows [r0, r1) x blocks [b0, b1) of a GGUF matrix (rows of `cols`
+// values) from host memory into a new device buffer in the device layout.
+cudaError_t upload_matrix(af_engine* e, DevMat& m, int type, const uint8_t* h, int cols, int r0, int r1, int b0,
+                          int b1) {
+    const int bb = type == AF_GGML_Q6_K ? 210 : (type == AF_GGML_Q4_K ? 144 : 0);
+    if (!bb) return fail("unsupported matrix type " + std::to_string(type) + " (Q4_K / Q6_K only)");
+    const size_t src_rb = (size_t)(cols / 256) * bb;
+    const int lcols = (b1 - b0) * 256, rows = r1 - r0;
+    const size_t gg_rb = (size_t)(b1 - b0) * bb;
+    m.type = type;
+    m.rows = rows;
+    m.cols = lcols;
+    m.stride = dev_row_stride(type, lcols);
+    m.w = static_cast<uint8_t*>(e->dalloc((size_t)rows * m.stride + 64));
+    uint8_t* stage = m.w;
+    if (type == AF_GGML_Q6_K) ENG_TRY(cudaMalloc(&stage, (size_t)rows * gg_rb + 16));
+    const uint8_t* src = h + (size_t)r0 * src_rb + (size_t)b0 * bb;
+    ENG_TRY(cudaMemcpy2D(stage, gg_rb, src, src_rb, gg_rb, rows, cudaMemcpyHostToDevice));
+    if (type == AF_GGML_Q6_K) {
+        ENG_TRY(q6k_repack(m.w, stage, rows, lcols, false, e->stream));
+        ENG_TRY(cudaStreamSynchronize(e->stream));
+        cudaFree(stage);
+    }
+    e->weight_bytes += (size_t)rows * m.stride;
+    return cudaSuccess;
+}
+
+cudaError_t upload_f32(af_engine* e, float*& dst, const void* h, size_t n, size_t off = 0) {
+    dst = static_cast<float*>(e->dalloc(n * 4));
+    ENG_TRY(cudaMemcpy(dst, static_cast<const float*>(h) + off, n * 4, cudaMemcpyHostToDevice));
+    return cudaSuccess;
+}
+
+GemvParams base_params(const af_engine* e, int K) {
+    GemvParams p = {};
+    p.K = K;
+    p.eps = e->cfg.eps;
+    return p;
+}
+
+GemvSeg seg_of(const DevMat& m, float* y, const float* bias) {
+    GemvSeg s = {};
+    s.w = m.w;
+    s.y = y;
+    s.bias = bias;
+    s.type = m.type;
+    s.rows = m.rows;
+    s.row_stride = m.stride;
+    return s;
+}
+
+// Event-bracketed eager launches for af_engine_profile: one event after every
+// launch; kind k of launch i is kinds[i], its algorithmic bytes bytes[i].
+struct Prof {
+    std::vector<cudaEvent_t> ev;
+    std::vector<int> kinds;
+    std::vector<double> bytes;
+    int pos = 0;
+    cudaError_t mark(cudaStream_t st, int kind, double b) {
+        cudaEvent_t x;
+        AF_CUDA_TRY(cudaEventCreate(&x));
+        AF_CUDA_TRY(cudaEventRecord(x, st));
+        ev.push_back(x);
+        kinds.push_back(kind);
+        bytes.push_back(b);
+        return cudaSuccess;
+    }
+};
+
+double gemv_bytes(const GemvParams& p) {
+    double b = (double)p.K * 4 * (p.x_add ? 2 : 1);
+    for (int s = 0; s < p.nseg; ++s) b += (double)p.seg[s].rows * (p.seg[s].row_stride + 4);
+    return b;
+}
+
+// Enqueue one decode step (token/pos read from device memory) on e->stream.
+// With `prof`, every launch is followed by a timing event (no graph capture).
+cudaError_t enqueue_step(af_engine* e, Prof* prof = nullptr) {
+#define AF_MARK(kind, b) \
+    if (prof) AF_CUDA_TRY(prof->mark(e->stream, kind, b))
+    const auto& c = e->cfg;
+    const int E = c.n_embd;
+    const bool tp = e->tp > 1;
+    int nk = 0;
+    int cur = 0;  // residual buffer holding the current stream (TP ping-pong)
+    ENG_TRY(embed_launch(e->x[0], e->tok_embd.w, e->tok_embd.type, E, e->tok_embd.stride, &e->tokpos[0], e->key,
+                         e->stream, true));
+    ++nk;
+    AF_MARK(AF_PROF_EMBED, (double)e->tok_embd.stride + E * 4.0);
+    bool pending = false;  // TP: ypart holds an un-added partial sum
+    for (int l = 0; l < c.n_layer; ++l) {
+        const LayerW& L = e->layers[l];
+        // --- RMSNorm + QKV
+        {
+            GemvParams p = base_params(e, E);
+            p.seg[0] = seg_of(L.wq, e->q, L.bq);
+            p.seg[1] = seg_of(L.wk, e->k, L.bk);
+            p.seg[2] = seg_of(L.wv, e->v, L.bv);
+            p.nseg = 3;
+            p.x = e->x[cur];
+            if (pending) {
+                p.x_add = e->ypart;
+                p.x_store = e->x[cur ^ 1];
+                cur ^= 1;
+            }
+            p.norm_w = L.attn_norm;
+            p.epi = EPI_STORE;
+            gemv_configure(p);
+            ENG_TRY(gemv_launch(p, e->sms, e->stream, true));
+            ++nk;
+            AF_MARK(AF_PROF_QKV, gemv_bytes(p));
+        }
+        // --- attention (RoPE, KV store, GQA softmax)
+        {
+            AttnParams a = {};
+            a.q = e->q;
+            a.k = e->k;
+            a.v = e->v;
+            const size_t lsz = (size_t)c.n_ctx * e->KVl * e->hd;
+            a.kc = e->kcache + (size_t)l * lsz;
+            a.vc = e->vcache + (size_t)l * lsz;
+            a.out = e->attn;
+            a.cos_t = e->cos_t;
+            a.sin_t = e->sin_t;
+            a.q_norm = L.q_norm;
+            a.k_norm = L.k_norm;
+            a.part = e->apart;
+            a.counter = e->acount;
+            a.pos = &e->tokpos[1];
+            a.n_heads = e->Hl;
+            a.n_kv_heads = e->KVl;
+            a.head_dim = e->hd;
+            a.n_ctx = c.n_ctx;
+            a.nsplit = e->nsplit;
+            a.qk_norm_order = c.qk_norm_order;
+            a.eps = c.eps;
+            a.scale = 1.f / std::sqrt((float)e->hd);
+            ENG_TRY(attention_launch(a, e->stream, true));
+            ++nk;
+            if (prof) {
+                const double kvb = 2.0 * (prof->pos + 1) * e->KVl * e->hd * 4.0;
+                AF_MARK(AF_PROF_ATTN, kvb + 2.0 * e->Hl * e->hd * 4.0);
+            }
+        }
+        // --- O projection (+ residual)
+        {
+            GemvParams p = base_params(e, e->Hl * e->hd);
+            p.seg[0] = seg_of(L.wo, e->ypart, nullptr);
+            p.nseg = 1;
+            p.x = e->attn;
+            if (tp) {
+                p.epi = EPI_STORE;
+            } else {
+                p.epi = EPI_RESID;
+                p.resid = e->x[cur];
+            }
+            gemv_configure(p);
+            ENG_TRY(gemv_launch(p, e->sms, e->stream, true));
+            ++nk;
+            AF_MARK(AF_PROF_O, gemv_bytes(p));
+            if (tp) {
+                NCCL_TRY(ncclAllReduce(e->ypart, e->ypart, E, ncclFloat32, ncclSum, e->comm, e->stream));
+                pending = true;
+                AF_MARK(AF_PROF_COMM, E * 4.0);
+            }
+        }
+        // --- RMSNorm + gate/up + SwiGLU
+        {
+            GemvParams p = base_params(e, E);
+            p.seg[0] = seg_of(L.wg, e->h, nullptr);
+            p.seg[1] = seg_of(L.wu, nullptr, nullptr);
+            p.nseg = 2;
+            p.x = e->x[cur];
+            if (pending) {
+                p.x_add = e->ypart;
+                p.x_store = e->x[cur ^ 1];
+                cur ^= 1;
+                pending = false;
+            }
+            p.norm_w = L.ffn_norm;
+            p.epi = EPI_SWIGLU;
+            gemv_configure(p);
+            ENG_TRY(gemv_launch(p, e->sms, e->stream, true));
+            ++nk;
+            AF_MARK(AF_PROF_GATEUP, gemv_bytes(p) - 4.0 * p.seg[1].rows);
+        }
+        // --- down projection (+ residual)
+        {
+            GemvParams p = base_params(e, e->Fl);
+            p.seg[0] = seg_of(L.wd, e->ypart, nullptr);
+            p.nseg = 1;
+            p.x = e->h;
+            if (tp) {
+                p.epi = EPI_STORE;
+            } else {
+                p.epi = EPI_RESID;
+                p.resid = e->x[cur];
+            }
+            gemv_configure(p);
+            ENG_TRY(gemv_launch(p, e->sms, e->stream, true));
+            ++nk;
+            AF_MARK(AF_PROF_DOWN, gemv_bytes(p));
+            if (tp) {
+                NCCL_TRY(ncclAllReduce(e->ypart, e->ypart, E, ncclFloat32, ncclSum, e->comm, e->stream));
+                pending = true;
+                AF_MARK(AF_PROF_COMM, E * 4.0);
+            }
+        }
+    }
+    // --- final RMSNorm + LM head + argmax
+    {
+        GemvParams p = base_params(e, E);
+        p.seg[0] = seg_of(e->output, e->logits, nullptr);
+        p.nseg = 1;
+        p.x = e->x[cur];
+        if (pending) {
+            p.x_add = e->ypart;
+            p.x_store = e->x[cur ^ 1];
+            cur ^= 1;
+        }
+        p.norm_w = e->out_norm;
+        p.epi = EPI_ARGMAX;
+        p.argmax = e->key;
+        p.argmax_base = e->V0;
+        gemv_configure(p);
+        ENG_TRY(gemv_launch(p, e->sms, e->stream, true));
+        ++nk;
+        AF_MARK(AF_PROF_LMHEAD, gemv_bytes(p));
+        if (tp) {
+            NCCL_TRY(ncclAllReduce(e->key, e->key, 1, ncclUint64, ncclMax, e->comm, e->stream));
+            AF_MARK(AF_PROF_COMM, 8.0);
+        }
+    }
+    if (cur != 0) return fail("internal: residual ping-pong did not return to buffer 0");
+    ENG_TRY(finalize_launch(e->key, &e->tokpos[0], &e->tokpos[1], e->hist, e->stream, true));
+    ++nk;
+    AF_MARK(AF_PROF_FINAL, 16.0);
+    e->kernels_per_step = nk;
+    return cudaSuccess;
+#undef AF_MARK
+}
+
+cudaError_t gather_logits(af_engine* e, float* h_logits) {
+    if (e->tp == 1) {
+        ENG_TRY(cudaMemcpyAsync(h_logits, e->logits, (size_t)e->Vl * 4, cudaMemcpyDeviceToHost, e->stream));
+        return cudaSuccess;
+    }
+    NCCL_TRY(ncclAllGather(e->logits, e->logits_all, e->Vmax, ncclFloat32, e->comm, e->stream));
+    ENG_TRY(cudaStreamSynchronize(e->stream));
+    int off = 0;
+    for (int r = 0; r < e->tp; ++r) {
+        int lo, hi;
+        block_split(e->cfg.vocab, r, e->tp, lo, hi);
+        ENG_TRY(cudaMemcpy(h_logits + off, e->logits_all + (size_t)r * e->Vmax, (size_t)(hi - lo) * 4,
+                           cudaMemcpyDeviceToHost));
+        off += hi - lo;
+    }
+    return cudaSuccess;
+}
+
+}  // namespace
+
+extern "C" {
+
+cudaError_t af_nccl_unique_id(void* h_id) {
+    if (!h_id) return fail("af_nccl_unique_id: null");
+    ncclUniqueId id;
+    NCCL_TRY(ncclGetUniqueId(&id));
+    std::memcpy(h_id, &id, sizeof(id));
+    return cudaSuccess;
+}
+
+cudaError_t af_engine_create(const af_model_config* cfg, int device, int tp_rank, int tp_size, const void* nccl_id,
+                             af_engine** out) {
+    if (!cfg || !out) return fail("af_engine_create: null argument");
+    *out = nullptr;
+    const auto& c = *cfg;
+    if (c.n_embd % 256 || c.ffn % 256 || c.n_head <= 0 || c.n_embd % c.n_head || c.n_kv_head <= 0 ||
+        c.n_head % c.n_kv_head || c.n_layer <= 0 || c.vocab <= 0 || c.n_ctx <= 0)
+        return fail("af_engine_create: unsupported model shape (n_embd, ffn multiples of 256)");
+    if (tp_size < 1 || tp_rank < 0 || tp_rank >= tp_size) return fail("af_engine_create: bad tp rank/size");
+    if (tp_size > 1 && (c.n_kv_head % tp_size || ((c.n_embd / tp_size) % 256)))
+        return fail("af_engine_create: tensor parallel needs n_kv_head and n_embd/256 divisible by tp_size");
+    std::unique_ptr<af_engine> e(new af_engine());
+    e->cfg = c;
+    e->device = device;
+    e->rank = tp_rank;
+    e->tp = tp_size;
+    ENG_TRY(cudaSetDevice(device));
+    ENG_TRY(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
+    e->sms = num_sms();
+    e->hd = c.n_embd / c.n_head;
+    e->Hl = c.n_head / tp_size;
+    e->KVl = c.n_kv_head / tp_size;
+    int f0, f1;
+    block_split(c.ffn / 256, tp_rank, tp_size, f0, f1);
+    e->F0 = f0 * 256;
+    e->F1 = f1 * 256;
+    e->Fl = e->F1 - e->F0;
+    block_split(c.vocab, tp_rank, tp_size, e->V0, e->V1);
+    e->Vl = e->V1 - e->V0;
+    e->Vmax = (c.vocab + tp_size - 1) / tp_size;
+    e->layers.resize(c.n_layer);
+    if (tp_size > 1) {
+        if (!nccl_id) return fail("af_engine_create: tp_size > 1 needs an ncclUniqueId");
+        ncclUniqueId id;
+        std::memcpy(&id, nccl_id, sizeof(id));
+        NCCL_TRY(ncclCommInitRank(&e->comm, tp_size, id, tp_rank));
+    }
+    *out = e.release();
+    return cudaSuccess;
+}
+
+cudaError_t af_engine_destroy(af_engine* e) {
+    if (!e) return cudaSuccess;
+    cudaSetDevice(e->device);
+    if (e->gexec) cudaGraphExecDestroy(e->gexec);
+    if (e->graph) cudaGraphDestroy(e->graph);
+    for (void* p : e->allocs) cudaFree(p);
+    if (e->h_tokpos) cudaFreeHost(e->h_tokpos);
+    if (e->comm) ncclCommDestroy(e->comm);
+    if (e->stream) cudaStreamDestroy(e->stream);
+    delete e;
+    return cudaSuccess;
+}
+
+cudaError_t af_engine_load_tensor(af_engine* e, const char* name_c, int type, const int64_t* dims, int n_dims,
+                                  const void* h_data, size_t nbytes) {
+    if (!e || !name_c || !dims || !h_data) return fail("af_engine_load_tensor: null argument");
+    if (e->finalized) return fail("af_engine_load_tensor: engine already finalized");
+    ENG_TRY(cudaSetDevice(e->device));
+    const std::string name(name_c);
+    int64_t numel = 1;
+    for (int i = 0; i < n_dims; ++i) numel *= dims[i];
+    if (ggml_nbytes(type, numel) != nbytes)
+        return fail("af_engine_load_tensor: " + name + ": byte size does not match its type and shape");
+    const auto& c = e->cfg;
+    const int cols = (int)dims[0];
+    const int rows = n_dims > 1 ? (int)(numel / dims[0]) : 1;
+    const uint8_t* hb = static_cast<const uint8_t*>(h_data);
+    const int E = c.n_embd, hd = e->hd;
+    auto need_f32 = [&](size_t n) -> bool { return type == AF_GGML_F32 && (size_t)numel == n; };
+    if (name == "token_embd.weight") {
+        if (cols != E || rows != c.vocab) return fail("token_embd.weight: shape mismatch");
+        return upload_matrix(e, e->tok_embd, type, hb, cols, 0, rows, 0, cols / 256);
+    }
+    if (name == "output.weight") {
+        if (cols != E || rows != c.vocab) return fail("output.weight: shape mismatch");
+        return upload_matrix(e, e->output, type, hb, cols, e->V0, e->V1, 0, cols / 256);
+    }
+    if (name == "output_norm.weight") {
+        if (!need_f32(E)) return fail("output_norm.weight: need f32[n_embd]");
+        return upload_f32(e, e->out_norm, h_data, E);
+    }
+    int l = -1;
+    char field[96] = {0};
+    if (std::sscanf(name_c, "blk.%d.%95s", &l, field) != 2 || l < 0 || l >= c.n_layer)
+        return cudaSuccess;  // tensors outside the decode path are ignored
+    LayerW& L = e->layers[l];
+    const std::string f(field);
+    const int q0 = e->rank * e->Hl * hd, q1 = q0 + e->Hl * hd;
+    const int k0 = e->rank * e->KVl * hd, k1 = k0 + e->KVl * hd;
+    if (f == "attn_norm.weight") return need_f32(E) ? upload_f32(e, L.attn_norm, h_data, E) : fail(name + ": need f32[n_embd]");
+    if (f == "ffn_norm.weight") return need_f32(E) ? upload_f32(e, L.ffn_norm, h_data, E) : fail(name + ": need f32[n_embd]");
+    if (f == "attn_q_norm.weight") return need_f32(hd) ? upload_f32(e, L.q_norm, h_data, hd) : fail(name + ": need f32[head_dim]");
+    if (f == "attn_k_norm.weight") return need_f32(hd) ? upload_f32(e, L.k_norm, h_data, hd) : fail(name + ": need f32[head_dim]");
+    if (f == "attn_q.bias") return need_f32(E) ? upload_f32(e, L.bq, h_data, q1 - q0, q0) : fail(name + ": shape");
+    if (f == "attn_k.bias") return need_f32((size_t)c.n_kv_head * hd) ? upload_f32(e, L.bk, h_data, k1 - k0, k0) : fail(name + ": shape");
+    if (f == "attn_v.bias") return need_f32((size_t)c.n_kv_head * hd) ? upload_f32(e, L.bv, h_data, k1 - k0, k0) : fail(name + ": shape");
+    if (f == "attn_q.weight") {
+        if (cols != E || rows != E) return fail(name + ": shape mismatch");
+        return upload_matrix(e, L.wq, type, hb, cols, q0, q1, 0, cols / 256);
+    }
+    if (f == "attn_k.weight" || f == "attn_v.weight") {
+        if (cols != E || rows != c.n_kv_head * hd) return fail(name + ": shape mismatch");
+        return upload_matrix(e, f == "attn_k.weight" ? L.wk : L.wv, type, hb, cols, k0, k1, 0, cols / 256);
+    }
+    if (f == "attn_output.weight") {
+        if (cols != E || rows != E) return fail(name + ": shape mismatch");
+        return upload_matrix(e, L.wo, type, hb, cols, 0, rows, q0 / 256, q1 / 256);
+    }
+    if (f == "ffn_gate.weight" || f == "ffn_up.weight") {
+        if (cols != E || rows != c.ffn) return fail(name + ": shape mismatch");
+        return upload_matrix(e, f == "ffn_gate.weight" ? L.wg : L.wu, type, hb, cols, e->F0, e->F1, 0, cols / 256);
+    }
+    if (f == "ffn_down.weight") {
+        if (cols != c.ffn || rows != E) return fail(name + ": shape mismatch");
+        return upload_matrix(e, L.wd, type, hb, cols, 0, rows, e->F0 / 256, e->F1 / 256);
+    }
+    return cudaSuccess;
+}
+
+cudaError_t af_gguf_read_config(const char* path, int max_context_len, af_model_config* cfg_out) {
+    try {
+        GgufFile g;
+        g.open(path);
+        // Engine::from_gguf (src/engine.cpp:85-118)
+        const std::string a = g.get_str("general.architecture", "unknown");
+        af_model_config c = {};
+        c.n_layer = (int)g.get_int(a + ".block_count", 0);
+        c.n_embd = (int)g.get_int(a + ".embedding_length", 0);
+        c.ffn = (int)g.get_int(a + ".feed_forward_length", 0);
+        c.n_head = (int)g.get_int(a + ".attention.head_count", 0);
+        c.n_kv_head = (int)g.get_int(a + ".attention.head_count_kv", c.n_head);
+        const int ctx = (int)g.get_int(a + ".context_length", 4096);
+        c.n_ctx = std::min(ctx, max_context_len > 0 ? max_context_len : 4096);
+        c.eps = (float)g.get_float(a + ".attention.layer_norm_rms_epsilon", 1e-5);
+        c.theta = (float)g.get_float(a + ".rope.freq_base", 10000.0);
+        c.vocab = (int)g.array_count("tokenizer.ggml.tokens");
+        if (c.vocab <= 0) c.vocab = 32000;
+        if (c.eps <= 0.f) c.eps = 1e-5f;
+        if (c.theta <= 0.f) c.theta = 10000.f;
+        if (c.ffn <= 0) c.ffn = 4 * c.n_embd;
+        c.qk_norm_order = a == "hunyuan-dense" ? 2 : (a == "qwen3" ? 1 : 0);
+        c.bos_id = (int)g.get_int("tokenizer.ggml.bos_token_id", 1);
+        c.eos_id = (int)g.get_int("tokenizer.ggml.eos_token_id", 2);
+        if (cfg_out) *cfg_out = c;
+        return cudaSuccess;
+    } catch (const std::exception& ex) {
+        return fail(ex.what());
+    }
+}
+
+cudaError_t af_engine_load_gguf(af_engine* e, const char* path) {
+    try {
+        GgufFile g;
+        g.open(path);
+        for (const auto& t : g.tensors()) {
+            cudaError_t r = af_engine_load_tensor(e, t.name.c_str(), t.type, t.dims.data(), (int)t.dims.size(),
+                                                  g.data(t), t.nbytes);
+            if (r != cudaSuccess) return r;
+        }
+        return cudaSuccess;
+    } catch (const std::exception& ex) {
+        return fail(ex.what());
+    }
+}
+
+cudaError_t af_engine_finalize(af_engine* e) {
+    if (!e) return fail("af_engine_finalize: null engine");
+    if (e->finalized) return cudaSuccess;
+    ENG_TRY(cudaSetDevice(e->device));
+    const auto& c = e->cfg;
+    try {
+        if (!e->tok_embd.present()) return fail("missing token_embd.weight");
+        if (!e->out_norm) return fail("missing output_norm.weight");
+        if (!e->output.present()) {
+            // tied head: output falls back to token_embd (make_wt_opt, llama_model.cpp:979)
+            e->output = e->tok_embd;
+            e->output.w = e->tok_embd.w + (size_t)e->V0 * e->tok_embd.stride;
+            e->output.rows = e->Vl;
+            e->weight_bytes += (size_t)e->Vl * e->tok_embd.stride;
+        }
+        // The embedding table is read one row per step: not part of the per-token stream.
+        e->weight_bytes -= (size_t)c.vocab * e->tok_embd.stride;
+        for (int l = 0; l < c.n_layer; ++l) {
+            const LayerW& L = e->layers[l];
+            if (!L.attn_norm || !L.ffn_norm || !L.wq.present() || !L.wk.present() || !L.wv.present() ||
+                !L.wo.present() || !L.wg.present() || !L.wu.present() || !L.wd.present())
+                return fail("missing weights for layer " + std::to_string(l));
+        }
+        const int E = c.n_embd, hd = e->hd;
+        e->x[0] = static_cast<float*>(e->dalloc((size_t)E * 4));
+        e->x[1] = static_cast<float*>(e->dalloc((size_t)E * 4));
+        e->q = static_cast<float*>(e->dalloc((size_t)e->Hl * hd * 4));
+        e->k = static_cast<float*>(e->dalloc((size_t)e->KVl * hd * 4));
+        e->v = static_cast<float*>(e->dalloc((size_t)e->KVl * hd * 4));
+        e->attn = static_cast<float*>(e->dalloc((size_t)e->Hl * hd * 4));
+        e->h = static_cast<float*>(e->dalloc((size_t)e->Fl * 4));
+        e->ypart = static_cast<float*>(e->dalloc((size_t)E * 4));
+        e->logits = static_cast<float*>(e->dalloc((size_t)e->Vmax * 4));
+        if (e->tp > 1) e->logits_all = static_cast<float*>(e->dalloc((size_t)e->Vmax * e->tp * 4));
+        const size_t kvn = (size_t)c.n_layer * c.n_ctx * e->KVl * hd;
+        e->kcache = static_cast<float*>(e->dalloc(kvn * 4));
+        e->vcache = static_cast<float*>(e->dalloc(kvn * 4));
+        ENG_TRY(cudaMemset(e->kcache, 0, kvn * 4));
+        ENG_TRY(cudaMemset(e->vcache, 0, kvn * 4));
+        // RoPE tables on the host with the reference's formula (RopeCache::build,
+        // llama_model.cpp:1024-1043) so the device uses bit-identical cos/sin.
+        const int half = hd / 2;
+        std::vector<float> ct((size_t)c.n_ctx * half), st((size_t)c.n_ctx * half);
+        for (int p = 0; p < c.n_ctx; ++p)
+            for (int i = 0; i < half; ++i) {
+                const float freq = 1.f / std::pow(c.theta, (float)(2 * i) / (float)hd);
+                const float ang = (float)p * freq;
+                ct[(size_t)p * half + i] = std::cos(ang);
+                st[(size_t)p * half + i] = std::sin(ang);
+            }
+        ENG_TRY(upload_f32(e, e->cos_t, ct.data(), ct.size()));
+        ENG_TRY(upload_f32(e, e->sin_t, st.data(), st.size()));
+        int ns = (2 * e->sms + e->KVl - 1) / e->KVl;
+        ns = std::max(1, std::min(ns, std::min(64, c.n_ctx)));
+        e->nsplit = ns;
+        e->apart = static_cast<float*>(e->dalloc((size_t)e->Hl * ns * (hd + 2) * 4));
+        e->acount = static_cast<unsigned int*>(e->dalloc((size_t)e->KVl * 4));
+        ENG_TRY(cudaMemset(e->acount, 0, (size_t)e->KVl * 4));
+        e->key = static_cast<unsigned long long*>(e->dalloc(8));
+        e->tokpos = static_cast<int*>(e->dalloc(8));
+        e->hist = static_cast<int*>(e->dalloc((size_t)(c.n_ctx + 1) * 4));
+        ENG_TRY(cudaMemset(e->tokpos, 0, 8));
+        ENG_TRY(cudaMallocHost(&e->h_tokpos, 16));
+        ENG_TRY(gemv_init());
+        ENG_TRY(attention_init());
+        ENG_TRY(cudaDeviceSynchronize());
+        // Capture one step into a graph.
+        ENG_TRY(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+        cudaError_t r = enqueue_step(e);
+        cudaGraph_t g = nullptr;
+        cudaError_t r2 = cudaStreamEndCapture(e->stream, &g);
+        if (r != cudaSuccess) {
+            if (g) cudaGraphDestroy(g);
+            return r;
+        }
+        ENG_TRY(r2);
+        e->graph = g;
+        ENG_TRY(cudaGraphInstantiate(&e->gexec, g, 0));
+        e->finalized = true;
+        return cudaSuccess;
+    } catch (const std::exception& ex) {
+        return fail(ex.what(), cudaErrorMemoryAllocation);
+    }
+}
+
+static cudaError_t check_ready(af_engine* e) {
+    if (!e || !e->finalized) return fail("engine not finalized");
+    ENG_TRY(cudaSetDevice(e->device));
+    return cudaSuccess;
+}
+
+cudaError_t af_engine_step(af_engine* e, int32_t token, int32_t pos, float* h_logits, int32_t* h_next) {
+    AF_CUDA_TRY(check_ready(e));
+    if (pos < 0 || pos >= e->cfg.n_ctx) return fail("af_engine_step: position outside the context");
+    if (token < 0 || token >= e->cfg.vocab) return fail("af_engine_step: token id outside the vocabulary");
+    e->h_tokpos[0] = token;
+    e->h_tokpos[1] = pos;
+    ENG_TRY(cudaMemcpyAsync(e->tokpos, e->h_tokpos, 8, cudaMemcpyHostToDevice, e->stream));
+    ENG_TRY(cudaGraphLaunch(e->gexec, e->stream));
+    ENG_TRY(cudaMemcpyAsync(e->h_tokpos + 2, e->tokpos, 4, cudaMemcpyDeviceToHost, e->stream));
+    if (h_logits) AF_CUDA_TRY(gather_logits(e, h_logits));
+    ENG_TRY(cudaStreamSynchronize(e->stream));
+    if (h_next) *h_next = e->h_tokpos[2];
+    return cudaSuccess;
+}
+
+cudaError_t af_engine_prefill(af_engine* e, const int32_t* h_tokens, int n, int32_t pos0, float* h_logits,
+                              int32_t* h_next) {
+    AF_CUDA_TRY(check_ready(e));
+    if (n <= 0 || pos0 < 0 || pos0 + n > e->cfg.n_ctx) return fail("af_engine_prefill: positions outside the context");
+    for (int i = 0; i < n; ++i)
+        if (h_tokens[i] < 0 || h_tokens[i] >= e->cfg.vocab) return fail("af_engine_prefill: token id outside the vocabulary");
+    // Each token has its own pinned slot, so the async copies need no host sync.
+    int* pin = nullptr;
+    ENG_TRY(cudaMallocHost(&pin, (size_t)(n + 1) * 4));
+    std::memcpy(pin, h_tokens, (size_t)n * 4);
+    pin[n] = pos0;
+    ENG_TRY(cudaMemcpyAsync(&e->tokpos[1], &pin[n], 4, cudaMemcpyHostToDevice, e->stream));
+    for (int i = 0; i < n; ++i) {
+        ENG_TRY(cudaMemcpyAsync(&e->tokpos[0], &pin[i], 4, cudaMemcpyHostToDevice, e->stream));
+        ENG_TRY(cudaGraphLaunch(e->gexec, e->stream));
+    }
+    ENG_TRY(cudaMemcpyAsync(e->h_tokpos + 2, e->tokpos, 4, cudaMemcpyDeviceToHost, e->stream));
+    if (h_logits) AF_CUDA_TRY(gather_logits(e, h_logits));
+    ENG_TRY(cudaStreamSynchronize(e->stream));
+    cudaFreeHost(pin);
+    if (h_next) *h_next = e->h_tokpos[2];
+    return cudaSuccess;
+}
+
+cudaError_t af_engine_decode_greedy(af_engine* e, int32_t first_token, int32_t pos0, int n_steps, int32_t* h_out) {
+    AF_CUDA_TRY(check_ready(e));
+    if (n_steps < 0 || pos0 < 0 || pos0 + n_steps > e->cfg.n_ctx) return fail("af_engine_decode_greedy: context overflow");
+    if (first_token < 0 || first_token >= e->cfg.vocab) return fail("af_engine_decode_greedy: bad token");
+    if (n_steps == 0) return cudaSuccess;
+    e->h_tokpos[0] = first_token;
+    e->h_tokpos[1] = pos0;
+    ENG_TRY(cudaMemcpyAsync(e->tokpos, e->h_tokpos, 8, cudaMemcpyHostToDevice, e->stream));
+    for (int i = 0; i < n_steps; ++i) ENG_TRY(cudaGraphLaunch(e->gexec, e->stream));
+    if (h_out)
+        ENG_TRY(cudaMemcpyAsync(h_out, e->hist + pos0, (size_t)n_steps * 4, cudaMemcpyDeviceToHost, e->stream));
+    ENG_TRY(cudaStreamSynchronize(e->stream));
+    return cudaSuccess;
+}
+
+cudaError_t af_engine_generate(af_engine* e, const int32_t* h_prompt, int n_prompt, int max_new, int32_t* h_out,
+                               int* n_out) {
+    AF_CUDA_TRY(check_ready(e));
+    if (!n_out || (max_new > 0 && !h_out)) return fail("af_engine_generate: null output");
+    if (n_prompt <= 0) return fail("llama_generate: empty prompt");
+    *n_out = 0;
+    std::vector<int32_t> ids(h_prompt, h_prompt + n_prompt);
+    if (ids[0] != e->cfg.bos_id) ids.insert(ids.begin(), e->cfg.bos_id);
+    const int np = (int)ids.size();
+    if (np > e->cfg.n_ctx) return fail("af_engine_generate: prompt longer than the context");
+    int32_t next = 0;
+    AF_CUDA_TRY(af_engine_prefill(e, ids.data(), np, 0, nullptr, &next));
+    // Every pushed token is forwarded (llama_model.cpp:1611-1624); ids stop at
+    // EOS (not emitted) or when n_past reaches the context cap.
+    const int budget = std::min(max_new, e->cfg.n_ctx - np);
+    std::vector<int32_t> gen;
+    if (budget > 0) {
+        std::vector<int32_t> dev(budget);
+        AF_CUDA_TRY(af_engine_decode_greedy(e, next, np, budget, dev.data()));
+        gen.push_back(next);
+        for (int i = 0; i + 1 < budget; ++i) gen.push_back(dev[i]);
+    }
+    int n = 0;
+    for (int32_t id : gen) {
+        if (id == e->cfg.eos_id) break;
+        h_out[n++] = id;
+    }
+    *n_out = n;
+    return cudaSuccess;
+}
+
+cudaError_t af_engine_hidden(af_engine* e, float* h_out) {
+    AF_CUDA_TRY(check_ready(e));
+    ENG_TRY(cudaMemcpy(h_out, e->x[0], (size_t)e->cfg.n_embd * 4, cudaMemcpyDeviceToHost));
+    return cudaSuccess;
+}
+
+cudaError_t af_engine_kv(af_engine* e, int layer, int which_v, int n_pos, float* h_out) {
+    AF_CUDA_TRY(check_ready(e));
+    if (layer < 0 || layer >= e->cfg.n_layer || n_pos < 0 || n_pos > e->cfg.n_ctx) return fail("af_engine_kv: range");
+    const size_t row = (size_t)e->KVl * e->hd;
+    const float* base = (which_v ? e->vcache : e->kcache) + (size_t)layer * e->cfg.n_ctx * row;
+    ENG_TRY(cudaMemcpy(h_out, base, (size_t)n_pos * row * 4, cudaMemcpyDeviceToHost));
+    return cudaSuccess;
+}
+
+cudaError_t af_engine_profile(af_engine* e, int32_t token, int32_t pos0, int n_steps, double* h_ms, double* h_bytes,
+                              int* h_count) {
+    AF_CUDA_TRY(check_ready(e));
+    if (n_steps <= 0 || pos0 < 0 || pos0 + n_steps > e->cfg.n_ctx) return fail("af_engine_profile: context overflow");
+    for (int k = 0; k < AF_PROF_KINDS; ++k) {
+        h_ms[k] = 0;
+        h_bytes[k] = 0;
+        h_count[k] = 0;
+    }
+    e->h_tokpos[0] = token;
+    e->h_tokpos[1] = pos0;
+    ENG_TRY(cudaMemcpyAsync(e->tokpos, e->h_tokpos, 8, cudaMemcpyHostToDevice, e->stream));
+    for (int s = 0; s < n_steps; ++s) {
+        Prof prof;
+        prof.pos = pos0 + s;
+        AF_CUDA_TRY(prof.mark(e->stream, -1, 0));
+        cudaError_t r = enqueue_step(e, &prof);
+        ENG_TRY(cudaStreamSynchronize(e->stream));
+        for (size_t i = 1; i < prof.ev.size() && r == cudaSuccess; ++i) {
+            float ms = 0.f;
+            cudaEventElapsedTime(&ms, prof.ev[i - 1], prof.ev[i]);
+            const int k = prof.kinds[i];
+            h_ms[k] += ms;
+            h_bytes[k] += prof.bytes[i];
+            h_count[k] += 1;
+        }
+        for (cudaEvent_t x : prof.ev) cudaEventDestroy(x);
+        AF_CUDA_TRY(r);
+    }
+    return cudaSuccess;
+}
+
+cudaStream_t af_engine_stream(af_engine* e) { return e ? e->stream : nullptr; }
+int af_engine_kernels_per_step(af_engine* e) { return e ? e->kernels_per_step : 0; }
+size_t af_engine_weight_bytes(af_engine* e) { return e ? e->weight_bytes : 0; }
+
+}  // extern "C"

@@ -1,0 +1,252 @@
+// af_ops.cu — C-ABI kernel launchers and the small decode kernels: Q6_K
+// regroup, embedding-row dequant, and the reference CUDA backend's op set
+// (RMSNorm, SiLU, Mul, RoPE; src/backend/cuda/cuda_kernels.hpp:8-19).
+#include <string>
+
+#include "af_gemv.cuh"
+#include "af_ops.cuh"
+
+namespace af {
+
+thread_local std::string g_last_error;
+
+void set_last_error(const std::string& s) { g_last_error = s; }
+
+int num_sms() {
+    int dev = 0, n = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n > 0 ? n : 148;
+}
+
+// ------------------------------------------------------------ Q6_K regroup
+
+// One CTA per row.  GGUF block j (210 B: ql 128, qh 64, scales 16, d 2) goes to
+// group j/8: bytes 0..207 to slot j%8, d to the group's d area.
+__global__ void q6k_repack_kernel(uint8_t* __restrict__ dst, const uint8_t* __restrict__ src, int nb,
+                                  int dst_stride, int unpack) {
+    const int row = blockIdx.x;
+    const uint8_t* s = src + (size_t)row * nb * 210;
+    uint8_t* d = dst + (size_t)row * dst_stride;
+    if (unpack) {
+        s = src + (size_t)row * dst_stride;
+        d = dst + (size_t)row * nb * 210;
+    }
+    for (int j = 0; j < nb; ++j) {
+        const int g = j >> 3, k = j & 7;
+        const int gsz = min(8, nb - g * 8);
+        const size_t goff = (size_t)g * 1680;
+        const size_t qoff = goff + (size_t)k * 208;
+        const size_t doff = goff + (size_t)gsz * 208 + 2 * k;
+        for (int i = threadIdx.x; i < 210; i += blockDim.x) {
+            const size_t o = i < 208 ? qoff + i : doff + (i - 208);
+            if (unpack) d[(size_t)j * 210 + i] = s[o];
+            else d[o] = s[(size_t)j * 210 + i];
+        }
+        if (!unpack && threadIdx.x < 16 && k == gsz - 1 && gsz < 8) {
+            // zero the pad after the last d of a partial group
+            const size_t pad0 = goff + (size_t)gsz * 208 + 2 * gsz;
+            const size_t pad1 = goff + (size_t)gsz * 208 + 16;
+            if (pad0 + threadIdx.x < pad1) d[pad0 + threadIdx.x] = 0;
+        }
+    }
+}
+
+cudaError_t q6k_repack(void* d_dst, const void* d_src, int rows, int cols, bool unpack, cudaStream_t st) {
+    if (rows <= 0) return cudaSuccess;
+    q6k_repack_kernel<<<rows, 128, 0, st>>>(static_cast<uint8_t*>(d_dst), static_cast<const uint8_t*>(d_src),
+                                            cols / 256, q6k_row_stride(cols), unpack ? 1 : 0);
+    return cudaGetLastError();
+}
+
+// --------------------------------------------------------- embedding lookup
+
+// x[0:cols] = dequant(row `*token` of W): emb_lookup (src/models/llama_model.cpp:882-934)
+// for Q4_K (GGUF rows) and Q6_K (regrouped rows).  Also resets the argmax
+// key for the step (this is the step's first kernel).
+__global__ void embed_kernel(float* __restrict__ x, const uint8_t* __restrict__ W, int type, int cols,
+                             int row_stride, const int* __restrict__ token, unsigned long long* argmax) {
+    pdl_launch_dependents();
+    pdl_wait();
+    if (argmax && blockIdx.x == 0 && threadIdx.x == 0) *argmax = 0ull;
+    const int nb = cols / 256;
+    const uint8_t* row = W + (size_t)(*token) * row_stride;
+    for (int v = blockIdx.x * blockDim.x + threadIdx.x; v < cols; v += gridDim.x * blockDim.x) {
+        const int b = v >> 8, w = v & 255;
+        float out;
+        if (type == AF_GGML_Q6_K) {
+            const int g = b >> 3, k = b & 7, gsz = min(8, nb - g * 8);
+            const uint8_t* blk = row + (size_t)g * 1680 + k * 208;
+            const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(row + (size_t)g * 1680 + gsz * 208 + 2 * k));
+            const int n = w >> 7, r = w & 127, s = r >> 5, l = r & 31;
+            const uint8_t* ql = blk + 64 * n;
+            const uint8_t* qh = blk + 128 + 32 * n;
+            const int8_t* sc = reinterpret_cast<const int8_t*>(blk + 192 + 8 * n);
+            const int qlb = (s & 1) ? ql[l + 32] : ql[l];
+            const int nib = (s & 2) ? (qlb >> 4) : (qlb & 0xF);
+            const int q = (nib | (((qh[l] >> (2 * s)) & 3) << 4)) - 32;
+            out = d * sc[(l >> 4) + 2 * s] * q;
+        } else {
+            const uint8_t* blk = row + (size_t)b * 144;
+            const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(blk));
+            const float dmin = half_bits_to_float(*reinterpret_cast<const uint16_t*>(blk + 2));
+            const uint8_t* sc = blk + 4;
+            const int chunk = w >> 6, r = w & 63, j = chunk * 2 + (r >> 5), l = r & 31;
+            int s, m;
+            if (j < 4) {
+                s = sc[j] & 63;
+                m = sc[j + 4] & 63;
+            } else {
+                s = (sc[j + 4] & 0xF) | ((sc[j - 4] >> 6) << 4);
+                m = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
+            }
+            const int qb = blk[16 + chunk * 32 + l];
+            const int q = (r < 32) ? (qb & 0xF) : (qb >> 4);
+            out = (d * s) * q - dmin * m;
+        }
+        x[v] = out;
+    }
+}
+
+cudaError_t embed_launch(float* x, const uint8_t* W, int type, int cols, int row_stride, const int* token,
+                         unsigned long long* argmax, cudaStream_t st, bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((cols + 255) / 256);
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, embed_kernel, x, W, type, cols, row_stride, token, argmax);
+}
+
+// -------------------------------------------------- reference CUDA op set
+
+__global__ void rms_norm_kernel(float* __restrict__ y, const float* __restrict__ x, const float* __restrict__ w,
+                                int n, float eps) {
+    __shared__ float red[32];
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) ss += x[i] * x[i];
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tot += red[i];
+    const float s = 1.f / sqrtf(tot / (float)n + eps);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) y[i] = w[i] * (x[i] * s);
+}
+
+__global__ void silu_kernel(float* y, const float* x, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) y[i] = x[i] / (1.f + expf(-x[i]));
+}
+
+__global__ void mul_kernel(float* y, const float* a, const float* b, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) y[i] = a[i] * b[i];
+}
+
+// freq = 1/theta^(2i/hd), angle = pos*freq (RopeCache::build,
+// src/models/llama_model.cpp:1024-1043); half-split pairs (i, i + hd/2).
+__global__ void rope_kernel(float* q, int n_heads, int head_dim, int pos, float theta) {
+    const int half = head_dim / 2;
+    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= n_heads * half) return;
+    const int h = idx / half, i = idx % half;
+    const float freq = 1.f / powf(theta, (float)(2 * i) / (float)head_dim);
+    const float ang = (float)pos * freq;
+    const float c = cosf(ang), s = sinf(ang);
+    float* hp = q + (size_t)h * head_dim;
+    const float x0 = hp[i], x1 = hp[i + half];
+    hp[i] = x0 * c - x1 * s;
+    hp[i + half] = x0 * s + x1 * c;
+}
+
+}  // namespace af
+
+using namespace af;
+
+extern "C" {
+
+const char* af_last_error(void) { return g_last_error.c_str(); }
+
+cudaError_t af_device_error(int* h_code, int clear) {
+    AF_CUDA_TRY(cudaMemcpyFromSymbol(h_code, g_err, sizeof(int)));
+    if (clear) {
+        const int z = 0;
+        AF_CUDA_TRY(cudaMemcpyToSymbol(g_err, &z, sizeof(int)));
+    }
+    return cudaSuccess;
+}
+
+size_t af_row_stride(int ggml_type, int cols) {
+    if (cols <= 0 || cols % 256) return 0;
+    if (ggml_type == AF_GGML_Q4_K || ggml_type == AF_GGML_Q6_K) return (size_t)dev_row_stride(ggml_type, cols);
+    if (ggml_type == AF_GGML_F32) return (size_t)cols * 4;
+    return 0;
+}
+
+cudaError_t af_q6k_repack(void* d_dst, const void* d_src, int rows, int cols, cudaStream_t stream) {
+    if (cols <= 0 || cols % 256 || rows < 0) return cudaErrorInvalidValue;
+    return q6k_repack(d_dst, d_src, rows, cols, false, stream);
+}
+
+cudaError_t af_q6k_unpack(void* d_dst, const void* d_src, int rows, int cols, cudaStream_t stream) {
+    if (cols <= 0 || cols % 256 || rows < 0) return cudaErrorInvalidValue;
+    return q6k_repack(d_dst, d_src, rows, cols, true, stream);
+}
+
+cudaError_t af_gemv_f32(float* d_y, const void* d_w, int ggml_type, const float* d_x, int rows, int cols,
+                        cudaStream_t stream) {
+    if ((ggml_type != AF_GGML_Q4_K && ggml_type != AF_GGML_Q6_K) || cols <= 0 || cols % 256 || rows < 0) {
+        set_last_error("af_gemv_f32: need Q4_K/Q6_K weights and cols % 256 == 0");
+        return cudaErrorInvalidValue;
+    }
+    if ((reinterpret_cast<uintptr_t>(d_w) & 15) || (reinterpret_cast<uintptr_t>(d_x) & 15)) {
+        set_last_error("af_gemv_f32: weights and x must be 16-byte aligned");
+        return cudaErrorInvalidValue;
+    }
+    if (rows == 0) return cudaSuccess;
+    GemvParams p = {};
+    p.seg[0].w = static_cast<const uint8_t*>(d_w);
+    p.seg[0].y = d_y;
+    p.seg[0].type = ggml_type;
+    p.seg[0].rows = rows;
+    p.seg[0].row_stride = dev_row_stride(ggml_type, cols);
+    p.nseg = 1;
+    p.K = cols;
+    p.x = d_x;
+    p.epi = EPI_STORE;
+    gemv_configure(p);
+    AF_CUDA_TRY(gemv_init());
+    return gemv_launch(p, num_sms(), stream, false);
+}
+
+cudaError_t af_rms_norm_f32(float* d_y, const float* d_x, const float* d_w, int n, float eps, cudaStream_t stream) {
+    if (n <= 0) return cudaErrorInvalidValue;
+    rms_norm_kernel<<<1, 1024, 0, stream>>>(d_y, d_x, d_w, n, eps);
+    return cudaGetLastError();
+}
+
+cudaError_t af_silu_f32(float* d_y, const float* d_x, int n, cudaStream_t stream) {
+    if (n <= 0) return n == 0 ? cudaSuccess : cudaErrorInvalidValue;
+    silu_kernel<<<(n + 255) / 256, 256, 0, stream>>>(d_y, d_x, n);
+    return cudaGetLastError();
+}
+
+cudaError_t af_mul_f32(float* d_y, const float* d_a, const float* d_b, int n, cudaStream_t stream) {
+    if (n <= 0) return n == 0 ? cudaSuccess : cudaErrorInvalidValue;
+    mul_kernel<<<(n + 255) / 256, 256, 0, stream>>>(d_y, d_a, d_b, n);
+    return cudaGetLastError();
+}
+
+cudaError_t af_rope_f32(float* d_q, int n_heads, int head_dim, int pos, float theta, cudaStream_t stream) {
+    if (n_heads <= 0 || head_dim <= 0 || head_dim % 2) return cudaErrorInvalidValue;
+    const int n = n_heads * head_dim / 2;
+    rope_kernel<<<(n + 127) / 128, 128, 0, stream>>>(d_q, n_heads, head_dim, pos, theta);
+    return cudaGetLastError();
+}
+
+}  // extern "C"

@@ -1,0 +1,468 @@
+/*
+ * af_oracle.c — CPU restatement of the reference decode path, for TESTS ONLY.
+ *
+ * This is test infrastructure: only tests/, the smoke check and bench.py's
+ * cpu_baseline leg load liboracle.so, and only as the checker.  The product
+ * path (llm_core_b200) never calls it and has no CPU fallback.
+ *
+ * Every function restates the algorithm of songqiuyu/llm_core ("AxonForge")
+ * at the cited file:line (paths relative to the reference project root).
+ * Parity pin: tests/test_oracle.py checks this file against the reference
+ * compiled in place (oracle/_ref/libaxref.so, built by oracle/ref.mk) and
+ * against the committed fixtures in tests/golden/ produced from that library by
+ * tests/golden/make_golden.py.
+ *
+ * Numerics: plain fp32 with the reference's expression order inside each dot
+ * product row; summation order differs from the AVX2 kernels (8-lane partial
+ * sums), so agreement is to ~1e-6 relative, not bit-exact.
+ */
+#include <math.h>
+#include <pthread.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#define QK_K 256
+#define Q4K_BYTES 144
+#define Q6K_BYTES 210
+#define GGML_F32 0
+#define GGML_Q4_K 12
+#define GGML_Q6_K 14
+
+/* f16 -> f32 bit conversion: llama_model.cpp:102-120. */
+float afo_f16_to_f32(uint16_t h) {
+    uint32_t sign = (h >> 15) & 1u, exponent = (h >> 10) & 0x1Fu, mantissa = h & 0x3FFu, bits;
+    if (exponent == 0) {
+        if (mantissa == 0) {
+            bits = sign << 31;
+        } else {
+            int e = 1;
+            while (!(mantissa & 0x400)) { mantissa <<= 1; e--; }
+            mantissa &= 0x3FF;
+            bits = (sign << 31) | ((uint32_t)(e + 127 - 15) << 23) | (mantissa << 13);
+        }
+    } else if (exponent == 31) {
+        bits = (sign << 31) | 0x7F800000u | (mantissa << 13);
+    } else {
+        bits = (sign << 31) | ((exponent + 127 - 15) << 23) | (mantissa << 13);
+    }
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+/* 6-bit (scale, min) pair j of the 12 packed bytes: llama_model.cpp:464-473,
+ * gemv_q4k_avx2.cpp:34-43. */
+static void q4k_get_scale_min(int j, const uint8_t* sc, uint8_t* d, uint8_t* m) {
+    if (j < 4) {
+        *d = sc[j] & 0x3F;
+        *m = sc[j + 4] & 0x3F;
+    } else {
+        *d = (sc[j + 4] & 0x0F) | ((sc[j - 4] >> 6) << 4);
+        *m = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
+    }
+}
+
+/* Dequantise one Q4_K row of `cols` values: emb_lookup Q4_K branch,
+ * llama_model.cpp:905-930. */
+void afo_q4k_row_to_f32(float* out, const uint8_t* row, int cols) {
+    const int nb = cols / QK_K;
+    for (int b = 0; b < nb; b++) {
+        const uint8_t* block = row + (size_t)b * Q4K_BYTES;
+        uint16_t db, mb;
+        memcpy(&db, block, 2);
+        memcpy(&mb, block + 2, 2);
+        const float d = afo_f16_to_f32(db), dmin = afo_f16_to_f32(mb);
+        const uint8_t* scales = block + 4;
+        const uint8_t* qs = block + 16;
+        float* ob = out + (size_t)b * QK_K;
+        for (int chunk = 0; chunk < 4; chunk++) {
+            uint8_t sc1, m1, sc2, m2;
+            q4k_get_scale_min(chunk * 2 + 0, scales, &sc1, &m1);
+            q4k_get_scale_min(chunk * 2 + 1, scales, &sc2, &m2);
+            const float d1 = d * sc1, mf1 = dmin * m1, d2 = d * sc2, mf2 = dmin * m2;
+            const uint8_t* q = qs + chunk * 32;
+            float* oc = ob + chunk * 64;
+            for (int l = 0; l < 32; l++) {
+                oc[l] = d1 * (q[l] & 0xF) - mf1;
+                oc[l + 32] = d2 * (q[l] >> 4) - mf2;
+            }
+        }
+    }
+}
+
+/* Dot of one Q4_K row with f32 x: q4k_dot_row, llama_model.cpp:476-504. */
+float afo_q4k_dot_row(const uint8_t* row, const float* x, int cols) {
+    float acc = 0.f;
+    const int nb = cols / QK_K;
+    for (int b = 0; b < nb; b++) {
+        const uint8_t* block = row + (size_t)b * Q4K_BYTES;
+        uint16_t db, mb;
+        memcpy(&db, block, 2);
+        memcpy(&mb, block + 2, 2);
+        const float d = afo_f16_to_f32(db), dmin = afo_f16_to_f32(mb);
+        const uint8_t* scales = block + 4;
+        const uint8_t* qs = block + 16;
+        const float* xb = x + (size_t)b * QK_K;
+        for (int chunk = 0; chunk < 4; chunk++) {
+            uint8_t sc1, m1, sc2, m2;
+            q4k_get_scale_min(chunk * 2 + 0, scales, &sc1, &m1);
+            q4k_get_scale_min(chunk * 2 + 1, scales, &sc2, &m2);
+            const float d1 = d * sc1, mf1 = dmin * m1, d2 = d * sc2, mf2 = dmin * m2;
+            const uint8_t* q = qs + chunk * 32;
+            const float* xi = xb + chunk * 64;
+            for (int l = 0; l < 32; l++) {
+                acc += (d1 * (q[l] & 0xF) - mf1) * xi[l];
+                acc += (d2 * (q[l] >> 4) - mf2) * xi[l + 32];
+            }
+        }
+    }
+    return acc;
+}
+
+/* Dequantise one Q6_K row: q6k_row_to_f32, llama_model.cpp:560-592. */
+void afo_q6k_row_to_f32(float* out, const uint8_t* row, int cols) {
+    const int nb = cols / QK_K;
+    for (int b = 0; b < nb; b++) {
+        const uint8_t* block = row + (size_t)b * Q6K_BYTES;
+        uint16_t db;
+        memcpy(&db, block + 208, 2);
+        const float d = afo_f16_to_f32(db);
+        const uint8_t* ql = block;
+        const uint8_t* qh = block + 128;
+        const int8_t* sc = (const int8_t*)(block + 192);
+        float* y = out + (size_t)b * QK_K;
+        for (int n = 0; n < 2; n++) {
+            for (int l = 0; l < 32; l++) {
+                const int is = l / 16;
+                const int q1 = ((ql[l] & 0x0F) | (((qh[l] >> 0) & 3) << 4)) - 32;
+                const int q2 = ((ql[l + 32] & 0x0F) | (((qh[l] >> 2) & 3) << 4)) - 32;
+                const int q3 = ((ql[l] >> 4) | (((qh[l] >> 4) & 3) << 4)) - 32;
+                const int q4 = ((ql[l + 32] >> 4) | (((qh[l] >> 6) & 3) << 4)) - 32;
+                y[l + 0] = d * sc[is + 0] * q1;
+                y[l + 32] = d * sc[is + 2] * q2;
+                y[l + 64] = d * sc[is + 4] * q3;
+                y[l + 96] = d * sc[is + 6] * q4;
+            }
+            ql += 64;
+            qh += 32;
+            sc += 8;
+            y += 128;
+        }
+    }
+}
+
+/* Dot of one Q6_K row with f32 x: q6k_dot_row, llama_model.cpp:595-629. */
+float afo_q6k_dot_row(const uint8_t* row, const float* x, int cols) {
+    float acc = 0.f;
+    const int nb = cols / QK_K;
+    for (int b = 0; b < nb; b++) {
+        const uint8_t* block = row + (size_t)b * Q6K_BYTES;
+        uint16_t db;
+        memcpy(&db, block + 208, 2);
+        const float d = afo_f16_to_f32(db);
+        const uint8_t* ql = block;
+        const uint8_t* qh = block + 128;
+        const int8_t* sc = (const int8_t*)(block + 192);
+        const float* xp = x + (size_t)b * QK_K;
+        for (int n = 0; n < 2; n++) {
+            for (int l = 0; l < 32; l++) {
+                const int is = l / 16;
+                const int q1 = ((ql[l] & 0x0F) | (((qh[l] >> 0) & 3) << 4)) - 32;
+                const int q2 = ((ql[l + 32] & 0x0F) | (((qh[l] >> 2) & 3) << 4)) - 32;
+                const int q3 = ((ql[l] >> 4) | (((qh[l] >> 4) & 3) << 4)) - 32;
+                const int q4 = ((ql[l + 32] >> 4) | (((qh[l] >> 6) & 3) << 4)) - 32;
+                acc += (d * sc[is + 0] * q1) * xp[l + 0];
+                acc += (d * sc[is + 2] * q2) * xp[l + 32];
+                acc += (d * sc[is + 4] * q3) * xp[l + 64];
+                acc += (d * sc[is + 6] * q4) * xp[l + 96];
+            }
+            ql += 64;
+            qh += 32;
+            sc += 8;
+            xp += 128;
+        }
+    }
+    return acc;
+}
+
+static size_t row_bytes_of(int type, int cols) {
+    if (type == GGML_Q4_K) return (size_t)(cols / QK_K) * Q4K_BYTES;
+    if (type == GGML_Q6_K) return (size_t)(cols / QK_K) * Q6K_BYTES;
+    return (size_t)cols * 4;
+}
+
+static int g_threads = 1;
+
+/* Number of host threads afo_gemv splits its rows over (default 1). */
+void afo_set_threads(int n) { g_threads = n < 1 ? 1 : n; }
+
+typedef struct {
+    float* y;
+    const uint8_t* W;
+    const float* x;
+    int type, cols, r0, r1;
+    size_t rb;
+} gemv_job;
+
+static void* gemv_rows(void* arg) {
+    const gemv_job* j = (const gemv_job*)arg;
+    for (int o = j->r0; o < j->r1; o++) {
+        const uint8_t* row = j->W + (size_t)o * j->rb;
+        if (j->type == GGML_Q4_K) {
+            j->y[o] = afo_q4k_dot_row(row, j->x, j->cols);
+        } else if (j->type == GGML_Q6_K) {
+            j->y[o] = afo_q6k_dot_row(row, j->x, j->cols);
+        } else {
+            const float* r = (const float*)row;
+            float acc = 0.f;
+            for (int i = 0; i < j->cols; i++) acc += r[i] * j->x[i];
+            j->y[o] = acc;
+        }
+    }
+    return NULL;
+}
+
+/* y[0:rows] = W·x for a Q4_K / Q6_K / F32 matrix: gemv_wt dtype dispatch,
+ * llama_model.cpp:670-730 (F32-activation path).  Rows are split over
+ * afo_set_threads() threads like ThreadPool::parallel_for (thread_pool.hpp:61-83). */
+void afo_gemv(float* y, const void* W, int type, const float* x, int rows, int cols) {
+    const size_t rb = row_bytes_of(type, cols);
+    int nt = g_threads;
+    if (nt > 64) nt = 64;
+    if (rows < 64) nt = 1;
+    gemv_job jobs[64];
+    pthread_t th[64];
+    const int chunk = (rows + nt - 1) / nt;
+    for (int t = 0; t < nt; t++) {
+        const int r0 = t * chunk, r1 = r0 + chunk < rows ? r0 + chunk : rows;
+        gemv_job j = {y, (const uint8_t*)W, x, type, cols, r0 < rows ? r0 : rows, r1, rb};
+        jobs[t] = j;
+    }
+    for (int t = 1; t < nt; t++) pthread_create(&th[t], NULL, gemv_rows, &jobs[t]);
+    gemv_rows(&jobs[0]);
+    for (int t = 1; t < nt; t++) pthread_join(th[t], NULL);
+}
+
+/* RMSNorm with separate output: rms_norm_out, llama_model.cpp:393-419. */
+void afo_rms_norm(float* dst, const float* src, const float* w, int n, float eps) {
+    float ss = 0.f;
+    for (int i = 0; i < n; i++) ss += src[i] * src[i];
+    ss = 1.f / sqrtf(ss / n + eps);
+    for (int i = 0; i < n; i++) dst[i] = w[i] * (src[i] * ss);
+}
+
+/* RoPE tables: RopeCache::build, llama_model.cpp:1024-1043.  cos/sin [n_pos][hd/2]. */
+void afo_rope_tables(float* cos_t, float* sin_t, int head_dim, float theta, int n_pos) {
+    const int half = head_dim / 2;
+    for (int p = 0; p < n_pos; p++) {
+        for (int i = 0; i < half; i++) {
+            const float freq = 1.f / powf(theta, (float)(2 * i) / (float)head_dim);
+            const float angle = (float)p * freq;
+            cos_t[(size_t)p * half + i] = cosf(angle);
+            sin_t[(size_t)p * half + i] = sinf(angle);
+        }
+    }
+}
+
+/* Half-split ("NeoX") rotation of n_heads heads: apply_rope,
+ * llama_model.cpp:1046-1060 (also rope_and_store_k, 1063-1080). */
+void afo_rope(float* dst, const float* src, int n_heads, int head_dim, const float* cos_row,
+              const float* sin_row) {
+    const int half = head_dim / 2;
+    for (int h = 0; h < n_heads; h++) {
+        const float* s = src + h * head_dim;
+        float* d = dst + h * head_dim;
+        for (int i = 0; i < half; i++) {
+            const float x0 = s[i], x1 = s[i + half];
+            d[i] = x0 * cos_row[i] - x1 * sin_row[i];
+            d[i + half] = x0 * sin_row[i] + x1 * cos_row[i];
+        }
+    }
+}
+
+/* ------------------------------------------------------------------------ */
+/* Whole-model single-token forward: llama_forward_token, llama_model.cpp:1207-1333 */
+
+typedef struct {
+    int n_layer, n_embd, n_head, n_kv_head, ffn, vocab, n_ctx;
+    float eps, theta;
+    int qk_norm_order; /* 0 none, 1 before RoPE (qwen3), 2 after RoPE (hunyuan) */
+} afo_cfg;
+
+typedef struct {
+    const float *attn_norm, *ffn_norm, *bq, *bk, *bv, *q_norm, *k_norm;
+    const void *wq, *wk, *wv, *wo, *wg, *wu, *wd;
+    int tq, tk, tv, to, tg, tu, td;
+} afo_layer;
+
+typedef struct {
+    afo_cfg c;
+    int head_dim, kv_dim;
+    const void* tok_embd;
+    int tok_type;
+    const float* out_norm;
+    const void* output;
+    int out_type;
+    afo_layer* layers;
+    float *kv_k, *kv_v, *cos_t, *sin_t;
+    float *x, *xb, *q, *k, *v, *att, *ao, *gate, *up, *ffo, *logits;
+} afo_model;
+
+void* afo_create(const afo_cfg* c) {
+    afo_model* m = (afo_model*)calloc(1, sizeof(afo_model));
+    m->c = *c;
+    m->head_dim = c->n_embd / c->n_head;
+    m->kv_dim = c->n_kv_head * m->head_dim;
+    m->layers = (afo_layer*)calloc((size_t)c->n_layer, sizeof(afo_layer));
+    const size_t kvn = (size_t)c->n_layer * c->n_ctx * m->kv_dim;
+    m->kv_k = (float*)calloc(kvn, 4);
+    m->kv_v = (float*)calloc(kvn, 4);
+    m->cos_t = (float*)malloc((size_t)c->n_ctx * (m->head_dim / 2) * 4);
+    m->sin_t = (float*)malloc((size_t)c->n_ctx * (m->head_dim / 2) * 4);
+    afo_rope_tables(m->cos_t, m->sin_t, m->head_dim, c->theta, c->n_ctx);
+    m->x = (float*)calloc(c->n_embd, 4);
+    m->xb = (float*)calloc(c->n_embd, 4);
+    m->q = (float*)calloc(c->n_embd, 4);
+    m->k = (float*)calloc(m->kv_dim, 4);
+    m->v = (float*)calloc(m->kv_dim, 4);
+    m->att = (float*)calloc(c->n_ctx, 4);
+    m->ao = (float*)calloc(c->n_embd, 4);
+    m->gate = (float*)calloc(c->ffn, 4);
+    m->up = (float*)calloc(c->ffn, 4);
+    m->ffo = (float*)calloc(c->n_embd, 4);
+    m->logits = (float*)calloc(c->vocab, 4);
+    return m;
+}
+
+void afo_destroy(void* h) {
+    afo_model* m = (afo_model*)h;
+    if (!m) return;
+    free(m->layers); free(m->kv_k); free(m->kv_v); free(m->cos_t); free(m->sin_t);
+    free(m->x); free(m->xb); free(m->q); free(m->k); free(m->v); free(m->att); free(m->ao);
+    free(m->gate); free(m->up); free(m->ffo); free(m->logits);
+    free(m);
+}
+
+/* `output` may be NULL: the LM head then falls back to token_embd
+ * (make_wt_opt, llama_model.cpp:979). */
+void afo_set_global(void* h, const void* tok_embd, int tok_type, const float* out_norm,
+                    const void* output, int out_type) {
+    afo_model* m = (afo_model*)h;
+    m->tok_embd = tok_embd;
+    m->tok_type = tok_type;
+    m->out_norm = out_norm;
+    m->output = output ? output : tok_embd;
+    m->out_type = output ? out_type : tok_type;
+}
+
+void afo_set_layer(void* h, int l, const afo_layer* lw) { ((afo_model*)h)->layers[l] = *lw; }
+
+static void add_bias(float* y, const float* b, int n) {
+    if (!b) return;
+    for (int i = 0; i < n; i++) y[i] += b[i];
+}
+
+static void rms_norm_heads(float* x, const float* w, int n_heads, int hd, float eps) {
+    if (!w) return;
+    for (int h = 0; h < n_heads; h++) afo_rms_norm(x + (size_t)h * hd, x + (size_t)h * hd, w, hd, eps);
+}
+
+/* Embedding lookup: emb_lookup, llama_model.cpp:882-934 (Q4_K / Q6_K / F32). */
+static void emb_row(float* out, const void* W, int type, int row, int cols) {
+    const uint8_t* base = (const uint8_t*)W + (size_t)row * row_bytes_of(type, cols);
+    if (type == GGML_Q4_K) afo_q4k_row_to_f32(out, base, cols);
+    else if (type == GGML_Q6_K) afo_q6k_row_to_f32(out, base, cols);
+    else memcpy(out, base, (size_t)cols * 4);
+}
+
+int afo_forward_token(void* h, int token, int pos, float* logits_out) {
+    afo_model* m = (afo_model*)h;
+    const afo_cfg* c = &m->c;
+    const int E = c->n_embd, H = c->n_head, KVH = c->n_kv_head, HD = m->head_dim, FD = c->ffn;
+    const int KVD = m->kv_dim;
+    if (pos < 0 || pos >= c->n_ctx || token < 0 || token >= c->vocab) return -1;
+    const float scale = 1.f / sqrtf((float)HD);
+    const float* cr = m->cos_t + (size_t)pos * (HD / 2);
+    const float* sr = m->sin_t + (size_t)pos * (HD / 2);
+    emb_row(m->x, m->tok_embd, m->tok_type, token, E);
+    for (int l = 0; l < c->n_layer; l++) {
+        const afo_layer* lw = &m->layers[l];
+        float* kc = m->kv_k + (size_t)l * c->n_ctx * KVD;
+        float* vc = m->kv_v + (size_t)l * c->n_ctx * KVD;
+        afo_rms_norm(m->xb, m->x, lw->attn_norm, E, c->eps);
+        afo_gemv(m->q, lw->wq, lw->tq, m->xb, H * HD, E);
+        afo_gemv(m->k, lw->wk, lw->tk, m->xb, KVD, E);
+        afo_gemv(m->v, lw->wv, lw->tv, m->xb, KVD, E);
+        add_bias(m->q, lw->bq, H * HD);
+        add_bias(m->k, lw->bk, KVD);
+        add_bias(m->v, lw->bv, KVD);
+        if (c->qk_norm_order == 1) {
+            rms_norm_heads(m->q, lw->q_norm, H, HD, c->eps);
+            rms_norm_heads(m->k, lw->k_norm, KVH, HD, c->eps);
+        }
+        afo_rope(m->q, m->q, H, HD, cr, sr);
+        if (c->qk_norm_order == 2) {
+            afo_rope(m->k, m->k, KVH, HD, cr, sr);
+            rms_norm_heads(m->q, lw->q_norm, H, HD, c->eps);
+            rms_norm_heads(m->k, lw->k_norm, KVH, HD, c->eps);
+            memcpy(kc + (size_t)pos * KVD, m->k, (size_t)KVD * 4);
+        } else {
+            afo_rope(kc + (size_t)pos * KVD, m->k, KVH, HD, cr, sr);
+        }
+        memcpy(vc + (size_t)pos * KVD, m->v, (size_t)KVD * 4);
+        /* GQA attention, llama_model.cpp:1253-1272: scores, max-subtracted
+         * softmax (llama_model.cpp:445-451), weighted V sum. */
+        const int seq = pos + 1, group = H / KVH;
+        memset(m->ao, 0, (size_t)E * 4);
+        for (int hh = 0; hh < H; hh++) {
+            const int kvh = hh / group;
+            const float* qh = m->q + hh * HD;
+            for (int t = 0; t < seq; t++) {
+                const float* kt = kc + (size_t)t * KVD + kvh * HD;
+                float s = 0.f;
+                for (int i = 0; i < HD; i++) s += qh[i] * kt[i];
+                m->att[t] = s * scale;
+            }
+            float mx = m->att[0], sum = 0.f;
+            for (int t = 1; t < seq; t++) if (m->att[t] > mx) mx = m->att[t];
+            for (int t = 0; t < seq; t++) { m->att[t] = expf(m->att[t] - mx); sum += m->att[t]; }
+            for (int t = 0; t < seq; t++) m->att[t] /= sum;
+            float* oh = m->ao + hh * HD;
+            for (int t = 0; t < seq; t++) {
+                const float* vt = vc + (size_t)t * KVD + kvh * HD;
+                for (int i = 0; i < HD; i++) oh[i] += m->att[t] * vt[i];
+            }
+        }
+        afo_gemv(m->xb, lw->wo, lw->to, m->ao, E, E);
+        for (int i = 0; i < E; i++) m->x[i] += m->xb[i];
+        afo_rms_norm(m->xb, m->x, lw->ffn_norm, E, c->eps);
+        afo_gemv(m->gate, lw->wg, lw->tg, m->xb, FD, E);
+        afo_gemv(m->up, lw->wu, lw->tu, m->xb, FD, E);
+        /* SwiGLU: silu(g)*u, llama_model.cpp:313-315 / 344-368. */
+        for (int i = 0; i < FD; i++) {
+            const float g = m->gate[i];
+            m->gate[i] = (g / (1.f + expf(-g))) * m->up[i];
+        }
+        afo_gemv(m->ffo, lw->wd, lw->td, m->gate, E, FD);
+        for (int i = 0; i < E; i++) m->x[i] += m->ffo[i];
+    }
+    afo_rms_norm(m->x, m->x, m->out_norm, E, c->eps);
+    afo_gemv(m->logits, m->output, m->out_type, m->x, c->vocab, E);
+    if (logits_out) memcpy(logits_out, m->logits, (size_t)c->vocab * 4);
+    return 0;
+}
+
+/* Greedy argmax, first maximum: sample() at temperature 0, llama_model.cpp:1466-1471. */
+int afo_argmax(const float* v, int n) {
+    int best = 0;
+    for (int i = 1; i < n; i++) if (v[i] > v[best]) best = i;
+    return best;
+}
+
+/* Residual stream after the last forward (the final RMSNorm is applied in
+ * place, as rms_norm_avx2(s.x) does at llama_model.cpp:1328). */
+void afo_hidden(void* h, float* out) {
+    afo_model* m = (afo_model*)h;
+    memcpy(out, m->x, (size_t)m->c.n_embd * 4);
+}

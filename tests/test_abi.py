@@ -1,0 +1,49 @@
+"""The C-ABI library loads and exports every symbol include/af_b200.h declares;
+host-side argument checks work without a GPU."""
+import ctypes as C
+import subprocess
+
+import pytest
+
+from llm_core_b200 import _lib
+
+
+def test_library_exports_every_header_symbol():
+    lib = _lib.load()
+    syms = _lib.header_symbols()
+    assert len(syms) >= 20
+    for s in syms:
+        assert hasattr(lib, s), s
+    out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True, text=True).stdout
+    exported = {ln.split()[-1] for ln in out.splitlines() if ln.strip()}
+    missing = [s for s in syms if s not in exported]
+    assert not missing, missing
+
+
+def test_row_stride():
+    lib = _lib.load()
+    assert lib.af_row_stride(12, 4096) == 16 * 144
+    assert lib.af_row_stride(14, 4096) == 2 * 1680 == 16 * 210      # whole groups: no padding
+    assert lib.af_row_stride(14, 11008) == 5 * 1680 + 3 * 208 + 16  # 9040 >= 43 * 210 = 9030
+    assert lib.af_row_stride(12, 100) == 0                           # not a multiple of 256
+
+
+def test_gemv_rejects_bad_arguments_without_touching_a_device():
+    lib = _lib.load()
+    assert lib.af_gemv_f32(None, None, 12, None, 4, 100, None) != 0   # cols % 256
+    assert b"256" in lib.af_last_error()
+    assert lib.af_gemv_f32(None, None, 3, None, 4, 256, None) != 0    # unsupported type
+
+
+def test_gguf_config_reader(tmp_path):
+    from llm_core_b200 import gguf
+    from llm_core_b200.engine import read_config
+    p = str(tmp_path / "q.gguf")
+    gguf.write_random_model(p, "tiny-qwen", seed=3)
+    c = read_config(p, 4096)
+    assert (c.n_layer, c.n_embd, c.n_head, c.n_kv_head, c.ffn, c.vocab, c.n_ctx) == (2, 512, 4, 2, 768, 1000, 512)
+    assert abs(c.eps - 1e-6) < 1e-12 and c.theta == 1e6 and c.bos_id == 1 and c.eos_id == -1
+    bad = tmp_path / "bad.gguf"
+    bad.write_bytes(b"GGUX" + b"\0" * 64)
+    with pytest.raises(_lib.AfError, match="magic"):
+        read_config(str(bad))
