@@ -98,7 +98,16 @@ class ClockSampler:
 
 def model_file(preset: str, rank: int, dist) -> str:
     from llm_core_b200 import gguf
-    d = os.environ.get("AF_BENCH_DIR", "/dev/shm" if os.path.isdir("/dev/shm") else tempfile.gettempdir())
+    d = os.environ.get("AF_BENCH_DIR")
+    if not d:
+        need = gguf.model_weight_bytes(gguf.PRESETS[preset]) * 1.2
+        d = tempfile.gettempdir()
+        try:
+            st = os.statvfs("/dev/shm")
+            if st.f_bavail * st.f_frsize > need * 1.5:
+                d = "/dev/shm"
+        except OSError:
+            pass
     path = os.path.join(d, f"af_bench_{preset}_s{SEED}.gguf")
     if rank == 0 and not os.path.exists(path):
         gguf.write_random_model(path, preset, SEED)
@@ -287,6 +296,60 @@ def run_b200(args):
     return 0
 
 
+def run_gemv_sweep(args):
+    """Standalone dequant-GEMV sweep (BASELINE config 0 shapes and the config 4
+    M x K grid, batch 1): one JSON line per shape, device-timed with CUDA
+    events; weight copies rotate so every launch streams from HBM (> L2)."""
+    import torch
+    from llm_core_b200 import _lib, gguf
+    lib = _lib.load()
+    peak, kind = peaks()
+    shapes = [(2048, 2048), (256, 2048), (5632, 2048), (2048, 5632)]
+    shapes += [(m, k) for m in (2048, 4096, 11008, 32000) for k in (2048, 4096, 11008)]
+    if args.shapes:
+        shapes = [tuple(int(v) for v in s.split("x")) for s in args.shapes.split(",")]
+    types = [gguf.GGML_Q4_K, gguf.GGML_Q6_K] if args.types == "both" else [int(args.types)]
+    rng = np.random.default_rng(0)
+    for t in types:
+        for (m, k) in shapes:
+            gen = gguf.random_q4k if t == gguf.GGML_Q4_K else gguf.random_q6k
+            host = gen(rng, m * k // 256).reshape(-1)
+            stride = lib.af_row_stride(t, k)
+            nbytes = m * stride
+            copies = max(1, int(np.ceil(300e6 / nbytes)))
+            src = torch.from_numpy(host).cuda()
+            ws = []
+            for _ in range(copies):
+                if t == gguf.GGML_Q4_K:
+                    ws.append(src.clone())
+                else:
+                    w = torch.empty(m * stride + 64, dtype=torch.uint8, device="cuda")
+                    assert lib.af_q6k_repack(w.data_ptr(), src.data_ptr(), m, k, None) == 0
+                    ws.append(w)
+            x = torch.randn(k, device="cuda")
+            y = torch.empty(m, device="cuda")
+            st = torch.cuda.current_stream().cuda_stream
+            for i in range(3):
+                assert lib.af_gemv_f32(y.data_ptr(), ws[i % copies].data_ptr(), t, x.data_ptr(), m, k, st) == 0
+            n = max(args.steps, copies)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record()
+            for i in range(n):
+                lib.af_gemv_f32(y.data_ptr(), ws[i % copies].data_ptr(), t, x.data_ptr(), m, k, st)
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1000 / n
+            alg = nbytes + 4 * (k + m)
+            gbs = alg / (us * 1e-6) / 1e9
+            print(json.dumps({"kernel": "gemv_kernel", "type": "Q4_K" if t == 12 else "Q6_K", "M": m, "K": k,
+                              "batch": 1, "us": round(us, 2), "bytes": alg, "GBps": round(gbs, 1),
+                              "frac": round(gbs / peak, 4), "peak": f"{peak} ({kind})", "copies": copies}))
+            del ws, src
+            torch.cuda.empty_cache()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -296,7 +359,12 @@ def main():
     ap.add_argument("--model", default="llama2-7b")
     ap.add_argument("--cpu-steps", type=int, default=12)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gemv-sweep", action="store_true", help="standalone GEMV sweep (not the headline line)")
+    ap.add_argument("--shapes", default="", help="sweep shapes, e.g. 4096x4096,32000x4096")
+    ap.add_argument("--types", default="both", help="12 (Q4_K), 14 (Q6_K) or both")
     args = ap.parse_args()
+    if args.gemv_sweep:
+        return run_gemv_sweep(args)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

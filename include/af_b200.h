@@ -68,6 +68,53 @@ cudaError_t af_q6k_unpack(void* d_dst, const void* d_src, int rows, int cols, cu
 cudaError_t af_gemv_f32(float* d_y, const void* d_w, int ggml_type, const float* d_x, int rows,
                         int cols, cudaStream_t stream);
 
+/* The fused GEMV the decode step is built from: up to three matrices sharing
+ * one input (e.g. attn_q/attn_k/attn_v), an optional residual add into the
+ * input (x + x_add, stored to x_store), an optional RMSNorm of the input
+ * (rms_norm_out, src/models/llama_model.cpp:393-419), and one epilogue:
+ *   AF_EPI_STORE  y_s[r] = (W_s·x)[r] (+ bias_s[r])
+ *   AF_EPI_SWIGLU y_0[r] = silu(W_0·x)[r] * (W_1·x)[r]   (gate, up; llama_model.cpp:344-368)
+ *   AF_EPI_RESID  resid[r] += (W_0·x)[r]                   (residual add, :1277, :1324)
+ *   AF_EPI_ARGMAX y_0 = W_0·x and *argmax = max over rows of the packed
+ *                 (ordered value << 32 | ~(argmax_base + r)) key (greedy, :1466-1471). */
+#define AF_EPI_STORE 0
+#define AF_EPI_SWIGLU 1
+#define AF_EPI_RESID 2
+#define AF_EPI_ARGMAX 3
+typedef struct {
+    const void* w[3];
+    int type[3];
+    int rows[3];
+    float* y[3];
+    const float* bias[3];
+    int nseg;
+    int cols;
+    const float* x;
+    const float* x_add;
+    float* x_store;
+    const float* norm_w;
+    float eps;
+    int epi;
+    float* resid;
+    unsigned long long* argmax;
+    int argmax_base;
+} af_gemv_fused_args;
+cudaError_t af_gemv_fused(const af_gemv_fused_args* args, cudaStream_t stream);
+
+/* GQA decode attention for one new token at *d_pos (device int): RoPE of q and
+ * k with the cos/sin tables [n_ctx][head_dim/2], optional per-head Q/K RMSNorm
+ * (qk_norm_order 1 before / 2 after RoPE), K/V stored into the fp32 caches
+ * [n_ctx][n_kv_heads*head_dim] at *d_pos, softmax attention over positions
+ * 0..*d_pos, output [n_heads*head_dim].  Scratch: d_part
+ * (n_heads*nsplit*(head_dim+2) floats) and d_counter (n_kv_heads uints, zero
+ * on entry and on return).  llama_model.cpp:1236-1272. */
+cudaError_t af_attention_decode_f32(float* d_out, const float* d_q, const float* d_k, const float* d_v,
+                                    float* d_kcache, float* d_vcache, const float* d_cos,
+                                    const float* d_sin, const float* d_q_norm, const float* d_k_norm,
+                                    const int* d_pos, int n_heads, int n_kv_heads, int head_dim,
+                                    int n_ctx, int qk_norm_order, float eps, int nsplit,
+                                    float* d_part, unsigned int* d_counter, cudaStream_t stream);
+
 /* y = w ⊙ x / sqrt(mean(x²) + eps): rms_norm_f32 (cuda_kernels.hpp:8). */
 cudaError_t af_rms_norm_f32(float* d_y, const float* d_x, const float* d_w, int n, float eps,
                             cudaStream_t stream);

@@ -28,6 +28,17 @@ class ModelConfig(C.Structure):
                 ("bos_id", C.c_int), ("eos_id", C.c_int)]
 
 
+class GemvFusedArgs(C.Structure):
+    """af_gemv_fused_args (include/af_b200.h)."""
+    _fields_ = [("w", C.c_void_p * 3), ("type", C.c_int * 3), ("rows", C.c_int * 3), ("y", C.c_void_p * 3),
+                ("bias", C.c_void_p * 3), ("nseg", C.c_int), ("cols", C.c_int), ("x", C.c_void_p),
+                ("x_add", C.c_void_p), ("x_store", C.c_void_p), ("norm_w", C.c_void_p), ("eps", C.c_float),
+                ("epi", C.c_int), ("resid", C.c_void_p), ("argmax", C.c_void_p), ("argmax_base", C.c_int)]
+
+
+EPI_STORE, EPI_SWIGLU, EPI_RESID, EPI_ARGMAX = 0, 1, 2, 3
+
+
 def header_symbols() -> list[str]:
     """Every function the public header declares."""
     txt = open(HEADER).read()
@@ -57,6 +68,9 @@ def load() -> C.CDLL:
         "af_q6k_unpack": (i, [vp, vp, i, i, vp]),
         "af_gemv_f32": (i, [vp, vp, i, vp, i, i, vp]),
         "af_rms_norm_f32": (i, [vp, vp, vp, i, f, vp]),
+        "af_gemv_fused": (i, [C.POINTER(GemvFusedArgs), vp]),
+        "af_attention_decode_f32": (i, [vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i, i, i, i, i, f, i, vp, vp,
+                                        vp]),
         "af_silu_f32": (i, [vp, vp, i, vp]),
         "af_mul_f32": (i, [vp, vp, vp, i, vp]),
         "af_rope_f32": (i, [vp, i, i, i, f, vp]),

@@ -17,6 +17,19 @@ namespace {
 
 constexpr int kAttnThreads = 128;
 
+// Score slots per head: positions per split rounded up to 4 floats so the
+// areas after the scores stay 16-byte aligned for float4 access.
+__host__ __device__ inline int attn_chunk_max(int n_ctx, int nsplit) {
+    return ((n_ctx + nsplit - 1) / nsplit + 3) & ~3;
+}
+
+// Floats of the scratch area shared by the score partials [4][G][32] and the
+// output partials [position groups][G][hd].
+__host__ __device__ inline int attn_red1_floats(int G, int hd) {
+    const int a = 4 * G * 32, b = (kAttnThreads / (hd / 4)) * G * hd;
+    return a > b ? a : b;
+}
+
 __device__ __forceinline__ void rms_norm_head(float* x, const float* w, int hd, float eps, float* red) {
     // one warp (warp 0) normalises one head in shared memory
     const int lane = threadIdx.x & 31;
@@ -37,13 +50,13 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
     const int kvh = blockIdx.x, split = blockIdx.y;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int kvd = p.n_kv_heads * hd;
-    const int chunk_max = (p.n_ctx + p.nsplit - 1) / p.nsplit;
+    const int chunk_max = attn_chunk_max(p.n_ctx, p.nsplit);
 
     float* qs = sm;                 // [G][hd]
     float* ks = qs + G * hd;        // [hd]
     float* vs = ks + hd;            // [hd]
     float* sc = vs + hd;            // [G][chunk_max]
-    float* red = sc + G * chunk_max;  // [64]
+    float* red = sc + G * chunk_max + attn_red1_floats(G, hd);  // [64]
 
     pdl_launch_dependents();
     pdl_wait();
@@ -90,24 +103,50 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
     const int t0 = split * chunk;
     const int t1 = min(seq, t0 + chunk);
     const int nt = max(0, t1 - t0);
+    const int q4 = hd / 4;              // float4 per row
+    float* red1 = sc + G * chunk_max;   // [4][G][32] partial scores, later [npg][G][hd]
 
-    // scores: one warp per position, lanes over the head dims
-    for (int j = warp; j < nt; j += kAttnThreads / 32) {
-        const int t = t0 + j;
-        const float* kr = (t == pos) ? ks : p.kc + (size_t)t * kvd + (size_t)kvh * hd;
-        float kv[4];
+    // scores: thread = (position lane, quarter of the head dims); all of a
+    // thread's K loads are independent, so a tile costs one memory latency.
+    for (int j0 = 0; j0 < nt; j0 += 32) {
+        const int j = j0 + lane;
+        const int quarter = warp;
+        const int d0 = quarter * (q4 / 4);  // first float4 of this quarter
+        float part[16];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) kv[k] = (lane + 32 * k < hd) ? kr[lane + 32 * k] : 0.f;
-        for (int g = 0; g < G; ++g) {
-            float s = 0.f;
+        for (int g = 0; g < 16; ++g) part[g] = 0.f;
+        if (j < nt) {
+            const int t = t0 + j;
+            const float4* kr = reinterpret_cast<const float4*>((t == pos) ? ks : p.kc + (size_t)t * kvd + (size_t)kvh * hd);
+            float4 kv[8];
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
-                if (lane + 32 * k < hd) s += qs[g * hd + lane + 32 * k] * kv[k];
-            s = warp_sum(s);
-            if (lane == 0) sc[g * chunk_max + j] = s * p.scale;
+            for (int i = 0; i < 8; ++i)
+                if (i < q4 / 4) kv[i] = kr[d0 + i];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                if (i >= q4 / 4) break;
+#pragma unroll
+                for (int g = 0; g < 16; ++g) {
+                    if (g >= G) break;
+                    const float4 qv = reinterpret_cast<const float4*>(qs + g * hd)[d0 + i];
+                    part[g] += qv.x * kv[i].x + qv.y * kv[i].y + qv.z * kv[i].z + qv.w * kv[i].w;
+                }
+            }
         }
+#pragma unroll
+        for (int g = 0; g < 16; ++g)
+            if (g < G) red1[(quarter * G + g) * 32 + lane] = part[g];
+        __syncthreads();
+        for (int idx = tid; idx < G * 32; idx += kAttnThreads) {
+            const int g = idx / 32, l = idx % 32;
+            if (j0 + l < nt) {
+                const float s = red1[(0 * G + g) * 32 + l] + red1[(1 * G + g) * 32 + l] +
+                                red1[(2 * G + g) * 32 + l] + red1[(3 * G + g) * 32 + l];
+                sc[g * chunk_max + j0 + l] = s * p.scale;
+            }
+        }
+        __syncthreads();
     }
-    __syncthreads();
     // softmax pieces per head: warp w handles heads w, w+4, ...
     float* mrow = red;       // [G] (G <= 32)
     float* lrow = red + 32;  // [G]
@@ -125,48 +164,55 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
         if (lane == 0) { mrow[g] = m; lrow[g] = l; }
     }
     __syncthreads();
-    // o_g[d] = Σ_t e_t v_t[d]; threads over (d, position parity)
-    const int lanes_per_pos = hd;  // hd <= 128
-    const int npar = kAttnThreads / lanes_per_pos;  // 1 (hd=128) or 2 (hd=64)
-    const int d = tid % lanes_per_pos, par = tid / lanes_per_pos;
-    float acc[16];
+    // o_g[d] = Σ_t e_t v_t[d]: thread = (float4 of dims, position group);
+    // positions unrolled by 4 so the V loads overlap.
+    const int npg = kAttnThreads / q4;  // 4 (hd=128) or 8 (hd=64)
+    const int d4 = tid % q4, pg = tid / q4;
+    float4 acc[16];
 #pragma unroll
-    for (int g = 0; g < 16; ++g) acc[g] = 0.f;
-    if (par < npar) {
-        for (int j = par; j < nt; j += npar) {
+    for (int g = 0; g < 16; ++g) acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int jb = pg * 4; jb < nt; jb += npg * 4) {
+        float4 vv[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int j = jb + u;
             const int t = t0 + j;
-            const float vv = (t == pos) ? vs[d] : p.vc[(size_t)t * kvd + (size_t)kvh * hd + d];
-#pragma unroll
-            for (int g = 0; g < 16; ++g)
-                if (g < G) acc[g] = fmaf(sc[g * chunk_max + j], vv, acc[g]);
+            vv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (j < nt)
+                vv[u] = (t == pos) ? reinterpret_cast<const float4*>(vs)[d4]
+                                   : reinterpret_cast<const float4*>(p.vc + (size_t)t * kvd + (size_t)kvh * hd)[d4];
         }
-    }
-    __syncthreads();
-    // reduce the parities through shared memory (reuse the score area)
-    if (npar > 1) {  // the q area ([G][hd]) is free again and holds the second parity
-        if (par == 1) {
 #pragma unroll
-            for (int g = 0; g < 16; ++g)
-                if (g < G) qs[g * hd + d] = acc[g];
-        }
-        __syncthreads();
-        if (par == 0) {
+        for (int u = 0; u < 4; ++u) {
+            const int j = jb + u;
+            if (j >= nt) break;
 #pragma unroll
-            for (int g = 0; g < 16; ++g)
-                if (g < G) acc[g] += qs[g * hd + d];
-        }
-    }
-    if (par == 0) {
-#pragma unroll
-        for (int g = 0; g < 16; ++g) {
-            if (g >= G) break;
-            const int h = kvh * G + g;
-            float* dst = p.part + ((size_t)h * p.nsplit + split) * (hd + 2);
-            dst[d] = acc[g];
-            if (d == 0) {
-                dst[hd] = nt > 0 ? mrow[g] : -INFINITY;
-                dst[hd + 1] = nt > 0 ? lrow[g] : 0.f;
+            for (int g = 0; g < 16; ++g) {
+                if (g >= G) break;
+                const float e = sc[g * chunk_max + j];
+                acc[g].x = fmaf(e, vv[u].x, acc[g].x);
+                acc[g].y = fmaf(e, vv[u].y, acc[g].y);
+                acc[g].z = fmaf(e, vv[u].z, acc[g].z);
+                acc[g].w = fmaf(e, vv[u].w, acc[g].w);
             }
+        }
+    }
+    // reduce the position groups through shared memory (red1 is free again)
+    float* ored = red1;
+#pragma unroll
+    for (int g = 0; g < 16; ++g)
+        if (g < G) reinterpret_cast<float4*>(ored + (pg * G + g) * hd)[d4] = acc[g];
+    __syncthreads();
+    for (int idx = tid; idx < G * hd; idx += kAttnThreads) {
+        const int g = idx / hd, d = idx % hd;
+        float o = 0.f;
+        for (int q = 0; q < npg; ++q) o += ored[(q * G + g) * hd + d];
+        const int h = kvh * G + g;
+        float* dst = p.part + ((size_t)h * p.nsplit + split) * (hd + 2);
+        dst[d] = o;
+        if (d == 0) {
+            dst[hd] = nt > 0 ? mrow[g] : -INFINITY;
+            dst[hd + 1] = nt > 0 ? lrow[g] : 0.f;
         }
     }
     // ---- last CTA of this kv head merges the splits
@@ -215,8 +261,9 @@ cudaError_t attention_init() {
 
 int attention_smem_bytes(const AttnParams& p) {
     const int G = p.n_heads / p.n_kv_heads;
-    const int chunk_max = (p.n_ctx + p.nsplit - 1) / p.nsplit;
-    return (G * p.head_dim + 2 * p.head_dim + G * chunk_max + 64) * (int)sizeof(float);
+    const int chunk_max = attn_chunk_max(p.n_ctx, p.nsplit);
+    return (G * p.head_dim + 2 * p.head_dim + G * chunk_max + attn_red1_floats(G, p.head_dim) + 64) *
+           (int)sizeof(float);
 }
 
 cudaError_t attention_launch(const AttnParams& p, cudaStream_t st, bool pdl) {

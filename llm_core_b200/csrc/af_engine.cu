@@ -23,6 +23,7 @@
 #include <nccl.h>
 
 #include <cmath>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <map>
@@ -69,6 +70,7 @@ struct af_engine {
     ncclComm_t comm = nullptr;
     cudaStream_t stream = nullptr;
     int sms = 148;
+    bool pdl = true;  // programmatic dependent launch between the step's kernels (AF_PDL=0 disables)
 
     // local shard geometry
     int hd = 0, Hl = 0, KVl = 0, F0 = 0, F1 = 0, Fl = 0, V0 = 0, V1 = 0, Vl = 0, Vmax = 0;
@@ -141,19 +143,21 @@ cudaError_t upload_matrix(af_engine* e, DevMat& m, int type, const uint8_t* h, i
     uint8_t* stage = m.w;
     if (type == AF_GGML_Q6_K) ENG_TRY(cudaMalloc(&stage, (size_t)rows * gg_rb + 16));
     const uint8_t* src = h + (size_t)r0 * src_rb + (size_t)b0 * bb;
-    ENG_TRY(cudaMemcpy2D(stage, gg_rb, src, src_rb, gg_rb, rows, cudaMemcpyHostToDevice));
-    if (type == AF_GGML_Q6_K) {
-        ENG_TRY(q6k_repack(m.w, stage, rows, lcols, false, e->stream));
-        ENG_TRY(cudaStreamSynchronize(e->stream));
-        cudaFree(stage);
-    }
+    // Copy and regroup on the engine's (non-blocking) stream and wait: a
+    // synchronous cudaMemcpy from pageable memory may return before its DMA
+    // lands, and a non-blocking stream is not ordered after it.
+    ENG_TRY(cudaMemcpy2DAsync(stage, gg_rb, src, src_rb, gg_rb, rows, cudaMemcpyHostToDevice, e->stream));
+    if (type == AF_GGML_Q6_K) ENG_TRY(q6k_repack(m.w, stage, rows, lcols, false, e->stream));
+    ENG_TRY(cudaStreamSynchronize(e->stream));
+    if (type == AF_GGML_Q6_K) cudaFree(stage);
     e->weight_bytes += (size_t)rows * m.stride;
     return cudaSuccess;
 }
 
 cudaError_t upload_f32(af_engine* e, float*& dst, const void* h, size_t n, size_t off = 0) {
     dst = static_cast<float*>(e->dalloc(n * 4));
-    ENG_TRY(cudaMemcpy(dst, static_cast<const float*>(h) + off, n * 4, cudaMemcpyHostToDevice));
+    ENG_TRY(cudaMemcpyAsync(dst, static_cast<const float*>(h) + off, n * 4, cudaMemcpyHostToDevice, e->stream));
+    ENG_TRY(cudaStreamSynchronize(e->stream));
     return cudaSuccess;
 }
 
@@ -210,7 +214,7 @@ cudaError_t enqueue_step(af_engine* e, Prof* prof = nullptr) {
     int nk = 0;
     int cur = 0;  // residual buffer holding the current stream (TP ping-pong)
     ENG_TRY(embed_launch(e->x[0], e->tok_embd.w, e->tok_embd.type, E, e->tok_embd.stride, &e->tokpos[0], e->key,
-                         e->stream, true));
+                         e->stream, e->pdl));
     ++nk;
     AF_MARK(AF_PROF_EMBED, (double)e->tok_embd.stride + E * 4.0);
     bool pending = false;  // TP: ypart holds an un-added partial sum
@@ -232,7 +236,7 @@ cudaError_t enqueue_step(af_engine* e, Prof* prof = nullptr) {
             p.norm_w = L.attn_norm;
             p.epi = EPI_STORE;
             gemv_configure(p);
-            ENG_TRY(gemv_launch(p, e->sms, e->stream, true));
+            ENG_TRY(gemv_launch(p, e->sms, e->stream, e->pdl));
             ++nk;
             AF_MARK(AF_PROF_QKV, gemv_bytes(p));
         }
@@ -261,7 +265,7 @@ cudaError_t enqueue_step(af_engine* e, Prof* prof = nullptr) {
             a.qk_norm_order = c.qk_norm_order;
             a.eps = c.eps;
             a.scale = 1.f / std::sqrt((float)e->hd);
-            ENG_TRY(attention_launch(a, e->stream, true));
+            ENG_TRY(attention_launch(a, e->stream, e->pdl));
             ++nk;
             if (prof) {
                 const double kvb = 2.0 * (prof->pos + 1) * e->KVl * e->hd * 4.0;
@@ -281,7 +285,7 @@ cudaError_t enqueue_step(af_engine* e, Prof* prof = nullptr) {
                 p.resid = e->x[cur];
             }
             gemv_configure(p);
-            ENG_TRY(gemv_launch(p, e->sms, e->stream, true));
+            ENG_TRY(gemv_launch(p, e->sms, e->stream, e->pdl));
             ++nk;
             AF_MARK(AF_PROF_O, gemv_bytes(p));
             if (tp) {
@@ -306,7 +310,7 @@ cudaError_t enqueue_step(af_engine* e, Prof* prof = nullptr) {
             p.norm_w = L.ffn_norm;
             p.epi = EPI_SWIGLU;
             gemv_configure(p);
-            ENG_TRY(gemv_launch(p, e->sms, e->stream, true));
+            ENG_TRY(gemv_launch(p, e->sms, e->stream, e->pdl));
             ++nk;
             AF_MARK(AF_PROF_GATEUP, gemv_bytes(p) - 4.0 * p.seg[1].rows);
         }
@@ -323,7 +327,7 @@ cudaError_t enqueue_step(af_engine* e, Prof* prof = nullptr) {
                 p.resid = e->x[cur];
             }
             gemv_configure(p);
-            ENG_TRY(gemv_launch(p, e->sms, e->stream, true));
+            ENG_TRY(gemv_launch(p, e->sms, e->stream, e->pdl));
             ++nk;
             AF_MARK(AF_PROF_DOWN, gemv_bytes(p));
             if (tp) {
@@ -349,7 +353,7 @@ cudaError_t enqueue_step(af_engine* e, Prof* prof = nullptr) {
         p.argmax = e->key;
         p.argmax_base = e->V0;
         gemv_configure(p);
-        ENG_TRY(gemv_launch(p, e->sms, e->stream, true));
+        ENG_TRY(gemv_launch(p, e->sms, e->stream, e->pdl));
         ++nk;
         AF_MARK(AF_PROF_LMHEAD, gemv_bytes(p));
         if (tp) {
@@ -358,7 +362,7 @@ cudaError_t enqueue_step(af_engine* e, Prof* prof = nullptr) {
         }
     }
     if (cur != 0) return fail("internal: residual ping-pong did not return to buffer 0");
-    ENG_TRY(finalize_launch(e->key, &e->tokpos[0], &e->tokpos[1], e->hist, e->stream, true));
+    ENG_TRY(finalize_launch(e->key, &e->tokpos[0], &e->tokpos[1], e->hist, e->stream, e->pdl));
     ++nk;
     AF_MARK(AF_PROF_FINAL, 16.0);
     e->kernels_per_step = nk;
@@ -377,8 +381,8 @@ cudaError_t gather_logits(af_engine* e, float* h_logits) {
     for (int r = 0; r < e->tp; ++r) {
         int lo, hi;
         block_split(e->cfg.vocab, r, e->tp, lo, hi);
-        ENG_TRY(cudaMemcpy(h_logits + off, e->logits_all + (size_t)r * e->Vmax, (size_t)(hi - lo) * 4,
-                           cudaMemcpyDeviceToHost));
+        ENG_TRY(cudaMemcpyAsync(h_logits + off, e->logits_all + (size_t)r * e->Vmax, (size_t)(hi - lo) * 4,
+                                cudaMemcpyDeviceToHost, e->stream));
         off += hi - lo;
     }
     return cudaSuccess;
@@ -404,6 +408,8 @@ cudaError_t af_engine_create(const af_model_config* cfg, int device, int tp_rank
     if (c.n_embd % 256 || c.ffn % 256 || c.n_head <= 0 || c.n_embd % c.n_head || c.n_kv_head <= 0 ||
         c.n_head % c.n_kv_head || c.n_layer <= 0 || c.vocab <= 0 || c.n_ctx <= 0)
         return fail("af_engine_create: unsupported model shape (n_embd, ffn multiples of 256)");
+    if (c.n_embd > kGemvMaxK || ((c.ffn / 256 + tp_size - 1) / tp_size) * 256 > kGemvMaxK)
+        return fail("af_engine_create: n_embd and the per-rank ffn must be <= 12288");
     if (tp_size < 1 || tp_rank < 0 || tp_rank >= tp_size) return fail("af_engine_create: bad tp rank/size");
     if (tp_size > 1 && (c.n_kv_head % tp_size || ((c.n_embd / tp_size) % 256)))
         return fail("af_engine_create: tensor parallel needs n_kv_head and n_embd/256 divisible by tp_size");
@@ -415,6 +421,7 @@ cudaError_t af_engine_create(const af_model_config* cfg, int device, int tp_rank
     ENG_TRY(cudaSetDevice(device));
     ENG_TRY(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
     e->sms = num_sms();
+    if (const char* v = std::getenv("AF_PDL")) e->pdl = std::atoi(v) != 0;
     e->hd = c.n_embd / c.n_head;
     e->Hl = c.n_head / tp_size;
     e->KVl = c.n_kv_head / tp_size;
@@ -740,7 +747,8 @@ cudaError_t af_engine_generate(af_engine* e, const int32_t* h_prompt, int n_prom
 
 cudaError_t af_engine_hidden(af_engine* e, float* h_out) {
     AF_CUDA_TRY(check_ready(e));
-    ENG_TRY(cudaMemcpy(h_out, e->x[0], (size_t)e->cfg.n_embd * 4, cudaMemcpyDeviceToHost));
+    ENG_TRY(cudaMemcpyAsync(h_out, e->x[0], (size_t)e->cfg.n_embd * 4, cudaMemcpyDeviceToHost, e->stream));
+    ENG_TRY(cudaStreamSynchronize(e->stream));
     return cudaSuccess;
 }
 
@@ -749,7 +757,8 @@ cudaError_t af_engine_kv(af_engine* e, int layer, int which_v, int n_pos, float*
     if (layer < 0 || layer >= e->cfg.n_layer || n_pos < 0 || n_pos > e->cfg.n_ctx) return fail("af_engine_kv: range");
     const size_t row = (size_t)e->KVl * e->hd;
     const float* base = (which_v ? e->vcache : e->kcache) + (size_t)layer * e->cfg.n_ctx * row;
-    ENG_TRY(cudaMemcpy(h_out, base, (size_t)n_pos * row * 4, cudaMemcpyDeviceToHost));
+    ENG_TRY(cudaMemcpyAsync(h_out, base, (size_t)n_pos * row * 4, cudaMemcpyDeviceToHost, e->stream));
+    ENG_TRY(cudaStreamSynchronize(e->stream));
     return cudaSuccess;
 }
 

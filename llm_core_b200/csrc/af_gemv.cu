@@ -9,6 +9,8 @@ namespace {
 
 constexpr int kConsumerWarps = 8;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
+// float4 registers per consumer thread for the input: K <= 256*12*4 = 12288.
+constexpr int kPrologueVec = kGemvMaxK / (kConsumerThreads * 4);
 
 struct Tile {
     int seg;     // segment of the tile's rows
@@ -266,20 +268,37 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
     }
 
     // ---------------- consumer warps: input prologue ----------------
+    // All global loads of the input are issued together (one memory latency),
+    // held in registers, then normalised and quantised.
     pdl_wait();
     const int tid = threadIdx.x;  // 0..255
     const int nvec = p.K / 4;
-    float inv_rms = 1.f;
-    if (p.norm_w) {
-        float ss = 0.f;
-        for (int v = tid; v < nvec; v += kConsumerThreads) {
-            float4 a = reinterpret_cast<const float4*>(p.x)[v];
+    const int niter = nst * 2;    // float4 slots per thread incl. the padded last stage
+    float4 a[kPrologueVec];
+#pragma unroll
+    for (int j = 0; j < kPrologueVec; ++j) {
+        a[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        const int v = j * kConsumerThreads + tid;
+        if (j < niter && v < nvec) {
+            a[j] = reinterpret_cast<const float4*>(p.x)[v];
             if (p.x_add) {
                 const float4 b = reinterpret_cast<const float4*>(p.x_add)[v];
-                a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+                a[j].x += b.x; a[j].y += b.y; a[j].z += b.z; a[j].w += b.w;
             }
-            ss += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w;
         }
+    }
+    if (p.x_store && blockIdx.x == 0) {
+#pragma unroll
+        for (int j = 0; j < kPrologueVec; ++j) {
+            const int v = j * kConsumerThreads + tid;
+            if (j < niter && v < nvec) reinterpret_cast<float4*>(p.x_store)[v] = a[j];
+        }
+    }
+    if (p.norm_w) {
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < kPrologueVec; ++j)
+            ss += a[j].x * a[j].x + a[j].y * a[j].y + a[j].z * a[j].z + a[j].w * a[j].w;
         ss = warp_sum(ss);
         if (lane == 0) red[warp] = ss;
         bar_consumers();
@@ -287,34 +306,32 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
 #pragma unroll
         for (int w = 0; w < kConsumerWarps; ++w) tot += red[w];
         // rms_norm_out (src/models/llama_model.cpp:393-419): 1/sqrt(ss/n + eps)
-        inv_rms = 1.f / sqrtf(tot / (float)p.K + p.eps);
-    }
-    // Quantise: 16 consecutive threads own one 64-value group.
-    for (int v0 = 0; v0 < nst * 512; v0 += kConsumerThreads) {
-        const int v = v0 + tid;  // float4 index (may exceed nvec in the padded last stage)
-        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (v < nvec) {
-            a = reinterpret_cast<const float4*>(p.x)[v];
-            if (p.x_add) {
-                const float4 b = reinterpret_cast<const float4*>(p.x_add)[v];
-                a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
-                if (p.x_store && blockIdx.x == 0) reinterpret_cast<float4*>(p.x_store)[v] = a;
-            }
-            if (p.norm_w) {
+        const float inv_rms = 1.f / sqrtf(tot / (float)p.K + p.eps);
+#pragma unroll
+        for (int j = 0; j < kPrologueVec; ++j) {
+            const int v = j * kConsumerThreads + tid;
+            if (j < niter && v < nvec) {
                 const float4 w = reinterpret_cast<const float4*>(p.norm_w)[v];
-                a.x = w.x * (a.x * inv_rms);
-                a.y = w.y * (a.y * inv_rms);
-                a.z = w.z * (a.z * inv_rms);
-                a.w = w.w * (a.w * inv_rms);
+                a[j].x = w.x * (a[j].x * inv_rms);
+                a[j].y = w.y * (a[j].y * inv_rms);
+                a[j].z = w.z * (a[j].z * inv_rms);
+                a[j].w = w.w * (a[j].w * inv_rms);
             }
         }
-        float amax = fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w)));
+    }
+    // Quantise: 16 consecutive threads own one 64-value group.
+#pragma unroll
+    for (int j = 0; j < kPrologueVec; ++j) {
+        if (j >= niter) break;
+        const int v = j * kConsumerThreads + tid;
+        const float4 q4 = a[j];
+        float amax = fmaxf(fmaxf(fabsf(q4.x), fabsf(q4.y)), fmaxf(fabsf(q4.z), fabsf(q4.w)));
 #pragma unroll
         for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
         // 16-bit grid of ±32639 so that hi = (q + 128) >> 8 stays within int8.
         const float xs = amax / 32639.f;
         const float inv = amax > 0.f ? 32639.f / amax : 0.f;
-        const float av[4] = {a.x, a.y, a.z, a.w};
+        const float av[4] = {q4.x, q4.y, q4.z, q4.w};
         uint32_t hw = 0, lw = 0;
         int isum = 0;
 #pragma unroll
@@ -327,7 +344,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
             lw |= (uint32_t)(lo & 0xFF) << (8 * e);
             isum += q;
         }
-        float fsum = a.x + a.y + a.z + a.w;
+        float fsum = q4.x + q4.y + q4.z + q4.w;
         fsum += __shfl_xor_sync(0xffffffffu, fsum, 1);
         fsum += __shfl_xor_sync(0xffffffffu, fsum, 2);
         isum += __shfl_xor_sync(0xffffffffu, isum, 1);

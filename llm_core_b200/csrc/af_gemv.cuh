@@ -62,6 +62,7 @@ struct GemvParams {
 constexpr int kGemvThreads = 288;  // 8 consumer warps + 1 producer warp
 constexpr int kGemvTileRows = 16;
 constexpr int kGemvMaxSlots = 6;
+constexpr int kGemvMaxK = 12288;  // input length held in registers by the prologue
 
 // Shared-memory bytes the GEMV needs for (K, pitch, nslots).
 __host__ __device__ inline int gemv_smem_bytes(int K, int pitch, int nslots) {

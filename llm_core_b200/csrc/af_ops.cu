@@ -204,6 +204,10 @@ cudaError_t af_gemv_f32(float* d_y, const void* d_w, int ggml_type, const float*
         set_last_error("af_gemv_f32: need Q4_K/Q6_K weights and cols % 256 == 0");
         return cudaErrorInvalidValue;
     }
+    if (cols > kGemvMaxK) {
+        set_last_error("af_gemv_f32: cols > 12288 is not supported");
+        return cudaErrorInvalidValue;
+    }
     if ((reinterpret_cast<uintptr_t>(d_w) & 15) || (reinterpret_cast<uintptr_t>(d_x) & 15)) {
         set_last_error("af_gemv_f32: weights and x must be 16-byte aligned");
         return cudaErrorInvalidValue;
@@ -222,6 +226,70 @@ cudaError_t af_gemv_f32(float* d_y, const void* d_w, int ggml_type, const float*
     gemv_configure(p);
     AF_CUDA_TRY(gemv_init());
     return gemv_launch(p, num_sms(), stream, false);
+}
+
+cudaError_t af_gemv_fused(const af_gemv_fused_args* a, cudaStream_t stream) {
+    if (!a || a->nseg < 1 || a->nseg > 3 || a->cols <= 0 || a->cols % 256 || a->cols > kGemvMaxK || !a->x) {
+        set_last_error("af_gemv_fused: need 1..3 segments, cols % 256 == 0, cols <= 12288");
+        return cudaErrorInvalidValue;
+    }
+    if (a->epi < AF_EPI_STORE || a->epi > AF_EPI_ARGMAX || (a->epi == AF_EPI_SWIGLU && a->nseg != 2) ||
+        (a->epi == AF_EPI_RESID && (!a->resid || a->nseg != 1)) || (a->epi == AF_EPI_ARGMAX && (!a->argmax || a->nseg != 1))) {
+        set_last_error("af_gemv_fused: epilogue / segment combination not supported");
+        return cudaErrorInvalidValue;
+    }
+    GemvParams p = {};
+    for (int s = 0; s < a->nseg; ++s) {
+        if ((a->type[s] != AF_GGML_Q4_K && a->type[s] != AF_GGML_Q6_K) || a->rows[s] < 0 ||
+            (reinterpret_cast<uintptr_t>(a->w[s]) & 15)) {
+            set_last_error("af_gemv_fused: bad segment");
+            return cudaErrorInvalidValue;
+        }
+        p.seg[s].w = static_cast<const uint8_t*>(a->w[s]);
+        p.seg[s].y = a->y[s];
+        p.seg[s].bias = a->bias[s];
+        p.seg[s].type = a->type[s];
+        p.seg[s].rows = a->rows[s];
+        p.seg[s].row_stride = dev_row_stride(a->type[s], a->cols);
+    }
+    if (a->epi == AF_EPI_SWIGLU && a->rows[0] != a->rows[1]) {
+        set_last_error("af_gemv_fused: SwiGLU needs equal gate/up rows");
+        return cudaErrorInvalidValue;
+    }
+    p.nseg = a->nseg;
+    p.K = a->cols;
+    p.x = a->x;
+    p.x_add = a->x_add;
+    p.x_store = a->x_store;
+    p.norm_w = a->norm_w;
+    p.eps = a->eps;
+    p.epi = a->epi;
+    p.resid = a->resid;
+    p.argmax = a->argmax;
+    p.argmax_base = a->argmax_base;
+    gemv_configure(p);
+    AF_CUDA_TRY(gemv_init());
+    return gemv_launch(p, num_sms(), stream, false);
+}
+
+cudaError_t af_attention_decode_f32(float* d_out, const float* d_q, const float* d_k, const float* d_v,
+                                    float* d_kcache, float* d_vcache, const float* d_cos, const float* d_sin,
+                                    const float* d_q_norm, const float* d_k_norm, const int* d_pos, int n_heads,
+                                    int n_kv_heads, int head_dim, int n_ctx, int qk_norm_order, float eps,
+                                    int nsplit, float* d_part, unsigned int* d_counter, cudaStream_t stream) {
+    if (n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads || nsplit <= 0 || n_ctx <= 0) {
+        set_last_error("af_attention_decode_f32: bad shape");
+        return cudaErrorInvalidValue;
+    }
+    AttnParams p = {};
+    p.q = d_q; p.k = d_k; p.v = d_v; p.kc = d_kcache; p.vc = d_vcache; p.out = d_out;
+    p.cos_t = d_cos; p.sin_t = d_sin; p.q_norm = d_q_norm; p.k_norm = d_k_norm;
+    p.part = d_part; p.counter = d_counter; p.pos = d_pos;
+    p.n_heads = n_heads; p.n_kv_heads = n_kv_heads; p.head_dim = head_dim; p.n_ctx = n_ctx;
+    p.nsplit = nsplit; p.qk_norm_order = qk_norm_order; p.eps = eps;
+    p.scale = 1.f / sqrtf((float)head_dim);
+    AF_CUDA_TRY(attention_init());
+    return attention_launch(p, stream, false);
 }
 
 cudaError_t af_rms_norm_f32(float* d_y, const float* d_x, const float* d_w, int n, float eps, cudaStream_t stream) {

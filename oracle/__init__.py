@@ -78,6 +78,7 @@ class COracle:
         L.afo_forward_token.argtypes = [C.c_void_p, C.c_int, C.c_int, _fp]
         L.afo_destroy.argtypes = [C.c_void_p]
         L.afo_hidden.argtypes = [C.c_void_p, _fp]
+        L.afo_kv.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, _fp]
         L.afo_set_threads(int(threads or min(os.cpu_count() or 1, 32)))
         self._model = None
 
@@ -158,6 +159,12 @@ class COracle:
         h = np.zeros(self.cfg.n_embd, np.float32)
         self.lib.afo_hidden(self._model, _f(h))
         return h
+
+    def kv(self, layer: int, which_v: bool, n_pos: int) -> np.ndarray:
+        kvd = self.cfg.n_kv_head * self.cfg.head_dim
+        out = np.zeros((n_pos, kvd), np.float32)
+        self.lib.afo_kv(self._model, layer, int(which_v), n_pos, _f(out))
+        return out
 
     def generate_greedy(self, prompt, max_new: int, bos: int = 1):
         """BOS prepend + per-token prefill + argmax decode (llama_model.cpp:1562-1624)."""

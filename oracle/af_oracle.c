@@ -447,8 +447,8 @@ int afo_forward_token(void* h, int token, int pos, float* logits_out) {
         afo_gemv(m->ffo, lw->wd, lw->td, m->gate, E, FD);
         for (int i = 0; i < E; i++) m->x[i] += m->ffo[i];
     }
-    afo_rms_norm(m->x, m->x, m->out_norm, E, c->eps);
-    afo_gemv(m->logits, m->output, m->out_type, m->x, c->vocab, E);
+    afo_rms_norm(m->xb, m->x, m->out_norm, E, c->eps);
+    afo_gemv(m->logits, m->output, m->out_type, m->xb, c->vocab, E);
     if (logits_out) memcpy(logits_out, m->logits, (size_t)c->vocab * 4);
     return 0;
 }
@@ -460,9 +460,17 @@ int afo_argmax(const float* v, int n) {
     return best;
 }
 
-/* Residual stream after the last forward (the final RMSNorm is applied in
- * place, as rms_norm_avx2(s.x) does at llama_model.cpp:1328). */
+/* Residual stream after the last forward, before the final RMSNorm (the
+ * reference normalises it in place, rms_norm_avx2(s.x) at llama_model.cpp:1328;
+ * here the normalised copy goes to a scratch buffer instead). */
 void afo_hidden(void* h, float* out) {
     afo_model* m = (afo_model*)h;
     memcpy(out, m->x, (size_t)m->c.n_embd * 4);
+}
+
+/* Rows [0, n_pos) of layer l's K (which_v = 0) or V cache. */
+void afo_kv(void* h, int l, int which_v, int n_pos, float* out) {
+    afo_model* m = (afo_model*)h;
+    const float* base = (which_v ? m->kv_v : m->kv_k) + (size_t)l * m->c.n_ctx * m->kv_dim;
+    memcpy(out, base, (size_t)n_pos * m->kv_dim * 4);
 }
