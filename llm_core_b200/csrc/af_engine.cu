@@ -70,6 +70,7 @@ struct af_engine {
     ncclComm_t comm = nullptr;
     cudaStream_t stream = nullptr;
     int sms = 148;
+    int gemv_ctas = 148;
     bool pdl = true;  // programmatic dependent launch between the step's kernels (AF_PDL=0 disables)
 
     // local shard geometry
@@ -236,7 +237,7 @@ cudaError_t enqueue_step(af_engine* e, Prof* prof = nullptr) {
             p.norm_w = L.attn_norm;
             p.epi = EPI_STORE;
             gemv_configure(p);
-            ENG_TRY(gemv_launch(p, e->sms, e->stream, e->pdl));
+            ENG_TRY(gemv_launch(p, e->gemv_ctas, e->stream, e->pdl));
             ++nk;
             AF_MARK(AF_PROF_QKV, gemv_bytes(p));
         }
@@ -285,7 +286,7 @@ cudaError_t enqueue_step(af_engine* e, Prof* prof = nullptr) {
                 p.resid = e->x[cur];
             }
             gemv_configure(p);
-            ENG_TRY(gemv_launch(p, e->sms, e->stream, e->pdl));
+            ENG_TRY(gemv_launch(p, e->gemv_ctas, e->stream, e->pdl));
             ++nk;
             AF_MARK(AF_PROF_O, gemv_bytes(p));
             if (tp) {
@@ -310,7 +311,7 @@ cudaError_t enqueue_step(af_engine* e, Prof* prof = nullptr) {
             p.norm_w = L.ffn_norm;
             p.epi = EPI_SWIGLU;
             gemv_configure(p);
-            ENG_TRY(gemv_launch(p, e->sms, e->stream, e->pdl));
+            ENG_TRY(gemv_launch(p, e->gemv_ctas, e->stream, e->pdl));
             ++nk;
             AF_MARK(AF_PROF_GATEUP, gemv_bytes(p) - 4.0 * p.seg[1].rows);
         }
@@ -327,7 +328,7 @@ cudaError_t enqueue_step(af_engine* e, Prof* prof = nullptr) {
                 p.resid = e->x[cur];
             }
             gemv_configure(p);
-            ENG_TRY(gemv_launch(p, e->sms, e->stream, e->pdl));
+            ENG_TRY(gemv_launch(p, e->gemv_ctas, e->stream, e->pdl));
             ++nk;
             AF_MARK(AF_PROF_DOWN, gemv_bytes(p));
             if (tp) {
@@ -353,7 +354,7 @@ cudaError_t enqueue_step(af_engine* e, Prof* prof = nullptr) {
         p.argmax = e->key;
         p.argmax_base = e->V0;
         gemv_configure(p);
-        ENG_TRY(gemv_launch(p, e->sms, e->stream, e->pdl));
+        ENG_TRY(gemv_launch(p, e->gemv_ctas, e->stream, e->pdl));
         ++nk;
         AF_MARK(AF_PROF_LMHEAD, gemv_bytes(p));
         if (tp) {
@@ -421,6 +422,7 @@ cudaError_t af_engine_create(const af_model_config* cfg, int device, int tp_rank
     ENG_TRY(cudaSetDevice(device));
     ENG_TRY(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
     e->sms = num_sms();
+    e->gemv_ctas = gemv_grid();
     if (const char* v = std::getenv("AF_PDL")) e->pdl = std::atoi(v) != 0;
     e->hd = c.n_embd / c.n_head;
     e->Hl = c.n_head / tp_size;

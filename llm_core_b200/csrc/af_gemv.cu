@@ -109,22 +109,24 @@ __device__ __forceinline__ float q4k_lane_dot(const uint8_t* blk, int c, const X
     const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
     const int* xh0 = reinterpret_cast<const int*>(&x.h[0]);
     const int* xl0 = reinterpret_cast<const int*>(&x.l[0]);
-    int lh = 0, ll = 0, hh = 0, hl = 0;
+    // two interleaved accumulator sets (even / odd words) halve the dp4a chains
+    int lh[2] = {0, 0}, ll[2] = {0, 0}, hh[2] = {0, 0}, hl[2] = {0, 0};
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
         // words 0-3: qs bytes 0-15 of the chunk -> x chunk 0 (lo) / 2 (hi);
         // words 4-7: bytes 16-31 -> x chunk 1 (lo) / 3 (hi).
         const uint32_t lo = qw[k] & 0x0F0F0F0Fu;
         const uint32_t hi = qw[k] & 0xF0F0F0F0u;  // 16 x high nibble
-        const int xi_lo = (k < 4 ? 0 : 4) + (k & 3);
-        const int xi_hi = (k < 4 ? 8 : 12) + (k & 3);
-        lh = dp4a_us(lo, xh0[xi_lo], lh);
-        ll = dp4a_us(lo, xl0[xi_lo], ll);
-        hh = dp4a_us(hi, xh0[xi_hi], hh);
-        hl = dp4a_us(hi, xl0[xi_hi], hl);
+        const int xi_lo = k;
+        const int xi_hi = 8 + k;
+        const int e = k & 1;
+        lh[e] = dp4a_us(lo, xh0[xi_lo], lh[e]);
+        ll[e] = dp4a_us(lo, xl0[xi_lo], ll[e]);
+        hh[e] = dp4a_us(hi, xh0[xi_hi], hh[e]);
+        hl[e] = dp4a_us(hi, xl0[xi_hi], hl[e]);
     }
-    const int tlo = lh * 256 + ll;
-    const int thi = (hh * 256 + hl) >> 4;  // exact: every term is a multiple of 16
+    const int tlo = (lh[0] + lh[1]) * 256 + (ll[0] + ll[1]);
+    const int thi = ((hh[0] + hh[1]) * 256 + (hl[0] + hl[1])) >> 4;  // exact: every term is a multiple of 16
     // 6-bit scale/min pairs j = 2c (low nibbles) and 2c+1 (high nibbles):
     // get_scale_min_k4 (gemv_q4k_avx2.cpp:34-43) four bytes at a time.
     const uint32_t w0 = hdr.y, w1 = hdr.z, w2 = hdr.w;
@@ -378,6 +380,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
         bool rv[2];
         rv[0] = tile_row(p, t, warp, seg[0], row[0]);
         rv[1] = tile_row(p, t, warp + 8, seg[1], row[1]);
+        const int ty0 = p.seg[seg[0]].type, ty1 = p.seg[seg[1]].type;
         for (int st = 0; st < nst; ++st) {
             const int slot = consumed % p.nslots;
             const uint32_t ph = (consumed / p.nslots) & 1u;
@@ -396,15 +399,33 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
                 x.xs = XS[st * 32 + lane];
                 x.s32[0] = XS32[st * 64 + lane];
                 x.s32[1] = XS32[st * 64 + 32 + lane];
+                // Both rows of the warp are evaluated without branches so their
+                // independent dp4a chains interleave; an invalid row reads
+                // stale shared memory and its result is discarded.
+                const uint8_t* rp0 = ring + (slot * kGemvTileRows + warp) * p.pitch;
+                const uint8_t* rp1 = ring + (slot * kGemvTileRows + warp + 8) * p.pitch;
+                if (ty0 == ty1 && ty0 == AF_GGML_Q6_K) {
+                    const float d0 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(rp0 + nbs * 208 + 2 * lb));
+                    const float d1 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(rp1 + nbs * 208 + 2 * lb));
+                    const float a0 = q6k_lane_dot(rp0 + lb * 208, d0, lc, x);
+                    const float a1 = q6k_lane_dot(rp1 + lb * 208, d1, lc, x);
+                    acc[0] += a0;
+                    acc[1] += a1;
+                } else if (ty0 == ty1) {
+                    const float a0 = q4k_lane_dot(rp0 + lb * 144, lc, x);
+                    const float a1 = q4k_lane_dot(rp1 + lb * 144, lc, x);
+                    acc[0] += a0;
+                    acc[1] += a1;
+                } else {
 #pragma unroll
-                for (int r = 0; r < 2; ++r) {
-                    if (!rv[r]) continue;
-                    const uint8_t* rp = ring + (slot * kGemvTileRows + warp + 8 * r) * p.pitch;
-                    if (p.seg[seg[r]].type == AF_GGML_Q6_K) {
-                        const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(rp + nbs * 208 + 2 * lb));
-                        acc[r] += q6k_lane_dot(rp + lb * 208, d, lc, x);
-                    } else {
-                        acc[r] += q4k_lane_dot(rp + lb * 144, lc, x);
+                    for (int r = 0; r < 2; ++r) {
+                        const uint8_t* rp = r ? rp1 : rp0;
+                        if ((r ? ty1 : ty0) == AF_GGML_Q6_K) {
+                            const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(rp + nbs * 208 + 2 * lb));
+                            acc[r] += q6k_lane_dot(rp + lb * 208, d, lc, x);
+                        } else {
+                            acc[r] += q4k_lane_dot(rp + lb * 144, lc, x);
+                        }
                     }
                 }
             }

@@ -1,6 +1,7 @@
 // af_ops.cu — C-ABI kernel launchers and the small decode kernels: Q6_K
 // regroup, embedding-row dequant, and the reference CUDA backend's op set
 // (RMSNorm, SiLU, Mul, RoPE; src/backend/cuda/cuda_kernels.hpp:8-19).
+#include <cstdlib>
 #include <string>
 
 #include "af_gemv.cuh"
@@ -11,6 +12,16 @@ namespace af {
 thread_local std::string g_last_error;
 
 void set_last_error(const std::string& s) { g_last_error = s; }
+
+// CTAs per SM of the GEMV grid (AF_GEMV_CTAS_PER_SM, default 1).
+int gemv_grid() {
+    static int per_sm = [] {
+        const char* v = std::getenv("AF_GEMV_CTAS_PER_SM");
+        const int n = v ? std::atoi(v) : 1;
+        return n < 1 ? 1 : (n > 4 ? 4 : n);
+    }();
+    return num_sms() * per_sm;
+}
 
 int num_sms() {
     int dev = 0, n = 0;
@@ -225,7 +236,7 @@ cudaError_t af_gemv_f32(float* d_y, const void* d_w, int ggml_type, const float*
     p.epi = EPI_STORE;
     gemv_configure(p);
     AF_CUDA_TRY(gemv_init());
-    return gemv_launch(p, num_sms(), stream, false);
+    return gemv_launch(p, gemv_grid(), stream, false);
 }
 
 cudaError_t af_gemv_fused(const af_gemv_fused_args* a, cudaStream_t stream) {
@@ -269,7 +280,7 @@ cudaError_t af_gemv_fused(const af_gemv_fused_args* a, cudaStream_t stream) {
     p.argmax_base = a->argmax_base;
     gemv_configure(p);
     AF_CUDA_TRY(gemv_init());
-    return gemv_launch(p, num_sms(), stream, false);
+    return gemv_launch(p, gemv_grid(), stream, false);
 }
 
 cudaError_t af_attention_decode_f32(float* d_out, const float* d_q, const float* d_k, const float* d_v,
