@@ -314,18 +314,14 @@ def run_gemv_sweep(args):
         for (m, k) in shapes:
             gen = gguf.random_q4k if t == gguf.GGML_Q4_K else gguf.random_q6k
             host = gen(rng, m * k // 256).reshape(-1)
-            stride = lib.af_row_stride(t, k)
-            nbytes = m * stride
+            nbytes = lib.af_weight_bytes(t, m, k)
             copies = max(1, int(np.ceil(300e6 / nbytes)))
             src = torch.from_numpy(host).cuda()
             ws = []
             for _ in range(copies):
-                if t == gguf.GGML_Q4_K:
-                    ws.append(src.clone())
-                else:
-                    w = torch.empty(m * stride + 64, dtype=torch.uint8, device="cuda")
-                    assert lib.af_q6k_repack(w.data_ptr(), src.data_ptr(), m, k, None) == 0
-                    ws.append(w)
+                w = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+                assert lib.af_weight_pack(w.data_ptr(), src.data_ptr(), t, m, k, None) == 0
+                ws.append(w)
             x = torch.randn(k, device="cuda")
             y = torch.empty(m, device="cuda")
             st = torch.cuda.current_stream().cuda_stream
@@ -340,7 +336,7 @@ def run_gemv_sweep(args):
             e1.record()
             torch.cuda.synchronize()
             us = e0.elapsed_time(e1) * 1000 / n
-            alg = nbytes + 4 * (k + m)
+            alg = m * k // 256 * (144 if t == gguf.GGML_Q4_K else 210) + 4 * (k + m)
             gbs = alg / (us * 1e-6) / 1e9
             print(json.dumps({"kernel": "gemv_kernel", "type": "Q4_K" if t == 12 else "Q6_K", "M": m, "K": k,
                               "batch": 1, "us": round(us, 2), "bytes": alg, "GBps": round(gbs, 1),

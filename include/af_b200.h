@@ -14,11 +14,14 @@
  *      weights uploaded byte-for-byte, fp32 KV cache on the device, one CUDA
  *      graph per decode step, optional tensor parallelism over NCCL.
  *
- * Weight layouts on the device: Q4_K rows are the GGUF bytes unchanged
- * (144-byte super-blocks, row stride = cols/256*144).  Q6_K rows are the GGUF
- * super-blocks regrouped once at upload by af_q6k_repack: groups of 8 blocks,
- * each [8 x (ql[128] qh[64] scales[16])][8 x f16 d], so every group starts on a
- * 16-byte boundary (af_q6k_row_stride gives the stride).
+ * Weight layout on the device ("packed"): the GGUF super-blocks, byte for byte,
+ * permuted once at upload by af_weight_pack so that every pipeline stage of the
+ * GEMV is one contiguous range.  Rows are grouped in tiles of 16 (the last tile
+ * zero-padded); a tile holds, stage after stage, the 16 rows' segments of 8
+ * super-blocks (the last stage fewer).  A Q4_K segment is its 144-byte blocks
+ * unchanged; a Q6_K segment is each block's ql/qh/scales (208 bytes) followed
+ * by the blocks' f16 d values padded to 16 bytes, so every segment starts on a
+ * 16-byte boundary.
  */
 #ifndef AF_B200_H
 #define AF_B200_H
@@ -47,19 +50,23 @@ cudaError_t af_device_error(int* h_code, int clear);
 
 /* ---------------------------------------------------------- weight layout */
 
-/* Bytes of one device row of `cols` values for `ggml_type` (Q4_K: GGUF row;
- * Q6_K: regrouped row, >= the GGUF row by at most 14 bytes). */
+/* Bytes of one packed row of `cols` values (Q4_K: cols/256*144; Q6_K:
+ * >= cols/256*210 by at most 14 bytes), 0 for unsupported arguments. */
 size_t af_row_stride(int ggml_type, int cols);
+/* Device bytes of a packed rows x cols matrix (whole 16-row tiles). */
+size_t af_weight_bytes(int ggml_type, int rows, int cols);
 
-/* Regroup `rows` GGUF Q6_K rows (d_src, stride cols/256*210) into the device
- * layout at d_dst (stride af_row_stride(AF_GGML_Q6_K, cols)).  Byte-preserving
- * permutation; af_q6k_unpack inverts it. */
-cudaError_t af_q6k_repack(void* d_dst, const void* d_src, int rows, int cols, cudaStream_t stream);
-cudaError_t af_q6k_unpack(void* d_dst, const void* d_src, int rows, int cols, cudaStream_t stream);
+/* Pack `rows` GGUF rows (d_src, contiguous GGUF bytes) of a Q4_K or Q6_K
+ * matrix into the packed layout at d_dst (af_weight_bytes bytes).
+ * Byte-preserving permutation; af_weight_unpack inverts it. */
+cudaError_t af_weight_pack(void* d_dst, const void* d_src, int ggml_type, int rows, int cols,
+                           cudaStream_t stream);
+cudaError_t af_weight_unpack(void* d_dst, const void* d_src, int ggml_type, int rows, int cols,
+                             cudaStream_t stream);
 
 /* ------------------------------------------------------- kernel launchers */
 
-/* y[rows] = W · x with W in the device layout above and f32 x[cols]: the fused
+/* y[rows] = W · x with W packed (af_weight_pack) and f32 x[cols]: the fused
  * dequant GEMV (fp32 accumulation).  Replaces q4km_gemv_f32
  * (src/backend/cuda/cuda_kernels.hpp:13-19, numerically wrong in the
  * reference) and adds Q6_K.  Parity target: gemv_q4k_avx2_range /

@@ -11,7 +11,7 @@ import re
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
-LIB_PATH = os.path.join(HERE, "libaf_b200.so")
+LIB_PATH = os.environ.get("AF_LIB_PATH") or os.path.join(HERE, "libaf_b200.so")
 HEADER = os.path.join(ROOT, "include", "af_b200.h")
 
 _lib = None
@@ -64,8 +64,9 @@ def load() -> C.CDLL:
         "af_last_error": (C.c_char_p, []),
         "af_device_error": (i, [C.POINTER(C.c_int), i]),
         "af_row_stride": (sz, [i, i]),
-        "af_q6k_repack": (i, [vp, vp, i, i, vp]),
-        "af_q6k_unpack": (i, [vp, vp, i, i, vp]),
+        "af_weight_bytes": (sz, [i, i, i]),
+        "af_weight_pack": (i, [vp, vp, i, i, i, vp]),
+        "af_weight_unpack": (i, [vp, vp, i, i, i, vp]),
         "af_gemv_f32": (i, [vp, vp, i, vp, i, i, vp]),
         "af_rms_norm_f32": (i, [vp, vp, vp, i, f, vp]),
         "af_gemv_fused": (i, [C.POINTER(GemvFusedArgs), vp]),

@@ -77,7 +77,7 @@ struct af_engine {
     int hd = 0, Hl = 0, KVl = 0, F0 = 0, F1 = 0, Fl = 0, V0 = 0, V1 = 0, Vl = 0, Vmax = 0;
 
     // weights
-    DevMat tok_embd, output;
+    DevMat tok_embd, output, tok_head;
     float* out_norm = nullptr;
     std::vector<LayerW> layers;
     std::vector<void*> allocs;
@@ -140,17 +140,17 @@ cudaError_t upload_matrix(af_engine* e, DevMat& m, int type, const uint8_t* h, i
     m.rows = rows;
     m.cols = lcols;
     m.stride = dev_row_stride(type, lcols);
-    m.w = static_cast<uint8_t*>(e->dalloc((size_t)rows * m.stride + 64));
-    uint8_t* stage = m.w;
-    if (type == AF_GGML_Q6_K) ENG_TRY(cudaMalloc(&stage, (size_t)rows * gg_rb + 16));
+    m.w = static_cast<uint8_t*>(e->dalloc(packed_bytes(type, rows, lcols) + 64));
+    uint8_t* stage = nullptr;
+    ENG_TRY(cudaMalloc(&stage, (size_t)rows * gg_rb + 16));
     const uint8_t* src = h + (size_t)r0 * src_rb + (size_t)b0 * bb;
-    // Copy and regroup on the engine's (non-blocking) stream and wait: a
+    // Copy and pack on the engine's (non-blocking) stream and wait: a
     // synchronous cudaMemcpy from pageable memory may return before its DMA
     // lands, and a non-blocking stream is not ordered after it.
     ENG_TRY(cudaMemcpy2DAsync(stage, gg_rb, src, src_rb, gg_rb, rows, cudaMemcpyHostToDevice, e->stream));
-    if (type == AF_GGML_Q6_K) ENG_TRY(q6k_repack(m.w, stage, rows, lcols, false, e->stream));
+    ENG_TRY(weight_pack(m.w, stage, type, rows, lcols, false, e->stream));
     ENG_TRY(cudaStreamSynchronize(e->stream));
-    if (type == AF_GGML_Q6_K) cudaFree(stage);
+    cudaFree(stage);
     e->weight_bytes += (size_t)rows * m.stride;
     return cudaSuccess;
 }
@@ -477,7 +477,11 @@ cudaError_t af_engine_load_tensor(af_engine* e, const char* name_c, int type, co
     auto need_f32 = [&](size_t n) -> bool { return type == AF_GGML_F32 && (size_t)numel == n; };
     if (name == "token_embd.weight") {
         if (cols != E || rows != c.vocab) return fail("token_embd.weight: shape mismatch");
-        return upload_matrix(e, e->tok_embd, type, hb, cols, 0, rows, 0, cols / 256);
+        AF_CUDA_TRY(upload_matrix(e, e->tok_embd, type, hb, cols, 0, rows, 0, cols / 256));
+        // A tied LM head needs this rank's vocabulary rows packed on their own
+        // (the packed layout is tile-major); with one rank it aliases the table.
+        if (e->tp > 1) return upload_matrix(e, e->tok_head, type, hb, cols, e->V0, e->V1, 0, cols / 256);
+        return cudaSuccess;
     }
     if (name == "output.weight") {
         if (cols != E || rows != c.vocab) return fail("output.weight: shape mismatch");
@@ -581,9 +585,12 @@ cudaError_t af_engine_finalize(af_engine* e) {
         if (!e->out_norm) return fail("missing output_norm.weight");
         if (!e->output.present()) {
             // tied head: output falls back to token_embd (make_wt_opt, llama_model.cpp:979)
-            e->output = e->tok_embd;
-            e->output.w = e->tok_embd.w + (size_t)e->V0 * e->tok_embd.stride;
-            e->output.rows = e->Vl;
+            if (e->tp > 1) {
+                e->output = e->tok_head;
+                e->weight_bytes -= (size_t)e->Vl * e->tok_embd.stride;  // counted below as the head
+            } else {
+                e->output = e->tok_embd;
+            }
             e->weight_bytes += (size_t)e->Vl * e->tok_embd.stride;
         }
         // The embedding table is read one row per step: not part of the per-token stream.

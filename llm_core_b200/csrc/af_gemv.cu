@@ -61,6 +61,10 @@ struct TileIter {
         long long stop = cur + cap;
         if (stop > end) stop = end;
         if (stop > base + p.seg[s].rows) stop = base + p.seg[s].rows;
+        // a fragment never crosses a 16-row tile of the packed layout, so each
+        // of its stages is one contiguous range
+        const long long tile_end = base + ((cur - base) / kGemvTileRows + 1) * kGemvTileRows;
+        if (stop > tile_end) stop = tile_end;
         t.seg = s;
         t.row0 = (int)(cur - base);
         t.n = (int)(stop - cur);
@@ -82,15 +86,19 @@ __device__ __forceinline__ bool tile_row(const GemvParams& p, const Tile& t, int
     return pr < t.n;
 }
 
-// Bytes of one row's segment for stage `st` of a row of type `type`.
-__device__ __forceinline__ uint32_t stage_row_bytes(int type, int nb, int st, uint32_t& src_off) {
-    const int nbs = min(8, nb - st * 8);
-    if (type == AF_GGML_Q6_K) {
-        src_off = (uint32_t)st * 1680u;
-        return (uint32_t)nbs * 208u + 16u;
-    }
-    src_off = (uint32_t)st * 8u * 144u;
-    return (uint32_t)nbs * 144u;
+// Bytes of one row's segment for stage `st` (8 super-blocks, fewer in the last
+// stage): Q4_K nbs*144; Q6_K nbs*208 + 16 (the group's d values).
+__device__ __forceinline__ uint32_t stage_seg_bytes(int type, int nbs) {
+    return type == AF_GGML_Q6_K ? (uint32_t)nbs * 208u + 16u : (uint32_t)nbs * 144u;
+}
+
+// Address of rows [row, row + n) of stage `st` in the packed (tile-major) layout:
+// tile t = row / 16 occupies 16 * row_stride bytes; inside it stage st starts at
+// 16 * st * full_seg and row i of the tile at i * seg(st).
+__device__ __forceinline__ const uint8_t* packed_stage_ptr(const GemvSeg& g, int row, int st, uint32_t seg) {
+    const uint32_t full = g.type == AF_GGML_Q6_K ? 1680u : 1152u;
+    return g.w + (size_t)(row / kGemvTileRows) * kGemvTileRows * g.row_stride +
+           (size_t)kGemvTileRows * st * full + (size_t)(row % kGemvTileRows) * seg;
 }
 
 struct XRegs {
@@ -240,20 +248,19 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
                 if (lane == 0) ok = mbar_wait(&empty[slot], ph ^ 1u);
                 ok = __shfl_sync(0xffffffffu, ok, 0);
                 if (!ok || *(volatile int*)abort_flag) { ok = false; break; }
-                // per-lane row copy (lanes 0..15)
-                uint32_t bytes = 0, off = 0;
-                int seg = 0, row = 0;
-                const bool valid = lane < kGemvTileRows && tile_row(p, t, lane, seg, row);
-                if (valid) bytes = stage_row_bytes(p.seg[seg].type, nb, st, off);
-                uint32_t tot = bytes;
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
-                if (lane == 0) mbar_arrive_expect_tx(&full[slot], tot);
-                __syncwarp();
-                if (valid) {
-                    const uint8_t* src = p.seg[seg].w + (size_t)row * p.seg[seg].row_stride + off;
-                    bulk_g2s(ring + (slot * kGemvTileRows + lane) * p.pitch, src, bytes, &full[slot], pol);
+                // one bulk copy per segment per stage (two for a gate/up pair)
+                if (lane == 0) {
+                    const int nbs = min(8, nb - st * 8);
+                    const GemvSeg& g0 = p.seg[p.epi == EPI_SWIGLU ? 0 : t.seg];
+                    const uint32_t segb = stage_seg_bytes(g0.type, nbs);
+                    const uint32_t bytes = (uint32_t)t.n * segb;
+                    uint8_t* dst = ring + slot * kGemvTileRows * p.pitch;
+                    mbar_arrive_expect_tx(&full[slot], p.epi == EPI_SWIGLU ? 2 * bytes : bytes);
+                    bulk_g2s(dst, packed_stage_ptr(g0, t.row0, st, segb), bytes, &full[slot], pol);
+                    if (p.epi == EPI_SWIGLU)
+                        bulk_g2s(dst + 8 * segb, packed_stage_ptr(p.seg[1], t.row0, st, segb), bytes, &full[slot], pol);
                 }
+                __syncwarp();
                 ++issued;
             }
         }
@@ -402,8 +409,9 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
                 // Both rows of the warp are evaluated without branches so their
                 // independent dp4a chains interleave; an invalid row reads
                 // stale shared memory and its result is discarded.
-                const uint8_t* rp0 = ring + (slot * kGemvTileRows + warp) * p.pitch;
-                const uint8_t* rp1 = ring + (slot * kGemvTileRows + warp + 8) * p.pitch;
+                const uint32_t segb = stage_seg_bytes(ty0, nbs);
+                const uint8_t* rp0 = ring + slot * kGemvTileRows * p.pitch + warp * segb;
+                const uint8_t* rp1 = rp0 + 8 * segb;
                 if (ty0 == ty1 && ty0 == AF_GGML_Q6_K) {
                     const float d0 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(rp0 + nbs * 208 + 2 * lb));
                     const float d1 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(rp1 + nbs * 208 + 2 * lb));
@@ -417,16 +425,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
                     acc[0] += a0;
                     acc[1] += a1;
                 } else {
-#pragma unroll
-                    for (int r = 0; r < 2; ++r) {
-                        const uint8_t* rp = r ? rp1 : rp0;
-                        if ((r ? ty1 : ty0) == AF_GGML_Q6_K) {
-                            const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(rp + nbs * 208 + 2 * lb));
-                            acc[r] += q6k_lane_dot(rp + lb * 208, d, lc, x);
-                        } else {
-                            acc[r] += q4k_lane_dot(rp + lb * 144, lc, x);
-                        }
-                    }
+                    set_err(kErrBadArgs);  // a tile never mixes types (checked on the host)
                 }
             }
             __syncwarp();

@@ -79,6 +79,11 @@ __host__ __device__ inline int dev_row_stride(int type, int cols) {
     return type == AF_GGML_Q6_K ? q6k_row_stride(cols) : (cols / 256) * 144;
 }
 
+// Device bytes of a packed matrix: whole 16-row tiles (the last one zero-padded).
+__host__ __device__ inline size_t packed_bytes(int type, int rows, int cols) {
+    return (size_t)((rows + kGemvTileRows - 1) / kGemvTileRows) * kGemvTileRows * dev_row_stride(type, cols);
+}
+
 // Per-device kernel attributes; call once per device before launching (and
 // before any stream capture).
 cudaError_t gemv_init();

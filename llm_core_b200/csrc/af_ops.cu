@@ -30,43 +30,45 @@ int num_sms() {
     return n > 0 ? n : 148;
 }
 
-// ------------------------------------------------------------ Q6_K regroup
+// ------------------------------------------------------- packed weight layout
 
-// One CTA per row.  GGUF block j (210 B: ql 128, qh 64, scales 16, d 2) goes to
-// group j/8: bytes 0..207 to slot j%8, d to the group's d area.
-__global__ void q6k_repack_kernel(uint8_t* __restrict__ dst, const uint8_t* __restrict__ src, int nb,
-                                  int dst_stride, int unpack) {
+// Byte offset of (row, stage st) in the packed layout (see af_gemv.cuh).
+__host__ __device__ inline size_t packed_off(int type, int nb, int row_stride, int row, int st) {
+    const int nbs = min(8, nb - st * 8);
+    const int seg = type == AF_GGML_Q6_K ? nbs * 208 + 16 : nbs * 144;
+    const int full = type == AF_GGML_Q6_K ? 1680 : 1152;
+    return (size_t)(row / kGemvTileRows) * kGemvTileRows * row_stride + (size_t)kGemvTileRows * st * full +
+           (size_t)(row % kGemvTileRows) * seg;
+}
+
+// One CTA per row; GGUF block j of the row goes to stage j/8, slot j%8 of that
+// stage's row segment (Q6_K: ql/qh/scales first, the f16 d values after the
+// segment's blocks).  `unpack` runs the same byte map backwards.
+__global__ void pack_kernel(uint8_t* __restrict__ packed, uint8_t* __restrict__ gguf, int type, int nb,
+                            int row_stride, int unpack) {
     const int row = blockIdx.x;
-    const uint8_t* s = src + (size_t)row * nb * 210;
-    uint8_t* d = dst + (size_t)row * dst_stride;
-    if (unpack) {
-        s = src + (size_t)row * dst_stride;
-        d = dst + (size_t)row * nb * 210;
-    }
-    for (int j = 0; j < nb; ++j) {
-        const int g = j >> 3, k = j & 7;
-        const int gsz = min(8, nb - g * 8);
-        const size_t goff = (size_t)g * 1680;
-        const size_t qoff = goff + (size_t)k * 208;
-        const size_t doff = goff + (size_t)gsz * 208 + 2 * k;
-        for (int i = threadIdx.x; i < 210; i += blockDim.x) {
-            const size_t o = i < 208 ? qoff + i : doff + (i - 208);
-            if (unpack) d[(size_t)j * 210 + i] = s[o];
-            else d[o] = s[(size_t)j * 210 + i];
-        }
-        if (!unpack && threadIdx.x < 16 && k == gsz - 1 && gsz < 8) {
-            // zero the pad after the last d of a partial group
-            const size_t pad0 = goff + (size_t)gsz * 208 + 2 * gsz;
-            const size_t pad1 = goff + (size_t)gsz * 208 + 16;
-            if (pad0 + threadIdx.x < pad1) d[pad0 + threadIdx.x] = 0;
-        }
+    const int BB = type == AF_GGML_Q6_K ? 210 : 144;
+    uint8_t* g = gguf + (size_t)row * nb * BB;
+    for (int idx = threadIdx.x; idx < nb * BB; idx += blockDim.x) {
+        const int j = idx / BB, i = idx % BB;
+        const int st = j >> 3, k = j & 7, nbs = min(8, nb - st * 8);
+        int o;
+        if (type == AF_GGML_Q6_K) o = i < 208 ? k * 208 + i : nbs * 208 + 2 * k + (i - 208);
+        else o = k * 144 + i;
+        const size_t d = packed_off(type, nb, row_stride, row, st) + o;
+        if (unpack) g[idx] = packed[d];
+        else packed[d] = g[idx];
     }
 }
 
-cudaError_t q6k_repack(void* d_dst, const void* d_src, int rows, int cols, bool unpack, cudaStream_t st) {
+cudaError_t weight_pack(void* d_dst, const void* d_src, int type, int rows, int cols, bool unpack,
+                        cudaStream_t st) {
     if (rows <= 0) return cudaSuccess;
-    q6k_repack_kernel<<<rows, 128, 0, st>>>(static_cast<uint8_t*>(d_dst), static_cast<const uint8_t*>(d_src),
-                                            cols / 256, q6k_row_stride(cols), unpack ? 1 : 0);
+    const int nb = cols / 256;
+    if (!unpack) AF_CUDA_TRY(cudaMemsetAsync(d_dst, 0, packed_bytes(type, rows, cols), st));
+    uint8_t* packed = static_cast<uint8_t*>(unpack ? const_cast<void*>(d_src) : d_dst);
+    uint8_t* gg = static_cast<uint8_t*>(unpack ? d_dst : const_cast<void*>(d_src));
+    pack_kernel<<<rows, 256, 0, st>>>(packed, gg, type, nb, dev_row_stride(type, cols), unpack ? 1 : 0);
     return cudaGetLastError();
 }
 
@@ -81,14 +83,15 @@ __global__ void embed_kernel(float* __restrict__ x, const uint8_t* __restrict__ 
     pdl_wait();
     if (argmax && blockIdx.x == 0 && threadIdx.x == 0) *argmax = 0ull;
     const int nb = cols / 256;
-    const uint8_t* row = W + (size_t)(*token) * row_stride;
     for (int v = blockIdx.x * blockDim.x + threadIdx.x; v < cols; v += gridDim.x * blockDim.x) {
         const int b = v >> 8, w = v & 255;
         float out;
+        const int tok = *token;
+        const int st = b >> 3, k = b & 7, nbs = min(8, nb - st * 8);
+        const uint8_t* seg = W + packed_off(type, nb, row_stride, tok, st);
         if (type == AF_GGML_Q6_K) {
-            const int g = b >> 3, k = b & 7, gsz = min(8, nb - g * 8);
-            const uint8_t* blk = row + (size_t)g * 1680 + k * 208;
-            const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(row + (size_t)g * 1680 + gsz * 208 + 2 * k));
+            const uint8_t* blk = seg + k * 208;
+            const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(seg + nbs * 208 + 2 * k));
             const int n = w >> 7, r = w & 127, s = r >> 5, l = r & 31;
             const uint8_t* ql = blk + 64 * n;
             const uint8_t* qh = blk + 128 + 32 * n;
@@ -98,7 +101,7 @@ __global__ void embed_kernel(float* __restrict__ x, const uint8_t* __restrict__ 
             const int q = (nib | (((qh[l] >> (2 * s)) & 3) << 4)) - 32;
             out = d * sc[(l >> 4) + 2 * s] * q;
         } else {
-            const uint8_t* blk = row + (size_t)b * 144;
+            const uint8_t* blk = seg + k * 144;
             const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(blk));
             const float dmin = half_bits_to_float(*reinterpret_cast<const uint16_t*>(blk + 2));
             const uint8_t* sc = blk + 4;
@@ -199,14 +202,19 @@ size_t af_row_stride(int ggml_type, int cols) {
     return 0;
 }
 
-cudaError_t af_q6k_repack(void* d_dst, const void* d_src, int rows, int cols, cudaStream_t stream) {
-    if (cols <= 0 || cols % 256 || rows < 0) return cudaErrorInvalidValue;
-    return q6k_repack(d_dst, d_src, rows, cols, false, stream);
+size_t af_weight_bytes(int ggml_type, int rows, int cols) {
+    if (cols <= 0 || cols % 256 || rows < 0 || (ggml_type != AF_GGML_Q4_K && ggml_type != AF_GGML_Q6_K)) return 0;
+    return packed_bytes(ggml_type, rows, cols);
 }
 
-cudaError_t af_q6k_unpack(void* d_dst, const void* d_src, int rows, int cols, cudaStream_t stream) {
-    if (cols <= 0 || cols % 256 || rows < 0) return cudaErrorInvalidValue;
-    return q6k_repack(d_dst, d_src, rows, cols, true, stream);
+cudaError_t af_weight_pack(void* d_dst, const void* d_src, int ggml_type, int rows, int cols, cudaStream_t stream) {
+    if (!af_weight_bytes(ggml_type, rows, cols)) return cudaErrorInvalidValue;
+    return weight_pack(d_dst, d_src, ggml_type, rows, cols, false, stream);
+}
+
+cudaError_t af_weight_unpack(void* d_dst, const void* d_src, int ggml_type, int rows, int cols, cudaStream_t stream) {
+    if (!af_weight_bytes(ggml_type, rows, cols)) return cudaErrorInvalidValue;
+    return weight_pack(d_dst, d_src, ggml_type, rows, cols, true, stream);
 }
 
 cudaError_t af_gemv_f32(float* d_y, const void* d_w, int ggml_type, const float* d_x, int rows, int cols,
@@ -263,8 +271,8 @@ cudaError_t af_gemv_fused(const af_gemv_fused_args* a, cudaStream_t stream) {
         p.seg[s].rows = a->rows[s];
         p.seg[s].row_stride = dev_row_stride(a->type[s], a->cols);
     }
-    if (a->epi == AF_EPI_SWIGLU && a->rows[0] != a->rows[1]) {
-        set_last_error("af_gemv_fused: SwiGLU needs equal gate/up rows");
+    if (a->epi == AF_EPI_SWIGLU && (a->rows[0] != a->rows[1] || a->type[0] != a->type[1])) {
+        set_last_error("af_gemv_fused: SwiGLU needs gate/up of equal rows and type");
         return cudaErrorInvalidValue;
     }
     p.nseg = a->nseg;

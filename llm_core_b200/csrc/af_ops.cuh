@@ -10,7 +10,7 @@ void set_last_error(const std::string& s);
 int num_sms();
 int gemv_grid();
 
-cudaError_t q6k_repack(void* d_dst, const void* d_src, int rows, int cols, bool unpack, cudaStream_t st);
+cudaError_t weight_pack(void* d_dst, const void* d_src, int type, int rows, int cols, bool unpack, cudaStream_t st);
 cudaError_t embed_launch(float* x, const uint8_t* W, int type, int cols, int row_stride, const int* token,
                          unsigned long long* argmax, cudaStream_t st, bool pdl);
 

@@ -18,10 +18,8 @@ def mat(lib, rng, t, rows, cols):
     gen = gguf.random_q4k if t == gguf.GGML_Q4_K else gguf.random_q6k
     W = gen(rng, rows * cols // 256).reshape(-1)
     src = dev(W)
-    if t == gguf.GGML_Q4_K:
-        return W, src
-    d = torch.zeros(rows * lib.af_row_stride(t, cols) + 64, dtype=torch.uint8, device="cuda")
-    assert lib.af_q6k_repack(d.data_ptr(), src.data_ptr(), rows, cols, None) == 0
+    d = torch.empty(lib.af_weight_bytes(t, rows, cols), dtype=torch.uint8, device="cuda")
+    assert lib.af_weight_pack(d.data_ptr(), src.data_ptr(), t, rows, cols, None) == 0
     return W, d
 
 

@@ -22,10 +22,8 @@ TIGHT = 1e-4
 def to_device_layout(lib, W: np.ndarray, t: int, rows: int, cols: int):
     import torch
     src = dev(W)
-    if t == gguf.GGML_Q4_K:
-        return src
-    dst = torch.zeros(rows * lib.af_row_stride(t, cols) + 64, dtype=torch.uint8, device="cuda")
-    assert lib.af_q6k_repack(dst.data_ptr(), src.data_ptr(), rows, cols, None) == 0
+    dst = torch.empty(lib.af_weight_bytes(t, rows, cols), dtype=torch.uint8, device="cuda")
+    assert lib.af_weight_pack(dst.data_ptr(), src.data_ptr(), t, rows, cols, None) == 0
     return dst
 
 
@@ -84,16 +82,23 @@ def test_gemv_edge_inputs(gpu):
             assert rel_l2(y, ref) < TIGHT
 
 
-def test_q6k_repack_round_trip(gpu):
+@pytest.mark.parametrize("t", [gguf.GGML_Q4_K, gguf.GGML_Q6_K])
+def test_weight_pack_round_trip(gpu, t):
+    """The packed layout is a byte-preserving permutation of the GGUF bytes."""
     import torch
     rng = np.random.default_rng(9)
-    for rows, cols in ((3, 256), (5, 2048), (7, 11008)):
-        W = gguf.random_q6k(rng, rows * cols // 256).reshape(-1)
-        packed = to_device_layout(gpu, W, gguf.GGML_Q6_K, rows, cols)
+    gen = gguf.random_q4k if t == gguf.GGML_Q4_K else gguf.random_q6k
+    for rows, cols in ((3, 256), (17, 2048), (40, 11008)):
+        W = gen(rng, rows * cols // 256).reshape(-1)
+        packed = to_device_layout(gpu, W, t, rows, cols)
+        assert packed.numel() == gpu.af_weight_bytes(t, rows, cols)
         back = torch.zeros(W.size, dtype=torch.uint8, device="cuda")
-        assert gpu.af_q6k_unpack(back.data_ptr(), packed.data_ptr(), rows, cols, None) == 0
+        assert gpu.af_weight_unpack(back.data_ptr(), packed.data_ptr(), t, rows, cols, None) == 0
         torch.cuda.synchronize()
         assert np.array_equal(back.cpu().numpy(), W)
+        # same multiset of bytes, plus zero padding
+        p = packed.cpu().numpy()
+        assert np.count_nonzero(p) == np.count_nonzero(W)
 
 
 def test_reference_op_set(gpu):
