@@ -240,6 +240,14 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
         p.out[(size_t)h * hd + dd] = O / L;
     }
     if (tid == 0) p.counter[kvh] = 0u;
+    if (p.xq_out) {
+        // quantise this kv head's G*hd outputs (whole 64-value groups) for the O projection
+        __threadfence();
+        __syncthreads();
+        const int g0 = kvh * G * hd / 64, ng = G * hd / 64;
+        for (int k = warp; k < ng; k += kAttnThreads / 32)
+            xq_quantize_group(p.xq_out, p.out, nullptr, p.n_heads * hd, g0 + k);
+    }
 }
 
 __global__ void finalize_kernel(const unsigned long long* key, int* token, int* pos, int* hist) {

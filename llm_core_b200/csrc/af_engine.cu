@@ -89,6 +89,8 @@ struct af_engine {
     float *logits = nullptr, *logits_all = nullptr;
     float *kcache = nullptr, *vcache = nullptr, *cos_t = nullptr, *sin_t = nullptr, *apart = nullptr;
     unsigned int* acount = nullptr;
+    uint8_t *xq_a = nullptr, *xq_o = nullptr, *xq_gu = nullptr, *xq_d = nullptr;  // quantised GEMV inputs
+    unsigned int *cnt_e = nullptr, *cnt_f = nullptr;  // per-64-group arrival counters
     unsigned long long* key = nullptr;
     int* tokpos = nullptr;  // [0] token, [1] pos
     int* hist = nullptr;
@@ -214,8 +216,11 @@ cudaError_t enqueue_step(af_engine* e, Prof* prof = nullptr) {
     const bool tp = e->tp > 1;
     int nk = 0;
     int cur = 0;  // residual buffer holding the current stream (TP ping-pong)
+    // Single-GPU steps hand quantised inputs (XQ) from kernel to kernel; tensor
+    // parallel ranks quantise inside each GEMV after the all-reduce.
+    const bool xq = !tp;
     ENG_TRY(embed_launch(e->x[0], e->tok_embd.w, e->tok_embd.type, E, e->tok_embd.stride, &e->tokpos[0], e->key,
-                         e->stream, e->pdl));
+                         xq ? e->xq_a : nullptr, e->layers[0].attn_norm, e->stream, e->pdl));
     ++nk;
     AF_MARK(AF_PROF_EMBED, (double)e->tok_embd.stride + E * 4.0);
     bool pending = false;  // TP: ypart holds an un-added partial sum
@@ -235,9 +240,13 @@ cudaError_t enqueue_step(af_engine* e, Prof* prof = nullptr) {
                 cur ^= 1;
             }
             p.norm_w = L.attn_norm;
+            if (xq) {
+                p.xq = e->xq_a;
+                p.xq_norm = 1;
+            }
             p.epi = EPI_STORE;
-            gemv_configure(p);
-            ENG_TRY(gemv_launch(p, e->gemv_ctas, e->stream, e->pdl));
+            gemv_configure(p, e->gemv_ctas);
+            ENG_TRY(gemv_launch(p, e->stream, e->pdl));
             ++nk;
             AF_MARK(AF_PROF_QKV, gemv_bytes(p));
         }
@@ -266,6 +275,7 @@ cudaError_t enqueue_step(af_engine* e, Prof* prof = nullptr) {
             a.qk_norm_order = c.qk_norm_order;
             a.eps = c.eps;
             a.scale = 1.f / std::sqrt((float)e->hd);
+            a.xq_out = xq ? e->xq_o : nullptr;
             ENG_TRY(attention_launch(a, e->stream, e->pdl));
             ++nk;
             if (prof) {
@@ -284,9 +294,13 @@ cudaError_t enqueue_step(af_engine* e, Prof* prof = nullptr) {
             } else {
                 p.epi = EPI_RESID;
                 p.resid = e->x[cur];
+                p.xq = e->xq_o;
+                p.q_out = e->xq_gu;
+                p.q_norm_w = L.ffn_norm;
+                p.q_cnt = e->cnt_e;
             }
-            gemv_configure(p);
-            ENG_TRY(gemv_launch(p, e->gemv_ctas, e->stream, e->pdl));
+            gemv_configure(p, e->gemv_ctas);
+            ENG_TRY(gemv_launch(p, e->stream, e->pdl));
             ++nk;
             AF_MARK(AF_PROF_O, gemv_bytes(p));
             if (tp) {
@@ -310,8 +324,14 @@ cudaError_t enqueue_step(af_engine* e, Prof* prof = nullptr) {
             }
             p.norm_w = L.ffn_norm;
             p.epi = EPI_SWIGLU;
-            gemv_configure(p);
-            ENG_TRY(gemv_launch(p, e->gemv_ctas, e->stream, e->pdl));
+            if (xq) {
+                p.xq = e->xq_gu;
+                p.xq_norm = 1;
+                p.q_out = e->xq_d;
+                p.q_cnt = e->cnt_f;
+            }
+            gemv_configure(p, e->gemv_ctas);
+            ENG_TRY(gemv_launch(p, e->stream, e->pdl));
             ++nk;
             AF_MARK(AF_PROF_GATEUP, gemv_bytes(p) - 4.0 * p.seg[1].rows);
         }
@@ -326,9 +346,13 @@ cudaError_t enqueue_step(af_engine* e, Prof* prof = nullptr) {
             } else {
                 p.epi = EPI_RESID;
                 p.resid = e->x[cur];
+                p.xq = e->xq_d;
+                p.q_out = e->xq_a;
+                p.q_norm_w = l + 1 < c.n_layer ? e->layers[l + 1].attn_norm : e->out_norm;
+                p.q_cnt = e->cnt_e;
             }
-            gemv_configure(p);
-            ENG_TRY(gemv_launch(p, e->gemv_ctas, e->stream, e->pdl));
+            gemv_configure(p, e->gemv_ctas);
+            ENG_TRY(gemv_launch(p, e->stream, e->pdl));
             ++nk;
             AF_MARK(AF_PROF_DOWN, gemv_bytes(p));
             if (tp) {
@@ -350,11 +374,15 @@ cudaError_t enqueue_step(af_engine* e, Prof* prof = nullptr) {
             cur ^= 1;
         }
         p.norm_w = e->out_norm;
+        if (xq) {
+            p.xq = e->xq_a;
+            p.xq_norm = 1;
+        }
         p.epi = EPI_ARGMAX;
         p.argmax = e->key;
         p.argmax_base = e->V0;
-        gemv_configure(p);
-        ENG_TRY(gemv_launch(p, e->gemv_ctas, e->stream, e->pdl));
+        gemv_configure(p, e->gemv_ctas);
+        ENG_TRY(gemv_launch(p, e->stream, e->pdl));
         ++nk;
         AF_MARK(AF_PROF_LMHEAD, gemv_bytes(p));
         if (tp) {
@@ -636,6 +664,18 @@ cudaError_t af_engine_finalize(af_engine* e) {
         e->apart = static_cast<float*>(e->dalloc((size_t)e->Hl * ns * (hd + 2) * 4));
         e->acount = static_cast<unsigned int*>(e->dalloc((size_t)e->KVl * 4));
         ENG_TRY(cudaMemset(e->acount, 0, (size_t)e->KVl * 4));
+        e->xq_a = static_cast<uint8_t*>(e->dalloc(xq_norm_bytes(E)));
+        e->xq_o = static_cast<uint8_t*>(e->dalloc(xq_norm_bytes(e->Hl * hd)));
+        e->xq_gu = static_cast<uint8_t*>(e->dalloc(xq_norm_bytes(E)));
+        e->xq_d = static_cast<uint8_t*>(e->dalloc(xq_norm_bytes(e->Fl)));
+        ENG_TRY(cudaMemset(e->xq_a, 0, xq_norm_bytes(E)));
+        ENG_TRY(cudaMemset(e->xq_o, 0, xq_norm_bytes(e->Hl * hd)));
+        ENG_TRY(cudaMemset(e->xq_gu, 0, xq_norm_bytes(E)));
+        ENG_TRY(cudaMemset(e->xq_d, 0, xq_norm_bytes(e->Fl)));
+        e->cnt_e = static_cast<unsigned int*>(e->dalloc((size_t)E / 64 * 4));
+        e->cnt_f = static_cast<unsigned int*>(e->dalloc((size_t)e->Fl / 64 * 4));
+        ENG_TRY(cudaMemset(e->cnt_e, 0, (size_t)E / 64 * 4));
+        ENG_TRY(cudaMemset(e->cnt_f, 0, (size_t)e->Fl / 64 * 4));
         e->key = static_cast<unsigned long long*>(e->dalloc(8));
         e->tokpos = static_cast<int*>(e->dalloc(8));
         e->hist = static_cast<int*>(e->dalloc((size_t)(c.n_ctx + 1) * 4));

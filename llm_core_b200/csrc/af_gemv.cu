@@ -5,100 +5,118 @@ namespace af {
 
 __device__ int g_err = 0;
 
+// One warp quantises 64-value group g of src into the XQ layout.  Values are
+// read through L2 (other CTAs wrote them); the 16-bit split matches the
+// consumers' dp4a form: q = rint(v·32639/amax), hi = (q + 128) >> 8, lo = q − 256·hi.
+__device__ void xq_quantize_group(uint8_t* xq, const float* src, const float* norm_w, int K, int g) {
+    const int lane = threadIdx.x & 31;
+    const int nst = (K / 256 + 7) / 8;
+    const int v0 = 64 * g + 2 * lane;
+    float a0 = __ldcg(src + v0), a1 = __ldcg(src + v0 + 1);
+    float ss = a0 * a0 + a1 * a1;
+    if (norm_w) {
+        a0 *= __ldg(norm_w + v0);
+        a1 *= __ldg(norm_w + v0 + 1);
+    }
+    const float amax = warp_max(fmaxf(fabsf(a0), fabsf(a1)));
+    const float inv = amax > 0.f ? 32639.f / amax : 0.f;
+    const int q0 = max(-32639, min(32639, __float2int_rn(a0 * inv)));
+    const int q1 = max(-32639, min(32639, __float2int_rn(a1 * inv)));
+    const int h0 = (q0 + 128) >> 8, h1 = (q1 + 128) >> 8;
+    const int l0 = q0 - 256 * h0, l1 = q1 - 256 * h1;
+    const int s = v0 >> 11, w = v0 & 2047;
+    const int b = w >> 8, c = (w >> 6) & 3, i = (w >> 4) & 3, e = w & 15;
+    const int L = b * 4 + c;
+    const int off = s * 2048 + i * 512 + L * 16 + e;
+    *reinterpret_cast<uint16_t*>(xq + off) = (uint16_t)((h0 & 0xFF) | ((h1 & 0xFF) << 8));
+    *reinterpret_cast<uint16_t*>(xq + nst * 2048 + off) = (uint16_t)((l0 & 0xFF) | ((l1 & 0xFF) << 8));
+    float* XS = reinterpret_cast<float*>(xq + 2 * nst * 2048);
+    float* XS32 = XS + nst * 32;
+    int* XI16 = reinterpret_cast<int*>(XS32 + nst * 64);
+    float fs = a0 + a1;
+    int is = q0 + q1;
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) {
+        fs += __shfl_xor_sync(0xffffffffu, fs, o);
+        is += __shfl_xor_sync(0xffffffffu, is, o);
+    }
+    fs += __shfl_xor_sync(0xffffffffu, fs, 8);  // 16 lanes = 32 values
+    if ((lane & 7) == 0) XI16[s * 128 + i * 32 + L] = is;
+    if ((lane & 15) == 0) XS32[s * 64 + (i >> 1) * 32 + L] = fs;
+    if (lane == 0) XS[s * 32 + L] = amax / 32639.f;
+    if (norm_w) {
+        ss = warp_sum(ss);
+        if (lane == 0) reinterpret_cast<float*>(xq + xq_bytes(K))[g] = ss;
+    }
+}
+
 namespace {
 
-constexpr int kConsumerWarps = 8;
-constexpr int kConsumerThreads = kConsumerWarps * 32;
-// float4 registers per consumer thread for the input: K <= 256*12*4 = 12288.
-constexpr int kPrologueVec = kGemvMaxK / (kConsumerThreads * 4);
+constexpr int kCW = kGemvConsumerWarps;
+constexpr int kCT = kCW * 32;
 
-struct Tile {
-    int seg;     // segment of the tile's rows
+__global__ void xq_quantize_kernel(uint8_t* xq, const float* x, const float* norm_w, int K) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int g = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+    if (g < K / 64) xq_quantize_group(xq, x, norm_w, K, g);
+}
+
+struct Frag {
+    int seg;     // segment of the fragment's rows
     int row0;    // first row within the segment (virtual row for SwiGLU pairs)
-    int n;       // rows in the tile (row pairs for SwiGLU)
+    int n;       // rows (row pairs for SwiGLU)
 };
 
-// Rows of a segment as seen by the CTA partition ("virtual rows": a SwiGLU
-// gate/up pair counts as one).
 __device__ __forceinline__ int n_vsegs(const GemvParams& p) { return p.epi == EPI_SWIGLU ? 1 : p.nseg; }
 
-__device__ __forceinline__ long long vrow_bytes(const GemvParams& p, int s) {
-    if (p.epi == EPI_SWIGLU) return (long long)p.seg[0].row_stride + p.seg[1].row_stride;
-    return p.seg[s].row_stride;
-}
-
-// First virtual row whose starting byte is >= b.
-__device__ long long vrow_at(const GemvParams& p, long long b) {
-    long long base = 0;
-    const int ns = n_vsegs(p);
-    for (int s = 0; s < ns; ++s) {
-        const long long rb = vrow_bytes(p, s);
-        const long long segb = rb * p.seg[s].rows;
-        if (b <= segb || s == ns - 1) {
-            long long r = (b + rb - 1) / rb;
-            if (r > p.seg[s].rows) r = p.seg[s].rows;
-            return base + r;
-        }
-        b -= segb;
-        base += p.seg[s].rows;
-    }
-    return base;
-}
-
-// Tile iterator over [vbeg, vend) of the concatenated virtual-row space.
-struct TileIter {
-    long long cur, end;
-    __device__ bool next(const GemvParams& p, Tile& t) {
+// Fragment iterator over [cur, end) of the concatenated virtual-row space.
+struct FragIter {
+    int cur, end;
+    __device__ bool next(const GemvParams& p, Frag& t) {
         if (cur >= end) return false;
-        long long base = 0;
+        int base = 0, s = 0;
         const int ns = n_vsegs(p);
-        int s = 0;
-        for (; s < ns; ++s) {
+        for (; s < ns - 1; ++s) {
             if (cur < base + p.seg[s].rows) break;
             base += p.seg[s].rows;
         }
-        const int cap = p.epi == EPI_SWIGLU ? kGemvTileRows / 2 : kGemvTileRows;
-        long long stop = cur + cap;
-        if (stop > end) stop = end;
-        if (stop > base + p.seg[s].rows) stop = base + p.seg[s].rows;
-        // a fragment never crosses a 16-row tile of the packed layout, so each
-        // of its stages is one contiguous range
-        const long long tile_end = base + ((cur - base) / kGemvTileRows + 1) * kGemvTileRows;
-        if (stop > tile_end) stop = tile_end;
+        const int cap = p.epi == EPI_SWIGLU ? kGemvFragRows / 2 : kGemvFragRows;
+        int stop = min(min(cur + cap, end), base + p.seg[s].rows);
         t.seg = s;
-        t.row0 = (int)(cur - base);
-        t.n = (int)(stop - cur);
+        t.row0 = cur - base;
+        t.n = stop - cur;
         cur = stop;
         return true;
     }
 };
 
-// Physical row p (0..15) of a tile: segment, row index, validity.
-__device__ __forceinline__ bool tile_row(const GemvParams& p, const Tile& t, int pr, int& seg, int& row) {
-    if (p.epi == EPI_SWIGLU) {
-        const int vr = pr & 7;
-        seg = pr >> 3;
-        row = t.row0 + vr;
-        return vr < t.n;
-    }
-    seg = t.seg;
-    row = t.row0 + pr;
-    return pr < t.n;
-}
-
-// Bytes of one row's segment for stage `st` (8 super-blocks, fewer in the last
-// stage): Q4_K nbs*144; Q6_K nbs*208 + 16 (the group's d values).
+// Bytes of one row's segment for a stage of nbs super-blocks: Q4_K nbs*144;
+// Q6_K nbs*208 + 16 (the group's d values).
 __device__ __forceinline__ uint32_t stage_seg_bytes(int type, int nbs) {
     return type == AF_GGML_Q6_K ? (uint32_t)nbs * 208u + 16u : (uint32_t)nbs * 144u;
 }
 
-// Address of rows [row, row + n) of stage `st` in the packed (tile-major) layout:
-// tile t = row / 16 occupies 16 * row_stride bytes; inside it stage st starts at
+// Address of row `row`, stage st in the packed (tile-major) layout: tile
+// t = row / 16 occupies 16 * row_stride bytes; inside it stage st starts at
 // 16 * st * full_seg and row i of the tile at i * seg(st).
 __device__ __forceinline__ const uint8_t* packed_stage_ptr(const GemvSeg& g, int row, int st, uint32_t seg) {
     const uint32_t full = g.type == AF_GGML_Q6_K ? 1680u : 1152u;
-    return g.w + (size_t)(row / kGemvTileRows) * kGemvTileRows * g.row_stride +
-           (size_t)kGemvTileRows * st * full + (size_t)(row % kGemvTileRows) * seg;
+    return g.w + (size_t)(row / kPackTile) * kPackTile * g.row_stride + (size_t)kPackTile * st * full +
+           (size_t)(row % kPackTile) * seg;
+}
+
+// Copy rows [row0, row0 + n) of one segment's stage st into smem (dense,
+// seg bytes per row): one bulk copy per packed tile the rows touch.
+__device__ __forceinline__ void copy_rows(uint8_t* dst, const GemvSeg& g, int row0, int n, int st, uint32_t seg,
+                                          uint64_t* bar, uint64_t pol) {
+    int r = row0;
+    while (r < row0 + n) {
+        const int stop = min(row0 + n, (r / kPackTile + 1) * kPackTile);
+        bulk_g2s(dst + (size_t)(r - row0) * seg, packed_stage_ptr(g, r, st, seg), (uint32_t)(stop - r) * seg, bar,
+                 pol);
+        r = stop;
+    }
 }
 
 struct XRegs {
@@ -198,151 +216,83 @@ __device__ __forceinline__ float q6k_lane_dot(const uint8_t* blk, float d, int c
     return (d * x.xs) * acc;
 }
 
-__device__ __forceinline__ void bar_consumers() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
-__global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_constant__ GemvParams p) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-    uint64_t* empty = full + kGemvMaxSlots;
-    int* abort_flag = reinterpret_cast<int*>(empty + kGemvMaxSlots);
-    uint8_t* ring = smem + 128;
-    const int nb = p.K / 256;
-    const int nst = (nb + 7) / 8;
-    uint8_t* XH = ring + p.nslots * kGemvTileRows * p.pitch;
-    uint8_t* XL = XH + nst * 2048;
-    float* XS = reinterpret_cast<float*>(XL + nst * 2048);
+__device__ __forceinline__ void bar_consumers() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
+
+// Legacy prologue: f32 input (+ pending residual, optionally RMS-normalised)
+// loaded with all NIT float4 loads per thread in flight, then quantised into
+// the shared XQ layout.  NIT = float4 slots per consumer thread = stages.
+template <int NIT>
+__device__ __forceinline__ void input_prologue(const GemvParams& p, uint8_t* xqs, float* red) {
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int nvec = p.K / 4;
+    const int nst = NIT;
+    uint8_t* XH = xqs;
+    uint8_t* XL = xqs + nst * 2048;
+    float* XS = reinterpret_cast<float*>(xqs + 2 * nst * 2048);
     float* XS32 = XS + nst * 32;
     int* XI16 = reinterpret_cast<int*>(XS32 + nst * 64);
-    float* red = reinterpret_cast<float*>(XI16 + nst * 128);
-
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-    // CTA row range, balanced by weight bytes.
-    long long total = 0;
-    for (int s = 0; s < n_vsegs(p); ++s) total += vrow_bytes(p, s) * p.seg[s].rows;
-    const long long vbeg = vrow_at(p, total * blockIdx.x / gridDim.x);
-    const long long vend = vrow_at(p, total * (blockIdx.x + 1) / gridDim.x);
-
-    if (threadIdx.x == 0) {
-        for (int i = 0; i < p.nslots; ++i) {
-            mbar_init(&full[i], 1);
-            mbar_init(&empty[i], kConsumerWarps);
-        }
-        *abort_flag = 0;
-        fence_mbar_init();
-    }
-    __syncthreads();
-    pdl_launch_dependents();
-
-    if (warp == kConsumerWarps) {
-        // ---------------- producer warp ----------------
-        const uint64_t pol = policy_evict_first();
-        TileIter it{vbeg, vend};
-        Tile t;
-        uint32_t issued = 0;
-        bool ok = true;
-        while (ok && it.next(p, t)) {
-            for (int st = 0; st < nst && ok; ++st) {
-                const int slot = issued % p.nslots;
-                const uint32_t ph = (issued / p.nslots) & 1u;
-                if (lane == 0) ok = mbar_wait(&empty[slot], ph ^ 1u);
-                ok = __shfl_sync(0xffffffffu, ok, 0);
-                if (!ok || *(volatile int*)abort_flag) { ok = false; break; }
-                // one bulk copy per segment per stage (two for a gate/up pair)
-                if (lane == 0) {
-                    const int nbs = min(8, nb - st * 8);
-                    const GemvSeg& g0 = p.seg[p.epi == EPI_SWIGLU ? 0 : t.seg];
-                    const uint32_t segb = stage_seg_bytes(g0.type, nbs);
-                    const uint32_t bytes = (uint32_t)t.n * segb;
-                    uint8_t* dst = ring + slot * kGemvTileRows * p.pitch;
-                    mbar_arrive_expect_tx(&full[slot], p.epi == EPI_SWIGLU ? 2 * bytes : bytes);
-                    bulk_g2s(dst, packed_stage_ptr(g0, t.row0, st, segb), bytes, &full[slot], pol);
-                    if (p.epi == EPI_SWIGLU)
-                        bulk_g2s(dst + 8 * segb, packed_stage_ptr(p.seg[1], t.row0, st, segb), bytes, &full[slot], pol);
-                }
-                __syncwarp();
-                ++issued;
-            }
-        }
-        if (!ok) {
-            *(volatile int*)abort_flag = 1;
-            // Drain: wait (bounded) for the copies still in flight.
-            if (lane == 0) {
-                const uint32_t first = issued > (uint32_t)p.nslots ? issued - p.nslots : 0u;
-                for (uint32_t i = first; i < issued; ++i)
-                    mbar_wait(&full[i % p.nslots], (i / p.nslots) & 1u);
-            }
-        }
-        return;
-    }
-
-    // ---------------- consumer warps: input prologue ----------------
-    // All global loads of the input are issued together (one memory latency),
-    // held in registers, then normalised and quantised.
-    pdl_wait();
-    const int tid = threadIdx.x;  // 0..255
-    const int nvec = p.K / 4;
-    const int niter = nst * 2;    // float4 slots per thread incl. the padded last stage
-    float4 a[kPrologueVec];
+    float4 a[NIT];
 #pragma unroll
-    for (int j = 0; j < kPrologueVec; ++j) {
-        a[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-        const int v = j * kConsumerThreads + tid;
-        if (j < niter && v < nvec) {
-            a[j] = reinterpret_cast<const float4*>(p.x)[v];
-            if (p.x_add) {
-                const float4 b = reinterpret_cast<const float4*>(p.x_add)[v];
-                a[j].x += b.x; a[j].y += b.y; a[j].z += b.z; a[j].w += b.w;
-            }
+    for (int j = 0; j < NIT; ++j) {
+        const int v = j * kCT + tid;
+        const int vc = v < nvec ? v : 0;
+        a[j] = reinterpret_cast<const float4*>(p.x)[vc];
+        if (p.x_add) {
+            const float4 b = reinterpret_cast<const float4*>(p.x_add)[vc];
+            a[j].x += b.x; a[j].y += b.y; a[j].z += b.z; a[j].w += b.w;
         }
+        if (v >= nvec) a[j] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
     if (p.x_store && blockIdx.x == 0) {
 #pragma unroll
-        for (int j = 0; j < kPrologueVec; ++j) {
-            const int v = j * kConsumerThreads + tid;
-            if (j < niter && v < nvec) reinterpret_cast<float4*>(p.x_store)[v] = a[j];
+        for (int j = 0; j < NIT; ++j) {
+            const int v = j * kCT + tid;
+            if (v < nvec) reinterpret_cast<float4*>(p.x_store)[v] = a[j];
         }
     }
     if (p.norm_w) {
         float ss = 0.f;
 #pragma unroll
-        for (int j = 0; j < kPrologueVec; ++j)
+        for (int j = 0; j < NIT; ++j)
             ss += a[j].x * a[j].x + a[j].y * a[j].y + a[j].z * a[j].z + a[j].w * a[j].w;
         ss = warp_sum(ss);
         if (lane == 0) red[warp] = ss;
         bar_consumers();
         float tot = 0.f;
 #pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) tot += red[w];
+        for (int w = 0; w < kCW; ++w) tot += red[w];
         // rms_norm_out (src/models/llama_model.cpp:393-419): 1/sqrt(ss/n + eps)
         const float inv_rms = 1.f / sqrtf(tot / (float)p.K + p.eps);
 #pragma unroll
-        for (int j = 0; j < kPrologueVec; ++j) {
-            const int v = j * kConsumerThreads + tid;
-            if (j < niter && v < nvec) {
-                const float4 w = reinterpret_cast<const float4*>(p.norm_w)[v];
-                a[j].x = w.x * (a[j].x * inv_rms);
-                a[j].y = w.y * (a[j].y * inv_rms);
-                a[j].z = w.z * (a[j].z * inv_rms);
-                a[j].w = w.w * (a[j].w * inv_rms);
-            }
+        for (int j = 0; j < NIT; ++j) {
+            const int v = j * kCT + tid;
+            const float4 w = reinterpret_cast<const float4*>(p.norm_w)[v < nvec ? v : 0];
+            a[j].x = w.x * (a[j].x * inv_rms);
+            a[j].y = w.y * (a[j].y * inv_rms);
+            a[j].z = w.z * (a[j].z * inv_rms);
+            a[j].w = w.w * (a[j].w * inv_rms);
         }
     }
-    // Quantise: 16 consecutive threads own one 64-value group.
+    float amax[NIT];
 #pragma unroll
-    for (int j = 0; j < kPrologueVec; ++j) {
-        if (j >= niter) break;
-        const int v = j * kConsumerThreads + tid;
-        const float4 q4 = a[j];
-        float amax = fmaxf(fmaxf(fabsf(q4.x), fabsf(q4.y)), fmaxf(fabsf(q4.z), fabsf(q4.w)));
+    for (int j = 0; j < NIT; ++j)
+        amax[j] = fmaxf(fmaxf(fabsf(a[j].x), fabsf(a[j].y)), fmaxf(fabsf(a[j].z), fabsf(a[j].w)));
 #pragma unroll
-        for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    for (int o = 8; o > 0; o >>= 1)
+#pragma unroll
+        for (int j = 0; j < NIT; ++j) amax[j] = fmaxf(amax[j], __shfl_xor_sync(0xffffffffu, amax[j], o));
+    float fsum[NIT];
+    int isum[NIT];
+#pragma unroll
+    for (int j = 0; j < NIT; ++j) {
+        const int v = j * kCT + tid;
         // 16-bit grid of ±32639 so that hi = (q + 128) >> 8 stays within int8.
-        const float xs = amax / 32639.f;
-        const float inv = amax > 0.f ? 32639.f / amax : 0.f;
-        const float av[4] = {q4.x, q4.y, q4.z, q4.w};
+        const float inv = amax[j] > 0.f ? 32639.f / amax[j] : 0.f;
+        const float av[4] = {a[j].x, a[j].y, a[j].z, a[j].w};
         uint32_t hw = 0, lw = 0;
-        int isum = 0;
+        int is = 0;
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             int q = __float2int_rn(av[e] * inv);
@@ -351,51 +301,182 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
             const int lo = q - hi * 256;
             hw |= (uint32_t)(hi & 0xFF) << (8 * e);
             lw |= (uint32_t)(lo & 0xFF) << (8 * e);
-            isum += q;
+            is += q;
         }
-        float fsum = q4.x + q4.y + q4.z + q4.w;
-        fsum += __shfl_xor_sync(0xffffffffu, fsum, 1);
-        fsum += __shfl_xor_sync(0xffffffffu, fsum, 2);
-        isum += __shfl_xor_sync(0xffffffffu, isum, 1);
-        isum += __shfl_xor_sync(0xffffffffu, isum, 2);
-        const float fsum32 = fsum + __shfl_xor_sync(0xffffffffu, fsum, 4);
-        // position -> lane-major layout [stage][chunk i][lane L][16 bytes]
+        isum[j] = is;
+        fsum[j] = a[j].x + a[j].y + a[j].z + a[j].w;
         const int val = v * 4;
         const int s = val >> 11, w = val & 2047;
         const int b = w >> 8, c = (w >> 6) & 3, i = (w >> 4) & 3, e = w & 15;
-        const int L = b * 4 + c;
-        const int off = s * 2048 + i * 512 + L * 16 + e;
+        const int off = s * 2048 + i * 512 + (b * 4 + c) * 16 + e;
         *reinterpret_cast<uint32_t*>(XH + off) = hw;
         *reinterpret_cast<uint32_t*>(XL + off) = lw;
-        if ((tid & 15) == 0) XS[s * 32 + L] = xs;
-        if ((tid & 7) == 0) XS32[s * 64 + (i >> 1) * 32 + L] = fsum32;
-        if ((tid & 3) == 0) XI16[s * 128 + i * 32 + L] = isum;
     }
-    bar_consumers();
+#pragma unroll
+    for (int o = 1; o <= 2; o <<= 1)
+#pragma unroll
+        for (int j = 0; j < NIT; ++j) {
+            fsum[j] += __shfl_xor_sync(0xffffffffu, fsum[j], o);
+            isum[j] += __shfl_xor_sync(0xffffffffu, isum[j], o);
+        }
+#pragma unroll
+    for (int j = 0; j < NIT; ++j) {
+        const float fsum32 = fsum[j] + __shfl_xor_sync(0xffffffffu, fsum[j], 4);
+        const int val = (j * kCT + tid) * 4;
+        const int s = val >> 11, w = val & 2047;
+        const int b = w >> 8, c = (w >> 6) & 3, i = (w >> 4) & 3;
+        const int L = b * 4 + c;
+        if ((tid & 15) == 0) XS[s * 32 + L] = amax[j] / 32639.f;
+        if ((tid & 7) == 0) XS32[s * 64 + (i >> 1) * 32 + L] = fsum32;
+        if ((tid & 3) == 0) XI16[s * 128 + i * 32 + L] = isum[j];
+    }
+}
+
+__global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_constant__ GemvParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + kGemvMaxSlots;
+    uint64_t* xbar = empty + kGemvMaxSlots;
+    int* flags = reinterpret_cast<int*>(xbar + 1);  // [0] abort, [1..] group list
+    uint8_t* ring = smem + 256;
+    const int nb = p.K / 256;
+    const int nst = (nb + 7) / 8;
+    uint8_t* xqs = ring + p.nslots * kGemvFragRows * p.pitch;
+    float* misc = reinterpret_cast<float*>(xqs + xq_norm_bytes(p.K));  // 64 floats
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int vbeg = p.vrange[blockIdx.x], vend = p.vrange[blockIdx.x + 1];
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < p.nslots; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], kCW);
+        }
+        mbar_init(xbar, 1);
+        flags[0] = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    pdl_launch_dependents();
+
+    if (warp == kCW) {
+        // ---------------- producer warp ----------------
+        if (lane != 0) return;
+        const uint64_t pol = policy_evict_first();
+        const uint32_t xbytes = p.xq ? (uint32_t)(p.xq_norm ? xq_norm_bytes(p.K) : xq_bytes(p.K)) : 0u;
+        bool xq_done = p.xq == nullptr;
+        FragIter it{vbeg, vend};
+        Frag t;
+        uint32_t issued = 0;
+        bool ok = true;
+        while (ok && it.next(p, t)) {
+            for (int st = 0; st < nst && ok; ++st) {
+                const int slot = issued % p.nslots;
+                const uint32_t ph = (issued / p.nslots) & 1u;
+                if (!xq_done && issued >= (uint32_t)p.nslots) {
+                    // ring full of prefetched weights: now fetch the input
+                    pdl_wait();
+                    mbar_arrive_expect_tx(xbar, xbytes);
+                    bulk_g2s(xqs, p.xq, xbytes, xbar, pol);
+                    xq_done = true;
+                }
+                ok = mbar_wait(&empty[slot], ph ^ 1u);
+                if (!ok || *(volatile int*)flags) { ok = false; break; }
+                const int nbs = min(8, nb - st * 8);
+                const GemvSeg& g0 = p.seg[p.epi == EPI_SWIGLU ? 0 : t.seg];
+                const uint32_t segb = stage_seg_bytes(g0.type, nbs);
+                uint8_t* dst = ring + slot * kGemvFragRows * p.pitch;
+                mbar_arrive_expect_tx(&full[slot], (p.epi == EPI_SWIGLU ? 2u : 1u) * (uint32_t)t.n * segb);
+                copy_rows(dst, g0, t.row0, t.n, st, segb, &full[slot], pol);
+                if (p.epi == EPI_SWIGLU)
+                    copy_rows(dst + (kGemvFragRows / 2) * segb, p.seg[1], t.row0, t.n, st, segb, &full[slot], pol);
+                ++issued;
+            }
+        }
+        if (!xq_done && ok) {
+            pdl_wait();
+            mbar_arrive_expect_tx(xbar, xbytes);
+            bulk_g2s(xqs, p.xq, xbytes, xbar, pol);
+            xq_done = true;
+        }
+        if (!ok) {
+            *(volatile int*)flags = 1;
+            // Drain: wait (bounded) for the copies still in flight.
+            const uint32_t first = issued > (uint32_t)p.nslots ? issued - p.nslots : 0u;
+            for (uint32_t i = first; i < issued; ++i) mbar_wait(&full[i % p.nslots], (i / p.nslots) & 1u);
+            if (xq_done && p.xq) mbar_wait(xbar, 0);
+        }
+        return;
+    }
+
+    // ---------------- consumer warps: input ----------------
+    pdl_wait();
+    float s_in = 1.f;  // RMSNorm scale folded into the per-group scales (XQ input)
+    if (p.xq) {
+        bool ok = true;
+        if (lane == 0) ok = mbar_wait(xbar, 0);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) {
+            *(volatile int*)flags = 1;
+        } else if (p.xq_norm) {
+            // s = 1/sqrt(Σx²/K + eps) from the producer's per-group sums, in a
+            // fixed order (deterministic)
+            const float* pss = reinterpret_cast<const float*>(xqs + xq_bytes(p.K));
+            float ss = 0.f;
+            for (int g = lane; g < p.K / 64; g += 32) ss += pss[g];
+            ss = warp_sum(ss);
+            s_in = 1.f / sqrtf(ss / (float)p.K + p.eps);
+        }
+    } else {
+        switch (nst) {
+            case 1: input_prologue<1>(p, xqs, misc); break;
+            case 2: input_prologue<2>(p, xqs, misc); break;
+            case 3: input_prologue<3>(p, xqs, misc); break;
+            case 4: input_prologue<4>(p, xqs, misc); break;
+            case 5: input_prologue<5>(p, xqs, misc); break;
+            default: input_prologue<6>(p, xqs, misc); break;
+        }
+        bar_consumers();
+    }
+    const uint8_t* XH = xqs;
+    const uint8_t* XL = xqs + nst * 2048;
+    const float* XS = reinterpret_cast<const float*>(xqs + 2 * nst * 2048);
+    const float* XS32 = XS + nst * 32;
+    const int* XI16 = reinterpret_cast<const int*>(XS32 + nst * 64);
 
     // ---------------- consumer main loop ----------------
     const int lb = lane >> 2, lc = lane & 3;
-    TileIter it{vbeg, vend};
-    Tile t;
+    FragIter it{vbeg, vend};
+    Frag t;
     uint32_t consumed = 0;
-    bool ok = true;
+    bool ok = !*(volatile int*)flags;
     float best = -INFINITY;
     uint32_t best_idx = 0;
+    const int half = kGemvFragRows / 2;
     while (ok && it.next(p, t)) {
         float acc[2] = {0.f, 0.f};
-        int seg[2], row[2];
         bool rv[2];
-        rv[0] = tile_row(p, t, warp, seg[0], row[0]);
-        rv[1] = tile_row(p, t, warp + 8, seg[1], row[1]);
-        const int ty0 = p.seg[seg[0]].type, ty1 = p.seg[seg[1]].type;
+        int seg[2], row[2];
+        if (p.epi == EPI_SWIGLU) {
+            rv[0] = rv[1] = warp < t.n;
+            seg[0] = 0; seg[1] = 1;
+            row[0] = row[1] = t.row0 + warp;
+        } else {
+            rv[0] = warp < t.n;
+            rv[1] = warp + half < t.n;
+            seg[0] = seg[1] = t.seg;
+            row[0] = t.row0 + warp;
+            row[1] = t.row0 + warp + half;
+        }
+        const int ty = p.seg[seg[0]].type;
         for (int st = 0; st < nst; ++st) {
             const int slot = consumed % p.nslots;
             const uint32_t ph = (consumed / p.nslots) & 1u;
             if (lane == 0) ok = mbar_wait(&full[slot], ph);
             ok = __shfl_sync(0xffffffffu, ok, 0);
-            if (!ok || *(volatile int*)abort_flag) { ok = false; break; }
+            if (!ok || *(volatile int*)flags) { ok = false; break; }
             const int nbs = min(8, nb - st * 8);
-            if (lb < nbs) {
+            if (lb < nbs && rv[0]) {
                 XRegs x;
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
@@ -403,29 +484,27 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
                     x.l[i] = *reinterpret_cast<const uint4*>(XL + st * 2048 + i * 512 + lane * 16);
                     x.is16[i] = XI16[st * 128 + i * 32 + lane];
                 }
-                x.xs = XS[st * 32 + lane];
-                x.s32[0] = XS32[st * 64 + lane];
-                x.s32[1] = XS32[st * 64 + 32 + lane];
-                // Both rows of the warp are evaluated without branches so their
-                // independent dp4a chains interleave; an invalid row reads
-                // stale shared memory and its result is discarded.
-                const uint32_t segb = stage_seg_bytes(ty0, nbs);
-                const uint8_t* rp0 = ring + slot * kGemvTileRows * p.pitch + warp * segb;
-                const uint8_t* rp1 = rp0 + 8 * segb;
-                if (ty0 == ty1 && ty0 == AF_GGML_Q6_K) {
+                x.xs = XS[st * 32 + lane] * s_in;
+                x.s32[0] = XS32[st * 64 + lane] * s_in;
+                x.s32[1] = XS32[st * 64 + 32 + lane] * s_in;
+                // Both rows evaluated without branches so their dp4a chains
+                // interleave; an invalid second row reads stale shared memory
+                // and its result is discarded.
+                const uint32_t segb = stage_seg_bytes(ty, nbs);
+                const uint8_t* rp0 = ring + slot * kGemvFragRows * p.pitch + warp * segb;
+                const uint8_t* rp1 = rp0 + half * segb;
+                if (ty == AF_GGML_Q6_K) {
                     const float d0 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(rp0 + nbs * 208 + 2 * lb));
                     const float d1 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(rp1 + nbs * 208 + 2 * lb));
                     const float a0 = q6k_lane_dot(rp0 + lb * 208, d0, lc, x);
                     const float a1 = q6k_lane_dot(rp1 + lb * 208, d1, lc, x);
                     acc[0] += a0;
                     acc[1] += a1;
-                } else if (ty0 == ty1) {
+                } else {
                     const float a0 = q4k_lane_dot(rp0 + lb * 144, lc, x);
                     const float a1 = q4k_lane_dot(rp1 + lb * 144, lc, x);
                     acc[0] += a0;
                     acc[1] += a1;
-                } else {
-                    set_err(kErrBadArgs);  // a tile never mixes types (checked on the host)
                 }
             }
             __syncwarp();
@@ -453,8 +532,6 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
                         if (sg.bias) v += sg.bias[row[r]];
                         sg.y[row[r]] = v;
                         if (p.epi == EPI_ARGMAX) {
-                            // strict '>' keeps the first maximum within the warp's rows,
-                            // which are visited in increasing order per warp.
                             const uint32_t gi = (uint32_t)(p.argmax_base + row[r]);
                             if (v > best || (v == best && gi < best_idx)) { best = v; best_idx = gi; }
                         }
@@ -463,36 +540,88 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const __grid_cons
             }
         }
     }
-    if (!ok) *(volatile int*)abort_flag = 1;
+    if (!ok) *(volatile int*)flags = 1;
     if (p.epi == EPI_ARGMAX && lane == 0 && best > -INFINITY) atomicMax(p.argmax, argmax_key(best, best_idx));
+
+    // ---------------- quantise the output for the next GEMV ----------------
+    if (p.q_out) {
+        // Each 64-row group is quantised by the CTA that completes it.
+        int* list = flags + 1;
+        bar_consumers();  // every epilogue store of this CTA is done
+        if (threadIdx.x == 0) {
+            __threadfence();
+            int n = 0;
+            for (int g = vbeg / 64; g * 64 < vend; ++g) {
+                const int lo = max(vbeg, g * 64), hi = min(vend, g * 64 + 64);
+                const unsigned int prev = atomicAdd(&p.q_cnt[g], (unsigned int)(hi - lo));
+                if (prev + (unsigned int)(hi - lo) == 64u) list[++n] = g;
+            }
+            list[0] = n;
+            __threadfence();
+        }
+        bar_consumers();
+        const int n = list[0];
+        const float* src = p.epi == EPI_RESID ? p.resid : p.seg[0].y;
+        const int Kout = p.seg[0].rows;
+        for (int k = warp; k < n; k += kCW) {
+            const int g = list[1 + k];
+            xq_quantize_group(p.q_out, src, p.q_norm_w, Kout, g);
+            if (lane == 0) p.q_cnt[g] = 0u;
+        }
+    }
 }
 
 }  // namespace
 
-int gemv_configure(GemvParams& p) {
+void gemv_configure(GemvParams& p, int grid) {
     int pitch = 0;
-    const int nsegs = p.nseg;
-    for (int s = 0; s < nsegs; ++s) {
+    for (int s = 0; s < p.nseg; ++s) {
         const int rb = p.seg[s].type == AF_GGML_Q6_K ? 8 * 208 + 16 : 8 * 144;
         pitch = pitch > rb ? pitch : rb;
     }
-    // Ring budget keeps two CTAs (this kernel and the next one under PDL) per SM.
-    const int budget = 84 * 1024;
-    int ns = budget / (kGemvTileRows * pitch);
-    ns = ns < 2 ? 2 : (ns > 4 ? 4 : ns);
+    const int budget = 165 * 1024;
+    int ns = budget / (kGemvFragRows * pitch);
+    ns = ns < 2 ? 2 : (ns > kGemvMaxSlots ? kGemvMaxSlots : ns);
     p.pitch = pitch;
     p.nslots = ns;
-    return gemv_smem_bytes(p.K, pitch, ns);
+    // CTA row ranges balanced by weight bytes (a gate/up pair is one virtual row)
+    grid = grid < 1 ? 1 : (grid > kGemvMaxGrid ? kGemvMaxGrid : grid);
+    p.grid = grid;
+    const bool sw = p.epi == EPI_SWIGLU;
+    const int nvs = sw ? 1 : p.nseg;
+    long long total = 0;
+    long long rb[3], rows[3];
+    for (int s = 0; s < nvs; ++s) {
+        rb[s] = sw ? (long long)p.seg[0].row_stride + p.seg[1].row_stride : p.seg[s].row_stride;
+        rows[s] = p.seg[s].rows;
+        total += rb[s] * rows[s];
+    }
+    for (int i = 0; i <= grid; ++i) {
+        long long b = total * i / grid, base = 0;
+        int v = 0;
+        for (int s = 0; s < nvs; ++s) {
+            const long long segb = rb[s] * rows[s];
+            if (b <= segb || s == nvs - 1) {
+                long long r = (b + rb[s] - 1) / rb[s];
+                if (r > rows[s]) r = rows[s];
+                v = (int)(base + r);
+                break;
+            }
+            b -= segb;
+            base += rows[s];
+        }
+        p.vrange[i] = v;
+    }
 }
 
 cudaError_t gemv_init() {
-    return cudaFuncSetAttribute(gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    return cudaFuncSetAttribute(gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
 }
 
-cudaError_t gemv_launch(const GemvParams& p, int grid, cudaStream_t stream, bool pdl) {
+cudaError_t gemv_launch(const GemvParams& p, cudaStream_t stream, bool pdl) {
     const int smem = gemv_smem_bytes(p.K, p.pitch, p.nslots);
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
+    cfg.gridDim = dim3(p.grid);
     cfg.blockDim = dim3(kGemvThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
@@ -502,6 +631,19 @@ cudaError_t gemv_launch(const GemvParams& p, int grid, cudaStream_t stream, bool
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, gemv_kernel, p);
+}
+
+cudaError_t xq_quantize_launch(uint8_t* xq, const float* x, const float* norm_w, int K, cudaStream_t st, bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((K / 64 + 3) / 4);
+    cfg.blockDim = dim3(128);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, xq_quantize_kernel, xq, x, norm_w, K);
 }
 
 }  // namespace af

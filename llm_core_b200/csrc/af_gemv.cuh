@@ -6,26 +6,33 @@
 // and its incorrect CUDA v1 kernel (src/backend/cuda/cuda_kernels.cu:71-109).
 //
 // Design (HBM-bound; one launch streams each weight byte exactly once):
+//  * Weights are "packed" once at upload (af_weight_pack): 16-row tiles, each
+//    holding stage after stage the rows' segments of 8 super-blocks, so one
+//    pipeline stage of up to 32 rows is one or two contiguous bulk copies.
 //  * Grid = one CTA per SM.  Each CTA owns a byte-balanced contiguous range of
-//    output rows and walks it in tiles of 16 rows (8 row pairs for SwiGLU).
-//  * Warp 8 is the producer: it streams every (tile, 8-block K chunk) stage
-//    into a ring of shared-memory slots with cp.async.bulk (the TMA engine,
-//    no tensor map, no multicast), one bulk copy per row, completion counted
-//    on an mbarrier.  Weights are read with an L2 evict-first policy.  The
-//    first ring-full of stages is issued before griddepcontrol.wait, so under
-//    programmatic dependent launch the weight stream overlaps the tail of the
-//    previous kernel.
-//  * Warps 0-7 are consumers.  Their prologue turns the f32 input (optionally
-//    plus a pending residual, optionally RMS-normalised) into a shared-memory
-//    copy split into two int8 planes: x ≈ xs·(256·hi + lo) per 64 values
-//    (|error| ≤ 2^-16·max|x| of the group), plus per-32 f32 sums and per-16
-//    integer sums for the min / offset terms.  Each lane then owns one
-//    (super-block, 64-value chunk) of the stage and evaluates the exact
-//    integer dot Σ q·(256·hi + lo) with dp4a, applying the block scales in
-//    f32 — the same w = d·sc·q − dmin·m (Q4_K) and w = d·sc·(q − 32) (Q6_K)
-//    the reference dequantises, accumulated in fp32.
+//    output rows (computed on the host) and walks it in fragments of up to 32
+//    rows (16 gate/up pairs for SwiGLU).
+//  * Warp 16 is the producer: it streams every (fragment, K stage) into a ring
+//    of shared-memory slots with cp.async.bulk (the TMA engine, no tensor map,
+//    no multicast), completion counted on an mbarrier, L2 evict-first.  The
+//    first ring-full is issued before griddepcontrol.wait.
+//  * The input vector arrives already quantised in the shared-memory layout
+//    ("XQ": x ≈ xs·(256·hi + lo) per 64 values as two int8 planes, per-32 f32
+//    sums, per-16 integer sums, and for a normalised input the per-64 sums of
+//    squares): the producer copies it with one bulk copy after
+//    griddepcontrol.wait.  The kernel that produced the vector quantised each
+//    64-value group once (the last CTA to finish a group does it), so no CTA
+//    re-reads and re-quantises the whole input.  A legacy in-CTA prologue
+//    quantises an f32 input for the standalone entry points and tensor
+//    parallel ranks.
+//  * Warps 0-15 are consumers: lane = (super-block, 64-value chunk) of the
+//    stage; each warp evaluates two rows with exact integer dp4a dots
+//    Σ q·(256·hi + lo) and applies the block scales in f32 — the same
+//    w = d·sc·q − dmin·m (Q4_K) and w = d·sc·(q − 32) (Q6_K) the reference
+//    dequantises, accumulated in fp32.
 //  * Epilogues: plain store (+bias), in-place residual add, SwiGLU of a
-//    gate/up row pair, and LM-head logits with a fused first-max argmax.
+//    gate/up row pair, LM-head logits with a fused first-max argmax; optionally
+//    the output vector is quantised into the next GEMV's XQ buffer.
 #pragma once
 #include "af_common.cuh"
 
@@ -33,42 +40,51 @@ namespace af {
 
 enum GemvEpi : int { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_RESID = 2, EPI_ARGMAX = 3 };
 
+constexpr int kGemvConsumerWarps = 16;
+constexpr int kGemvThreads = (kGemvConsumerWarps + 1) * 32;
+constexpr int kPackTile = 16;        // rows per tile of the packed weight layout
+constexpr int kGemvFragRows = 32;    // rows per pipeline stage
+constexpr int kGemvMaxSlots = 6;
+constexpr int kGemvMaxK = 12288;     // input length held in registers by the legacy prologue
+constexpr int kGemvMaxGrid = 296;
+
 struct GemvSeg {
-    const uint8_t* w;      // device rows (Q4_K GGUF rows or Q6_K regrouped rows)
+    const uint8_t* w;      // packed rows
     float* y;              // output rows (EPI_STORE / EPI_ARGMAX / SWIGLU seg 0)
     const float* bias;     // optional per-row bias (EPI_STORE)
     int type;              // AF_GGML_Q4_K or AF_GGML_Q6_K
     int rows;
-    int row_stride;        // bytes
+    int row_stride;        // bytes per row (sum of the row's stage segments)
 };
 
 struct GemvParams {
     GemvSeg seg[3];
     int nseg;
     int K;                 // input length, multiple of 256
-    const float* x;        // f32 input [K]
-    const float* x_add;    // optional: input = x + x_add (deferred residual) ...
-    float* x_store;        // ... and CTA 0 stores that sum here
-    const float* norm_w;   // optional RMSNorm weight [K]
+    // input, quantised form (preferred): XQ layout of xq_bytes(K) bytes, and
+    // with xq_norm the per-64 sums of squares after it (RMSNorm input)
+    const uint8_t* xq;
+    int xq_norm;
+    // input, f32 form (legacy prologue): x (+ x_add, stored to x_store) [+ RMSNorm]
+    const float* x;
+    const float* x_add;
+    float* x_store;
+    const float* norm_w;
     float eps;
     int epi;
     float* resid;          // EPI_RESID: resid[row] += W·x
     unsigned long long* argmax;  // EPI_ARGMAX: packed (value, ~index) maximum
     int argmax_base;       // global index of row 0 (vocab shard offset)
-    int pitch;             // shared-memory bytes per row slot
+    // optional: quantise the output vector (resid for EPI_RESID, y_0 otherwise)
+    // into q_out for the next GEMV, with RMSNorm weights q_norm_w (NULL: plain)
+    uint8_t* q_out;
+    const float* q_norm_w;
+    unsigned int* q_cnt;   // per-64-row-group arrival counters, zero between launches
+    int pitch;             // max bytes of one row's stage segment
     int nslots;            // ring depth
+    int grid;
+    int vrange[kGemvMaxGrid + 1];  // CTA i owns virtual rows [vrange[i], vrange[i+1])
 };
-
-constexpr int kGemvThreads = 288;  // 8 consumer warps + 1 producer warp
-constexpr int kGemvTileRows = 16;
-constexpr int kGemvMaxSlots = 6;
-constexpr int kGemvMaxK = 12288;  // input length held in registers by the prologue
-
-// Shared-memory bytes the GEMV needs for (K, pitch, nslots).
-__host__ __device__ inline int gemv_smem_bytes(int K, int pitch, int nslots) {
-    const int nst = (K / 256 + 7) / 8;
-    return 128 + nslots * kGemvTileRows * pitch + nst * (2048 * 2 + 32 * 4 + 64 * 4 + 128 * 4) + 64 * 4;
-}
 
 __host__ __device__ inline int q6k_row_stride(int cols) {
     const int nb = cols / 256, full = nb / 8, rem = nb % 8;
@@ -81,14 +97,33 @@ __host__ __device__ inline int dev_row_stride(int type, int cols) {
 
 // Device bytes of a packed matrix: whole 16-row tiles (the last one zero-padded).
 __host__ __device__ inline size_t packed_bytes(int type, int rows, int cols) {
-    return (size_t)((rows + kGemvTileRows - 1) / kGemvTileRows) * kGemvTileRows * dev_row_stride(type, cols);
+    return (size_t)((rows + kPackTile - 1) / kPackTile) * kPackTile * dev_row_stride(type, cols);
+}
+
+// Bytes of the quantised-input (XQ) layout for K values: per stage of 2048
+// values: hi plane 2048, lo plane 2048, 32 f32 scales, 64 f32 sums of 32,
+// 128 int sums of 16.  A normalised input appends K/64 f32 sums of squares.
+__host__ __device__ inline int xq_bytes(int K) { return ((K / 256 + 7) / 8) * 4992; }
+__host__ __device__ inline int xq_norm_bytes(int K) { return xq_bytes(K) + K / 16; }
+
+// Shared-memory bytes the GEMV needs.
+__host__ __device__ inline int gemv_smem_bytes(int K, int pitch, int nslots) {
+    return 256 + nslots * kGemvFragRows * pitch + xq_norm_bytes(K) + 256;
 }
 
 // Per-device kernel attributes; call once per device before launching (and
 // before any stream capture).
 cudaError_t gemv_init();
-cudaError_t gemv_launch(const GemvParams& p, int grid, cudaStream_t stream, bool pdl);
-// Fill pitch / nslots for the segments in p; returns the dynamic smem bytes.
-int gemv_configure(GemvParams& p);
+// Fill pitch / nslots / grid / CTA ranges for the segments in p.
+void gemv_configure(GemvParams& p, int grid);
+cudaError_t gemv_launch(const GemvParams& p, cudaStream_t stream, bool pdl);
+
+// Quantise an f32 vector (RMSNorm weights applied when norm_w is set) into XQ
+// form, for inputs no producing kernel writes.
+cudaError_t xq_quantize_launch(uint8_t* xq, const float* x, const float* norm_w, int K, cudaStream_t st, bool pdl);
+
+// One warp quantises 64-value group g of src (global f32) into the XQ buffer;
+// with norm_w, w·x is quantised and Σx² stored after the layout.
+__device__ void xq_quantize_group(uint8_t* xq, const float* src, const float* norm_w, int K, int g);
 
 }  // namespace af

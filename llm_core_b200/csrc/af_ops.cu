@@ -37,8 +37,8 @@ __host__ __device__ inline size_t packed_off(int type, int nb, int row_stride, i
     const int nbs = min(8, nb - st * 8);
     const int seg = type == AF_GGML_Q6_K ? nbs * 208 + 16 : nbs * 144;
     const int full = type == AF_GGML_Q6_K ? 1680 : 1152;
-    return (size_t)(row / kGemvTileRows) * kGemvTileRows * row_stride + (size_t)kGemvTileRows * st * full +
-           (size_t)(row % kGemvTileRows) * seg;
+    return (size_t)(row / kPackTile) * kPackTile * row_stride + (size_t)kPackTile * st * full +
+           (size_t)(row % kPackTile) * seg;
 }
 
 // One CTA per row; GGUF block j of the row goes to stage j/8, slot j%8 of that
@@ -78,7 +78,8 @@ cudaError_t weight_pack(void* d_dst, const void* d_src, int type, int rows, int 
 // for Q4_K (GGUF rows) and Q6_K (regrouped rows).  Also resets the argmax
 // key for the step (this is the step's first kernel).
 __global__ void embed_kernel(float* __restrict__ x, const uint8_t* __restrict__ W, int type, int cols,
-                             int row_stride, const int* __restrict__ token, unsigned long long* argmax) {
+                             int row_stride, const int* __restrict__ token, unsigned long long* argmax,
+                             uint8_t* xq, const float* xq_norm_w) {
     pdl_launch_dependents();
     pdl_wait();
     if (argmax && blockIdx.x == 0 && threadIdx.x == 0) *argmax = 0ull;
@@ -120,10 +121,18 @@ __global__ void embed_kernel(float* __restrict__ x, const uint8_t* __restrict__ 
         }
         x[v] = out;
     }
+    if (xq) {
+        // quantise this block's 64-value groups for the first GEMV
+        __threadfence();
+        __syncthreads();
+        const int g = (blockIdx.x * blockDim.x) / 64 + (threadIdx.x >> 5);
+        if ((threadIdx.x >> 5) < (int)blockDim.x / 64 && g < cols / 64) xq_quantize_group(xq, x, xq_norm_w, cols, g);
+    }
 }
 
 cudaError_t embed_launch(float* x, const uint8_t* W, int type, int cols, int row_stride, const int* token,
-                         unsigned long long* argmax, cudaStream_t st, bool pdl) {
+                         unsigned long long* argmax, uint8_t* xq, const float* xq_norm_w, cudaStream_t st,
+                         bool pdl) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((cols + 255) / 256);
     cfg.blockDim = dim3(256);
@@ -133,7 +142,7 @@ cudaError_t embed_launch(float* x, const uint8_t* W, int type, int cols, int row
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, embed_kernel, x, W, type, cols, row_stride, token, argmax);
+    return cudaLaunchKernelEx(&cfg, embed_kernel, x, W, type, cols, row_stride, token, argmax, xq, xq_norm_w);
 }
 
 // -------------------------------------------------- reference CUDA op set
@@ -242,9 +251,9 @@ cudaError_t af_gemv_f32(float* d_y, const void* d_w, int ggml_type, const float*
     p.K = cols;
     p.x = d_x;
     p.epi = EPI_STORE;
-    gemv_configure(p);
+    gemv_configure(p, gemv_grid());
     AF_CUDA_TRY(gemv_init());
-    return gemv_launch(p, gemv_grid(), stream, false);
+    return gemv_launch(p, stream, false);
 }
 
 cudaError_t af_gemv_fused(const af_gemv_fused_args* a, cudaStream_t stream) {
@@ -286,9 +295,9 @@ cudaError_t af_gemv_fused(const af_gemv_fused_args* a, cudaStream_t stream) {
     p.resid = a->resid;
     p.argmax = a->argmax;
     p.argmax_base = a->argmax_base;
-    gemv_configure(p);
+    gemv_configure(p, gemv_grid());
     AF_CUDA_TRY(gemv_init());
-    return gemv_launch(p, gemv_grid(), stream, false);
+    return gemv_launch(p, stream, false);
 }
 
 cudaError_t af_attention_decode_f32(float* d_out, const float* d_q, const float* d_k, const float* d_v,

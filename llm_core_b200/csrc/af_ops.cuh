@@ -3,6 +3,7 @@
 #include <string>
 
 #include "af_common.cuh"
+#include "af_gemv.cuh"
 
 namespace af {
 
@@ -12,7 +13,8 @@ int gemv_grid();
 
 cudaError_t weight_pack(void* d_dst, const void* d_src, int type, int rows, int cols, bool unpack, cudaStream_t st);
 cudaError_t embed_launch(float* x, const uint8_t* W, int type, int cols, int row_stride, const int* token,
-                         unsigned long long* argmax, cudaStream_t st, bool pdl);
+                         unsigned long long* argmax, uint8_t* xq, const float* xq_norm_w, cudaStream_t st,
+                         bool pdl);
 
 // Decode attention (af_attention.cu).
 struct AttnParams {
@@ -31,6 +33,7 @@ struct AttnParams {
     const int* pos;        // device position of the new token
     int n_heads, n_kv_heads, head_dim, n_ctx, nsplit, qk_norm_order;
     float eps, scale;
+    uint8_t* xq_out;       // optional: quantised copy of `out` for the next GEMV
 };
 
 cudaError_t attention_init();
