@@ -122,6 +122,24 @@ cudaError_t af_attention_decode_f32(float* d_out, const float* d_q, const float*
                                     int n_ctx, int qk_norm_order, float eps, int nsplit,
                                     float* d_part, unsigned int* d_counter, cudaStream_t stream);
 
+/* af_attention_decode_f32 without caller-provided scratch, for callers that
+ * cannot call cudaMalloc while serving (a host that owns a fixed device arena,
+ * or a plugin only handed input and output pointers).  No counterpart in the
+ * reference.  The split-K partials and counters live in a 1 MiB device array
+ * of the library that every GPU loading it keeps until exit, so
+ * n_heads*nsplit*(head_dim+2) <= 262144 and n_kv_heads <= 256 (larger calls
+ * return cudaErrorInvalidValue).  The first call on a device looks the array's
+ * address up (cudaGetSymbolAddress) and should come before any stream capture.
+ * All calls share the array: calls that overlap on the GPU race.  Allocates
+ * nothing (no cudaMalloc / cudaFree). */
+cudaError_t af_attention_decode_f32_noalloc(float* d_out, const float* d_q, const float* d_k,
+                                            const float* d_v, float* d_kcache, float* d_vcache,
+                                            const float* d_cos, const float* d_sin,
+                                            const float* d_q_norm, const float* d_k_norm,
+                                            const int* d_pos, int n_heads, int n_kv_heads,
+                                            int head_dim, int n_ctx, int qk_norm_order, float eps,
+                                            int nsplit, cudaStream_t stream);
+
 /* y = w ⊙ x / sqrt(mean(x²) + eps): rms_norm_f32 (cuda_kernels.hpp:8). */
 cudaError_t af_rms_norm_f32(float* d_y, const float* d_x, const float* d_w, int n, float eps,
                             cudaStream_t stream);

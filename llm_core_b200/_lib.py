@@ -72,6 +72,8 @@ def load() -> C.CDLL:
         "af_gemv_fused": (i, [C.POINTER(GemvFusedArgs), vp]),
         "af_attention_decode_f32": (i, [vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i, i, i, i, i, f, i, vp, vp,
                                         vp]),
+        "af_attention_decode_f32_noalloc": (i, [vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i, i, i, i, i, f, i,
+                                                vp]),
         "af_silu_f32": (i, [vp, vp, i, vp]),
         "af_mul_f32": (i, [vp, vp, vp, i, vp]),
         "af_rope_f32": (i, [vp, i, i, i, f, vp]),

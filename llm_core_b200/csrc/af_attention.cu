@@ -10,6 +10,9 @@
 // (o, running max, sum) and the last CTA of a kv head merges the partials with
 // the usual exp(m_s − M) rescaling.  Cache layout is the reference's:
 // [n_ctx][n_kv_heads * head_dim] per layer, fp32.
+#include <mutex>
+#include <string>
+
 #include "af_ops.cuh"
 
 namespace af {
@@ -309,3 +312,84 @@ cudaError_t finalize_launch(const unsigned long long* key, int* token, int* pos,
 }
 
 }  // namespace af
+
+// ---------------------------------------------------------------------------
+// Attention entry point that allocates nothing.
+//
+// Some callers cannot call cudaMalloc on the serving path: a host that owns a
+// fixed device arena and forbids further allocation once it is serving, or a
+// plugin that is only handed input/output pointers and must not change the
+// process's memory footprint.  For them the split-K partials and the per-kv-head
+// counters live in this file-scope device array instead of caller-provided
+// scratch.  Every GPU that loads the library holds the array until exit.
+namespace af {
+namespace {
+
+constexpr int kNoAllocPartFloats = 256 * 1024;  // 1 MiB of partials
+constexpr int kNoAllocCounters = 256;
+
+struct NoAllocScratch {
+    float part[kNoAllocPartFloats];
+    unsigned int counter[kNoAllocCounters];
+};
+
+static __device__ __align__(256) NoAllocScratch g_attn_scratch;
+
+// Device addresses of g_attn_scratch, looked up once per device.
+constexpr int kMaxDevices = 64;
+NoAllocScratch* g_scratch_ptr[kMaxDevices] = {};
+std::mutex g_scratch_mu;
+
+cudaError_t scratch_for_current_device(NoAllocScratch** out) {
+    int dev = 0;
+    AF_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    if (!g_scratch_ptr[dev]) {
+        void* p = nullptr;
+        const cudaError_t r = cudaGetSymbolAddress(&p, g_attn_scratch);
+        if (r != cudaSuccess) {
+            set_last_error(std::string("af_attention_decode_f32_noalloc: cudaGetSymbolAddress: ") +
+                           cudaGetErrorString(r));
+            return r;
+        }
+        g_scratch_ptr[dev] = static_cast<NoAllocScratch*>(p);
+    }
+    *out = g_scratch_ptr[dev];
+    return cudaSuccess;
+}
+
+}  // namespace
+}  // namespace af
+
+extern "C" cudaError_t af_attention_decode_f32_noalloc(
+    float* d_out, const float* d_q, const float* d_k, const float* d_v, float* d_kcache, float* d_vcache,
+    const float* d_cos, const float* d_sin, const float* d_q_norm, const float* d_k_norm, const int* d_pos,
+    int n_heads, int n_kv_heads, int head_dim, int n_ctx, int qk_norm_order, float eps, int nsplit,
+    cudaStream_t stream) {
+    using namespace af;
+    if (n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads || nsplit <= 0 || n_ctx <= 0 || head_dim <= 0) {
+        set_last_error("af_attention_decode_f32_noalloc: bad shape");
+        return cudaErrorInvalidValue;
+    }
+    if ((long long)n_heads * nsplit * (head_dim + 2) > kNoAllocPartFloats || n_kv_heads > kNoAllocCounters) {
+        set_last_error("af_attention_decode_f32_noalloc: n_heads*nsplit*(head_dim+2) must be <= 262144 and "
+                       "n_kv_heads <= 256 (fixed scratch of this entry point)");
+        return cudaErrorInvalidValue;
+    }
+    NoAllocScratch* s = nullptr;
+    AF_CUDA_TRY(scratch_for_current_device(&s));
+    // The counters must start at zero; a call that ended early could have left
+    // them dirty, so clear them on the stream (no allocation involved).
+    AF_CUDA_TRY(cudaMemsetAsync(s->counter, 0, sizeof(unsigned int) * n_kv_heads, stream));
+    AttnParams p = {};
+    p.q = d_q; p.k = d_k; p.v = d_v; p.kc = d_kcache; p.vc = d_vcache; p.out = d_out;
+    p.cos_t = d_cos; p.sin_t = d_sin; p.q_norm = d_q_norm; p.k_norm = d_k_norm;
+    p.part = s->part; p.counter = s->counter; p.pos = d_pos;
+    p.n_heads = n_heads; p.n_kv_heads = n_kv_heads; p.head_dim = head_dim; p.n_ctx = n_ctx;
+    p.nsplit = nsplit; p.qk_norm_order = qk_norm_order; p.eps = eps;
+    p.scale = 1.f / sqrtf((float)head_dim);
+    AF_CUDA_TRY(attention_init());
+    return attention_launch(p, stream, false);
+}
+
