@@ -116,12 +116,34 @@ def model_file(preset: str, rank: int, dist) -> str:
     return path
 
 
+class _QuietStdout:
+    """The reference library prints a banner on stdout when its backend
+    initialises; keep the bench's stdout to the one JSON line."""
+
+    def __enter__(self):
+        sys.stdout.flush()
+        self.fd = os.dup(1)
+        devnull = os.open(os.devnull, os.O_WRONLY)
+        os.dup2(devnull, 1)
+        os.close(devnull)
+
+    def __exit__(self, *a):
+        os.dup2(self.fd, 1)
+        os.close(self.fd)
+
+
+def open_ref(path: str, threads: int):
+    from oracle import RefLib
+    with _QuietStdout():
+        return RefLib().open(path, threads=threads, f32_mode=False, max_ctx=4096)
+
+
 def cpu_baseline_sample(path: str, steps: int, threads: int) -> dict | None:
     """The reference CPU decode (production Q8_0 path), `steps` tokens from position 0."""
     from oracle import RefLib
     if not RefLib.available():
         return None
-    ref = RefLib().open(path, threads=threads, f32_mode=False, max_ctx=4096)
+    ref = open_ref(path, threads)
     ref.set_n_past(0)
     ref.time_decode(1, 2)  # warm the r8 weight cache / page in
     ref.set_n_past(0)
@@ -145,7 +167,7 @@ def run_reference(args):
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libaxref.so was not built "
                           "(reference sources absent when the repo was built)"}))
         return 0
-    ref = RefLib().open(path, threads=threads, f32_mode=False, max_ctx=4096)
+    ref = open_ref(path, threads)
     ref.set_n_past(0)
     ref.time_decode(1, max(1, args.warmup))
     # each timed step: one reference decode token (context grows from W)
