@@ -156,14 +156,10 @@ __device__ __forceinline__ float q4k_lane_dot(const uint8_t* blk, int c, const X
     // 6-bit scale/min pairs j = 2c (low nibbles) and 2c+1 (high nibbles):
     // get_scale_min_k4 (gemv_q4k_avx2.cpp:34-43) four bytes at a time.
     const uint32_t w0 = hdr.y, w1 = hdr.z, w2 = hdr.w;
-    uint32_t S, M;
-    if (c < 2) {
-        S = w0 & 0x3F3F3F3Fu;
-        M = w1 & 0x3F3F3F3Fu;
-    } else {
-        S = (w2 & 0x0F0F0F0Fu) | ((w0 >> 2) & 0x30303030u);
-        M = ((w2 >> 4) & 0x0F0F0F0Fu) | ((w1 >> 2) & 0x30303030u);
-    }
+    // branch-free: c is per lane, so a branch would diverge within the warp
+    const bool upper = c >= 2;
+    const uint32_t S = upper ? ((w2 & 0x0F0F0F0Fu) | ((w0 >> 2) & 0x30303030u)) : (w0 & 0x3F3F3F3Fu);
+    const uint32_t M = upper ? (((w2 >> 4) & 0x0F0F0F0Fu) | ((w1 >> 2) & 0x30303030u)) : (w1 & 0x3F3F3F3Fu);
     const int sh = (c & 1) * 16;
     const int sc_lo = (S >> sh) & 0xFF, sc_hi = (S >> (sh + 8)) & 0xFF;
     const int m_lo = (M >> sh) & 0xFF, m_hi = (M >> (sh + 8)) & 0xFF;
@@ -217,17 +213,20 @@ __device__ __forceinline__ float q6k_lane_dot(const uint8_t* blk, float d, int c
 }
 
 
-__device__ __forceinline__ void bar_consumers() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
+__device__ __forceinline__ void bar_consumers() { asm volatile("bar.sync 1, %0;" ::"n"(kCT) : "memory"); }
 
 // Legacy prologue: f32 input (+ pending residual, optionally RMS-normalised)
 // loaded with all NIT float4 loads per thread in flight, then quantised into
-// the shared XQ layout.  NIT = float4 slots per consumer thread = stages.
-template <int NIT>
+// the shared XQ layout (NST stages of 512 float4; the padded tail is zero).
+template <int NST>
 __device__ __forceinline__ void input_prologue(const GemvParams& p, uint8_t* xqs, float* red) {
+    constexpr int NIT = (NST * 512 + kCT - 1) / kCT;
+    static_assert(kCT % 16 == 0, "16 consecutive threads own one 64-value group");
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
     const int nvec = p.K / 4;
-    const int nst = NIT;
+    const int nst = NST;
+    const int nslot = NST * 512;
     uint8_t* XH = xqs;
     uint8_t* XL = xqs + nst * 2048;
     float* XS = reinterpret_cast<float*>(xqs + 2 * nst * 2048);
@@ -288,7 +287,10 @@ __device__ __forceinline__ void input_prologue(const GemvParams& p, uint8_t* xqs
 #pragma unroll
     for (int j = 0; j < NIT; ++j) {
         const int v = j * kCT + tid;
+        isum[j] = 0;
+        fsum[j] = 0.f;
         // 16-bit grid of ±32639 so that hi = (q + 128) >> 8 stays within int8.
+        if (v >= nslot) continue;  // beyond the padded last stage (kCT does not divide 512)
         const float inv = amax[j] > 0.f ? 32639.f / amax[j] : 0.f;
         const float av[4] = {a[j].x, a[j].y, a[j].z, a[j].w};
         uint32_t hw = 0, lw = 0;
@@ -322,6 +324,7 @@ __device__ __forceinline__ void input_prologue(const GemvParams& p, uint8_t* xqs
 #pragma unroll
     for (int j = 0; j < NIT; ++j) {
         const float fsum32 = fsum[j] + __shfl_xor_sync(0xffffffffu, fsum[j], 4);
+        if (j * kCT + tid >= nslot) continue;
         const int val = (j * kCT + tid) * 4;
         const int s = val >> 11, w = val & 2047;
         const int b = w >> 8, c = (w >> 6) & 3, i = (w >> 4) & 3;
@@ -366,31 +369,37 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
         const uint32_t xbytes = p.xq ? (uint32_t)(p.xq_norm ? xq_norm_bytes(p.K) : xq_bytes(p.K)) : 0u;
         bool xq_done = p.xq == nullptr;
         FragIter it{vbeg, vend};
-        Frag t;
+        Frag fr[2];
         uint32_t issued = 0;
         bool ok = true;
-        while (ok && it.next(p, t)) {
+        // fragments are taken in pairs; both fragments' stage st go to two
+        // consecutive slots, so a consumer warp reuses one x load for 4 rows
+        while (ok && it.next(p, fr[0])) {
+            const int nf = it.next(p, fr[1]) ? 2 : 1;
             for (int st = 0; st < nst && ok; ++st) {
-                const int slot = issued % p.nslots;
-                const uint32_t ph = (issued / p.nslots) & 1u;
-                if (!xq_done && issued >= (uint32_t)p.nslots) {
-                    // ring full of prefetched weights: now fetch the input
-                    pdl_wait();
-                    mbar_arrive_expect_tx(xbar, xbytes);
-                    bulk_g2s(xqs, p.xq, xbytes, xbar, pol);
-                    xq_done = true;
+                for (int f = 0; f < nf && ok; ++f) {
+                    const Frag& t = fr[f];
+                    const int slot = issued % p.nslots;
+                    const uint32_t ph = (issued / p.nslots) & 1u;
+                    if (!xq_done && issued >= (uint32_t)p.nslots) {
+                        // ring full of prefetched weights: now fetch the input
+                        pdl_wait();
+                        mbar_arrive_expect_tx(xbar, xbytes);
+                        bulk_g2s(xqs, p.xq, xbytes, xbar, pol);
+                        xq_done = true;
+                    }
+                    ok = mbar_wait(&empty[slot], ph ^ 1u);
+                    if (!ok || *(volatile int*)flags) { ok = false; break; }
+                    const int nbs = min(8, nb - st * 8);
+                    const GemvSeg& g0 = p.seg[p.epi == EPI_SWIGLU ? 0 : t.seg];
+                    const uint32_t segb = stage_seg_bytes(g0.type, nbs);
+                    uint8_t* dst = ring + slot * kGemvFragRows * p.pitch;
+                    mbar_arrive_expect_tx(&full[slot], (p.epi == EPI_SWIGLU ? 2u : 1u) * (uint32_t)t.n * segb);
+                    copy_rows(dst, g0, t.row0, t.n, st, segb, &full[slot], pol);
+                    if (p.epi == EPI_SWIGLU)
+                        copy_rows(dst + (kGemvFragRows / 2) * segb, p.seg[1], t.row0, t.n, st, segb, &full[slot], pol);
+                    ++issued;
                 }
-                ok = mbar_wait(&empty[slot], ph ^ 1u);
-                if (!ok || *(volatile int*)flags) { ok = false; break; }
-                const int nbs = min(8, nb - st * 8);
-                const GemvSeg& g0 = p.seg[p.epi == EPI_SWIGLU ? 0 : t.seg];
-                const uint32_t segb = stage_seg_bytes(g0.type, nbs);
-                uint8_t* dst = ring + slot * kGemvFragRows * p.pitch;
-                mbar_arrive_expect_tx(&full[slot], (p.epi == EPI_SWIGLU ? 2u : 1u) * (uint32_t)t.n * segb);
-                copy_rows(dst, g0, t.row0, t.n, st, segb, &full[slot], pol);
-                if (p.epi == EPI_SWIGLU)
-                    copy_rows(dst + (kGemvFragRows / 2) * segb, p.seg[1], t.row0, t.n, st, segb, &full[slot], pol);
-                ++issued;
             }
         }
         if (!xq_done && ok) {
@@ -447,36 +456,46 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
     // ---------------- consumer main loop ----------------
     const int lb = lane >> 2, lc = lane & 3;
     FragIter it{vbeg, vend};
-    Frag t;
+    Frag fr[2];
     uint32_t consumed = 0;
     bool ok = !*(volatile int*)flags;
     float best = -INFINITY;
     uint32_t best_idx = 0;
     const int half = kGemvFragRows / 2;
-    while (ok && it.next(p, t)) {
-        float acc[2] = {0.f, 0.f};
-        bool rv[2];
-        int seg[2], row[2];
-        if (p.epi == EPI_SWIGLU) {
-            rv[0] = rv[1] = warp < t.n;
-            seg[0] = 0; seg[1] = 1;
-            row[0] = row[1] = t.row0 + warp;
-        } else {
-            rv[0] = warp < t.n;
-            rv[1] = warp + half < t.n;
-            seg[0] = seg[1] = t.seg;
-            row[0] = t.row0 + warp;
-            row[1] = t.row0 + warp + half;
+    while (ok && it.next(p, fr[0])) {
+        const int nf = it.next(p, fr[1]) ? 2 : 1;
+        // rows of this warp: (fragment f, r) -> slot row warp + r*half
+        float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+        bool rv[2][2];
+        int row[2][2];
+        int ty[2];
+        for (int f = 0; f < 2; ++f) {
+            const Frag& t = fr[f];
+            const bool have = f < nf;
+            if (p.epi == EPI_SWIGLU) {
+                rv[f][0] = rv[f][1] = have && warp < t.n;
+                row[f][0] = row[f][1] = t.row0 + warp;
+                ty[f] = p.seg[0].type;
+            } else {
+                rv[f][0] = have && warp < t.n;
+                rv[f][1] = have && warp + half < t.n;
+                row[f][0] = t.row0 + warp;
+                row[f][1] = t.row0 + warp + half;
+                ty[f] = have ? p.seg[t.seg].type : p.seg[fr[0].seg].type;
+            }
         }
-        const int ty = p.seg[seg[0]].type;
         for (int st = 0; st < nst; ++st) {
-            const int slot = consumed % p.nslots;
-            const uint32_t ph = (consumed / p.nslots) & 1u;
-            if (lane == 0) ok = mbar_wait(&full[slot], ph);
+            const int slot0 = consumed % p.nslots;
+            const int slot1 = (consumed + 1) % p.nslots;
+            if (lane == 0) {
+                ok = mbar_wait(&full[slot0], (consumed / p.nslots) & 1u);
+                if (ok && nf == 2) ok = mbar_wait(&full[slot1], ((consumed + 1) / p.nslots) & 1u);
+            }
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok || *(volatile int*)flags) { ok = false; break; }
             const int nbs = min(8, nb - st * 8);
-            if (lb < nbs && rv[0]) {
+            // a fragment cut short at a segment end may precede a full one
+            if (lb < nbs && (rv[0][0] || rv[1][0])) {
                 XRegs x;
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
@@ -487,54 +506,84 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
                 x.xs = XS[st * 32 + lane] * s_in;
                 x.s32[0] = XS32[st * 64 + lane] * s_in;
                 x.s32[1] = XS32[st * 64 + 32 + lane] * s_in;
-                // Both rows evaluated without branches so their dp4a chains
-                // interleave; an invalid second row reads stale shared memory
+                // Up to four rows evaluated without branches so their dp4a
+                // chains interleave; an invalid row reads stale shared memory
                 // and its result is discarded.
-                const uint32_t segb = stage_seg_bytes(ty, nbs);
-                const uint8_t* rp0 = ring + slot * kGemvFragRows * p.pitch + warp * segb;
-                const uint8_t* rp1 = rp0 + half * segb;
-                if (ty == AF_GGML_Q6_K) {
-                    const float d0 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(rp0 + nbs * 208 + 2 * lb));
-                    const float d1 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(rp1 + nbs * 208 + 2 * lb));
-                    const float a0 = q6k_lane_dot(rp0 + lb * 208, d0, lc, x);
-                    const float a1 = q6k_lane_dot(rp1 + lb * 208, d1, lc, x);
-                    acc[0] += a0;
-                    acc[1] += a1;
+                const uint8_t* rp[2][2];
+#pragma unroll
+                for (int f = 0; f < 2; ++f) {
+                    const uint32_t segb = stage_seg_bytes(ty[f], nbs);
+                    rp[f][0] = ring + (f ? slot1 : slot0) * kGemvFragRows * p.pitch + warp * segb;
+                    rp[f][1] = rp[f][0] + half * segb;
+                }
+                if (nf == 2 && ty[0] == ty[1]) {
+                    if (ty[0] == AF_GGML_Q6_K) {
+                        float d[4], a[4];
+#pragma unroll
+                        for (int k = 0; k < 4; ++k)
+                            d[k] = half_bits_to_float(*reinterpret_cast<const uint16_t*>(rp[k >> 1][k & 1] + nbs * 208 + 2 * lb));
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) a[k] = q6k_lane_dot(rp[k >> 1][k & 1] + lb * 208, d[k], lc, x);
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) acc[k >> 1][k & 1] += a[k];
+                    } else {
+                        float a[4];
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) a[k] = q4k_lane_dot(rp[k >> 1][k & 1] + lb * 144, lc, x);
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) acc[k >> 1][k & 1] += a[k];
+                    }
                 } else {
-                    const float a0 = q4k_lane_dot(rp0 + lb * 144, lc, x);
-                    const float a1 = q4k_lane_dot(rp1 + lb * 144, lc, x);
-                    acc[0] += a0;
-                    acc[1] += a1;
+                    for (int f = 0; f < nf; ++f) {
+                        if (ty[f] == AF_GGML_Q6_K) {
+                            const float d0 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(rp[f][0] + nbs * 208 + 2 * lb));
+                            const float d1 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(rp[f][1] + nbs * 208 + 2 * lb));
+                            const float a0 = q6k_lane_dot(rp[f][0] + lb * 208, d0, lc, x);
+                            const float a1 = q6k_lane_dot(rp[f][1] + lb * 208, d1, lc, x);
+                            acc[f][0] += a0;
+                            acc[f][1] += a1;
+                        } else {
+                            const float a0 = q4k_lane_dot(rp[f][0] + lb * 144, lc, x);
+                            const float a1 = q4k_lane_dot(rp[f][1] + lb * 144, lc, x);
+                            acc[f][0] += a0;
+                            acc[f][1] += a1;
+                        }
+                    }
                 }
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[slot]);
-            ++consumed;
+            if (lane == 0) {
+                mbar_arrive(&empty[slot0]);
+                if (nf == 2) mbar_arrive(&empty[slot1]);
+            }
+            consumed += nf;
         }
         if (!ok) break;
-        acc[0] = warp_sum(acc[0]);
-        acc[1] = warp_sum(acc[1]);
-        if (lane == 0) {
+        for (int f = 0; f < nf; ++f) {
+            acc[f][0] = warp_sum(acc[f][0]);
+            acc[f][1] = warp_sum(acc[f][1]);
+            if (lane != 0) continue;
             if (p.epi == EPI_SWIGLU) {
-                if (rv[0]) {
-                    const float g = acc[0], u = acc[1];
-                    p.seg[0].y[row[0]] = (g / (1.f + expf(-g))) * u;
+                if (rv[f][0]) {
+                    const float g = acc[f][0], u = acc[f][1];
+                    p.seg[0].y[row[f][0]] = (g / (1.f + expf(-g))) * u;
                 }
-            } else {
+                continue;
+            }
+            const GemvSeg& sg = p.seg[fr[f].seg];
 #pragma unroll
-                for (int r = 0; r < 2; ++r) {
-                    if (!rv[r]) continue;
-                    const GemvSeg& sg = p.seg[seg[r]];
-                    float v = acc[r];
-                    if (p.epi == EPI_RESID) {
-                        p.resid[row[r]] += v;
-                    } else {
-                        if (sg.bias) v += sg.bias[row[r]];
-                        sg.y[row[r]] = v;
-                        if (p.epi == EPI_ARGMAX) {
-                            const uint32_t gi = (uint32_t)(p.argmax_base + row[r]);
-                            if (v > best || (v == best && gi < best_idx)) { best = v; best_idx = gi; }
-                        }
+            for (int r = 0; r < 2; ++r) {
+                if (!rv[f][r]) continue;
+                float v = acc[f][r];
+                if (p.epi == EPI_RESID) {
+                    p.resid[row[f][r]] += v;
+                } else {
+                    if (sg.bias) v += sg.bias[row[f][r]];
+                    sg.y[row[f][r]] = v;
+                    if (p.epi == EPI_ARGMAX) {
+                        // rows reach a lane in increasing order; ties keep the lowest index
+                        const uint32_t gi = (uint32_t)(p.argmax_base + row[f][r]);
+                        if (v > best || (v == best && gi < best_idx)) { best = v; best_idx = gi; }
                     }
                 }
             }

@@ -8,11 +8,11 @@
 // Design (HBM-bound; one launch streams each weight byte exactly once):
 //  * Weights are "packed" once at upload (af_weight_pack): 16-row tiles, each
 //    holding stage after stage the rows' segments of 8 super-blocks, so one
-//    pipeline stage of up to 32 rows is one or two contiguous bulk copies.
+//    pipeline stage of up to 30 rows is a few contiguous bulk copies.
 //  * Grid = one CTA per SM.  Each CTA owns a byte-balanced contiguous range of
-//    output rows (computed on the host) and walks it in fragments of up to 32
-//    rows (16 gate/up pairs for SwiGLU).
-//  * Warp 16 is the producer: it streams every (fragment, K stage) into a ring
+//    output rows (computed on the host) and walks it in fragments of up to 30
+//    rows (15 gate/up pairs for SwiGLU), two fragments per K stage.
+//  * Warp 15 is the producer: it streams every (fragment, K stage) into a ring
 //    of shared-memory slots with cp.async.bulk (the TMA engine, no tensor map,
 //    no multicast), completion counted on an mbarrier, L2 evict-first.  The
 //    first ring-full is issued before griddepcontrol.wait.
@@ -25,8 +25,8 @@
 //    re-reads and re-quantises the whole input.  A legacy in-CTA prologue
 //    quantises an f32 input for the standalone entry points and tensor
 //    parallel ranks.
-//  * Warps 0-15 are consumers: lane = (super-block, 64-value chunk) of the
-//    stage; each warp evaluates two rows with exact integer dp4a dots
+//  * Warps 0-14 are consumers: lane = (super-block, 64-value chunk) of the
+//    stage; each warp evaluates four rows (two per fragment) with exact integer dp4a dots
 //    Σ q·(256·hi + lo) and applies the block scales in f32 — the same
 //    w = d·sc·q − dmin·m (Q4_K) and w = d·sc·(q − 32) (Q6_K) the reference
 //    dequantises, accumulated in fp32.
@@ -40,10 +40,12 @@ namespace af {
 
 enum GemvEpi : int { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_RESID = 2, EPI_ARGMAX = 3 };
 
-constexpr int kGemvConsumerWarps = 16;
+// 15 consumer warps + 1 producer = 16 warps: 4 per SM sub-partition, so each
+// thread may use 128 registers (the register file is split across the 4).
+constexpr int kGemvConsumerWarps = 15;
 constexpr int kGemvThreads = (kGemvConsumerWarps + 1) * 32;
 constexpr int kPackTile = 16;        // rows per tile of the packed weight layout
-constexpr int kGemvFragRows = 32;    // rows per pipeline stage
+constexpr int kGemvFragRows = 2 * kGemvConsumerWarps;  // rows per pipeline stage
 constexpr int kGemvMaxSlots = 6;
 constexpr int kGemvMaxK = 12288;     // input length held in registers by the legacy prologue
 constexpr int kGemvMaxGrid = 296;
