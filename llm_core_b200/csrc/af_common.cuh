@@ -16,6 +16,7 @@ extern __device__ int g_err;
 
 constexpr int kErrMbarTimeout = 1;     // an mbarrier wait exceeded its limit
 constexpr int kErrBadArgs = 2;         // launch arguments failed a device check
+constexpr int kErrBadToken = 3;        // a step saw a token id outside the vocabulary (or no argmax)
 
 // Iteration limit of every spin on an mbarrier.  Each try_wait suspends for
 // up to the hardware time limit, so this is seconds of wall time at most.
@@ -75,10 +76,14 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// With `abort`, the wait also gives up (without an error code) once *abort
+// is set by another thread of the CTA.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const volatile int* abort = nullptr) {
     if (mbar_test_wait(bar, parity)) return true;  // already complete: no suspend
-    for (uint32_t i = 0; i < kSpinLimit; ++i)
+    for (uint32_t i = 0; i < kSpinLimit; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
+        if (abort && (i & 15) == 15 && *abort) return false;
+    }
     set_err(kErrMbarTimeout);
     return false;
 }

@@ -35,6 +35,7 @@
 #include "af_gemv.cuh"
 #include "af_gguf.h"
 #include "af_ops.cuh"
+#include "af_step.cuh"
 
 using namespace af;
 
@@ -96,6 +97,12 @@ struct af_engine {
     int* hist = nullptr;
     int* h_tokpos = nullptr;  // pinned host mirror
     int nsplit = 1;
+
+    // persistent step kernel (single GPU): phase table in device memory
+    bool use_step = false;
+    StepPhase* d_phases = nullptr;
+    unsigned int* step_bar = nullptr;
+    StepParams step{};
 
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t gexec = nullptr;
@@ -219,6 +226,11 @@ cudaError_t enqueue_step(af_engine* e, Prof* prof = nullptr) {
     // Single-GPU steps hand quantised inputs (XQ) from kernel to kernel; tensor
     // parallel ranks quantise inside each GEMV after the all-reduce.
     const bool xq = !tp;
+    if (e->use_step && !prof) {
+        ENG_TRY(step_launch(e->step, e->stream));
+        e->kernels_per_step = 1;
+        return cudaSuccess;
+    }
     ENG_TRY(embed_launch(e->x[0], e->tok_embd.w, e->tok_embd.type, E, e->tok_embd.stride, &e->tokpos[0], e->key,
                          xq ? e->xq_a : nullptr, e->layers[0].attn_norm, e->stream, e->pdl));
     ++nk;
@@ -397,6 +409,139 @@ cudaError_t enqueue_step(af_engine* e, Prof* prof = nullptr) {
     e->kernels_per_step = nk;
     return cudaSuccess;
 #undef AF_MARK
+}
+
+// Phase table of the persistent step kernel (single GPU, quantised inputs
+// handed from phase to phase), mirroring enqueue_step's kernel sequence.
+cudaError_t build_step(af_engine* e) {
+    const auto& c = e->cfg;
+    const int E = c.n_embd;
+    ENG_TRY(step_init());
+    std::vector<StepPhase> ph;
+    StepPhase embed = {};
+    embed.kind = PH_EMBED;
+    ph.push_back(embed);
+    for (int l = 0; l < c.n_layer; ++l) {
+        const LayerW& L = e->layers[l];
+        StepPhase q = {};
+        q.kind = PH_GEMV;
+        q.g = base_params(e, E);
+        q.g.seg[0] = seg_of(L.wq, e->q, L.bq);
+        q.g.seg[1] = seg_of(L.wk, e->k, L.bk);
+        q.g.seg[2] = seg_of(L.wv, e->v, L.bv);
+        q.g.nseg = 3;
+        q.g.xq = e->xq_a;
+        q.g.xq_norm = 1;
+        q.g.epi = EPI_STORE;
+        gemv_configure(q.g, e->sms);
+        ph.push_back(q);
+
+        StepPhase at = {};
+        at.kind = PH_ATTN;
+        AttnParams& a = at.a;
+        a.q = e->q;
+        a.k = e->k;
+        a.v = e->v;
+        const size_t lsz = (size_t)c.n_ctx * e->KVl * e->hd;
+        a.kc = e->kcache + (size_t)l * lsz;
+        a.vc = e->vcache + (size_t)l * lsz;
+        a.out = e->attn;
+        a.cos_t = e->cos_t;
+        a.sin_t = e->sin_t;
+        a.q_norm = L.q_norm;
+        a.k_norm = L.k_norm;
+        a.part = e->apart;
+        a.counter = e->acount;
+        a.pos = &e->tokpos[1];
+        a.n_heads = e->Hl;
+        a.n_kv_heads = e->KVl;
+        a.head_dim = e->hd;
+        a.n_ctx = c.n_ctx;
+        a.nsplit = std::max(1, std::min(e->nsplit, e->sms / e->KVl));
+        a.qk_norm_order = c.qk_norm_order;
+        a.eps = c.eps;
+        a.scale = 1.f / std::sqrt((float)e->hd);
+        a.xq_out = e->xq_o;
+        ph.push_back(at);
+
+        StepPhase o = {};
+        o.kind = PH_GEMV;
+        o.g = base_params(e, e->Hl * e->hd);
+        o.g.seg[0] = seg_of(L.wo, e->ypart, nullptr);
+        o.g.nseg = 1;
+        o.g.epi = EPI_RESID;
+        o.g.resid = e->x[0];
+        o.g.xq = e->xq_o;
+        o.g.q_out = e->xq_gu;
+        o.g.q_norm_w = L.ffn_norm;
+        o.g.q_cnt = e->cnt_e;
+        gemv_configure(o.g, e->sms);
+        ph.push_back(o);
+
+        StepPhase gu = {};
+        gu.kind = PH_GEMV;
+        gu.g = base_params(e, E);
+        gu.g.seg[0] = seg_of(L.wg, e->h, nullptr);
+        gu.g.seg[1] = seg_of(L.wu, nullptr, nullptr);
+        gu.g.nseg = 2;
+        gu.g.epi = EPI_SWIGLU;
+        gu.g.xq = e->xq_gu;
+        gu.g.xq_norm = 1;
+        gu.g.q_out = e->xq_d;
+        gu.g.q_cnt = e->cnt_f;
+        gemv_configure(gu.g, e->sms);
+        ph.push_back(gu);
+
+        StepPhase d = {};
+        d.kind = PH_GEMV;
+        d.g = base_params(e, e->Fl);
+        d.g.seg[0] = seg_of(L.wd, e->ypart, nullptr);
+        d.g.nseg = 1;
+        d.g.epi = EPI_RESID;
+        d.g.resid = e->x[0];
+        d.g.xq = e->xq_d;
+        d.g.q_out = e->xq_a;
+        d.g.q_norm_w = l + 1 < c.n_layer ? e->layers[l + 1].attn_norm : e->out_norm;
+        d.g.q_cnt = e->cnt_e;
+        gemv_configure(d.g, e->sms);
+        ph.push_back(d);
+    }
+    StepPhase lm = {};
+    lm.kind = PH_GEMV;
+    lm.g = base_params(e, E);
+    lm.g.seg[0] = seg_of(e->output, e->logits, nullptr);
+    lm.g.nseg = 1;
+    lm.g.xq = e->xq_a;
+    lm.g.xq_norm = 1;
+    lm.g.epi = EPI_ARGMAX;
+    lm.g.argmax = e->key;
+    lm.g.argmax_base = e->V0;
+    gemv_configure(lm.g, e->sms);
+    ph.push_back(lm);
+
+    e->d_phases = static_cast<StepPhase*>(e->dalloc(ph.size() * sizeof(StepPhase)));
+    ENG_TRY(cudaMemcpyAsync(e->d_phases, ph.data(), ph.size() * sizeof(StepPhase), cudaMemcpyHostToDevice,
+                            e->stream));
+    ENG_TRY(cudaStreamSynchronize(e->stream));
+    e->step_bar = static_cast<unsigned int*>(e->dalloc(64));
+    StepParams& sp = e->step;
+    sp.ph = e->d_phases;
+    sp.nph = (int)ph.size();
+    sp.bar = e->step_bar;
+    sp.tok_w = e->tok_embd.w;
+    sp.tok_type = e->tok_embd.type;
+    sp.tok_stride = e->tok_embd.stride;
+    sp.n_embd = E;
+    sp.vocab = c.vocab;
+    sp.x = e->x[0];
+    sp.xq = e->xq_a;
+    sp.xq_norm_w = e->layers[0].attn_norm;
+    sp.key = e->key;
+    sp.token = &e->tokpos[0];
+    sp.pos = &e->tokpos[1];
+    sp.hist = e->hist;
+    sp.ring_bytes = kStepSmem - kStepHdr - kStepUnion;
+    return cudaSuccess;
 }
 
 cudaError_t gather_logits(af_engine* e, float* h_logits) {
@@ -683,6 +828,10 @@ cudaError_t af_engine_finalize(af_engine* e) {
         ENG_TRY(cudaMallocHost(&e->h_tokpos, 16));
         ENG_TRY(gemv_init());
         ENG_TRY(attention_init());
+        const char* sv = std::getenv("AF_STEP_KERNEL");
+        e->use_step = e->tp == 1 && (!sv || std::atoi(sv) != 0) &&
+                      step_supported(e->Hl, e->KVl, e->hd, c.n_embd, e->Fl);
+        if (e->use_step) ENG_TRY(build_step(e));
         ENG_TRY(cudaDeviceSynchronize());
         // Capture one step into a graph.
         ENG_TRY(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));

@@ -8,31 +8,34 @@
 // Design (HBM-bound; one launch streams each weight byte exactly once):
 //  * Weights are "packed" once at upload (af_weight_pack): 16-row tiles, each
 //    holding stage after stage the rows' segments of 8 super-blocks, so one
-//    pipeline stage of up to 30 rows is a few contiguous bulk copies.
+//    pipeline entry (a fragment of up to 30 rows × one stage) is a few
+//    contiguous bulk copies.
 //  * Grid = one CTA per SM.  Each CTA owns a byte-balanced contiguous range of
 //    output rows (computed on the host) and walks it in fragments of up to 30
 //    rows (15 gate/up pairs for SwiGLU), two fragments per K stage.
-//  * Warp 15 is the producer: it streams every (fragment, K stage) into a ring
-//    of shared-memory slots with cp.async.bulk (the TMA engine, no tensor map,
-//    no multicast), completion counted on an mbarrier, L2 evict-first.  The
-//    first ring-full is issued before griddepcontrol.wait.
-//  * The input vector arrives already quantised in the shared-memory layout
-//    ("XQ": x ≈ xs·(256·hi + lo) per 64 values as two int8 planes, per-32 f32
-//    sums, per-16 integer sums, and for a normalised input the per-64 sums of
-//    squares): the producer copies it with one bulk copy after
-//    griddepcontrol.wait.  The kernel that produced the vector quantised each
-//    64-value group once (the last CTA to finish a group does it), so no CTA
-//    re-reads and re-quantises the whole input.  A legacy in-CTA prologue
-//    quantises an f32 input for the standalone entry points and tensor
-//    parallel ranks.
+//  * Warp 15 is the producer: one thread streams every (fragment, K stage)
+//    entry into a byte ring in shared memory with cp.async.bulk (the TMA
+//    engine, no tensor map, no multicast), completion counted on an mbarrier,
+//    L2 evict-first.  Weights do not depend on the previous kernel, so the
+//    producer never waits for it (griddepcontrol.wait is the consumers' only).
+//  * The input vector arrives already quantised ("XQ": x ≈ xs·(256·hi + lo)
+//    per 64 values as two int8 planes, per-32 f32 sums, per-16 integer sums,
+//    and for a normalised input the per-64 sums of squares); the consumers
+//    copy it into shared memory with L2 loads.  The kernel that produced the
+//    vector quantised each 64-value group once (the last CTA to finish a group
+//    does it), so no CTA re-reads and re-quantises the whole input.  A legacy
+//    in-CTA prologue quantises an f32 input for the standalone entry points
+//    and tensor-parallel ranks.
 //  * Warps 0-14 are consumers: lane = (super-block, 64-value chunk) of the
-//    stage; each warp evaluates four rows (two per fragment) with exact integer dp4a dots
-//    Σ q·(256·hi + lo) and applies the block scales in f32 — the same
-//    w = d·sc·q − dmin·m (Q4_K) and w = d·sc·(q − 32) (Q6_K) the reference
-//    dequantises, accumulated in fp32.
+//    stage; each warp evaluates four rows (two per fragment) with exact integer
+//    dp4a dots Σ q·(256·hi + lo) and applies the block scales in f32 — the
+//    same w = d·sc·q − dmin·m (Q4_K) and w = d·sc·(q − 32) (Q6_K) the
+//    reference dequantises, accumulated in fp32.
 //  * Epilogues: plain store (+bias), in-place residual add, SwiGLU of a
 //    gate/up row pair, LM-head logits with a fused first-max argmax; optionally
 //    the output vector is quantised into the next GEMV's XQ buffer.
+//  * The same building blocks (af_gemv_dev.cuh) run inside the persistent
+//    decode-step kernel (af_step.cu), where the ring persists across phases.
 #pragma once
 #include "af_common.cuh"
 
@@ -46,7 +49,7 @@ constexpr int kGemvConsumerWarps = 15;
 constexpr int kGemvThreads = (kGemvConsumerWarps + 1) * 32;
 constexpr int kPackTile = 16;        // rows per tile of the packed weight layout
 constexpr int kGemvFragRows = 2 * kGemvConsumerWarps;  // rows per pipeline stage
-constexpr int kGemvMaxSlots = 6;
+constexpr int kGemvSmemHdr = 1024;  // mbarriers, abort flag, group list
 constexpr int kGemvMaxK = 12288;     // input length held in registers by the legacy prologue
 constexpr int kGemvMaxGrid = 296;
 
@@ -82,8 +85,7 @@ struct GemvParams {
     uint8_t* q_out;
     const float* q_norm_w;
     unsigned int* q_cnt;   // per-64-row-group arrival counters, zero between launches
-    int pitch;             // max bytes of one row's stage segment
-    int nslots;            // ring depth
+    int ring_bytes;        // weight ring in shared memory (multiple of 16)
     int grid;
     int vrange[kGemvMaxGrid + 1];  // CTA i owns virtual rows [vrange[i], vrange[i+1])
 };
@@ -108,15 +110,15 @@ __host__ __device__ inline size_t packed_bytes(int type, int rows, int cols) {
 __host__ __device__ inline int xq_bytes(int K) { return ((K / 256 + 7) / 8) * 4992; }
 __host__ __device__ inline int xq_norm_bytes(int K) { return xq_bytes(K) + K / 16; }
 
-// Shared-memory bytes the GEMV needs.
-__host__ __device__ inline int gemv_smem_bytes(int K, int pitch, int nslots) {
-    return 256 + nslots * kGemvFragRows * pitch + xq_norm_bytes(K) + 256;
+// Shared-memory bytes of the standalone GEMV: header, ring, XQ input, misc.
+__host__ __device__ inline int gemv_smem_bytes(int K, int ring_bytes) {
+    return kGemvSmemHdr + ring_bytes + xq_norm_bytes(K) + 256;
 }
 
 // Per-device kernel attributes; call once per device before launching (and
 // before any stream capture).
 cudaError_t gemv_init();
-// Fill pitch / nslots / grid / CTA ranges for the segments in p.
+// Fill ring size / grid / CTA ranges for the segments in p.
 void gemv_configure(GemvParams& p, int grid);
 cudaError_t gemv_launch(const GemvParams& p, cudaStream_t stream, bool pdl);
 
@@ -127,5 +129,7 @@ cudaError_t xq_quantize_launch(uint8_t* xq, const float* x, const float* norm_w,
 // One warp quantises 64-value group g of src (global f32) into the XQ buffer;
 // with norm_w, w·x is quantised and Σx² stored after the layout.
 __device__ void xq_quantize_group(uint8_t* xq, const float* src, const float* norm_w, int K, int g);
+// Same, from values already in registers: lane l holds group values 2l, 2l+1.
+__device__ void xq_quantize_vals(uint8_t* xq, float a0, float a1, const float* norm_w, int K, int g);
 
 }  // namespace af

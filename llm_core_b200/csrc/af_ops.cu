@@ -32,15 +32,6 @@ int num_sms() {
 
 // ------------------------------------------------------- packed weight layout
 
-// Byte offset of (row, stage st) in the packed layout (see af_gemv.cuh).
-__host__ __device__ inline size_t packed_off(int type, int nb, int row_stride, int row, int st) {
-    const int nbs = min(8, nb - st * 8);
-    const int seg = type == AF_GGML_Q6_K ? nbs * 208 + 16 : nbs * 144;
-    const int full = type == AF_GGML_Q6_K ? 1680 : 1152;
-    return (size_t)(row / kPackTile) * kPackTile * row_stride + (size_t)kPackTile * st * full +
-           (size_t)(row % kPackTile) * seg;
-}
-
 // One CTA per row; GGUF block j of the row goes to stage j/8, slot j%8 of that
 // stage's row segment (Q6_K: ql/qh/scales first, the f16 d values after the
 // segment's blocks).  `unpack` runs the same byte map backwards.
@@ -85,41 +76,7 @@ __global__ void embed_kernel(float* __restrict__ x, const uint8_t* __restrict__ 
     if (argmax && blockIdx.x == 0 && threadIdx.x == 0) *argmax = 0ull;
     const int nb = cols / 256;
     for (int v = blockIdx.x * blockDim.x + threadIdx.x; v < cols; v += gridDim.x * blockDim.x) {
-        const int b = v >> 8, w = v & 255;
-        float out;
-        const int tok = *token;
-        const int st = b >> 3, k = b & 7, nbs = min(8, nb - st * 8);
-        const uint8_t* seg = W + packed_off(type, nb, row_stride, tok, st);
-        if (type == AF_GGML_Q6_K) {
-            const uint8_t* blk = seg + k * 208;
-            const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(seg + nbs * 208 + 2 * k));
-            const int n = w >> 7, r = w & 127, s = r >> 5, l = r & 31;
-            const uint8_t* ql = blk + 64 * n;
-            const uint8_t* qh = blk + 128 + 32 * n;
-            const int8_t* sc = reinterpret_cast<const int8_t*>(blk + 192 + 8 * n);
-            const int qlb = (s & 1) ? ql[l + 32] : ql[l];
-            const int nib = (s & 2) ? (qlb >> 4) : (qlb & 0xF);
-            const int q = (nib | (((qh[l] >> (2 * s)) & 3) << 4)) - 32;
-            out = d * sc[(l >> 4) + 2 * s] * q;
-        } else {
-            const uint8_t* blk = seg + k * 144;
-            const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(blk));
-            const float dmin = half_bits_to_float(*reinterpret_cast<const uint16_t*>(blk + 2));
-            const uint8_t* sc = blk + 4;
-            const int chunk = w >> 6, r = w & 63, j = chunk * 2 + (r >> 5), l = r & 31;
-            int s, m;
-            if (j < 4) {
-                s = sc[j] & 63;
-                m = sc[j + 4] & 63;
-            } else {
-                s = (sc[j + 4] & 0xF) | ((sc[j - 4] >> 6) << 4);
-                m = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
-            }
-            const int qb = blk[16 + chunk * 32 + l];
-            const int q = (r < 32) ? (qb & 0xF) : (qb >> 4);
-            out = (d * s) * q - dmin * m;
-        }
-        x[v] = out;
+        x[v] = embed_value(W, type, nb, row_stride, *token, v);
     }
     if (xq) {
         // quantise this block's 64-value groups for the first GEMV

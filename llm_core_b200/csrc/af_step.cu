@@ -1,0 +1,473 @@
+// af_step.cu — persistent decode-step kernel (see af_step.cuh for the design).
+#include <cstddef>
+
+#include "af_gemv_dev.cuh"
+#include "af_step.cuh"
+
+namespace af {
+namespace {
+
+using namespace gdev;
+
+constexpr int kParamOff = 1024;  // shared copies of the current phase's parameters
+static_assert(offsetof(GemvParams, vrange) <= 448, "GemvParams head must fit its shared-memory slot");
+static_assert(sizeof(AttnParams) <= 512, "AttnParams must fit its shared-memory slot");
+static_assert(kParamOff + 448 + 64 + sizeof(AttnParams) <= kStepHdr, "step header overflow");
+
+// Spin limit of the grid-wide waits (each iteration sleeps ~0.1 µs or more).
+constexpr uint32_t kGridSpinLimit = 1u << 24;
+
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ unsigned atom_add_acq_rel(unsigned* p, unsigned v) {
+    unsigned old;
+    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
+// Consumer threads: wait until every CTA has arrived `target` times in total.
+// Thread 0 spins (bounded) and the consumer barrier publishes the result.
+__device__ bool grid_wait(const unsigned* bar, unsigned target, volatile int* flags) {
+    if (threadIdx.x == 0) {
+        bool ok = false;
+        for (uint32_t i = 0; i < kGridSpinLimit; ++i) {
+            if (ld_acquire(bar) >= target) {
+                ok = true;
+                break;
+            }
+            if (flags[0]) break;
+            __nanosleep(64);
+        }
+        if (!ok) {
+            if (!flags[0]) set_err(kErrMbarTimeout);
+            flags[0] = 1;
+        }
+    }
+    bar_consumers();
+    return flags[0] == 0;
+}
+
+// Copy `bytes` (multiple of 4) of a parameter block into shared memory.
+__device__ __forceinline__ void copy_params(void* dst, const void* src, int bytes) {
+    for (int i = threadIdx.x; i < bytes / 4; i += kCT)
+        reinterpret_cast<int*>(dst)[i] = __ldg(reinterpret_cast<const int*>(src) + i);
+    bar_consumers();
+}
+
+// ------------------------------------------------------------------ embedding
+
+// x = dequant(row token of the embedding) and its quantised, attn_norm-
+// weighted form for the first QKV GEMV: one warp per 64-value group.
+__device__ void embed_phase(const StepParams& sp, int tok) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (blockIdx.x == 0 && threadIdx.x == 0) *sp.key = 0ull;  // argmax of this step starts empty
+    if (tok < 0 || tok >= sp.vocab) {  // never index outside the table
+        if (blockIdx.x == 0 && threadIdx.x == 0) set_err(kErrBadToken);
+        tok = 0;
+    }
+    const int nb = sp.n_embd / 256, ng = sp.n_embd / 64;
+    for (int g = blockIdx.x * kCW + warp; g < ng; g += gridDim.x * kCW) {
+        const int v0 = 64 * g + 2 * lane;
+        const float a0 = embed_value(sp.tok_w, sp.tok_type, nb, sp.tok_stride, tok, v0);
+        const float a1 = embed_value(sp.tok_w, sp.tok_type, nb, sp.tok_stride, tok, v0 + 1);
+        sp.x[v0] = a0;
+        sp.x[v0 + 1] = a1;
+        xq_quantize_vals(sp.xq, a0, a1, sp.xq_norm_w, sp.n_embd, g);
+    }
+}
+
+// ------------------------------------------------------------------ attention
+
+// Shared scratch of one attention item (floats), inside the union area.
+struct AttnSmem {
+    float* qs;    // [G][hd]
+    float* ks;    // [hd]
+    float* vs;    // [hd]
+    float* kt;    // [tile][hd]
+    float* vt;    // [tile][hd]
+    float* sc;    // [G][tile]
+    float* mrow;  // [G]
+    float* lrow;  // [G]
+    float* corr;  // [G]
+    int* last;
+    __device__ explicit AttnSmem(uint8_t* base) {
+        qs = reinterpret_cast<float*>(base);
+        ks = qs + kStepMaxG * 128;
+        vs = ks + 128;
+        kt = vs + 128;
+        vt = kt + kStepAttnTile * 128;
+        sc = vt + kStepAttnTile * 128;
+        mrow = sc + kStepMaxG * kStepAttnTile;
+        lrow = mrow + kStepMaxG;
+        corr = lrow + kStepMaxG;
+        last = reinterpret_cast<int*>(corr + kStepMaxG);
+    }
+};
+static_assert((kStepMaxG * 128 + 256 + 2 * kStepAttnTile * 128 + kStepMaxG * kStepAttnTile + 3 * kStepMaxG + 4) * 4 <=
+                  kStepUnion,
+              "attention scratch exceeds the union area");
+
+// Splits of each kv head's positions for this step: about one tile per split,
+// at most the configured maximum (the partial buffer's depth).
+__device__ __forceinline__ int attn_splits(const AttnParams& a, int pos) {
+    const int s = (pos + 1 + kStepAttnTile - 1) / kStepAttnTile;
+    return max(1, min(a.nsplit, s));
+}
+
+// One warp RMS-normalises one head in shared memory (qwen3 / hunyuan Q/K norm,
+// rms_norm_out of src/models/llama_model.cpp:393-419 over hd values).
+__device__ __forceinline__ void rms_norm_head(float* x, const float* w, int hd, float eps) {
+    const int lane = threadIdx.x & 31;
+    float ss = 0.f;
+    for (int i = lane; i < hd; i += 32) ss += x[i] * x[i];
+    ss = warp_sum(ss);
+    const float s = 1.f / sqrtf(ss / (float)hd + eps);
+    __syncwarp();
+    for (int i = lane; i < hd; i += 32) x[i] = w[i] * (x[i] * s);
+    __syncwarp();
+}
+
+// Issue cp.async loads of tile positions [p0, p0 + n) ∩ [0, pos) of one kv head
+// (rows older than the new token: they do not depend on this step's QKV).
+__device__ __forceinline__ void attn_tile_prefetch(const AttnParams& a, const AttnSmem& s, int kvh, int p0, int n,
+                                                   int pos) {
+    const int hd = a.head_dim, Q4 = hd / 4, kvd = a.n_kv_heads * hd;
+    for (int idx = threadIdx.x; idx < n * Q4; idx += kCT) {
+        const int j = idx / Q4, c = idx % Q4, p = p0 + j;
+        if (p >= pos) continue;
+        const size_t off = (size_t)p * kvd + (size_t)kvh * hd + 4 * c;
+        const uint32_t dk = smem_u32(s.kt + j * hd + 4 * c), dv = smem_u32(s.vt + j * hd + 4 * c);
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dk), "l"(a.kc + off) : "memory");
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dv), "l"(a.vc + off) : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Range of positions of split `split` of `ns` for sequence length seq.
+__device__ __forceinline__ void attn_range(int seq, int ns, int split, int& t0, int& t1) {
+    const int chunk = (seq + ns - 1) / ns;
+    t0 = min(seq, split * chunk);
+    t1 = min(seq, t0 + chunk);
+}
+
+// One (kv head, split) item: llama_forward_token's attention
+// (src/models/llama_model.cpp:1236-1272) for the G query heads of kv head kvh
+// over positions [t0, t1), as an online softmax over tiles of 32 positions;
+// the un-normalised partial (o, max, sum) goes to a.part and the last split
+// of the kv head to finish merges them and quantises the output for the O
+// GEMV.  `prefetched`: tile 0 rows older than pos were already requested.
+__device__ void attn_item(const AttnParams& a, const AttnSmem& s, int pos, int kvh, int split, int ns,
+                          bool prefetched) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int hd = a.head_dim, half = hd / 2, Q4 = hd / 4;
+    const int G = a.n_heads / a.n_kv_heads;
+    const int kvd = a.n_kv_heads * hd;
+    const int seq = pos + 1;
+    int t0, t1;
+    attn_range(seq, ns, split, t0, t1);
+
+    // ---- q (G heads), k, v of the new token (written by the QKV phase)
+    for (int i = tid; i < G * hd; i += kCT) s.qs[i] = __ldcg(a.q + (size_t)kvh * G * hd + i);
+    for (int i = tid; i < hd; i += kCT) {
+        s.ks[i] = __ldcg(a.k + (size_t)kvh * hd + i);
+        s.vs[i] = __ldcg(a.v + (size_t)kvh * hd + i);
+    }
+    if (tid < kStepMaxG) {
+        s.mrow[tid] = -INFINITY;
+        s.lrow[tid] = 0.f;
+    }
+    bar_consumers();
+    if (a.qk_norm_order == 1) {  // qwen3: per-head norm before RoPE
+        if (warp < G && a.q_norm) rms_norm_head(s.qs + warp * hd, a.q_norm, hd, a.eps);
+        if (warp == G && a.k_norm) rms_norm_head(s.ks, a.k_norm, hd, a.eps);
+        bar_consumers();
+    }
+    // RoPE, half-split pairs (i, i + hd/2) (apply_rope, llama_model.cpp:1046-1080)
+    const float* cr = a.cos_t + (size_t)pos * half;
+    const float* sr = a.sin_t + (size_t)pos * half;
+    for (int idx = tid; idx < (G + 1) * half; idx += kCT) {
+        const int g = idx / half, i = idx % half;
+        float* hp = g < G ? s.qs + g * hd : s.ks;
+        const float x0 = hp[i], x1 = hp[i + half];
+        const float c = __ldg(cr + i), sn = __ldg(sr + i);
+        hp[i] = x0 * c - x1 * sn;
+        hp[i + half] = x0 * sn + x1 * c;
+    }
+    bar_consumers();
+    if (a.qk_norm_order == 2) {  // hunyuan: per-head norm after RoPE
+        if (warp < G && a.q_norm) rms_norm_head(s.qs + warp * hd, a.q_norm, hd, a.eps);
+        if (warp == G && a.k_norm) rms_norm_head(s.ks, a.k_norm, hd, a.eps);
+        bar_consumers();
+    }
+    if (split == 0) {
+        for (int i = tid; i < hd; i += kCT) {
+            a.kc[(size_t)pos * kvd + (size_t)kvh * hd + i] = s.ks[i];
+            a.vc[(size_t)pos * kvd + (size_t)kvh * hd + i] = s.vs[i];
+        }
+    }
+
+    // ---- tiles
+    const int npg = kCT / Q4;  // position groups of the P·V product
+    const int d4 = tid % Q4, pg = tid / Q4;
+    float4 o[kStepMaxG];
+#pragma unroll
+    for (int g = 0; g < kStepMaxG; ++g) o[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int p0 = t0; p0 < t1; p0 += kStepAttnTile) {
+        const int n = min(kStepAttnTile, t1 - p0);
+        if (!(prefetched && p0 == t0)) attn_tile_prefetch(a, s, kvh, p0, n, pos);
+        // the new token's row comes from shared memory, not the cache
+        if (pos >= p0 && pos < p0 + n) {
+            const int j = pos - p0;
+            for (int i = tid; i < hd; i += kCT) {
+                s.kt[j * hd + i] = s.ks[i];
+                s.vt[j * hd + i] = s.vs[i];
+            }
+        }
+        cp_async_wait_all();
+        bar_consumers();
+        // scores: warp per position, lanes over the head dims
+        for (int j = warp; j < n; j += kCW) {
+            for (int g = 0; g < G; ++g) {
+                float dot = 0.f;
+                for (int i = lane; i < hd; i += 32) dot = fmaf(s.qs[g * hd + i], s.kt[j * hd + i], dot);
+                dot = warp_sum(dot);
+                if (lane == 0) s.sc[g * kStepAttnTile + j] = dot * a.scale;
+            }
+        }
+        bar_consumers();
+        // online softmax update, warp per head (max-subtracted exp, llama_model.cpp:445-451)
+        if (warp < G) {
+            const float v = lane < n ? s.sc[warp * kStepAttnTile + lane] : -INFINITY;
+            const float mt = warp_max(v);
+            const float m_old = s.mrow[warp];
+            const float m_new = fmaxf(m_old, mt);
+            const float e = lane < n ? expf(v - m_new) : 0.f;
+            s.sc[warp * kStepAttnTile + lane] = e;
+            const float l = warp_sum(e);
+            if (lane == 0) {
+                const float c = expf(m_old - m_new);  // 0 on the first tile (m_old = -inf)
+                s.corr[warp] = c;
+                s.lrow[warp] = s.lrow[warp] * c + l;
+                s.mrow[warp] = m_new;
+            }
+        }
+        bar_consumers();
+        if (pg < npg) {
+#pragma unroll
+            for (int g = 0; g < kStepMaxG; ++g) {
+                if (g >= G) break;
+                const float c = s.corr[g];
+                o[g].x *= c;
+                o[g].y *= c;
+                o[g].z *= c;
+                o[g].w *= c;
+                for (int j = pg; j < n; j += npg) {
+                    const float e = s.sc[g * kStepAttnTile + j];
+                    const float4 v = reinterpret_cast<const float4*>(s.vt + j * hd)[d4];
+                    o[g].x = fmaf(e, v.x, o[g].x);
+                    o[g].y = fmaf(e, v.y, o[g].y);
+                    o[g].z = fmaf(e, v.z, o[g].z);
+                    o[g].w = fmaf(e, v.w, o[g].w);
+                }
+            }
+        }
+        bar_consumers();
+    }
+    // ---- reduce the position groups, write this split's partial
+    float* red = s.kt;  // [npg][hd]
+#pragma unroll
+    for (int g = 0; g < kStepMaxG; ++g) {
+        if (g >= G) break;
+        if (pg < npg) reinterpret_cast<float4*>(red + pg * hd)[d4] = o[g];
+        bar_consumers();
+        const int h = kvh * G + g;
+        float* dst = a.part + ((size_t)h * a.nsplit + split) * (hd + 2);
+        for (int d = tid; d < hd; d += kCT) {
+            float acc = 0.f;
+            for (int q = 0; q < npg; ++q) acc += red[q * hd + d];
+            dst[d] = acc;
+            if (d == 0) {
+                dst[hd] = s.mrow[g];
+                dst[hd + 1] = s.lrow[g];
+            }
+        }
+        bar_consumers();
+    }
+    // ---- the last split of this kv head merges (exp(m_s − M) rescaling)
+    __threadfence();
+    bar_consumers();
+    if (tid == 0) *s.last = atomicAdd(&a.counter[kvh], 1u) == (unsigned)(ns - 1) ? 1 : 0;
+    bar_consumers();
+    if (!*s.last) return;
+    __threadfence();
+    for (int idx = tid; idx < G * hd; idx += kCT) {
+        const int g = idx / hd, dd = idx % hd;
+        const int h = kvh * G + g;
+        const float* base = a.part + (size_t)h * a.nsplit * (hd + 2);
+        float M = -INFINITY;
+        for (int q = 0; q < ns; ++q) M = fmaxf(M, __ldcg(base + q * (hd + 2) + hd));
+        float L = 0.f, O = 0.f;
+        for (int q = 0; q < ns; ++q) {
+            const float ms = __ldcg(base + q * (hd + 2) + hd);
+            if (ms == -INFINITY) continue;
+            const float w = expf(ms - M);
+            L += __ldcg(base + q * (hd + 2) + hd + 1) * w;
+            O += __ldcg(base + q * (hd + 2) + dd) * w;
+        }
+        a.out[(size_t)h * hd + dd] = O / L;
+    }
+    if (tid == 0) a.counter[kvh] = 0u;
+    if (a.xq_out) {
+        // quantise this kv head's G*hd outputs (whole 64-value groups) for the O GEMV
+        __threadfence();
+        bar_consumers();
+        const int g0 = kvh * G * hd / 64, ng = G * hd / 64;
+        for (int k = warp; k < ng; k += kCW) xq_quantize_group(a.xq_out, a.out, nullptr, a.n_heads * hd, g0 + k);
+    }
+}
+
+// ------------------------------------------------------------------ kernel
+
+__global__ void __launch_bounds__(kGemvThreads, 1) step_kernel(const __grid_constant__ StepParams sp) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    Ring ring;
+    ring.full = reinterpret_cast<uint64_t*>(smem);
+    ring.empty = ring.full + kRingDesc;
+    int* flags = reinterpret_cast<int*>(smem + 256);  // [0] abort, [1..] group list
+    GemvParams* gp = reinterpret_cast<GemvParams*>(smem + kParamOff);
+    AttnParams* ap = reinterpret_cast<AttnParams*>(smem + kParamOff + 512);
+    uint8_t* uni = smem + kStepHdr;
+    ring.buf = uni + kStepUnion;
+    ring.bytes = sp.ring_bytes;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kRingDesc; ++i) {
+            mbar_init(&ring.full[i], 1);
+            mbar_init(&ring.empty[i], kCW);
+        }
+        flags[0] = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    volatile int* abort = flags;
+
+    if (warp == kCW) {
+        // ---- producer: the weights of every GEMV phase, in order
+        if (lane != 0) return;
+        Producer pr;
+        const uint64_t pol = policy_evict_first();
+        for (int i = 0; i < sp.nph; ++i) {
+            const StepPhase& ph = sp.ph[i];
+            if (ph.kind != PH_GEMV) continue;
+            const int vbeg = ph.g.vrange[blockIdx.x], vend = ph.g.vrange[blockIdx.x + 1];
+            if (!pr.produce(ph.g, vbeg, vend, ring, abort, pol)) {
+                *abort = 1;
+                pr.drain(ring);
+                return;
+            }
+        }
+        return;
+    }
+
+    // ---- consumers: the phases, separated by grid-wide arrivals
+    const int pos = __ldcg(sp.pos);
+    const int tok = __ldcg(sp.token);
+    uint32_t consumed = 0;
+    int head = 0;
+    int next_attn = -1;  // phase index whose tile 0 was prefetched
+    const unsigned grid = gridDim.x;
+    for (int i = 0; i < sp.nph; ++i) {
+        const StepPhase& ph = sp.ph[i];
+        const int kind = ph.kind;
+        if (kind == PH_ATTN) {
+            // KV rows older than the new token do not depend on the QKV phase:
+            // request this CTA's first tile before waiting for it.
+            copy_params(ap, &ph.a, sizeof(AttnParams));
+            const int ns = attn_splits(*ap, pos);
+            if ((int)blockIdx.x < ap->n_kv_heads * ns && ap->head_dim <= 128) {
+                const int item = blockIdx.x, kvh = item / ns, split = item % ns;
+                int t0, t1;
+                attn_range(pos + 1, ns, split, t0, t1);
+                if (t1 > t0) attn_tile_prefetch(*ap, AttnSmem(uni), kvh, t0, min(kStepAttnTile, t1 - t0), pos);
+                next_attn = i;
+            }
+        }
+        if (i > 0 && !grid_wait(sp.bar, (unsigned)i * grid, abort)) break;
+        if (kind == PH_EMBED) {
+            embed_phase(sp, tok);
+        } else if (kind == PH_GEMV) {
+            copy_params(gp, &ph.g, offsetof(GemvParams, vrange));
+            const int vbeg = ph.g.vrange[blockIdx.x], vend = ph.g.vrange[blockIdx.x + 1];
+            const float s_in = load_xq(*gp, uni);
+            if (!consume(*gp, vbeg, vend, ring, consumed, head, uni, s_in, abort)) {
+                *abort = 1;
+                break;
+            }
+            if (gp->q_out) quantise_output(*gp, vbeg, vend, flags + 1);
+        } else {
+            const AttnParams& a = *ap;
+            const AttnSmem s(uni);
+            const int ns = attn_splits(a, pos);
+            const int items = a.n_kv_heads * ns;
+            for (int item = blockIdx.x; item < items; item += gridDim.x) {
+                attn_item(a, s, pos, item / ns, item % ns, ns, next_attn == i && item == (int)blockIdx.x);
+                bar_consumers();
+            }
+            cp_async_wait_all();  // a prefetch whose item did not run (none in practice)
+        }
+        // arrive: every store of this phase by this CTA happens before the count
+        bar_consumers();
+        if (threadIdx.x == 0) {
+            __threadfence();
+            const unsigned old = atom_add_acq_rel(sp.bar, 1u);
+            if (i == sp.nph - 1 && old == (unsigned)sp.nph * grid - 1u) {
+                // last arrival of the step: argmax key -> next token, pos + 1
+                const unsigned long long k = __ldcg(sp.key);
+                int id = (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
+                if (k == 0ull || id < 0 || id >= sp.vocab) {  // no finite logit reached the argmax
+                    set_err(kErrBadToken);
+                    id = 0;
+                }
+                *sp.token = id;
+                if (sp.hist) sp.hist[pos] = id;
+                *sp.pos = pos + 1;
+            }
+        }
+    }
+}
+
+}  // namespace
+
+bool step_supported(int n_heads, int n_kv_heads, int head_dim, int n_embd, int ffn) {
+    const int G = n_kv_heads > 0 ? n_heads / n_kv_heads : 0;
+    return G >= 1 && G <= kStepMaxG && (head_dim == 64 || head_dim == 128) && n_embd % 256 == 0 && ffn % 256 == 0 &&
+           xq_norm_bytes(n_embd) <= kStepUnion && xq_norm_bytes(ffn) <= kStepUnion && (G * head_dim) % 64 == 0;
+}
+
+cudaError_t step_init() {
+    return cudaFuncSetAttribute(step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kStepSmem);
+}
+
+cudaError_t step_launch(const StepParams& sp, cudaStream_t st) {
+    AF_CUDA_TRY(cudaMemsetAsync(sp.bar, 0, sizeof(unsigned int), st));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(num_sms());
+    cfg.blockDim = dim3(kGemvThreads);
+    cfg.dynamicSmemBytes = kStepSmem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, step_kernel, sp);
+}
+
+}  // namespace af

@@ -1,0 +1,62 @@
+// af_step.cuh — the persistent decode-step kernel: one launch per token.
+//
+// The separate-kernel step (embed, 5 kernels per layer, LM head, finalize)
+// pays a kernel boundary per phase: the last CTA's tail, the grid drain and
+// the next kernel's ramp, during which HBM idles.  Here one cooperative grid
+// (one CTA per SM) runs every phase of the step.  The producer thread of each
+// CTA streams the weight rows that CTA owns for ALL GEMV phases in order,
+// limited only by the ring in shared memory, so weight streaming never waits
+// for a phase boundary; the consumer warps wait for the previous phase on a
+// grid-wide arrival counter (bounded spin) and then run the phase:
+//
+//   EMBED  token row dequant → x, quantised (attn_norm) input of QKV
+//   GEMV   QKV(+bias) | O(+resid) | gate/up SwiGLU | down(+resid) | LM head+argmax
+//   ATTN   RoPE, Q/K norm, KV store, split attention, quantised output
+//
+// and the CTA that completes the last phase turns the argmax into the next
+// token and advances the position.
+#pragma once
+#include "af_gemv.cuh"
+#include "af_ops.cuh"
+
+namespace af {
+
+enum StepPhaseKind : int { PH_EMBED = 0, PH_GEMV = 1, PH_ATTN = 2 };
+
+constexpr int kStepMaxG = 8;            // query heads per kv head
+constexpr int kStepAttnTile = 32;       // KV positions per attention tile
+constexpr int kStepHdr = 2048;          // mbarriers, flags, phase parameter copies
+constexpr int kStepUnion = 40 * 1024;   // XQ input of a GEMV phase / attention scratch
+constexpr int kStepSmem = 227 * 1024;
+
+struct StepPhase {
+    int kind;
+    GemvParams g;  // PH_GEMV
+    AttnParams a;  // PH_ATTN (nsplit = splits per kv head)
+};
+
+struct StepParams {
+    const StepPhase* ph;  // device array
+    int nph;
+    unsigned int* bar;    // grid arrival counter, zero at launch
+    // embedding
+    const uint8_t* tok_w;
+    int tok_type, tok_stride, n_embd, vocab;
+    float* x;
+    uint8_t* xq;
+    const float* xq_norm_w;
+    // finalize
+    unsigned long long* key;
+    int* token;
+    int* pos;
+    int* hist;
+    int ring_bytes;
+};
+
+// Whether a model shape runs on the step kernel (else: separate kernels).
+bool step_supported(int n_heads, int n_kv_heads, int head_dim, int n_embd, int ffn);
+cudaError_t step_init();
+// Zero the arrival counter and launch the cooperative step grid on `st`.
+cudaError_t step_launch(const StepParams& sp, cudaStream_t st);
+
+}  // namespace af
