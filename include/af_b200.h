@@ -51,14 +51,15 @@ cudaError_t af_device_error(int* h_code, int clear);
 /* ---------------------------------------------------------- weight layout */
 
 /* Bytes of one packed row of `cols` values (Q4_K: cols/256*144; Q6_K:
- * >= cols/256*210 by at most 14 bytes), 0 for unsupported arguments. */
+ * cols/256*210), 0 for unsupported arguments. */
 size_t af_row_stride(int ggml_type, int cols);
 /* Device bytes of a packed rows x cols matrix (whole 16-row tiles). */
 size_t af_weight_bytes(int ggml_type, int rows, int cols);
 
 /* Pack `rows` GGUF rows (d_src, contiguous GGUF bytes) of a Q4_K or Q6_K
  * matrix into the packed layout at d_dst (af_weight_bytes bytes).
- * Byte-preserving permutation; af_weight_unpack inverts it. */
+ * A bit-preserving permutation (Q4_K: of bytes; Q6_K: of the 6-bit values'
+ * nibble and 2-bit fields); af_weight_unpack inverts it. */
 cudaError_t af_weight_pack(void* d_dst, const void* d_src, int ggml_type, int rows, int cols,
                            cudaStream_t stream);
 cudaError_t af_weight_unpack(void* d_dst, const void* d_src, int ggml_type, int rows, int cols,

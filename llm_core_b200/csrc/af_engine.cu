@@ -430,8 +430,8 @@ cudaError_t build_step(af_engine* e) {
         q.g.seg[1] = seg_of(L.wk, e->k, L.bk);
         q.g.seg[2] = seg_of(L.wv, e->v, L.bv);
         q.g.nseg = 3;
-        q.g.xq = e->xq_a;
-        q.g.xq_norm = 1;
+        q.g.x = e->x[0];
+        q.g.norm_w = L.attn_norm;
         q.g.epi = EPI_STORE;
         gemv_configure(q.g, e->sms);
         ph.push_back(q);
@@ -461,7 +461,7 @@ cudaError_t build_step(af_engine* e) {
         a.qk_norm_order = c.qk_norm_order;
         a.eps = c.eps;
         a.scale = 1.f / std::sqrt((float)e->hd);
-        a.xq_out = e->xq_o;
+        a.xq_out = nullptr;
         ph.push_back(at);
 
         StepPhase o = {};
@@ -471,10 +471,7 @@ cudaError_t build_step(af_engine* e) {
         o.g.nseg = 1;
         o.g.epi = EPI_RESID;
         o.g.resid = e->x[0];
-        o.g.xq = e->xq_o;
-        o.g.q_out = e->xq_gu;
-        o.g.q_norm_w = L.ffn_norm;
-        o.g.q_cnt = e->cnt_e;
+        o.g.x = e->attn;
         gemv_configure(o.g, e->sms);
         ph.push_back(o);
 
@@ -485,10 +482,8 @@ cudaError_t build_step(af_engine* e) {
         gu.g.seg[1] = seg_of(L.wu, nullptr, nullptr);
         gu.g.nseg = 2;
         gu.g.epi = EPI_SWIGLU;
-        gu.g.xq = e->xq_gu;
-        gu.g.xq_norm = 1;
-        gu.g.q_out = e->xq_d;
-        gu.g.q_cnt = e->cnt_f;
+        gu.g.x = e->x[0];
+        gu.g.norm_w = L.ffn_norm;
         gemv_configure(gu.g, e->sms);
         ph.push_back(gu);
 
@@ -499,10 +494,7 @@ cudaError_t build_step(af_engine* e) {
         d.g.nseg = 1;
         d.g.epi = EPI_RESID;
         d.g.resid = e->x[0];
-        d.g.xq = e->xq_d;
-        d.g.q_out = e->xq_a;
-        d.g.q_norm_w = l + 1 < c.n_layer ? e->layers[l + 1].attn_norm : e->out_norm;
-        d.g.q_cnt = e->cnt_e;
+        d.g.x = e->h;
         gemv_configure(d.g, e->sms);
         ph.push_back(d);
     }
@@ -511,8 +503,8 @@ cudaError_t build_step(af_engine* e) {
     lm.g = base_params(e, E);
     lm.g.seg[0] = seg_of(e->output, e->logits, nullptr);
     lm.g.nseg = 1;
-    lm.g.xq = e->xq_a;
-    lm.g.xq_norm = 1;
+    lm.g.x = e->x[0];
+    lm.g.norm_w = e->out_norm;
     lm.g.epi = EPI_ARGMAX;
     lm.g.argmax = e->key;
     lm.g.argmax_base = e->V0;
@@ -534,8 +526,8 @@ cudaError_t build_step(af_engine* e) {
     sp.n_embd = E;
     sp.vocab = c.vocab;
     sp.x = e->x[0];
-    sp.xq = e->xq_a;
-    sp.xq_norm_w = e->layers[0].attn_norm;
+    sp.xq = nullptr;  // phases quantise their own f32 inputs
+    sp.xq_norm_w = nullptr;
     sp.key = e->key;
     sp.token = &e->tokpos[0];
     sp.pos = &e->tokpos[1];
@@ -773,6 +765,8 @@ cudaError_t af_engine_finalize(af_engine* e) {
             if (!L.attn_norm || !L.ffn_norm || !L.wq.present() || !L.wk.present() || !L.wv.present() ||
                 !L.wo.present() || !L.wg.present() || !L.wu.present() || !L.wd.present())
                 return fail("missing weights for layer " + std::to_string(l));
+            if (L.wg.type != L.wu.type)
+                return fail("layer " + std::to_string(l) + ": ffn_gate and ffn_up must share a quantisation type");
         }
         const int E = c.n_embd, hd = e->hd;
         e->x[0] = static_cast<float*>(e->dalloc((size_t)E * 4));

@@ -6,34 +6,37 @@
 // and its incorrect CUDA v1 kernel (src/backend/cuda/cuda_kernels.cu:71-109).
 //
 // Design (HBM-bound; one launch streams each weight byte exactly once):
-//  * Weights are "packed" once at upload (af_weight_pack): 16-row tiles, each
-//    holding stage after stage the rows' segments of 8 super-blocks, so one
-//    pipeline entry (a fragment of up to 30 rows × one stage) is a few
-//    contiguous bulk copies.
+//  * Weights are "packed" once at upload (af_weight_pack) into units of 16
+//    rows × one 256-value super-block, laid out in the register order of the
+//    tensor-core instruction mma.sync.m16n8k32 (u8 weights × s8 inputs, s32
+//    accumulators): every lane fetches its A fragments with 16-byte shared
+//    loads.  A tile (16 rows) is its units in K order, so a K stage of a tile
+//    is one contiguous bulk copy.
+//  * The input x is quantised per 64 values to a 16-bit grid
+//    x ≈ xs·(256·hi + lo) (two int8 planes).  Each mma multiplies 16 rows ×
+//    32 values of nibbles (or 6-bit values) by a block-diagonal B whose column
+//    pairs hold the hi / lo planes of one 32-value sub-block (Q4_K) or 16-value
+//    group (Q6_K), so the s32 accumulators come out as exact per-sub-block
+//    integer dots Σ q·hi, Σ q·lo — the granularity at which the block scales
+//    apply.  Scales are applied in f32 — the same w = d·sc·q − dmin·m (Q4_K)
+//    and w = d·sc·(q − 32) (Q6_K) the reference dequantises.
 //  * Grid = one CTA per SM.  Each CTA owns a byte-balanced contiguous range of
-//    output rows (computed on the host) and walks it in fragments of up to 30
-//    rows (15 gate/up pairs for SwiGLU), two fragments per K stage.
-//  * Warp 15 is the producer: one thread streams every (fragment, K stage)
+//    16-row tiles (computed on the host) and walks it in fragments of two
+//    tiles (SwiGLU: the gate and up tile of the same rows).
+//  * One producer thread streams every (fragment, 8-super-block K stage)
 //    entry into a byte ring in shared memory with cp.async.bulk (the TMA
 //    engine, no tensor map, no multicast), completion counted on an mbarrier,
 //    L2 evict-first.  Weights do not depend on the previous kernel, so the
-//    producer never waits for it (griddepcontrol.wait is the consumers' only).
-//  * The input vector arrives already quantised ("XQ": x ≈ xs·(256·hi + lo)
-//    per 64 values as two int8 planes, per-32 f32 sums, per-16 integer sums,
-//    and for a normalised input the per-64 sums of squares); the consumers
-//    copy it into shared memory with L2 loads.  The kernel that produced the
-//    vector quantised each 64-value group once (the last CTA to finish a group
-//    does it), so no CTA re-reads and re-quantises the whole input.  A legacy
-//    in-CTA prologue quantises an f32 input for the standalone entry points
-//    and tensor-parallel ranks.
-//  * Warps 0-14 are consumers: lane = (super-block, 64-value chunk) of the
-//    stage; each warp evaluates four rows (two per fragment) with exact integer
-//    dp4a dots Σ q·(256·hi + lo) and applies the block scales in f32 — the
-//    same w = d·sc·q − dmin·m (Q4_K) and w = d·sc·(q − 32) (Q6_K) the
-//    reference dequantises, accumulated in fp32.
-//  * Epilogues: plain store (+bias), in-place residual add, SwiGLU of a
-//    gate/up row pair, LM-head logits with a fused first-max argmax; optionally
-//    the output vector is quantised into the next GEMV's XQ buffer.
+//    producer never waits for it.
+//  * 8 consumer warps: warp w evaluates super-block w of every stage for both
+//    tiles of the fragment, accumulating per row in registers across stages;
+//    at the end of a fragment the 8 warps' row sums are added in a fixed
+//    order through shared memory (deterministic) and the epilogue runs: plain
+//    store (+bias), in-place residual add, SwiGLU of a gate/up pair, LM-head
+//    logits with a fused first-max argmax.
+//  * The input arrives either as an f32 vector the consumers quantise in
+//    shared memory (RMSNorm folded in), or already quantised ("XQ") by the
+//    kernel that produced it.
 //  * The same building blocks (af_gemv_dev.cuh) run inside the persistent
 //    decode-step kernel (af_step.cu), where the ring persists across phases.
 #pragma once
@@ -43,15 +46,33 @@ namespace af {
 
 enum GemvEpi : int { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_RESID = 2, EPI_ARGMAX = 3 };
 
-// 15 consumer warps + 1 producer = 16 warps: 4 per SM sub-partition, so each
-// thread may use 128 registers (the register file is split across the 4).
-constexpr int kGemvConsumerWarps = 15;
+// 8 consumer warps + 1 producer warp.
+constexpr int kGemvConsumerWarps = 8;
 constexpr int kGemvThreads = (kGemvConsumerWarps + 1) * 32;
 constexpr int kPackTile = 16;        // rows per tile of the packed weight layout
-constexpr int kGemvFragRows = 2 * kGemvConsumerWarps;  // rows per pipeline stage
-constexpr int kGemvSmemHdr = 1024;  // mbarriers, abort flag, group list
-constexpr int kGemvMaxK = 12288;     // input length held in registers by the legacy prologue
+constexpr int kGemvFragTiles = 2;    // tiles per fragment
+constexpr int kGemvStageBlocks = 8;  // super-blocks per K stage (one per consumer warp)
+constexpr int kGemvMaxK = 12288;     // input length quantised by the f32 prologue
 constexpr int kGemvMaxGrid = 296;
+constexpr int kGemvSmemHdr = 4096;   // mbarriers, abort flag, group list, phase parameters, reduction scratch
+
+static_assert(kGemvStageBlocks == kGemvConsumerWarps, "one super-block per consumer warp");
+
+// Bytes of one unit (16 rows × 256 values).
+__host__ __device__ inline int unit_bytes(int type) { return type == AF_GGML_Q6_K ? 16 * 210 : 16 * 144; }
+
+// Q4_K unit: [2048: qs words in fragment order][256: the 16 rows' 16-byte headers]
+//   qs offset c*512 + lane*16 + e*4 (chunk c = 64 values) holds GGUF qs word
+//   w of chunk c of row r, with g = lane/4, t = lane%4 and
+//   e = 0: (r = g,   w = t)   e = 1: (r = g+8, w = t)
+//   e = 2: (r = g,   w = t+4) e = 3: (r = g+8, w = t+4).
+// Q6_K unit: [2048: low nibbles][1024: high bit pairs][256: row scales][32: row d]
+//   low-nibble word at P*512 + lane*16 + e*4 (P = 64-value pair of tiles),
+//   byte i = lo4(q(r, 64P + 4w + i)) | lo4(q(r, 64P + 32 + 4w + i)) << 4;
+//   high word at 2048 + Q*512 + lane*16 + e*4 (Q = 128-value quad),
+//   byte i = Σ_s hi2(q(r, 128Q + 32s + 4w + i)) << 2s;  (r, w) as for Q4_K.
+constexpr int kQ4Hdr = 2048;
+constexpr int kQ6Hi = 2048, kQ6Sc = 3072, kQ6D = 3328;
 
 struct GemvSeg {
     const uint8_t* w;      // packed rows
@@ -59,18 +80,18 @@ struct GemvSeg {
     const float* bias;     // optional per-row bias (EPI_STORE)
     int type;              // AF_GGML_Q4_K or AF_GGML_Q6_K
     int rows;
-    int row_stride;        // bytes per row (sum of the row's stage segments)
+    int row_stride;        // bytes per row = super-blocks × 144 (Q4_K) or 210 (Q6_K)
 };
 
 struct GemvParams {
     GemvSeg seg[3];
     int nseg;
     int K;                 // input length, multiple of 256
-    // input, quantised form (preferred): XQ layout of xq_bytes(K) bytes, and
-    // with xq_norm the per-64 sums of squares after it (RMSNorm input)
+    // input, quantised form: XQ layout of xq_bytes(K) bytes, and with xq_norm
+    // the per-64 sums of squares after it (RMSNorm input)
     const uint8_t* xq;
     int xq_norm;
-    // input, f32 form (legacy prologue): x (+ x_add, stored to x_store) [+ RMSNorm]
+    // input, f32 form (prologue): x (+ x_add, stored to x_store) [+ RMSNorm]
     const float* x;
     const float* x_add;
     float* x_store;
@@ -87,16 +108,11 @@ struct GemvParams {
     unsigned int* q_cnt;   // per-64-row-group arrival counters, zero between launches
     int ring_bytes;        // weight ring in shared memory (multiple of 16)
     int grid;
-    int vrange[kGemvMaxGrid + 1];  // CTA i owns virtual rows [vrange[i], vrange[i+1])
+    int vrange[kGemvMaxGrid + 1];  // CTA i owns virtual tiles [vrange[i], vrange[i+1])
 };
 
-__host__ __device__ inline int q6k_row_stride(int cols) {
-    const int nb = cols / 256, full = nb / 8, rem = nb % 8;
-    return full * 1680 + (rem ? rem * 208 + 16 : 0);
-}
-
 __host__ __device__ inline int dev_row_stride(int type, int cols) {
-    return type == AF_GGML_Q6_K ? q6k_row_stride(cols) : (cols / 256) * 144;
+    return (cols / 256) * (type == AF_GGML_Q6_K ? 210 : 144);
 }
 
 // Device bytes of a packed matrix: whole 16-row tiles (the last one zero-padded).
@@ -104,10 +120,13 @@ __host__ __device__ inline size_t packed_bytes(int type, int rows, int cols) {
     return (size_t)((rows + kPackTile - 1) / kPackTile) * kPackTile * dev_row_stride(type, cols);
 }
 
-// Bytes of the quantised-input (XQ) layout for K values: per stage of 2048
-// values: hi plane 2048, lo plane 2048, 32 f32 scales, 64 f32 sums of 32,
-// 128 int sums of 16.  A normalised input appends K/64 f32 sums of squares.
-__host__ __device__ inline int xq_bytes(int K) { return ((K / 256 + 7) / 8) * 4992; }
+// Quantised-input (XQ) layout for K values, per 256-value super-block
+// (kXqSb bytes): hi plane [256] int8, lo plane [256] int8 (value order), then
+// xs[4] f32 (per 64 values), sum32[8] f32 (Σx per 32), isum16[16] int32
+// (Σ 256·hi + lo per 16).  A normalised input appends K/64 f32 sums of squares.
+constexpr int kXqSb = 512 + 16 + 32 + 64;
+constexpr int kXqXs = 512, kXqS32 = 528, kXqI16 = 560;
+__host__ __device__ inline int xq_bytes(int K) { return (K / 256) * kXqSb; }
 __host__ __device__ inline int xq_norm_bytes(int K) { return xq_bytes(K) + K / 16; }
 
 // Shared-memory bytes of the standalone GEMV: header, ring, XQ input, misc.
@@ -118,7 +137,7 @@ __host__ __device__ inline int gemv_smem_bytes(int K, int ring_bytes) {
 // Per-device kernel attributes; call once per device before launching (and
 // before any stream capture).
 cudaError_t gemv_init();
-// Fill ring size / grid / CTA ranges for the segments in p.
+// Fill ring size / grid / CTA tile ranges for the segments in p.
 void gemv_configure(GemvParams& p, int grid);
 cudaError_t gemv_launch(const GemvParams& p, cudaStream_t stream, bool pdl);
 

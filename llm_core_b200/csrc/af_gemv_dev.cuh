@@ -1,6 +1,6 @@
 // af_gemv_dev.cuh — device building blocks of the dequant GEMV, shared by the
 // standalone GEMV kernel (af_gemv.cu) and the persistent decode-step kernel
-// (af_step.cu).
+// (af_step.cu).  Layouts are described in af_gemv.cuh.
 //
 // Weight streaming uses a byte ring in shared memory: entry i of a CTA's
 // sequence (one fragment × one 8-super-block K stage) is placed at
@@ -21,75 +21,61 @@ constexpr int kCW = kGemvConsumerWarps;
 constexpr int kCT = kCW * 32;
 constexpr int kRingDesc = 8;  // entries in flight at most
 
+// Shared-memory header of the GEMV kernels (kGemvSmemHdr bytes).
+constexpr int kHdrFlags = 256;    // int[0] abort, [1..] group list
+constexpr int kHdrRed = 2048;     // [2 buffers][2 tiles][kCW warps][16 rows] f32
+static_assert(kHdrRed + 2 * 2 * kCW * 16 * 4 <= kGemvSmemHdr, "GEMV header overflow");
+constexpr int kGroupListMax = (1024 - kHdrFlags) / 4 - 2;  // groups one CTA can complete
+
 // Named barrier 1 over the consumer warps only (the producer never joins).
 __device__ __forceinline__ void bar_consumers() { asm volatile("bar.sync 1, %0;" ::"n"(kCT) : "memory"); }
 
+// ---------------------------------------------------------------- fragments
+
+// Fragment = up to two tiles of one segment (SwiGLU: gate tile t of segment 0
+// and up tile t of segment 1, as one virtual tile).
 struct Frag {
-    int seg;   // segment of the fragment's rows
-    int row0;  // first row within the segment (virtual row for SwiGLU pairs)
-    int n;     // rows (row pairs for SwiGLU)
+    int seg;   // segment of tile 0
+    int tile;  // first tile (within the segment)
+    int nt;    // tiles streamed (1 or 2)
 };
 
-__device__ __forceinline__ int n_vsegs(const GemvParams& p) { return p.epi == EPI_SWIGLU ? 1 : p.nseg; }
+__device__ __forceinline__ int seg_tiles(const GemvSeg& s) { return (s.rows + kPackTile - 1) / kPackTile; }
 
-// Fragment iterator over [cur, end) of the concatenated virtual-row space.
+// Iterator over [cur, end) of the virtual-tile space: the segments' tiles
+// concatenated (SwiGLU: gate/up tile pairs).
 struct FragIter {
     int cur, end;
     __device__ bool next(const GemvParams& p, Frag& t) {
         if (cur >= end) return false;
-        int base = 0, s = 0;
-        const int ns = n_vsegs(p);
-        for (; s < ns - 1; ++s) {
-            if (cur < base + p.seg[s].rows) break;
-            base += p.seg[s].rows;
+        if (p.epi == EPI_SWIGLU) {
+            t.seg = 0;
+            t.tile = cur;
+            t.nt = 2;
+            cur += 1;
+            return true;
         }
-        const int cap = p.epi == EPI_SWIGLU ? kGemvFragRows / 2 : kGemvFragRows;
-        const int stop = min(min(cur + cap, end), base + p.seg[s].rows);
+        int base = 0, s = 0;
+        for (; s < p.nseg - 1; ++s) {
+            const int n = seg_tiles(p.seg[s]);
+            if (cur < base + n) break;
+            base += n;
+        }
+        const int stop = min(min(cur + kGemvFragTiles, end), base + seg_tiles(p.seg[s]));
         t.seg = s;
-        t.row0 = cur - base;
-        t.n = stop - cur;
+        t.tile = cur - base;
+        t.nt = stop - cur;
         cur = stop;
         return true;
     }
 };
 
-// Bytes of one row's segment for a stage of nbs super-blocks: Q4_K nbs*144;
-// Q6_K nbs*208 + 16 (the group's d values).  Both are multiples of 16.
-__device__ __forceinline__ uint32_t stage_seg_bytes(int type, int nbs) {
-    return type == AF_GGML_Q6_K ? (uint32_t)nbs * 208u + 16u : (uint32_t)nbs * 144u;
+// Segment and tile of tile k of a fragment.
+__device__ __forceinline__ const GemvSeg& frag_seg(const GemvParams& p, const Frag& t, int k) {
+    return p.seg[p.epi == EPI_SWIGLU ? k : t.seg];
 }
-
-// Address of row `row`, stage st in the packed (tile-major) layout: tile
-// t = row / 16 occupies 16 * row_stride bytes; inside it stage st starts at
-// 16 * st * full_seg and row i of the tile at i * seg(st).
-__device__ __forceinline__ const uint8_t* packed_stage_ptr(const GemvSeg& g, int row, int st, uint32_t seg) {
-    const uint32_t full = g.type == AF_GGML_Q6_K ? 1680u : 1152u;
-    return g.w + (size_t)(row / kPackTile) * kPackTile * g.row_stride + (size_t)kPackTile * st * full +
-           (size_t)(row % kPackTile) * seg;
-}
-
-// Copy rows [row0, row0 + n) of one segment's stage st into smem (dense,
-// seg bytes per row): one bulk copy per packed tile the rows touch.
-__device__ __forceinline__ void copy_rows(uint8_t* dst, const GemvSeg& g, int row0, int n, int st, uint32_t seg,
-                                          uint64_t* bar, uint64_t pol) {
-    int r = row0;
-    while (r < row0 + n) {
-        const int stop = min(row0 + n, (r / kPackTile + 1) * kPackTile);
-        bulk_g2s(dst + (size_t)(r - row0) * seg, packed_stage_ptr(g, r, st, seg), (uint32_t)(stop - r) * seg, bar,
-                 pol);
-        r = stop;
-    }
-}
-
-// Type of the rows a fragment streams (SwiGLU: gate and up share a type).
-__device__ __forceinline__ int frag_type(const GemvParams& p, const Frag& t) {
-    return p.seg[p.epi == EPI_SWIGLU ? 0 : t.seg].type;
-}
-
-// Ring bytes of one entry: (fragment t, stage of nbs super-blocks).  SwiGLU
-// entries hold the gate rows then the up rows.
-__device__ __forceinline__ int entry_bytes(const GemvParams& p, const Frag& t, int nbs) {
-    return (p.epi == EPI_SWIGLU ? 2 : 1) * t.n * (int)stage_seg_bytes(frag_type(p, t), nbs);
+__device__ __forceinline__ int frag_tile(const GemvParams& p, const Frag& t, int k) {
+    return p.epi == EPI_SWIGLU ? t.tile : t.tile + k;
 }
 
 __device__ __forceinline__ int ring_place(int& head, int size, int ring_bytes) {
@@ -122,7 +108,7 @@ struct Producer {
         return true;
     }
 
-    // Reserve `bytes` at the next placement; false on timeout.
+    // Reserve `bytes` at the next placement; false on timeout or abort.
     __device__ bool reserve(const Ring& r, int bytes, int& at, const volatile int* abort) {
         int h = head;
         at = ring_place(h, bytes, r.bytes);
@@ -142,30 +128,29 @@ struct Producer {
         return true;
     }
 
-    // Stream every (fragment, stage) entry of rows [vbeg, vend) of p, in the
-    // order the consumers take them: fragment pairs, stage-major inside a pair.
+    // Stream every (fragment, stage) entry of virtual tiles [vbeg, vend) of p
+    // in the order the consumers take them.
     __device__ bool produce(const GemvParams& p, int vbeg, int vend, const Ring& r, volatile int* abort,
                             uint64_t pol) {
-        const int nb = p.K / 256, nst = (nb + 7) / 8;
+        const int nb = p.K / 256, nst = (nb + kGemvStageBlocks - 1) / kGemvStageBlocks;
         FragIter it{vbeg, vend};
-        Frag fr[2];
-        while (it.next(p, fr[0])) {
-            const int nf = it.next(p, fr[1]) ? 2 : 1;
+        Frag t;
+        while (it.next(p, t)) {
+            const int ub = unit_bytes(p.seg[t.seg].type);
             for (int st = 0; st < nst; ++st) {
-                const int nbs = min(8, nb - st * 8);
-                for (int f = 0; f < nf; ++f) {
-                    const Frag& t = fr[f];
-                    const int bytes = entry_bytes(p, t, nbs);
-                    int at;
-                    if (*abort || !reserve(r, bytes, at, abort)) return false;
-                    uint64_t* bar = &r.full[issued % kRingDesc];
-                    const GemvSeg& g0 = p.seg[p.epi == EPI_SWIGLU ? 0 : t.seg];
-                    const uint32_t segb = stage_seg_bytes(g0.type, nbs);
-                    mbar_arrive_expect_tx(bar, (uint32_t)bytes);
-                    copy_rows(r.buf + at, g0, t.row0, t.n, st, segb, bar, pol);
-                    if (p.epi == EPI_SWIGLU) copy_rows(r.buf + at + t.n * segb, p.seg[1], t.row0, t.n, st, segb, bar, pol);
-                    ++issued;
+                const int nbs = min(kGemvStageBlocks, nb - st * kGemvStageBlocks);
+                const int bytes = t.nt * nbs * ub;
+                int at;
+                if (*abort || !reserve(r, bytes, at, abort)) return false;
+                uint64_t* bar = &r.full[issued % kRingDesc];
+                mbar_arrive_expect_tx(bar, (uint32_t)bytes);
+                for (int k = 0; k < t.nt; ++k) {
+                    const GemvSeg& g = frag_seg(p, t, k);
+                    const uint8_t* src = g.w + (size_t)frag_tile(p, t, k) * kPackTile * g.row_stride +
+                                         (size_t)st * kGemvStageBlocks * ub;
+                    bulk_g2s(r.buf + at + k * nbs * ub, src, (uint32_t)(nbs * ub), bar, pol);
                 }
+                ++issued;
             }
         }
         return true;
@@ -178,97 +163,266 @@ struct Producer {
     }
 };
 
-// ---------------------------------------------------------------- consumers
+// ---------------------------------------------------------------- tensor-core units
 
-struct XRegs {
-    uint4 h[4], l[4];
-    float xs;
-    float s32[2];
-    int is16[4];
-};
-
-// Dot of one Q4_K (block b, chunk c) with the lane's x registers.
-// Block: [d f16][dmin f16][scales 12][qs 128] (gemv_q4k_avx2.cpp:6-15).
-__device__ __forceinline__ float q4k_lane_dot(const uint8_t* blk, int c, const XRegs& x) {
-    const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
-    const uint4 qa = *reinterpret_cast<const uint4*>(blk + 16 + 32 * c);
-    const uint4 qb = *reinterpret_cast<const uint4*>(blk + 32 + 32 * c);
-    const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-    const int* xh0 = reinterpret_cast<const int*>(&x.h[0]);
-    const int* xl0 = reinterpret_cast<const int*>(&x.l[0]);
-    // two interleaved accumulator sets (even / odd words) halve the dp4a chains
-    int lh[2] = {0, 0}, ll[2] = {0, 0}, hh[2] = {0, 0}, hl[2] = {0, 0};
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-        // words 0-3: qs bytes 0-15 of the chunk -> x chunk 0 (lo) / 2 (hi);
-        // words 4-7: bytes 16-31 -> x chunk 1 (lo) / 3 (hi).
-        const uint32_t lo = qw[k] & 0x0F0F0F0Fu;
-        const uint32_t hi = qw[k] & 0xF0F0F0F0u;  // 16 x high nibble
-        const int e = k & 1;
-        lh[e] = dp4a_us(lo, xh0[k], lh[e]);
-        ll[e] = dp4a_us(lo, xl0[k], ll[e]);
-        hh[e] = dp4a_us(hi, xh0[8 + k], hh[e]);
-        hl[e] = dp4a_us(hi, xl0[8 + k], hl[e]);
-    }
-    const int tlo = (lh[0] + lh[1]) * 256 + (ll[0] + ll[1]);
-    const int thi = ((hh[0] + hh[1]) * 256 + (hl[0] + hl[1])) >> 4;  // exact: every term is a multiple of 16
-    // 6-bit scale/min pairs j = 2c (low nibbles) and 2c+1 (high nibbles):
-    // get_scale_min_k4 (gemv_q4k_avx2.cpp:34-43) four bytes at a time.
-    const uint32_t w0 = hdr.y, w1 = hdr.z, w2 = hdr.w;
-    // branch-free: c is per lane, so a branch would diverge within the warp
-    const bool upper = c >= 2;
-    const uint32_t S = upper ? ((w2 & 0x0F0F0F0Fu) | ((w0 >> 2) & 0x30303030u)) : (w0 & 0x3F3F3F3Fu);
-    const uint32_t M = upper ? (((w2 >> 4) & 0x0F0F0F0Fu) | ((w1 >> 2) & 0x30303030u)) : (w1 & 0x3F3F3F3Fu);
-    const int sh = (c & 1) * 16;
-    const int sc_lo = (S >> sh) & 0xFF, sc_hi = (S >> (sh + 8)) & 0xFF;
-    const int m_lo = (M >> sh) & 0xFF, m_hi = (M >> (sh + 8)) & 0xFF;
-    const float d = half_bits_to_float(hdr.x & 0xFFFFu);
-    const float dmin = half_bits_to_float(hdr.x >> 16);
-    const int T = sc_lo * tlo + sc_hi * thi;
-    return (d * x.xs) * (float)T - dmin * ((float)m_lo * x.s32[0] + (float)m_hi * x.s32[1]);
+// d(16×8, s32) += a(16×32, u8) · b(32×8, s8)
+__device__ __forceinline__ void mma_u8s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// Dot of one Q6_K (block b, chunk c = 2n+u) with the lane's x registers.
-// Regrouped block: [ql 128][qh 64][scales 16] (+ d in the group's d area);
-// value mapping of q6k_row_to_f32 (src/models/llama_model.cpp:560-592).
-__device__ __forceinline__ float q6k_lane_dot(const uint8_t* blk, float d, int c, const XRegs& x) {
-    const int n = c >> 1, u = c & 1;
-    const uint4 a0 = *reinterpret_cast<const uint4*>(blk + 64 * n);
-    const uint4 a1 = *reinterpret_cast<const uint4*>(blk + 64 * n + 16);
-    const uint4 b0 = *reinterpret_cast<const uint4*>(blk + 64 * n + 32);
-    const uint4 b1 = *reinterpret_cast<const uint4*>(blk + 64 * n + 48);
-    const uint4 h0 = *reinterpret_cast<const uint4*>(blk + 128 + 32 * n);
-    const uint4 h1 = *reinterpret_cast<const uint4*>(blk + 128 + 32 * n + 16);
-    const uint32_t scw = *reinterpret_cast<const uint32_t*>(blk + 192 + 4 * c);
-    const uint32_t A[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-    const uint32_t B[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-    const uint32_t H[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-    const int* xh = reinterpret_cast<const int*>(&x.h[0]);
-    const int* xl = reinterpret_cast<const int*>(&x.l[0]);
-    const int s4 = 4 * u;
-    int gh[4] = {0, 0, 0, 0}, gl[4] = {0, 0, 0, 0};
+__device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
+
+// The lane's share of one super-block of the quantised input, Q4_K form.
+// Lane (g, t): B column g = (sub-block slot g/2, plane g%2); it supplies the
+// plane's words of sub-blocks g/2 (a) and 4 + g/2 (b).
+struct XQ4 {
+    uint32_t a0, a1, b0, b1;
+    float xs0, xs1;  // xs of the chunks of this lane's output sub-blocks t and 4+t (1/16 folded in for odd t)
+    float s0, s1;    // Σx of sub-blocks t and 4+t
+};
+__device__ __forceinline__ XQ4 load_xq4(const uint8_t* xsb, int lane, float s_in) {
+    const int g = lane >> 2, t = lane & 3, m = g >> 1;
+    const uint32_t* X = reinterpret_cast<const uint32_t*>(xsb + (g & 1) * 256);
+    XQ4 x;
+    x.a0 = X[8 * m + t];
+    x.a1 = X[8 * m + 4 + t];
+    x.b0 = X[8 * (m + 4) + t];
+    x.b1 = X[8 * (m + 4) + 4 + t];
+    const float* XS = reinterpret_cast<const float*>(xsb + kXqXs);
+    const float* S32 = reinterpret_cast<const float*>(xsb + kXqS32);
+    const float f = (t & 1) ? s_in * 0.0625f : s_in;  // odd sub-blocks are high nibbles (×16)
+    x.xs0 = XS[t >> 1] * f;
+    x.xs1 = XS[2 + (t >> 1)] * f;
+    x.s0 = S32[t] * s_in;
+    x.s1 = S32[4 + t] * s_in;
+    return x;
+}
+
+// One Q4_K unit (16 rows × 256 values at u): the lane's contribution to rows
+// g and g+8 from its sub-blocks t and 4+t.  Block math of q4k_dot_row
+// (src/models/llama_model.cpp:476-504) / get_scale_min_k4 (gemv_q4k_avx2.cpp:34-43).
+__device__ __forceinline__ float2 q4_unit(const uint8_t* u, const XQ4& x, int lane) {
+    const int g = lane >> 2, t = lane & 3, m = g >> 1;
+    uint4 a[4];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-        const uint32_t h = H[k] >> s4;
-        // first stream (x local 0..31): ql[l] nibble u, qh bits 4u..4u+1
-        const uint32_t q1 = ((A[k] >> s4) & 0x0F0F0F0Fu) | ((h << 4) & 0x30303030u);
-        // second stream (x local 32..63): ql[l+32] nibble u, qh bits 4u+2..4u+3
-        const uint32_t q2 = ((B[k] >> s4) & 0x0F0F0F0Fu) | ((h << 2) & 0x30303030u);
-        const int g1 = k >> 2;        // group 0 or 1 (16 values each)
-        const int g2 = 2 + (k >> 2);  // group 2 or 3
-        gh[g1] = dp4a_us(q1, xh[k], gh[g1]);
-        gl[g1] = dp4a_us(q1, xl[k], gl[g1]);
-        gh[g2] = dp4a_us(q2, xh[8 + k], gh[g2]);
-        gl[g2] = dp4a_us(q2, xl[8 + k], gl[g2]);
-    }
-    float acc = 0.f;
+    for (int c = 0; c < 4; ++c) a[c] = lds128(u + c * 512 + lane * 16);
+    int C0[4] = {0, 0, 0, 0}, C1[4] = {0, 0, 0, 0};
 #pragma unroll
-    for (int g = 0; g < 4; ++g) {
-        const int t = gh[g] * 256 + gl[g] - 32 * x.is16[g];  // Σ (q − 32)·xint
-        const float sc = (float)(int8_t)((scw >> (8 * g)) & 0xFF);
-        acc = fmaf(sc, (float)t, acc);
+    for (int j = 0; j < 8; ++j) {
+        const uint32_t M = (j & 1) ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
+        const uint4 q = a[j >> 1];
+        const bool sel = (j & 3) == m;
+        const uint32_t b0 = sel ? (j < 4 ? x.a0 : x.b0) : 0u;
+        const uint32_t b1 = sel ? (j < 4 ? x.a1 : x.b1) : 0u;
+        if (j < 4) mma_u8s8(C0, q.x & M, q.y & M, q.z & M, q.w & M, b0, b1);
+        else mma_u8s8(C1, q.x & M, q.y & M, q.z & M, q.w & M, b0, b1);
     }
-    return (d * x.xs) * acc;
+    const int sh = 8 * t;
+    float y[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const uint4 h = lds128(u + kQ4Hdr + (g + 8 * r) * 16);
+        // exact integer dots Σ q·(256·hi + lo) of sub-blocks t and 4+t
+        const int T0 = C0[2 * r] * 256 + C0[2 * r + 1];
+        const int T1 = C1[2 * r] * 256 + C1[2 * r + 1];
+        const uint32_t w0 = h.y >> sh, w1 = h.z >> sh, w2 = h.w >> sh;
+        const int sc0 = w0 & 63, m0 = w1 & 63;
+        const int sc1 = (w2 & 0xF) | ((w0 >> 2) & 0x30), m1 = ((w2 >> 4) & 0xF) | ((w1 >> 2) & 0x30);
+        const float d = half_bits_to_float(h.x & 0xFFFFu), dmin = half_bits_to_float(h.x >> 16);
+        y[r] = d * (x.xs0 * ((float)sc0 * (float)T0) + x.xs1 * ((float)sc1 * (float)T1)) -
+               dmin * ((float)m0 * x.s0 + (float)m1 * x.s1);
+    }
+    return make_float2(y[0], y[1]);
+}
+
+// The lane's share of one super-block, Q6_K form: B column g = (16-value group
+// slot g/2, plane g%2); slot s of tile pair P is tile 2P + s/2, group s%2, so
+// the lane supplies group (g/2)%2 of tiles g/4 + 2i.
+struct XQ6 {
+    uint32_t w[4];
+    float xs[4];   // per 64 values (tile pair)
+    int is16[4];   // Σ(256·hi + lo) of this lane's output groups 4P + t
+};
+__device__ __forceinline__ XQ6 load_xq6(const uint8_t* xsb, int lane, float s_in) {
+    const int g = lane >> 2, t = lane & 3, m = g >> 1;
+    const uint32_t* X = reinterpret_cast<const uint32_t*>(xsb + (g & 1) * 256);
+    const float* XS = reinterpret_cast<const float*>(xsb + kXqXs);
+    const int* I16 = reinterpret_cast<const int*>(xsb + kXqI16);
+    XQ6 x;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int j = (m >> 1) + 2 * i;
+        x.w[i] = X[8 * j + 4 * (m & 1) + t];
+        x.xs[i] = XS[i] * s_in;
+        x.is16[i] = I16[4 * i + t];
+    }
+    return x;
+}
+
+// One Q6_K unit: value mapping of q6k_row_to_f32 (src/models/llama_model.cpp:560-592),
+// w = d·sc·(q − 32).
+__device__ __forceinline__ float2 q6_unit(const uint8_t* u, const XQ6& x, int lane) {
+    const int g = lane >> 2, t = lane & 3, m = g >> 1;
+    uint4 L[4], H[2];
+#pragma unroll
+    for (int P = 0; P < 4; ++P) L[P] = lds128(u + P * 512 + lane * 16);
+#pragma unroll
+    for (int Q = 0; Q < 2; ++Q) H[Q] = lds128(u + kQ6Hi + Q * 512 + lane * 16);
+    int C[4][4];
+#pragma unroll
+    for (int P = 0; P < 4; ++P) C[P][0] = C[P][1] = C[P][2] = C[P][3] = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int P = j >> 1, odd = j & 1, Q = j >> 2, s = j & 3;
+        const uint32_t l[4] = {L[P].x, L[P].y, L[P].z, L[P].w};
+        const uint32_t h[4] = {H[Q].x, H[Q].y, H[Q].z, H[Q].w};
+        uint32_t a[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const uint32_t lo = (odd ? (l[e] >> 4) : l[e]) & 0x0F0F0F0Fu;
+            const uint32_t hi = s < 3 ? (h[e] << (4 - 2 * s)) & 0x30303030u : (h[e] >> 2) & 0x30303030u;
+            a[e] = lo | hi;
+        }
+        const bool own = (j & 1) == (m >> 1);
+        const uint32_t wv = x.w[j >> 1];
+        const uint32_t b0 = own && !(m & 1) ? wv : 0u;
+        const uint32_t b1 = own && (m & 1) ? wv : 0u;
+        mma_u8s8(C[P], a[0], a[1], a[2], a[3], b0, b1);
+    }
+    float y[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const int row = g + 8 * r;
+        const uint4 scw = lds128(u + kQ6Sc + row * 16);
+        const uint32_t sw[4] = {scw.x, scw.y, scw.z, scw.w};
+        const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(u + kQ6D + 2 * row));
+        float acc = 0.f;
+#pragma unroll
+        for (int P = 0; P < 4; ++P) {
+            const int T = C[P][2 * r] * 256 + C[P][2 * r + 1] - 32 * x.is16[P];  // Σ (q − 32)·xint
+            const int sc = (int)(int8_t)((sw[P] >> (8 * t)) & 0xFF);
+            acc = fmaf(x.xs[P], (float)sc * (float)T, acc);
+        }
+        y[r] = d * acc;
+    }
+    return make_float2(y[0], y[1]);
+}
+
+// ---------------------------------------------------------------- input
+
+// f32-input prologue: x (+ pending residual, optionally RMS-normalised)
+// loaded with all NIT float4 loads per thread in flight (norm weights too),
+// then quantised into the shared XQ layout.
+template <int NIT>
+__device__ __forceinline__ void input_prologue_t(const GemvParams& p, uint8_t* xqs, float* red) {
+    static_assert(kCT % 16 == 0, "16 consecutive threads own one 64-value group");
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int nvec = p.K / 4;
+    float4 a[NIT], w[NIT];
+#pragma unroll
+    for (int j = 0; j < NIT; ++j) {
+        const int v = j * kCT + tid;
+        const int vc = v < nvec ? v : 0;
+        a[j] = __ldcg(reinterpret_cast<const float4*>(p.x) + vc);
+        if (p.x_add) {
+            const float4 b = __ldcg(reinterpret_cast<const float4*>(p.x_add) + vc);
+            a[j].x += b.x;
+            a[j].y += b.y;
+            a[j].z += b.z;
+            a[j].w += b.w;
+        }
+        if (p.norm_w) w[j] = __ldg(reinterpret_cast<const float4*>(p.norm_w) + vc);
+        if (v >= nvec) a[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    if (p.x_store && blockIdx.x == 0) {
+#pragma unroll
+        for (int j = 0; j < NIT; ++j) {
+            const int v = j * kCT + tid;
+            if (v < nvec) reinterpret_cast<float4*>(p.x_store)[v] = a[j];
+        }
+    }
+    if (p.norm_w) {
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < NIT; ++j) ss += a[j].x * a[j].x + a[j].y * a[j].y + a[j].z * a[j].z + a[j].w * a[j].w;
+        ss = warp_sum(ss);
+        if (lane == 0) red[warp] = ss;
+        bar_consumers();
+        float tot = 0.f;
+#pragma unroll
+        for (int k = 0; k < kCW; ++k) tot += red[k];
+        // rms_norm_out (src/models/llama_model.cpp:393-419): 1/sqrt(ss/n + eps)
+        const float inv_rms = 1.f / sqrtf(tot / (float)p.K + p.eps);
+#pragma unroll
+        for (int j = 0; j < NIT; ++j) {
+            a[j].x = w[j].x * (a[j].x * inv_rms);
+            a[j].y = w[j].y * (a[j].y * inv_rms);
+            a[j].z = w[j].z * (a[j].z * inv_rms);
+            a[j].w = w[j].w * (a[j].w * inv_rms);
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < NIT; ++j) {
+        const int v = j * kCT + tid;
+        float amax = fmaxf(fmaxf(fabsf(a[j].x), fabsf(a[j].y)), fmaxf(fabsf(a[j].z), fabsf(a[j].w)));
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        // 16-bit grid of ±32639 so that hi = (q + 128) >> 8 stays within int8.
+        const float inv = amax > 0.f ? 32639.f / amax : 0.f;
+        const float av[4] = {a[j].x, a[j].y, a[j].z, a[j].w};
+        uint32_t hw = 0, lw = 0;
+        int is = 0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            int q = __float2int_rn(av[e] * inv);
+            q = max(-32639, min(32639, q));
+            const int hi = (q + 128) >> 8;
+            const int lo = q - hi * 256;
+            hw |= (uint32_t)(hi & 0xFF) << (8 * e);
+            lw |= (uint32_t)(lo & 0xFF) << (8 * e);
+            is += q;
+        }
+        float fs = a[j].x + a[j].y + a[j].z + a[j].w;
+        is += __shfl_xor_sync(0xffffffffu, is, 1);
+        is += __shfl_xor_sync(0xffffffffu, is, 2);
+        fs += __shfl_xor_sync(0xffffffffu, fs, 1);
+        fs += __shfl_xor_sync(0xffffffffu, fs, 2);
+        fs += __shfl_xor_sync(0xffffffffu, fs, 4);
+        if (v < nvec) {
+            uint8_t* sb = xqs + (v >> 6) * kXqSb;
+            const int ko = (4 * v) & 255;
+            *reinterpret_cast<uint32_t*>(sb + ko) = hw;
+            *reinterpret_cast<uint32_t*>(sb + 256 + ko) = lw;
+            if ((tid & 15) == 0) reinterpret_cast<float*>(sb + kXqXs)[ko >> 6] = amax / 32639.f;
+            if ((tid & 7) == 0) reinterpret_cast<float*>(sb + kXqS32)[ko >> 5] = fs;
+            if ((tid & 3) == 0) reinterpret_cast<int*>(sb + kXqI16)[ko >> 4] = is;
+        }
+    }
+}
+
+// Quantise the f32 input of p into the shared XQ layout (all consumer warps;
+// `red` is kCW floats of shared scratch).  Ends with a consumer barrier.
+__device__ __forceinline__ void input_prologue(const GemvParams& p, uint8_t* xqs, float* red) {
+    switch ((p.K / 4 + kCT - 1) / kCT) {
+        case 1: input_prologue_t<1>(p, xqs, red); break;
+        case 2: input_prologue_t<2>(p, xqs, red); break;
+        case 3: input_prologue_t<3>(p, xqs, red); break;
+        case 4: input_prologue_t<4>(p, xqs, red); break;
+        case 5: input_prologue_t<5>(p, xqs, red); break;
+        case 6: input_prologue_t<6>(p, xqs, red); break;
+        case 7: input_prologue_t<7>(p, xqs, red); break;
+        case 8: input_prologue_t<8>(p, xqs, red); break;
+        case 9: input_prologue_t<9>(p, xqs, red); break;
+        case 10: input_prologue_t<10>(p, xqs, red); break;
+        case 11: input_prologue_t<11>(p, xqs, red); break;
+        default: input_prologue_t<12>(p, xqs, red); break;
+    }
+    bar_consumers();
 }
 
 // Copy the quantised input (XQ layout, written by other CTAs or an earlier
@@ -280,7 +434,7 @@ __device__ __forceinline__ float load_xq(const GemvParams& p, uint8_t* xqs) {
     const uint4* src = reinterpret_cast<const uint4*>(p.xq);
     uint4* dst = reinterpret_cast<uint4*>(xqs);
     const int tid = threadIdx.x;
-    constexpr int kU = 4;
+    constexpr int kU = 8;
     for (int i0 = tid; i0 < n16; i0 += kU * kCT) {
         uint4 v[kU];
 #pragma unroll
@@ -289,9 +443,6 @@ __device__ __forceinline__ float load_xq(const GemvParams& p, uint8_t* xqs) {
 #pragma unroll
         for (int u = 0; u < kU; ++u)
             if (i0 + u * kCT < n16) dst[i0 + u * kCT] = v[u];
-    }
-    if (bytes % 16) {  // K/16 tail of the norm sums (K multiple of 256: never)
-        for (int i = n16 * 16 + tid; i < bytes; i += kCT) xqs[i] = p.xq[i];
     }
     bar_consumers();
     float s_in = 1.f;
@@ -307,156 +458,105 @@ __device__ __forceinline__ float load_xq(const GemvParams& p, uint8_t* xqs) {
     return s_in;
 }
 
-// Consumer warps: evaluate rows [vbeg, vend) of p from the ring, apply the
-// epilogue.  `consumed` / `head` persist across calls (the entry sequence of
-// a step spans its phases).  Returns false on a timeout or an abort.
+// ---------------------------------------------------------------- consumers
+
+// Consumer warps: evaluate virtual tiles [vbeg, vend) of p from the ring and
+// apply the epilogue.  `consumed` / `head` persist across calls (the entry
+// sequence of a step spans its phases).  `hdr` is the kernel's shared header.
+// Returns false on a timeout or an abort.
 __device__ __forceinline__ bool consume(const GemvParams& p, int vbeg, int vend, const Ring& r, uint32_t& consumed,
-                                        int& head, const uint8_t* xqs, float s_in, volatile int* abort) {
+                                        int& head, const uint8_t* xqs, float s_in, uint8_t* hdr) {
+    volatile int* abort = reinterpret_cast<volatile int*>(hdr + kHdrFlags);
+    float* red = reinterpret_cast<float*>(hdr + kHdrRed);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nb = p.K / 256, nst = (nb + 7) / 8;
-    const uint8_t* XH = xqs;
-    const uint8_t* XL = xqs + nst * 2048;
-    const float* XS = reinterpret_cast<const float*>(xqs + 2 * nst * 2048);
-    const float* XS32 = XS + nst * 32;
-    const int* XI16 = reinterpret_cast<const int*>(XS32 + nst * 64);
-    const int lb = lane >> 2, lc = lane & 3;
+    const int nb = p.K / 256, nst = (nb + kGemvStageBlocks - 1) / kGemvStageBlocks;
     FragIter it{vbeg, vend};
-    Frag fr[2];
+    Frag t;
     bool ok = !*abort;
     float best = -INFINITY;
     uint32_t best_idx = 0;
-    const int half = kGemvFragRows / 2;
-    while (ok && it.next(p, fr[0])) {
-        const int nf = it.next(p, fr[1]) ? 2 : 1;
-        // rows of this warp: (fragment f, r) -> entry row warp + r*half
-        // (SwiGLU: gate row warp, up row n + warp)
-        float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
-        bool rv[2][2];
-        int row[2][2];
-        int ty[2];
-        for (int f = 0; f < 2; ++f) {
-            const Frag& t = fr[f];
-            const bool have = f < nf;
-            if (p.epi == EPI_SWIGLU) {
-                rv[f][0] = rv[f][1] = have && warp < t.n;
-                row[f][0] = row[f][1] = t.row0 + warp;
-                ty[f] = p.seg[0].type;
-            } else {
-                rv[f][0] = have && warp < t.n;
-                rv[f][1] = have && warp + half < t.n;
-                row[f][0] = t.row0 + warp;
-                row[f][1] = t.row0 + warp + half;
-                ty[f] = have ? p.seg[t.seg].type : p.seg[fr[0].seg].type;
-            }
-        }
+    int fcount = 0;
+    while (ok && it.next(p, t)) {
+        const int type = p.seg[t.seg].type;
+        const int ub = unit_bytes(type);
+        // warp 0 owns the epilogue rows: lane = (tile k = lane/16, row lane%16)
+        const int ek = lane >> 4, er = lane & 15;
+        const GemvSeg& eseg = frag_seg(p, t, ek);
+        const int erow = frag_tile(p, t, ek) * kPackTile + er;
+        const bool evalid = ek < t.nt && erow < eseg.rows;
+        float rpre = 0.f;
+        if (warp == 0 && p.epi == EPI_RESID && evalid) rpre = __ldcg(p.resid + erow);  // in flight during the stages
+        float y[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
         for (int st = 0; st < nst; ++st) {
-            const int nbs = min(8, nb - st * 8);
-            const uint32_t d0 = consumed % kRingDesc, d1 = (consumed + 1) % kRingDesc;
-            const int at0 = ring_place(head, entry_bytes(p, fr[0], nbs), r.bytes);
-            const int at1 = nf == 2 ? ring_place(head, entry_bytes(p, fr[1], nbs), r.bytes) : at0;
-            if (lane == 0) {
-                ok = mbar_wait(&r.full[d0], (consumed / kRingDesc) & 1u, abort);
-                if (ok && nf == 2) ok = mbar_wait(&r.full[d1], ((consumed + 1) / kRingDesc) & 1u, abort);
-            }
+            const int nbs = min(kGemvStageBlocks, nb - st * kGemvStageBlocks);
+            const int at = ring_place(head, t.nt * nbs * ub, r.bytes);
+            const uint32_t d = consumed % kRingDesc;
+            if (lane == 0) ok = mbar_wait(&r.full[d], (consumed / kRingDesc) & 1u, abort);
             ok = __shfl_sync(0xffffffffu, ok, 0);
-            if (!ok || *abort) { ok = false; break; }
-            // a fragment cut short at a segment end may precede a full one
-            if (lb < nbs && (rv[0][0] || rv[1][0])) {
-                XRegs x;
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    x.h[i] = *reinterpret_cast<const uint4*>(XH + st * 2048 + i * 512 + lane * 16);
-                    x.l[i] = *reinterpret_cast<const uint4*>(XL + st * 2048 + i * 512 + lane * 16);
-                    x.is16[i] = XI16[st * 128 + i * 32 + lane];
-                }
-                x.xs = XS[st * 32 + lane] * s_in;
-                x.s32[0] = XS32[st * 64 + lane] * s_in;
-                x.s32[1] = XS32[st * 64 + 32 + lane] * s_in;
-                // Up to four rows evaluated without branches so their dp4a
-                // chains interleave.  Entries are packed end to end in the
-                // ring, so a row past a fragment's end could lie past the ring
-                // (and the shared allocation): an invalid row re-reads a valid
-                // row of the same type instead, and its result is discarded.
-                const uint8_t* rp[2][2];
-#pragma unroll
-                for (int f = 0; f < 2; ++f) {
-                    const uint32_t segb = stage_seg_bytes(ty[f], nbs);
-                    const uint8_t* row0 = r.buf + (f ? at1 : at0);
-                    const uint8_t* own = row0 + warp * segb;
-                    const uint8_t* safe = rv[f][0] ? own : row0;  // row 0 of an entry always exists
-                    rp[f][0] = safe;
-                    rp[f][1] = rv[f][1] ? own + (p.epi == EPI_SWIGLU ? fr[f].n : half) * segb : safe;
-                }
-                if (nf == 2 && ty[0] == ty[1]) {
-                    if (ty[0] == AF_GGML_Q6_K) {
-                        float d[4], a[4];
-#pragma unroll
-                        for (int k = 0; k < 4; ++k)
-                            d[k] = half_bits_to_float(
-                                *reinterpret_cast<const uint16_t*>(rp[k >> 1][k & 1] + nbs * 208 + 2 * lb));
-#pragma unroll
-                        for (int k = 0; k < 4; ++k) a[k] = q6k_lane_dot(rp[k >> 1][k & 1] + lb * 208, d[k], lc, x);
-#pragma unroll
-                        for (int k = 0; k < 4; ++k) acc[k >> 1][k & 1] += a[k];
-                    } else {
-                        float a[4];
-#pragma unroll
-                        for (int k = 0; k < 4; ++k) a[k] = q4k_lane_dot(rp[k >> 1][k & 1] + lb * 144, lc, x);
-#pragma unroll
-                        for (int k = 0; k < 4; ++k) acc[k >> 1][k & 1] += a[k];
+            if (!ok || *abort) {
+                ok = false;
+                break;
+            }
+            if (warp < nbs) {
+                const uint8_t* xsb = xqs + (st * kGemvStageBlocks + warp) * kXqSb;
+                const uint8_t* u = r.buf + at + warp * ub;
+                if (type == AF_GGML_Q6_K) {
+                    const XQ6 x = load_xq6(xsb, lane, s_in);
+                    const float2 v0 = q6_unit(u, x, lane);
+                    y[0][0] += v0.x;
+                    y[0][1] += v0.y;
+                    if (t.nt > 1) {
+                        const float2 v1 = q6_unit(u + nbs * ub, x, lane);
+                        y[1][0] += v1.x;
+                        y[1][1] += v1.y;
                     }
                 } else {
-                    for (int f = 0; f < nf; ++f) {
-                        if (ty[f] == AF_GGML_Q6_K) {
-                            const float e0 = half_bits_to_float(
-                                *reinterpret_cast<const uint16_t*>(rp[f][0] + nbs * 208 + 2 * lb));
-                            const float e1 = half_bits_to_float(
-                                *reinterpret_cast<const uint16_t*>(rp[f][1] + nbs * 208 + 2 * lb));
-                            const float a0 = q6k_lane_dot(rp[f][0] + lb * 208, e0, lc, x);
-                            const float a1 = q6k_lane_dot(rp[f][1] + lb * 208, e1, lc, x);
-                            acc[f][0] += a0;
-                            acc[f][1] += a1;
-                        } else {
-                            const float a0 = q4k_lane_dot(rp[f][0] + lb * 144, lc, x);
-                            const float a1 = q4k_lane_dot(rp[f][1] + lb * 144, lc, x);
-                            acc[f][0] += a0;
-                            acc[f][1] += a1;
-                        }
+                    const XQ4 x = load_xq4(xsb, lane, s_in);
+                    const float2 v0 = q4_unit(u, x, lane);
+                    y[0][0] += v0.x;
+                    y[0][1] += v0.y;
+                    if (t.nt > 1) {
+                        const float2 v1 = q4_unit(u + nbs * ub, x, lane);
+                        y[1][0] += v1.x;
+                        y[1][1] += v1.y;
                     }
                 }
             }
             __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&r.empty[d0]);
-                if (nf == 2) mbar_arrive(&r.empty[d1]);
-            }
-            consumed += nf;
+            if (lane == 0) mbar_arrive(&r.empty[d]);
+            ++consumed;
         }
         if (!ok) break;
-        for (int f = 0; f < nf; ++f) {
-            acc[f][0] = warp_sum(acc[f][0]);
-            acc[f][1] = warp_sum(acc[f][1]);
-            if (lane != 0) continue;
-            if (p.epi == EPI_SWIGLU) {
-                if (rv[f][0]) {
-                    const float g = acc[f][0], u = acc[f][1];
-                    p.seg[0].y[row[f][0]] = (g / (1.f + expf(-g))) * u;
-                }
-                continue;
-            }
-            const GemvSeg& sg = p.seg[fr[f].seg];
+        // rows g, g+8 of each tile: sum the 4 lanes of a row group, then the
+        // 8 warps in a fixed order (deterministic)
+        float* rb = red + (fcount & 1) * 2 * kCW * 16;
+#pragma unroll
+        for (int k = 0; k < 2; ++k)
 #pragma unroll
             for (int rr = 0; rr < 2; ++rr) {
-                if (!rv[f][rr]) continue;
-                float v = acc[f][rr];
+                float v = y[k][rr];
+                v += __shfl_xor_sync(0xffffffffu, v, 1);
+                v += __shfl_xor_sync(0xffffffffu, v, 2);
+                if ((lane & 3) == 0) rb[(k * kCW + warp) * 16 + (lane >> 2) + 8 * rr] = v;
+            }
+        bar_consumers();
+        ++fcount;
+        if (warp == 0) {
+            float v = 0.f;
+#pragma unroll
+            for (int w = 0; w < kCW; ++w) v += rb[(ek * kCW + w) * 16 + er];
+            if (p.epi == EPI_SWIGLU) {
+                const float u = __shfl_down_sync(0xffffffffu, v, 16);  // up row of the same row index
+                if (lane < 16 && evalid) p.seg[0].y[erow] = (v / (1.f + expf(-v))) * u;
+            } else if (evalid) {
                 if (p.epi == EPI_RESID) {
-                    p.resid[row[f][rr]] = __ldcg(p.resid + row[f][rr]) + v;
+                    p.resid[erow] = rpre + v;
                 } else {
-                    if (sg.bias) v += sg.bias[row[f][rr]];
-                    sg.y[row[f][rr]] = v;
+                    if (eseg.bias) v += eseg.bias[erow];
+                    eseg.y[erow] = v;
                     if (p.epi == EPI_ARGMAX) {
-                        // rows reach a lane in increasing order; ties keep the lowest index
-                        const uint32_t gi = (uint32_t)(p.argmax_base + row[f][rr]);
+                        // a lane's rows arrive in increasing order; ties keep the lowest index
+                        const uint32_t gi = (uint32_t)(p.argmax_base + erow);
                         if (v > best || (v == best && gi < best_idx)) {
                             best = v;
                             best_idx = gi;
@@ -466,36 +566,47 @@ __device__ __forceinline__ bool consume(const GemvParams& p, int vbeg, int vend,
             }
         }
     }
-    if (p.epi == EPI_ARGMAX && lane == 0 && best > -INFINITY) atomicMax(p.argmax, argmax_key(best, best_idx));
+    if (p.epi == EPI_ARGMAX && warp == 0) {
+        unsigned long long key = best > -INFINITY ? argmax_key(best, best_idx) : 0ull;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+            key = other > key ? other : key;
+        }
+        if (lane == 0 && key) atomicMax(p.argmax, key);
+    }
     return ok;
 }
 
-// After the epilogue stores of rows [vbeg, vend): every 64-row output group
-// this CTA completes (per-group arrival counters) is quantised into q_out for
-// the next GEMV.  Consumer warps only; `list` is shared scratch of at least
-// (vend − vbeg) / 64 + 3 ints.
+// After the epilogue stores of virtual tiles [vbeg, vend): every 64-row
+// output group this CTA completes (per-group arrival counters) is quantised
+// into q_out for the next GEMV.  Consumer warps only; `list` is the header's
+// group list (kGroupListMax + 1 ints).
 __device__ __forceinline__ void quantise_output(const GemvParams& p, int vbeg, int vend, int* list) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    bar_consumers();  // every epilogue store of this CTA is done
-    if (threadIdx.x == 0) {
-        __threadfence();
-        int n = 0;
-        for (int g = vbeg / 64; g * 64 < vend; ++g) {
-            const int lo = max(vbeg, g * 64), hi = min(vend, g * 64 + 64);
-            const unsigned int prev = atomicAdd(&p.q_cnt[g], (unsigned int)(hi - lo));
-            if (prev + (unsigned int)(hi - lo) == 64u) list[++n] = g;
-        }
-        list[0] = n;
-        __threadfence();
-    }
-    bar_consumers();
-    const int n = list[0];
-    const float* src = p.epi == EPI_RESID ? p.resid : p.seg[0].y;
     const int Kout = p.seg[0].rows;
+    const int rbeg = vbeg * kPackTile, rend = min(vend * kPackTile, Kout);
+    if (threadIdx.x == 0) list[0] = 0;
+    bar_consumers();  // every epilogue store of this CTA is done
+    // one thread per touched group: the arrival atomics run in parallel
+    for (int g = rbeg / 64 + threadIdx.x; rend > rbeg && g * 64 < rend; g += kCT) {
+        const int lo = max(rbeg, g * 64), hi = min(rend, g * 64 + 64);
+        __threadfence();
+        const unsigned int prev = atomicAdd(&p.q_cnt[g], (unsigned int)(hi - lo));
+        if (prev + (unsigned int)(hi - lo) == 64u) {
+            const int at = atomicAdd(&list[0], 1);
+            if (at < kGroupListMax) list[1 + at] = g;
+            else set_err(kErrBadArgs);  // more rows per CTA than the list holds
+        }
+    }
+    __threadfence();
+    bar_consumers();
+    const int n = min(list[0], kGroupListMax);
+    const float* src = p.epi == EPI_RESID ? p.resid : p.seg[0].y;
     for (int k = warp; k < n; k += kCW) {
-        const int g = list[1 + k];
-        xq_quantize_group(p.q_out, src, p.q_norm_w, Kout, g);
-        if (lane == 0) p.q_cnt[g] = 0u;
+        const int gg = list[1 + k];
+        xq_quantize_group(p.q_out, src, p.q_norm_w, Kout, gg);
+        if (lane == 0) p.q_cnt[gg] = 0u;
     }
 }
 

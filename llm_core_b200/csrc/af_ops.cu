@@ -32,23 +32,90 @@ int num_sms() {
 
 // ------------------------------------------------------- packed weight layout
 
-// One CTA per row; GGUF block j of the row goes to stage j/8, slot j%8 of that
-// stage's row segment (Q6_K: ql/qh/scales first, the f16 d values after the
-// segment's blocks).  `unpack` runs the same byte map backwards.
-__global__ void pack_kernel(uint8_t* __restrict__ packed, uint8_t* __restrict__ gguf, int type, int nb,
-                            int row_stride, int unpack) {
-    const int row = blockIdx.x;
-    const int BB = type == AF_GGML_Q6_K ? 210 : 144;
-    uint8_t* g = gguf + (size_t)row * nb * BB;
-    for (int idx = threadIdx.x; idx < nb * BB; idx += blockDim.x) {
-        const int j = idx / BB, i = idx % BB;
-        const int st = j >> 3, k = j & 7, nbs = min(8, nb - st * 8);
-        int o;
-        if (type == AF_GGML_Q6_K) o = i < 208 ? k * 208 + i : nbs * 208 + 2 * k + (i - 208);
-        else o = k * 144 + i;
-        const size_t d = packed_off(type, nb, row_stride, row, st) + o;
-        if (unpack) g[idx] = packed[d];
-        else packed[d] = g[idx];
+// One CTA per unit (16-row tile × super-block): every output byte of the
+// unit gathered from the GGUF rows (padding rows past `rows` are zero);
+// `unpack` writes the GGUF bytes back from the unit (the inverse map).
+__device__ __forceinline__ uint8_t q6_gguf_value(const uint8_t* blk, int k) {
+    // 6-bit value k of a GGUF Q6_K block (q6k_row_to_f32, llama_model.cpp:560-592)
+    const int n = k >> 7, kk = k & 127, s = kk >> 5, l = kk & 31;
+    const int qlb = blk[64 * n + l + ((s & 1) ? 32 : 0)];
+    const int lo = (s & 2) ? (qlb >> 4) : (qlb & 0xF);
+    const int hi = (blk[128 + 32 * n + l] >> (2 * s)) & 3;
+    return (uint8_t)(lo | (hi << 4));
+}
+
+__global__ void pack_kernel(uint8_t* __restrict__ packed, uint8_t* __restrict__ gguf, int type, int rows, int nb,
+                            int unpack) {
+    const int tile = blockIdx.x, b = blockIdx.y;
+    const bool q6 = type == AF_GGML_Q6_K;
+    const int BB = q6 ? 210 : 144, UB = 16 * BB;
+    uint8_t* unit = packed + ((size_t)tile * nb + b) * UB;
+    auto src_blk = [&](int r) { return gguf + ((size_t)(tile * 16 + r) * nb + b) * BB; };
+    if (!unpack) {
+        for (int o = threadIdx.x; o < UB; o += blockDim.x) {
+            int r, v = 0;
+            if (!q6) {
+                if (o < kQ4Hdr) {
+                    const int c = o >> 9, lane = (o >> 4) & 31, e = (o >> 2) & 3, i = o & 3;
+                    r = (lane >> 2) + 8 * (e & 1);
+                    const int w = (lane & 3) + 4 * (e >> 1);
+                    if (tile * 16 + r < rows) v = src_blk(r)[16 + 32 * c + 4 * w + i];
+                } else {
+                    r = (o - kQ4Hdr) >> 4;
+                    if (tile * 16 + r < rows) v = src_blk(r)[(o - kQ4Hdr) & 15];
+                }
+            } else if (o < kQ6Sc) {
+                const int part = o < kQ6Hi ? 0 : 1, oo = part ? o - kQ6Hi : o;
+                const int blkq = oo >> 9, lane = (oo >> 4) & 31, e = (oo >> 2) & 3, i = oo & 3;
+                r = (lane >> 2) + 8 * (e & 1);
+                const int w = (lane & 3) + 4 * (e >> 1);
+                if (tile * 16 + r < rows) {
+                    const uint8_t* blk = src_blk(r);
+                    if (!part) {
+                        const int k = 64 * blkq + 4 * w + i;
+                        v = (q6_gguf_value(blk, k) & 0xF) | ((q6_gguf_value(blk, k + 32) & 0xF) << 4);
+                    } else {
+                        for (int sx = 0; sx < 4; ++sx)
+                            v |= ((q6_gguf_value(blk, 128 * blkq + 32 * sx + 4 * w + i) >> 4) & 3) << (2 * sx);
+                    }
+                }
+            } else if (o < kQ6D) {
+                r = (o - kQ6Sc) >> 4;
+                if (tile * 16 + r < rows) v = src_blk(r)[192 + ((o - kQ6Sc) & 15)];
+            } else {
+                r = (o - kQ6D) >> 1;
+                if (tile * 16 + r < rows) v = src_blk(r)[208 + ((o - kQ6D) & 1)];
+            }
+            unit[o] = (uint8_t)v;
+        }
+        return;
+    }
+    // unpack: GGUF byte j of row r's block b
+    for (int idx = threadIdx.x; idx < 16 * BB; idx += blockDim.x) {
+        const int r = idx / BB, j = idx % BB;
+        if (tile * 16 + r >= rows) continue;
+        int v;
+        if (!q6) {
+            if (j < 16) {
+                v = unit[kQ4Hdr + 16 * r + j];
+            } else {
+                const int c = (j - 16) >> 5, l = (j - 16) & 31;
+                v = unit[c * 512 + packed_frag_off(r, l >> 2, l & 3)];
+            }
+        } else if (j < 128) {
+            const int n = j >> 6, l = j & 63;
+            const int k = 128 * n + l;  // low nibble value k, high nibble value k + 64
+            v = (packed_q6_value(unit, r, k) & 0xF) | ((packed_q6_value(unit, r, k + 64) & 0xF) << 4);
+        } else if (j < 192) {
+            const int n = (j - 128) >> 5, l = (j - 128) & 31;
+            v = 0;
+            for (int sx = 0; sx < 4; ++sx) v |= ((packed_q6_value(unit, r, 128 * n + 32 * sx + l) >> 4) & 3) << (2 * sx);
+        } else if (j < 208) {
+            v = unit[kQ6Sc + 16 * r + (j - 192)];
+        } else {
+            v = unit[kQ6D + 2 * r + (j - 208)];
+        }
+        src_blk(r)[j] = (uint8_t)v;
     }
 }
 
@@ -59,7 +126,8 @@ cudaError_t weight_pack(void* d_dst, const void* d_src, int type, int rows, int 
     if (!unpack) AF_CUDA_TRY(cudaMemsetAsync(d_dst, 0, packed_bytes(type, rows, cols), st));
     uint8_t* packed = static_cast<uint8_t*>(unpack ? const_cast<void*>(d_src) : d_dst);
     uint8_t* gg = static_cast<uint8_t*>(unpack ? d_dst : const_cast<void*>(d_src));
-    pack_kernel<<<rows, 256, 0, st>>>(packed, gg, type, nb, dev_row_stride(type, cols), unpack ? 1 : 0);
+    const dim3 grid((rows + kPackTile - 1) / kPackTile, nb);
+    pack_kernel<<<grid, 256, 0, st>>>(packed, gg, type, rows, nb, unpack ? 1 : 0);
     return cudaGetLastError();
 }
 

@@ -11,39 +11,38 @@ void set_last_error(const std::string& s);
 int num_sms();
 int gemv_grid();
 
-// Byte offset of (row, stage st) in the packed layout (see af_gemv.cuh).
-__host__ __device__ inline size_t packed_off(int type, int nb, int row_stride, int row, int st) {
-    const int nbs = min(8, nb - st * 8);
-    const int seg = type == AF_GGML_Q6_K ? nbs * 208 + 16 : nbs * 144;
-    const int full = type == AF_GGML_Q6_K ? 1680 : 1152;
-    return (size_t)(row / kPackTile) * kPackTile * row_stride + (size_t)kPackTile * st * full +
-           (size_t)(row % kPackTile) * seg;
+// Byte offset, inside a 512-byte fragment block of a unit, of byte i of
+// word w (of a 32-byte chunk) of tile row r (see af_gemv.cuh).
+__host__ __device__ inline int packed_frag_off(int r, int w, int i) {
+    const int lane = 4 * (r & 7) + (w & 3), e = (r >> 3) + 2 * (w >> 2);
+    return lane * 16 + e * 4 + i;
+}
+
+// 6-bit value k (0..255) of tile row r of a packed Q6_K unit.
+__host__ __device__ inline int packed_q6_value(const uint8_t* unit, int r, int k) {
+    const int P = k >> 6, kk = k & 63, l = kk & 31;
+    const int lo = unit[P * 512 + packed_frag_off(r, l >> 2, l & 3)];
+    const int Q = k >> 7, s = (k & 127) >> 5;
+    const int hi = unit[kQ6Hi + Q * 512 + packed_frag_off(r, l >> 2, l & 3)];
+    return ((kk >= 32 ? lo >> 4 : lo) & 0xF) | (((hi >> (2 * s)) & 3) << 4);
 }
 
 // Value v of packed row `tok` of an embedding matrix (nb super-blocks per
 // row), dequantised as emb_lookup does (src/models/llama_model.cpp:882-934).
 __device__ __forceinline__ float embed_value(const uint8_t* __restrict__ W, int type, int nb, int row_stride, int tok,
                                              int v) {
-    const int b = v >> 8, w = v & 255;
-    const int st = b >> 3, k = b & 7, nbs = min(8, nb - st * 8);
-    const uint8_t* seg = W + packed_off(type, nb, row_stride, tok, st);
+    const int b = v >> 8, k = v & 255, r = tok & (kPackTile - 1);
+    const uint8_t* unit = W + (size_t)(tok / kPackTile) * kPackTile * row_stride + (size_t)b * unit_bytes(type);
     if (type == AF_GGML_Q6_K) {
-        const uint8_t* blk = seg + k * 208;
-        const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(seg + nbs * 208 + 2 * k));
-        const int n = w >> 7, r = w & 127, s = r >> 5, l = r & 31;
-        const uint8_t* ql = blk + 64 * n;
-        const uint8_t* qh = blk + 128 + 32 * n;
-        const int8_t* sc = reinterpret_cast<const int8_t*>(blk + 192 + 8 * n);
-        const int qlb = (s & 1) ? ql[l + 32] : ql[l];
-        const int nib = (s & 2) ? (qlb >> 4) : (qlb & 0xF);
-        const int q = (nib | (((qh[l] >> (2 * s)) & 3) << 4)) - 32;
-        return d * sc[(l >> 4) + 2 * s] * q;
+        const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(unit + kQ6D + 2 * r));
+        const int sc = (int8_t)unit[kQ6Sc + 16 * r + (k >> 4)];
+        return d * sc * (packed_q6_value(unit, r, k) - 32);
     }
-    const uint8_t* blk = seg + k * 144;
-    const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(blk));
-    const float dmin = half_bits_to_float(*reinterpret_cast<const uint16_t*>(blk + 2));
-    const uint8_t* sc = blk + 4;
-    const int chunk = w >> 6, r = w & 63, j = chunk * 2 + (r >> 5), l = r & 31;
+    const uint8_t* hdr = unit + kQ4Hdr + 16 * r;
+    const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(hdr));
+    const float dmin = half_bits_to_float(*reinterpret_cast<const uint16_t*>(hdr + 2));
+    const uint8_t* sc = hdr + 4;
+    const int chunk = k >> 6, rr = k & 63, j = chunk * 2 + (rr >> 5), l = rr & 31;
     int s, m;
     if (j < 4) {
         s = sc[j] & 63;
@@ -52,8 +51,8 @@ __device__ __forceinline__ float embed_value(const uint8_t* __restrict__ W, int 
         s = (sc[j + 4] & 0xF) | ((sc[j - 4] >> 6) << 4);
         m = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
     }
-    const int qb = blk[16 + chunk * 32 + l];
-    const int q = (r < 32) ? (qb & 0xF) : (qb >> 4);
+    const int qb = unit[chunk * 512 + packed_frag_off(r, l >> 2, l & 3)];
+    const int q = (rr < 32) ? (qb & 0xF) : (qb >> 4);
     return (d * s) * q - dmin * m;
 }
 

@@ -12,9 +12,11 @@ using namespace gdev;
 constexpr int kParamOff = 1024;  // shared copies of the current phase's parameters
 static_assert(offsetof(GemvParams, vrange) <= 448, "GemvParams head must fit its shared-memory slot");
 static_assert(sizeof(AttnParams) <= 512, "AttnParams must fit its shared-memory slot");
-static_assert(kParamOff + 448 + 64 + sizeof(AttnParams) <= kStepHdr, "step header overflow");
+static_assert(kParamOff + 512 + sizeof(AttnParams) <= kHdrRed, "step header overflow");
+static_assert(kCW <= 16, "prologue scratch holds 16 warp sums");
 
-// Spin limit of the grid-wide waits (each iteration sleeps ~0.1 µs or more).
+// Spin limit of the grid-wide waits (each iteration is one L2 round trip,
+// a few hundred ns: seconds in all).
 constexpr uint32_t kGridSpinLimit = 1u << 24;
 
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
@@ -39,8 +41,7 @@ __device__ bool grid_wait(const unsigned* bar, unsigned target, volatile int* fl
                 ok = true;
                 break;
             }
-            if (flags[0]) break;
-            __nanosleep(64);
+            if ((i & 63) == 63 && flags[0]) break;
         }
         if (!ok) {
             if (!flags[0]) set_err(kErrMbarTimeout);
@@ -76,7 +77,7 @@ __device__ void embed_phase(const StepParams& sp, int tok) {
         const float a1 = embed_value(sp.tok_w, sp.tok_type, nb, sp.tok_stride, tok, v0 + 1);
         sp.x[v0] = a0;
         sp.x[v0 + 1] = a1;
-        xq_quantize_vals(sp.xq, a0, a1, sp.xq_norm_w, sp.n_embd, g);
+        if (sp.xq) xq_quantize_vals(sp.xq, a0, a1, sp.xq_norm_w, sp.n_embd, g);
     }
 }
 
@@ -184,8 +185,10 @@ __device__ void attn_item(const AttnParams& a, const AttnSmem& s, int pos, int k
     }
     bar_consumers();
     if (a.qk_norm_order == 1) {  // qwen3: per-head norm before RoPE
-        if (warp < G && a.q_norm) rms_norm_head(s.qs + warp * hd, a.q_norm, hd, a.eps);
-        if (warp == G && a.k_norm) rms_norm_head(s.ks, a.k_norm, hd, a.eps);
+        for (int h = warp; h <= G; h += kCW) {
+            if (h < G && a.q_norm) rms_norm_head(s.qs + h * hd, a.q_norm, hd, a.eps);
+            if (h == G && a.k_norm) rms_norm_head(s.ks, a.k_norm, hd, a.eps);
+        }
         bar_consumers();
     }
     // RoPE, half-split pairs (i, i + hd/2) (apply_rope, llama_model.cpp:1046-1080)
@@ -201,8 +204,10 @@ __device__ void attn_item(const AttnParams& a, const AttnSmem& s, int pos, int k
     }
     bar_consumers();
     if (a.qk_norm_order == 2) {  // hunyuan: per-head norm after RoPE
-        if (warp < G && a.q_norm) rms_norm_head(s.qs + warp * hd, a.q_norm, hd, a.eps);
-        if (warp == G && a.k_norm) rms_norm_head(s.ks, a.k_norm, hd, a.eps);
+        for (int h = warp; h <= G; h += kCW) {
+            if (h < G && a.q_norm) rms_norm_head(s.qs + h * hd, a.q_norm, hd, a.eps);
+            if (h == G && a.k_norm) rms_norm_head(s.ks, a.k_norm, hd, a.eps);
+        }
         bar_consumers();
     }
     if (split == 0) {
@@ -242,6 +247,7 @@ __device__ void attn_item(const AttnParams& a, const AttnSmem& s, int pos, int k
         }
         bar_consumers();
         // online softmax update, warp per head (max-subtracted exp, llama_model.cpp:445-451)
+        static_assert(kStepMaxG <= kCW, "one warp per query head");
         if (warp < G) {
             const float v = lane < n ? s.sc[warp * kStepAttnTile + lane] : -INFINITY;
             const float mt = warp_max(v);
@@ -339,8 +345,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) step_kernel(const __grid_cons
     Ring ring;
     ring.full = reinterpret_cast<uint64_t*>(smem);
     ring.empty = ring.full + kRingDesc;
-    int* flags = reinterpret_cast<int*>(smem + 256);  // [0] abort, [1..] group list
+    int* flags = reinterpret_cast<int*>(smem + kHdrFlags);  // [0] abort, [1..] group list
     GemvParams* gp = reinterpret_cast<GemvParams*>(smem + kParamOff);
+    float* red = reinterpret_cast<float*>(smem + kParamOff + 448);  // 16 floats
     AttnParams* ap = reinterpret_cast<AttnParams*>(smem + kParamOff + 512);
     uint8_t* uni = smem + kStepHdr;
     ring.buf = uni + kStepUnion;
@@ -405,8 +412,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) step_kernel(const __grid_cons
         } else if (kind == PH_GEMV) {
             copy_params(gp, &ph.g, offsetof(GemvParams, vrange));
             const int vbeg = ph.g.vrange[blockIdx.x], vend = ph.g.vrange[blockIdx.x + 1];
-            const float s_in = load_xq(*gp, uni);
-            if (!consume(*gp, vbeg, vend, ring, consumed, head, uni, s_in, abort)) {
+            float s_in = 1.f;
+            if (gp->xq) s_in = load_xq(*gp, uni);
+            else input_prologue(*gp, uni, red);
+            if (!consume(*gp, vbeg, vend, ring, consumed, head, uni, s_in, smem)) {
                 *abort = 1;
                 break;
             }

@@ -9,9 +9,14 @@
 // for a phase boundary; the consumer warps wait for the previous phase on a
 // grid-wide arrival counter (bounded spin) and then run the phase:
 //
-//   EMBED  token row dequant → x, quantised (attn_norm) input of QKV
+//   EMBED  token row dequant → x
 //   GEMV   QKV(+bias) | O(+resid) | gate/up SwiGLU | down(+resid) | LM head+argmax
-//   ATTN   RoPE, Q/K norm, KV store, split attention, quantised output
+//   ATTN   RoPE, Q/K norm, KV store, split attention
+//
+// Every GEMV phase reads its f32 input (the previous phase's output, through
+// L2) and quantises it in shared memory itself, RMSNorm included, so a phase
+// ends with its epilogue stores: no cross-CTA quantisation pass, counters or
+// fences between phases other than the arrival itself.
 //
 // and the CTA that completes the last phase turns the argmax into the next
 // token and advances the position.
@@ -25,7 +30,7 @@ enum StepPhaseKind : int { PH_EMBED = 0, PH_GEMV = 1, PH_ATTN = 2 };
 
 constexpr int kStepMaxG = 8;            // query heads per kv head
 constexpr int kStepAttnTile = 32;       // KV positions per attention tile
-constexpr int kStepHdr = 2048;          // mbarriers, flags, phase parameter copies
+constexpr int kStepHdr = kGemvSmemHdr;  // mbarriers, flags, phase parameter copies, reduction scratch
 constexpr int kStepUnion = 40 * 1024;   // XQ input of a GEMV phase / attention scratch
 constexpr int kStepSmem = 227 * 1024;
 

@@ -23,11 +23,11 @@ def test_library_exports_every_header_symbol():
 def test_row_stride():
     lib = _lib.load()
     assert lib.af_row_stride(12, 4096) == 16 * 144
-    assert lib.af_row_stride(14, 4096) == 2 * 1680 == 16 * 210      # whole groups: no padding
-    assert lib.af_row_stride(14, 11008) == 5 * 1680 + 3 * 208 + 16  # 9040 >= 43 * 210 = 9030
+    assert lib.af_row_stride(14, 4096) == 16 * 210                   # units are whole GGUF blocks
+    assert lib.af_row_stride(14, 11008) == 43 * 210
     assert lib.af_row_stride(12, 100) == 0                           # not a multiple of 256
     assert lib.af_weight_bytes(12, 17, 4096) == 32 * 16 * 144          # whole 16-row tiles
-    assert lib.af_weight_bytes(14, 16, 11008) == 16 * 9040
+    assert lib.af_weight_bytes(14, 16, 11008) == 16 * 43 * 210
     assert lib.af_weight_bytes(3, 16, 4096) == 0
 
 
