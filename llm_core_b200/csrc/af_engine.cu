@@ -515,7 +515,7 @@ cudaError_t build_step(af_engine* e) {
     ENG_TRY(cudaMemcpyAsync(e->d_phases, ph.data(), ph.size() * sizeof(StepPhase), cudaMemcpyHostToDevice,
                             e->stream));
     ENG_TRY(cudaStreamSynchronize(e->stream));
-    e->step_bar = static_cast<unsigned int*>(e->dalloc(64));
+    e->step_bar = static_cast<unsigned int*>(e->dalloc(256));
     StepParams& sp = e->step;
     sp.ph = e->d_phases;
     sp.nph = (int)ph.size();

@@ -317,13 +317,13 @@ __device__ __forceinline__ float2 q6_unit(const uint8_t* u, const XQ6& x, int la
 // f32-input prologue: x (+ pending residual, optionally RMS-normalised)
 // loaded with all NIT float4 loads per thread in flight (norm weights too),
 // then quantised into the shared XQ layout.
-template <int NIT>
+template <int NIT, bool NORM>
 __device__ __forceinline__ void input_prologue_t(const GemvParams& p, uint8_t* xqs, float* red) {
     static_assert(kCT % 16 == 0, "16 consecutive threads own one 64-value group");
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
     const int nvec = p.K / 4;
-    float4 a[NIT], w[NIT];
+    float4 a[NIT], w[NORM ? NIT : 1];
 #pragma unroll
     for (int j = 0; j < NIT; ++j) {
         const int v = j * kCT + tid;
@@ -336,7 +336,7 @@ __device__ __forceinline__ void input_prologue_t(const GemvParams& p, uint8_t* x
             a[j].z += b.z;
             a[j].w += b.w;
         }
-        if (p.norm_w) w[j] = __ldg(reinterpret_cast<const float4*>(p.norm_w) + vc);
+        if (NORM) w[NORM ? j : 0] = __ldg(reinterpret_cast<const float4*>(p.norm_w) + vc);
         if (v >= nvec) a[j] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
     if (p.x_store && blockIdx.x == 0) {
@@ -346,7 +346,7 @@ __device__ __forceinline__ void input_prologue_t(const GemvParams& p, uint8_t* x
             if (v < nvec) reinterpret_cast<float4*>(p.x_store)[v] = a[j];
         }
     }
-    if (p.norm_w) {
+    if (NORM) {
         float ss = 0.f;
 #pragma unroll
         for (int j = 0; j < NIT; ++j) ss += a[j].x * a[j].x + a[j].y * a[j].y + a[j].z * a[j].z + a[j].w * a[j].w;
@@ -360,10 +360,11 @@ __device__ __forceinline__ void input_prologue_t(const GemvParams& p, uint8_t* x
         const float inv_rms = 1.f / sqrtf(tot / (float)p.K + p.eps);
 #pragma unroll
         for (int j = 0; j < NIT; ++j) {
-            a[j].x = w[j].x * (a[j].x * inv_rms);
-            a[j].y = w[j].y * (a[j].y * inv_rms);
-            a[j].z = w[j].z * (a[j].z * inv_rms);
-            a[j].w = w[j].w * (a[j].w * inv_rms);
+            const float4 wj = w[NORM ? j : 0];
+            a[j].x = wj.x * (a[j].x * inv_rms);
+            a[j].y = wj.y * (a[j].y * inv_rms);
+            a[j].z = wj.z * (a[j].z * inv_rms);
+            a[j].w = wj.w * (a[j].w * inv_rms);
         }
     }
 #pragma unroll
@@ -408,20 +409,20 @@ __device__ __forceinline__ void input_prologue_t(const GemvParams& p, uint8_t* x
 // Quantise the f32 input of p into the shared XQ layout (all consumer warps;
 // `red` is kCW floats of shared scratch).  Ends with a consumer barrier.
 __device__ __forceinline__ void input_prologue(const GemvParams& p, uint8_t* xqs, float* red) {
-    switch ((p.K / 4 + kCT - 1) / kCT) {
-        case 1: input_prologue_t<1>(p, xqs, red); break;
-        case 2: input_prologue_t<2>(p, xqs, red); break;
-        case 3: input_prologue_t<3>(p, xqs, red); break;
-        case 4: input_prologue_t<4>(p, xqs, red); break;
-        case 5: input_prologue_t<5>(p, xqs, red); break;
-        case 6: input_prologue_t<6>(p, xqs, red); break;
-        case 7: input_prologue_t<7>(p, xqs, red); break;
-        case 8: input_prologue_t<8>(p, xqs, red); break;
-        case 9: input_prologue_t<9>(p, xqs, red); break;
-        case 10: input_prologue_t<10>(p, xqs, red); break;
-        case 11: input_prologue_t<11>(p, xqs, red); break;
-        default: input_prologue_t<12>(p, xqs, red); break;
+    const int nit = (p.K / 4 + kCT - 1) / kCT;
+#define AF_PRO(N)                                                       \
+    case N:                                                             \
+        if (p.norm_w) input_prologue_t<N, true>(p, xqs, red);           \
+        else input_prologue_t<N, false>(p, xqs, red);                   \
+        break;
+    switch (nit) {
+        AF_PRO(1) AF_PRO(2) AF_PRO(3) AF_PRO(4) AF_PRO(5) AF_PRO(6)
+        AF_PRO(7) AF_PRO(8) AF_PRO(9) AF_PRO(10) AF_PRO(11)
+        default:
+            if (p.norm_w) input_prologue_t<12, true>(p, xqs, red);
+            else input_prologue_t<12, false>(p, xqs, red);
     }
+#undef AF_PRO
     bar_consumers();
 }
 

@@ -25,15 +25,20 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
     return v;
 }
 
-__device__ __forceinline__ unsigned atom_add_acq_rel(unsigned* p, unsigned v) {
-    unsigned old;
-    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-    return old;
+// Grid-wide phase arrivals: one release-reduction per CTA per phase on a
+// counter that the waiters poll with acquire loads (a single L2 round trip
+// on each side; no fence, no returned atomic on the critical path).
+__device__ __forceinline__ void red_release(unsigned* p, unsigned v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Consumer threads: wait until every CTA has arrived `target` times in total.
+// Thread 0: count this CTA's arrival (its stores of the phase, ordered
+// before by the consumer barrier, are released with it).
+__device__ __forceinline__ void grid_arrive(unsigned* bar) { red_release(bar, 1u); }
+
+// Consumer threads: wait until `target` arrivals have been counted.
 // Thread 0 spins (bounded) and the consumer barrier publishes the result.
-__device__ bool grid_wait(const unsigned* bar, unsigned target, volatile int* flags) {
+__device__ bool grid_wait(unsigned* bar, unsigned target, volatile int* flags) {
     if (threadIdx.x == 0) {
         bool ok = false;
         for (uint32_t i = 0; i < kGridSpinLimit; ++i) {
@@ -433,22 +438,28 @@ __global__ void __launch_bounds__(kGemvThreads, 1) step_kernel(const __grid_cons
         }
         // arrive: every store of this phase by this CTA happens before the count
         bar_consumers();
-        if (threadIdx.x == 0) {
-            __threadfence();
-            const unsigned old = atom_add_acq_rel(sp.bar, 1u);
-            if (i == sp.nph - 1 && old == (unsigned)sp.nph * grid - 1u) {
-                // last arrival of the step: argmax key -> next token, pos + 1
-                const unsigned long long k = __ldcg(sp.key);
-                int id = (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
-                if (k == 0ull || id < 0 || id >= sp.vocab) {  // no finite logit reached the argmax
-                    set_err(kErrBadToken);
-                    id = 0;
-                }
-                *sp.token = id;
-                if (sp.hist) sp.hist[pos] = id;
-                *sp.pos = pos + 1;
-            }
+        if (threadIdx.x == 0) grid_arrive(sp.bar);
+    }
+    // CTA 0 turns the step's argmax into the next token once every CTA has
+    // finished the LM head, and advances the position.
+    if (blockIdx.x == 0 && threadIdx.x == 0 && !*abort) {
+        const unsigned target = (unsigned)sp.nph * grid;
+        uint32_t it = 0;
+        while (ld_acquire(sp.bar) < target && ++it < kGridSpinLimit) {
         }
+        if (it >= kGridSpinLimit) {
+            set_err(kErrMbarTimeout);
+            return;
+        }
+        const unsigned long long k = __ldcg(sp.key);
+        int id = (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
+        if (k == 0ull || id < 0 || id >= sp.vocab) {  // no finite logit reached the argmax
+            set_err(kErrBadToken);
+            id = 0;
+        }
+        *sp.token = id;
+        if (sp.hist) sp.hist[pos] = id;
+        *sp.pos = pos + 1;
     }
 }
 

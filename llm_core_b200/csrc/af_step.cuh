@@ -18,8 +18,8 @@
 // ends with its epilogue stores: no cross-CTA quantisation pass, counters or
 // fences between phases other than the arrival itself.
 //
-// and the CTA that completes the last phase turns the argmax into the next
-// token and advances the position.
+// and CTA 0, once every CTA has finished the last phase, turns the argmax
+// into the next token and advances the position.
 #pragma once
 #include "af_gemv.cuh"
 #include "af_ops.cuh"
@@ -43,7 +43,7 @@ struct StepPhase {
 struct StepParams {
     const StepPhase* ph;  // device array
     int nph;
-    unsigned int* bar;    // grid arrival counter, zero at launch
+    unsigned int* bar;    // grid arrival counter, zeroed at launch
     // embedding
     const uint8_t* tok_w;
     int tok_type, tok_stride, n_embd, vocab;
