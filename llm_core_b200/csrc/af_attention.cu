@@ -244,10 +244,10 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
     }
     if (tid == 0) p.counter[kvh] = 0u;
     if (p.xq_out) {
-        // quantise this kv head's G*hd outputs (whole 64-value groups) for the O projection
+        // quantise this kv head's G*hd outputs (whole 16-value groups) for the O projection
         __threadfence();
         __syncthreads();
-        const int g0 = kvh * G * hd / 64, ng = G * hd / 64;
+        const int g0 = kvh * G * hd / 32, ng = G * hd / 32;  // 32-value warp groups
         for (int k = warp; k < ng; k += kAttnThreads / 32)
             xq_quantize_group(p.xq_out, p.out, nullptr, p.n_heads * hd, g0 + k);
     }

@@ -91,7 +91,6 @@ struct af_engine {
     float *kcache = nullptr, *vcache = nullptr, *cos_t = nullptr, *sin_t = nullptr, *apart = nullptr;
     unsigned int* acount = nullptr;
     uint8_t *xq_a = nullptr, *xq_o = nullptr, *xq_gu = nullptr, *xq_d = nullptr;  // quantised GEMV inputs
-    unsigned int *cnt_e = nullptr, *cnt_f = nullptr;  // per-64-group arrival counters
     unsigned long long* key = nullptr;
     int* tokpos = nullptr;  // [0] token, [1] pos
     int* hist = nullptr;
@@ -309,7 +308,6 @@ cudaError_t enqueue_step(af_engine* e, Prof* prof = nullptr) {
                 p.xq = e->xq_o;
                 p.q_out = e->xq_gu;
                 p.q_norm_w = L.ffn_norm;
-                p.q_cnt = e->cnt_e;
             }
             gemv_configure(p, e->gemv_ctas);
             ENG_TRY(gemv_launch(p, e->stream, e->pdl));
@@ -340,7 +338,6 @@ cudaError_t enqueue_step(af_engine* e, Prof* prof = nullptr) {
                 p.xq = e->xq_gu;
                 p.xq_norm = 1;
                 p.q_out = e->xq_d;
-                p.q_cnt = e->cnt_f;
             }
             gemv_configure(p, e->gemv_ctas);
             ENG_TRY(gemv_launch(p, e->stream, e->pdl));
@@ -361,7 +358,6 @@ cudaError_t enqueue_step(af_engine* e, Prof* prof = nullptr) {
                 p.xq = e->xq_d;
                 p.q_out = e->xq_a;
                 p.q_norm_w = l + 1 < c.n_layer ? e->layers[l + 1].attn_norm : e->out_norm;
-                p.q_cnt = e->cnt_e;
             }
             gemv_configure(p, e->gemv_ctas);
             ENG_TRY(gemv_launch(p, e->stream, e->pdl));
@@ -430,8 +426,8 @@ cudaError_t build_step(af_engine* e) {
         q.g.seg[1] = seg_of(L.wk, e->k, L.bk);
         q.g.seg[2] = seg_of(L.wv, e->v, L.bv);
         q.g.nseg = 3;
-        q.g.x = e->x[0];
-        q.g.norm_w = L.attn_norm;
+        q.g.xq = e->xq_a;
+        q.g.xq_norm = 1;
         q.g.epi = EPI_STORE;
         gemv_configure(q.g, e->sms);
         ph.push_back(q);
@@ -461,7 +457,7 @@ cudaError_t build_step(af_engine* e) {
         a.qk_norm_order = c.qk_norm_order;
         a.eps = c.eps;
         a.scale = 1.f / std::sqrt((float)e->hd);
-        a.xq_out = nullptr;
+        a.xq_out = e->xq_o;
         ph.push_back(at);
 
         StepPhase o = {};
@@ -471,7 +467,9 @@ cudaError_t build_step(af_engine* e) {
         o.g.nseg = 1;
         o.g.epi = EPI_RESID;
         o.g.resid = e->x[0];
-        o.g.x = e->attn;
+        o.g.xq = e->xq_o;
+        o.g.q_out = e->xq_gu;
+        o.g.q_norm_w = L.ffn_norm;
         gemv_configure(o.g, e->sms);
         ph.push_back(o);
 
@@ -482,8 +480,9 @@ cudaError_t build_step(af_engine* e) {
         gu.g.seg[1] = seg_of(L.wu, nullptr, nullptr);
         gu.g.nseg = 2;
         gu.g.epi = EPI_SWIGLU;
-        gu.g.x = e->x[0];
-        gu.g.norm_w = L.ffn_norm;
+        gu.g.xq = e->xq_gu;
+        gu.g.xq_norm = 1;
+        gu.g.q_out = e->xq_d;
         gemv_configure(gu.g, e->sms);
         ph.push_back(gu);
 
@@ -494,7 +493,9 @@ cudaError_t build_step(af_engine* e) {
         d.g.nseg = 1;
         d.g.epi = EPI_RESID;
         d.g.resid = e->x[0];
-        d.g.x = e->h;
+        d.g.xq = e->xq_d;
+        d.g.q_out = e->xq_a;
+        d.g.q_norm_w = l + 1 < c.n_layer ? e->layers[l + 1].attn_norm : e->out_norm;
         gemv_configure(d.g, e->sms);
         ph.push_back(d);
     }
@@ -503,8 +504,8 @@ cudaError_t build_step(af_engine* e) {
     lm.g = base_params(e, E);
     lm.g.seg[0] = seg_of(e->output, e->logits, nullptr);
     lm.g.nseg = 1;
-    lm.g.x = e->x[0];
-    lm.g.norm_w = e->out_norm;
+    lm.g.xq = e->xq_a;
+    lm.g.xq_norm = 1;
     lm.g.epi = EPI_ARGMAX;
     lm.g.argmax = e->key;
     lm.g.argmax_base = e->V0;
@@ -526,8 +527,8 @@ cudaError_t build_step(af_engine* e) {
     sp.n_embd = E;
     sp.vocab = c.vocab;
     sp.x = e->x[0];
-    sp.xq = nullptr;  // phases quantise their own f32 inputs
-    sp.xq_norm_w = nullptr;
+    sp.xq = e->xq_a;
+    sp.xq_norm_w = e->layers[0].attn_norm;
     sp.key = e->key;
     sp.token = &e->tokpos[0];
     sp.pos = &e->tokpos[1];
@@ -811,10 +812,6 @@ cudaError_t af_engine_finalize(af_engine* e) {
         ENG_TRY(cudaMemset(e->xq_o, 0, xq_norm_bytes(e->Hl * hd)));
         ENG_TRY(cudaMemset(e->xq_gu, 0, xq_norm_bytes(E)));
         ENG_TRY(cudaMemset(e->xq_d, 0, xq_norm_bytes(e->Fl)));
-        e->cnt_e = static_cast<unsigned int*>(e->dalloc((size_t)E / 64 * 4));
-        e->cnt_f = static_cast<unsigned int*>(e->dalloc((size_t)e->Fl / 64 * 4));
-        ENG_TRY(cudaMemset(e->cnt_e, 0, (size_t)E / 64 * 4));
-        ENG_TRY(cudaMemset(e->cnt_f, 0, (size_t)e->Fl / 64 * 4));
         e->key = static_cast<unsigned long long*>(e->dalloc(8));
         e->tokpos = static_cast<int*>(e->dalloc(8));
         e->hist = static_cast<int*>(e->dalloc((size_t)(c.n_ctx + 1) * 4));

@@ -1,54 +1,53 @@
 // af_gemv.cu — fused dequant GEMV kernel (see af_gemv.cuh for the design).
+#include <algorithm>
+#include <vector>
+
 #include "af_gemv_dev.cuh"
 
 namespace af {
 
 __device__ int g_err = 0;
 
-// Quantise one 64-value group (lane l holds values 2l, 2l+1) into the XQ
-// layout.  The 16-bit split matches the consumers' integer form:
-// q = rint(v·32639/amax), hi = (q + 128) >> 8, lo = q − 256·hi.  With norm_w,
-// w·v is quantised and Σv² (of the un-weighted values) stored after the layout.
-__device__ void xq_quantize_vals(uint8_t* xq, float a0, float a1, const float* norm_w, int K, int g) {
+// Quantise value v (index idx = 32·g + lane) into the XQ layout.  The 16-bit
+// split matches the consumers' integer form: q = rint(v·32639/amax),
+// hi = (q + 128) >> 8, lo = q − 256·hi.
+__device__ void xq_store32(uint8_t* xq, float v, const float* norm_w, int K, int idx) {
+    const bool in = idx >= 0 && idx < K;
+    xq_store32w(xq, v, norm_w && in ? __ldg(norm_w + idx) : 1.f, norm_w != nullptr, K, idx);
+}
+
+__device__ void xq_store32w(uint8_t* xq, float v, float wgt, bool norm, int K, int idx) {
     const int lane = threadIdx.x & 31;
-    const int v0 = 64 * g + 2 * lane;
-    float ss = a0 * a0 + a1 * a1;
-    if (norm_w) {
-        a0 *= __ldg(norm_w + v0);
-        a1 *= __ldg(norm_w + v0 + 1);
-    }
-    const float amax = warp_max(fmaxf(fabsf(a0), fabsf(a1)));
+    const bool in = idx >= 0 && idx < K;
+    if (!in) v = 0.f;
+    const float a = v * wgt;
+    const float amax = warp_max(fabsf(a));
     const float inv = amax > 0.f ? 32639.f / amax : 0.f;
-    const int q0 = max(-32639, min(32639, __float2int_rn(a0 * inv)));
-    const int q1 = max(-32639, min(32639, __float2int_rn(a1 * inv)));
-    const int h0 = (q0 + 128) >> 8, h1 = (q1 + 128) >> 8;
-    const int l0 = q0 - 256 * h0, l1 = q1 - 256 * h1;
-    uint8_t* sb = xq + (v0 >> 8) * kXqSb;
-    const int ko = v0 & 255;
-    *reinterpret_cast<uint16_t*>(sb + ko) = (uint16_t)((h0 & 0xFF) | ((h1 & 0xFF) << 8));
-    *reinterpret_cast<uint16_t*>(sb + 256 + ko) = (uint16_t)((l0 & 0xFF) | ((l1 & 0xFF) << 8));
-    float fs = a0 + a1;
-    int is = q0 + q1;
+    const int q = max(-32639, min(32639, __float2int_rn(a * inv)));
+    const int hi = (q + 128) >> 8, lo = q - 256 * hi;
+    int is = q;
 #pragma unroll
-    for (int o = 1; o < 8; o <<= 1) {
-        fs += __shfl_xor_sync(0xffffffffu, fs, o);
-        is += __shfl_xor_sync(0xffffffffu, is, o);
-    }
-    fs += __shfl_xor_sync(0xffffffffu, fs, 8);  // 16 lanes = 32 values
-    if ((lane & 7) == 0) reinterpret_cast<int*>(sb + kXqI16)[ko >> 4] = is;
-    if ((lane & 15) == 0) reinterpret_cast<float*>(sb + kXqS32)[ko >> 5] = fs;
-    if (lane == 0) reinterpret_cast<float*>(sb + kXqXs)[ko >> 6] = amax / 32639.f;
-    if (norm_w) {
-        ss = warp_sum(ss);
-        if (lane == 0) reinterpret_cast<float*>(xq + xq_bytes(K))[g] = ss;
+    for (int o = 1; o < 16; o <<= 1) is += __shfl_xor_sync(0xffffffffu, is, o);  // per 16
+    const float fs = warp_sum(a);
+    const float ss = norm ? warp_sum(v * v) : 0.f;
+    if (!in) return;
+    uint8_t* sb = xq + (idx >> 8) * kXqSb;
+    const int ko = idx & 255;
+    sb[ko] = (uint8_t)(hi & 0xFF);
+    sb[256 + ko] = (uint8_t)(lo & 0xFF);
+    if ((lane & 15) == 0) reinterpret_cast<int*>(sb + kXqI16)[ko >> 4] = is;
+    if (lane == 0) {
+        reinterpret_cast<float*>(sb + kXqXs)[ko >> 5] = amax / 32639.f;
+        reinterpret_cast<float*>(sb + kXqS32)[ko >> 5] = fs;
+        if (norm) reinterpret_cast<float*>(xq + xq_bytes(K))[idx >> 5] = ss;
     }
 }
 
-// One warp quantises 64-value group g of src (global f32, written by other
-// CTAs: read through L2).
+// One warp quantises values [32·g, 32·g + 32) of src (global f32, written by
+// other CTAs: read through L2).
 __device__ void xq_quantize_group(uint8_t* xq, const float* src, const float* norm_w, int K, int g) {
-    const int v0 = 64 * g + 2 * (threadIdx.x & 31);
-    xq_quantize_vals(xq, __ldcg(src + v0), __ldcg(src + v0 + 1), norm_w, K, g);
+    const int idx = 32 * g + (threadIdx.x & 31);
+    xq_store32(xq, idx < K ? __ldcg(src + idx) : 0.f, norm_w, K, idx);
 }
 
 namespace {
@@ -59,7 +58,7 @@ __global__ void xq_quantize_kernel(uint8_t* xq, const float* x, const float* nor
     pdl_launch_dependents();
     pdl_wait();
     const int g = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
-    if (g < K / 64) xq_quantize_group(xq, x, norm_w, K, g);
+    if (g < (K + 31) / 32) xq_quantize_group(xq, x, norm_w, K, g);
 }
 
 __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_constant__ GemvParams p) {
@@ -111,7 +110,6 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
     int head = 0;
     const bool ok = consume(p, vbeg, vend, ring, consumed, head, xqs, s_in, smem);
     if (!ok) *abort = 1;
-    if (p.q_out) quantise_output(p, vbeg, vend, flags + 1);
 }
 
 }  // namespace
@@ -119,34 +117,27 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
 void gemv_configure(GemvParams& p, int grid) {
     // the rest of the 227 KB after the header, the XQ input and 256 B of scratch
     p.ring_bytes = (227 * 1024 - kGemvSmemHdr - xq_norm_bytes(p.K) - 256) & ~15;
-    // CTA tile ranges balanced by weight bytes (a gate/up pair is one virtual tile)
     grid = grid < 1 ? 1 : (grid > kGemvMaxGrid ? kGemvMaxGrid : grid);
     p.grid = grid;
+    // Fragment sizes in the order the kernel walks them (see FragIter), then
+    // CTA ranges balanced by weight bytes at fragment boundaries.
     const bool sw = p.epi == EPI_SWIGLU;
-    const int nvs = sw ? 1 : p.nseg;
-    long long total = 0;
-    long long tb[3], tiles[3];
-    for (int s = 0; s < nvs; ++s) {
-        const long long rs = sw ? (long long)p.seg[0].row_stride + p.seg[1].row_stride : p.seg[s].row_stride;
-        tb[s] = rs * kPackTile;
-        tiles[s] = (p.seg[s].rows + kPackTile - 1) / kPackTile;
-        total += tb[s] * tiles[s];
+    std::vector<long long> fb;
+    for (int s = 0; s < (sw ? 1 : p.nseg); ++s) {
+        const int tiles = (p.seg[s].rows + kPackTile - 1) / kPackTile;
+        const long long tb = (long long)kPackTile * p.seg[s].row_stride * (sw ? 2 : 1);
+        for (int t = 0; t < tiles; t += kGemvFragTiles) fb.push_back(tb * std::min(kGemvFragTiles, tiles - t));
     }
-    for (int i = 0; i <= grid; ++i) {
-        long long b = total * i / grid, base = 0;
-        int v = 0;
-        for (int s = 0; s < nvs; ++s) {
-            const long long segb = tb[s] * tiles[s];
-            if (b <= segb || s == nvs - 1) {
-                long long t = (b + tb[s] / 2) / tb[s];  // nearest tile boundary
-                if (t > tiles[s]) t = tiles[s];
-                v = (int)(base + t);
-                break;
-            }
-            b -= segb;
-            base += tiles[s];
-        }
-        p.vrange[i] = i == 0 ? 0 : (v < p.vrange[i - 1] ? p.vrange[i - 1] : v);
+    std::vector<long long> pre(fb.size() + 1, 0);
+    for (size_t i = 0; i < fb.size(); ++i) pre[i + 1] = pre[i] + fb[i];
+    const long long total = pre.back();
+    size_t f = 0;
+    p.vrange[0] = 0;
+    for (int i = 1; i <= grid; ++i) {
+        const long long target = total * i / grid;
+        // nearest fragment boundary at or after the previous one
+        while (f < fb.size() && pre[f + 1] - target < target - pre[f]) ++f;
+        p.vrange[i] = i == grid ? (int)fb.size() : (int)f;
     }
 }
 
@@ -171,7 +162,7 @@ cudaError_t gemv_launch(const GemvParams& p, cudaStream_t stream, bool pdl) {
 
 cudaError_t xq_quantize_launch(uint8_t* xq, const float* x, const float* norm_w, int K, cudaStream_t st, bool pdl) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((K / 64 + 3) / 4);
+    cfg.gridDim = dim3(((K + 31) / 32 + 3) / 4);
     cfg.blockDim = dim3(128);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];

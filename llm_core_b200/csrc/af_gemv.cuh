@@ -12,7 +12,7 @@
 //    accumulators): every lane fetches its A fragments with 16-byte shared
 //    loads.  A tile (16 rows) is its units in K order, so a K stage of a tile
 //    is one contiguous bulk copy.
-//  * The input x is quantised per 64 values to a 16-bit grid
+//  * The input x is quantised per 32 values to a 16-bit grid
 //    x ≈ xs·(256·hi + lo) (two int8 planes).  Each mma multiplies 16 rows ×
 //    32 values of nibbles (or 6-bit values) by a block-diagonal B whose column
 //    pairs hold the hi / lo planes of one 32-value sub-block (Q4_K) or 16-value
@@ -21,22 +21,27 @@
 //    apply.  Scales are applied in f32 — the same w = d·sc·q − dmin·m (Q4_K)
 //    and w = d·sc·(q − 32) (Q6_K) the reference dequantises.
 //  * Grid = one CTA per SM.  Each CTA owns a byte-balanced contiguous range of
-//    16-row tiles (computed on the host) and walks it in fragments of two
-//    tiles (SwiGLU: the gate and up tile of the same rows).
+//    fragments (computed on the host): two 16-row tiles starting at an even
+//    tile, i.e. 32 output rows (SwiGLU: the gate and the up tiles of the same
+//    32 rows).
 //  * One producer thread streams every (fragment, 8-super-block K stage)
 //    entry into a byte ring in shared memory with cp.async.bulk (the TMA
 //    engine, no tensor map, no multicast), completion counted on an mbarrier,
 //    L2 evict-first.  Weights do not depend on the previous kernel, so the
 //    producer never waits for it.
-//  * 8 consumer warps: warp w evaluates super-block w of every stage for both
+//  * 8 consumer warps: warp w evaluates super-block w of every stage for all
 //    tiles of the fragment, accumulating per row in registers across stages;
 //    at the end of a fragment the 8 warps' row sums are added in a fixed
-//    order through shared memory (deterministic) and the epilogue runs: plain
-//    store (+bias), in-place residual add, SwiGLU of a gate/up pair, LM-head
-//    logits with a fused first-max argmax.
-//  * The input arrives either as an f32 vector the consumers quantise in
-//    shared memory (RMSNorm folded in), or already quantised ("XQ") by the
-//    kernel that produced it.
+//    order through shared memory (deterministic) and one warp (the duty
+//    rotates) runs the epilogue for the fragment's 32 rows: plain store
+//    (+bias), in-place residual add, SwiGLU of a gate/up pair, LM-head logits
+//    with a fused first-max argmax.
+//  * The input arrives either quantised ("XQ") or as an f32 vector the
+//    consumers quantise in shared memory (RMSNorm folded in).  The GEMV that
+//    produces a vector quantises each finished 32-row fragment in its
+//    epilogue (RMSNorm-weighted for the next GEMV where it normalises), so the
+//    consumer of the vector only copies it: no cross-CTA pass, counters or
+//    second read of the f32 vector.
 //  * The same building blocks (af_gemv_dev.cuh) run inside the persistent
 //    decode-step kernel (af_step.cu), where the ring persists across phases.
 #pragma once
@@ -50,11 +55,11 @@ enum GemvEpi : int { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_RESID = 2, EPI_ARGMAX = 
 constexpr int kGemvConsumerWarps = 8;
 constexpr int kGemvThreads = (kGemvConsumerWarps + 1) * 32;
 constexpr int kPackTile = 16;        // rows per tile of the packed weight layout
-constexpr int kGemvFragTiles = 2;    // tiles per fragment
+constexpr int kGemvFragTiles = 2;    // tiles per fragment (per gate / up part)
 constexpr int kGemvStageBlocks = 8;  // super-blocks per K stage (one per consumer warp)
 constexpr int kGemvMaxK = 12288;     // input length quantised by the f32 prologue
 constexpr int kGemvMaxGrid = 296;
-constexpr int kGemvSmemHdr = 4096;   // mbarriers, abort flag, group list, phase parameters, reduction scratch
+constexpr int kGemvSmemHdr = 6144;   // mbarriers, abort flag, phase parameters, reduction scratch
 
 static_assert(kGemvStageBlocks == kGemvConsumerWarps, "one super-block per consumer warp");
 
@@ -102,13 +107,13 @@ struct GemvParams {
     unsigned long long* argmax;  // EPI_ARGMAX: packed (value, ~index) maximum
     int argmax_base;       // global index of row 0 (vocab shard offset)
     // optional: quantise the output vector (resid for EPI_RESID, y_0 otherwise)
-    // into q_out for the next GEMV, with RMSNorm weights q_norm_w (NULL: plain)
+    // into q_out (XQ of the next GEMV), weighted by q_norm_w when set, with
+    // the per-16 sums of squares for that GEMV's RMSNorm
     uint8_t* q_out;
     const float* q_norm_w;
-    unsigned int* q_cnt;   // per-64-row-group arrival counters, zero between launches
     int ring_bytes;        // weight ring in shared memory (multiple of 16)
     int grid;
-    int vrange[kGemvMaxGrid + 1];  // CTA i owns virtual tiles [vrange[i], vrange[i+1])
+    int vrange[kGemvMaxGrid + 1];  // CTA i owns fragments [vrange[i], vrange[i+1])
 };
 
 __host__ __device__ inline int dev_row_stride(int type, int cols) {
@@ -122,12 +127,13 @@ __host__ __device__ inline size_t packed_bytes(int type, int rows, int cols) {
 
 // Quantised-input (XQ) layout for K values, per 256-value super-block
 // (kXqSb bytes): hi plane [256] int8, lo plane [256] int8 (value order), then
-// xs[4] f32 (per 64 values), sum32[8] f32 (Σx per 32), isum16[16] int32
-// (Σ 256·hi + lo per 16).  A normalised input appends K/64 f32 sums of squares.
-constexpr int kXqSb = 512 + 16 + 32 + 64;
-constexpr int kXqXs = 512, kXqS32 = 528, kXqI16 = 560;
+// xs[8] f32 and sum32[8] f32 (Σx) per 32-value group, isum16[16] int32
+// (Σ 256·hi + lo per 16 values).  A normalised input appends K/32 f32 sums of
+// squares of the un-weighted values.
+constexpr int kXqSb = 512 + 32 + 32 + 64;
+constexpr int kXqXs = 512, kXqS32 = 544, kXqI16 = 576;
 __host__ __device__ inline int xq_bytes(int K) { return (K / 256) * kXqSb; }
-__host__ __device__ inline int xq_norm_bytes(int K) { return xq_bytes(K) + K / 16; }
+__host__ __device__ inline int xq_norm_bytes(int K) { return xq_bytes(K) + K / 8; }
 
 // Shared-memory bytes of the standalone GEMV: header, ring, XQ input, misc.
 __host__ __device__ inline int gemv_smem_bytes(int K, int ring_bytes) {
@@ -145,10 +151,14 @@ cudaError_t gemv_launch(const GemvParams& p, cudaStream_t stream, bool pdl);
 // form, for inputs no producing kernel writes.
 cudaError_t xq_quantize_launch(uint8_t* xq, const float* x, const float* norm_w, int K, cudaStream_t st, bool pdl);
 
-// One warp quantises 64-value group g of src (global f32) into the XQ buffer;
-// with norm_w, w·x is quantised and Σx² stored after the layout.
+// Quantise value v (this lane's; the warp's 32 lanes hold one 32-value group,
+// indices idx = 32·g + lane) into the XQ buffer.  With norm_w the weighted
+// value w·v is quantised and Σv² of the group stored after the layout.  All
+// 32 lanes must call (lanes past the vector pass any v; they store nothing).
+__device__ void xq_store32(uint8_t* xq, float v, const float* norm_w, int K, int idx);
+// Same with the lane's RMSNorm weight already loaded (norm: store Σv²).
+__device__ void xq_store32w(uint8_t* xq, float v, float wgt, bool norm, int K, int idx);
+// One warp quantises values [32·g, 32·g + 32) of src (global f32).
 __device__ void xq_quantize_group(uint8_t* xq, const float* src, const float* norm_w, int K, int g);
-// Same, from values already in registers: lane l holds group values 2l, 2l+1.
-__device__ void xq_quantize_vals(uint8_t* xq, float a0, float a1, const float* norm_w, int K, int g);
 
 }  // namespace af

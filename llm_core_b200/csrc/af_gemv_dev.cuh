@@ -22,61 +22,59 @@ constexpr int kCT = kCW * 32;
 constexpr int kRingDesc = 8;  // entries in flight at most
 
 // Shared-memory header of the GEMV kernels (kGemvSmemHdr bytes).
-constexpr int kHdrFlags = 256;    // int[0] abort, [1..] group list
-constexpr int kHdrRed = 2048;     // [2 buffers][2 tiles][kCW warps][16 rows] f32
-static_assert(kHdrRed + 2 * 2 * kCW * 16 * 4 <= kGemvSmemHdr, "GEMV header overflow");
-constexpr int kGroupListMax = (1024 - kHdrFlags) / 4 - 2;  // groups one CTA can complete
+constexpr int kHdrFlags = 256;    // int[0] abort
+constexpr int kFragUnits = 2 * kGemvFragTiles;  // units of a fragment at most (SwiGLU)
+constexpr int kHdrRed = 2048;     // [2 buffers][kFragUnits][kCW warps][16 rows] f32
+static_assert(kHdrRed + 2 * kFragUnits * kCW * 16 * 4 <= kGemvSmemHdr, "GEMV header overflow");
 
 // Named barrier 1 over the consumer warps only (the producer never joins).
 __device__ __forceinline__ void bar_consumers() { asm volatile("bar.sync 1, %0;" ::"n"(kCT) : "memory"); }
 
 // ---------------------------------------------------------------- fragments
 
-// Fragment = up to two tiles of one segment (SwiGLU: gate tile t of segment 0
-// and up tile t of segment 1, as one virtual tile).
+// Fragment = up to two consecutive tiles of one segment starting at an even
+// tile (32 output rows); SwiGLU: the same tiles of the gate (segment 0) and
+// the up (segment 1) matrix, streamed gate tiles first.
 struct Frag {
-    int seg;   // segment of tile 0
-    int tile;  // first tile (within the segment)
-    int nt;    // tiles streamed (1 or 2)
+    int seg;    // segment (SwiGLU: 0)
+    int tile;   // first tile within the segment (even)
+    int nt;     // tiles per part (1 or 2)
+    int parts;  // 1, or 2 for SwiGLU (gate, up)
+    __device__ int units() const { return nt * parts; }
 };
 
 __device__ __forceinline__ int seg_tiles(const GemvSeg& s) { return (s.rows + kPackTile - 1) / kPackTile; }
+__device__ __forceinline__ int seg_frags(const GemvSeg& s) { return (seg_tiles(s) + kGemvFragTiles - 1) / kGemvFragTiles; }
 
-// Iterator over [cur, end) of the virtual-tile space: the segments' tiles
-// concatenated (SwiGLU: gate/up tile pairs).
+// Iterator over fragments [cur, end) of the virtual fragment space: the
+// segments' fragments concatenated (SwiGLU: gate/up pairs).
 struct FragIter {
     int cur, end;
     __device__ bool next(const GemvParams& p, Frag& t) {
         if (cur >= end) return false;
-        if (p.epi == EPI_SWIGLU) {
-            t.seg = 0;
-            t.tile = cur;
-            t.nt = 2;
-            cur += 1;
-            return true;
-        }
+        const bool sw = p.epi == EPI_SWIGLU;
         int base = 0, s = 0;
-        for (; s < p.nseg - 1; ++s) {
-            const int n = seg_tiles(p.seg[s]);
-            if (cur < base + n) break;
-            base += n;
+        if (!sw) {
+            for (; s < p.nseg - 1; ++s) {
+                const int n = seg_frags(p.seg[s]);
+                if (cur < base + n) break;
+                base += n;
+            }
         }
-        const int stop = min(min(cur + kGemvFragTiles, end), base + seg_tiles(p.seg[s]));
         t.seg = s;
-        t.tile = cur - base;
-        t.nt = stop - cur;
-        cur = stop;
+        t.tile = (cur - base) * kGemvFragTiles;
+        t.nt = min(kGemvFragTiles, seg_tiles(p.seg[s]) - t.tile);
+        t.parts = sw ? 2 : 1;
+        ++cur;
         return true;
     }
 };
 
-// Segment and tile of tile k of a fragment.
+// Segment and tile of unit k (0 .. units-1) of a fragment.
 __device__ __forceinline__ const GemvSeg& frag_seg(const GemvParams& p, const Frag& t, int k) {
-    return p.seg[p.epi == EPI_SWIGLU ? k : t.seg];
+    return p.seg[t.parts == 2 ? k / t.nt : t.seg];
 }
-__device__ __forceinline__ int frag_tile(const GemvParams& p, const Frag& t, int k) {
-    return p.epi == EPI_SWIGLU ? t.tile : t.tile + k;
-}
+__device__ __forceinline__ int frag_tile(const Frag& t, int k) { return t.tile + k % t.nt; }
 
 __device__ __forceinline__ int ring_place(int& head, int size, int ring_bytes) {
     const int h = head + size > ring_bytes ? 0 : head;
@@ -139,14 +137,14 @@ struct Producer {
             const int ub = unit_bytes(p.seg[t.seg].type);
             for (int st = 0; st < nst; ++st) {
                 const int nbs = min(kGemvStageBlocks, nb - st * kGemvStageBlocks);
-                const int bytes = t.nt * nbs * ub;
+                const int bytes = t.units() * nbs * ub;
                 int at;
                 if (*abort || !reserve(r, bytes, at, abort)) return false;
                 uint64_t* bar = &r.full[issued % kRingDesc];
                 mbar_arrive_expect_tx(bar, (uint32_t)bytes);
-                for (int k = 0; k < t.nt; ++k) {
+                for (int k = 0; k < t.units(); ++k) {
                     const GemvSeg& g = frag_seg(p, t, k);
-                    const uint8_t* src = g.w + (size_t)frag_tile(p, t, k) * kPackTile * g.row_stride +
+                    const uint8_t* src = g.w + (size_t)frag_tile(t, k) * kPackTile * g.row_stride +
                                          (size_t)st * kGemvStageBlocks * ub;
                     bulk_g2s(r.buf + at + k * nbs * ub, src, (uint32_t)(nbs * ub), bar, pol);
                 }
@@ -176,27 +174,34 @@ __device__ __forceinline__ void mma_u8s8(int (&c)[4], uint32_t a0, uint32_t a1, 
 
 __device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
 
+// Exact int -> float for |v| < 2^22 on the FMA / ALU pipes (no conversion
+// unit): the integer lands in the mantissa of 1.5·2^23.
+__device__ __forceinline__ float i2f_small(int v) {
+    return __int_as_float(0x4B400000 + v) - 12582912.f;
+}
+
 // The lane's share of one super-block of the quantised input, Q4_K form.
 // Lane (g, t): B column g = (sub-block slot g/2, plane g%2); it supplies the
-// plane's words of sub-blocks g/2 (a) and 4 + g/2 (b).
+// plane's words of sub-blocks g/2 and 4 + g/2.  Its outputs (C slot t of the
+// two accumulators) are sub-blocks t and 4 + t.
 struct XQ4 {
     uint32_t a0, a1, b0, b1;
-    float xs0, xs1;  // xs of the chunks of this lane's output sub-blocks t and 4+t (1/16 folded in for odd t)
+    float xs0, xs1;  // xs of sub-blocks t and 4+t (1/16 folded in for odd t: high nibbles)
     float s0, s1;    // Σx of sub-blocks t and 4+t
 };
 __device__ __forceinline__ XQ4 load_xq4(const uint8_t* xsb, int lane, float s_in) {
     const int g = lane >> 2, t = lane & 3, m = g >> 1;
     const uint32_t* X = reinterpret_cast<const uint32_t*>(xsb + (g & 1) * 256);
+    const float* XS = reinterpret_cast<const float*>(xsb + kXqXs);
+    const float* S32 = reinterpret_cast<const float*>(xsb + kXqS32);
     XQ4 x;
     x.a0 = X[8 * m + t];
     x.a1 = X[8 * m + 4 + t];
     x.b0 = X[8 * (m + 4) + t];
     x.b1 = X[8 * (m + 4) + 4 + t];
-    const float* XS = reinterpret_cast<const float*>(xsb + kXqXs);
-    const float* S32 = reinterpret_cast<const float*>(xsb + kXqS32);
-    const float f = (t & 1) ? s_in * 0.0625f : s_in;  // odd sub-blocks are high nibbles (×16)
-    x.xs0 = XS[t >> 1] * f;
-    x.xs1 = XS[2 + (t >> 1)] * f;
+    const float f = (t & 1) ? s_in * 0.0625f : s_in;
+    x.xs0 = XS[t] * f;
+    x.xs1 = XS[4 + t] * f;
     x.s0 = S32[t] * s_in;
     x.s1 = S32[4 + t] * s_in;
     return x;
@@ -226,26 +231,27 @@ __device__ __forceinline__ float2 q4_unit(const uint8_t* u, const XQ4& x, int la
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
         const uint4 h = lds128(u + kQ4Hdr + (g + 8 * r) * 16);
-        // exact integer dots Σ q·(256·hi + lo) of sub-blocks t and 4+t
-        const int T0 = C0[2 * r] * 256 + C0[2 * r + 1];
-        const int T1 = C1[2 * r] * 256 + C1[2 * r + 1];
+        // exact integer dots Σ q·(256·hi + lo) of sub-blocks t and 4+t, as f32
+        const float T0 = fmaf(256.f, i2f_small(C0[2 * r]), i2f_small(C0[2 * r + 1]));
+        const float T1 = fmaf(256.f, i2f_small(C1[2 * r]), i2f_small(C1[2 * r + 1]));
         const uint32_t w0 = h.y >> sh, w1 = h.z >> sh, w2 = h.w >> sh;
-        const int sc0 = w0 & 63, m0 = w1 & 63;
-        const int sc1 = (w2 & 0xF) | ((w0 >> 2) & 0x30), m1 = ((w2 >> 4) & 0xF) | ((w1 >> 2) & 0x30);
+        const float sc0 = i2f_small(w0 & 63), m0 = i2f_small(w1 & 63);
+        const float sc1 = i2f_small((w2 & 0xF) | ((w0 >> 2) & 0x30));
+        const float m1 = i2f_small(((w2 >> 4) & 0xF) | ((w1 >> 2) & 0x30));
         const float d = half_bits_to_float(h.x & 0xFFFFu), dmin = half_bits_to_float(h.x >> 16);
-        y[r] = d * (x.xs0 * ((float)sc0 * (float)T0) + x.xs1 * ((float)sc1 * (float)T1)) -
-               dmin * ((float)m0 * x.s0 + (float)m1 * x.s1);
+        y[r] = d * fmaf(x.xs0 * sc0, T0, x.xs1 * sc1 * T1) - dmin * fmaf(m0, x.s0, m1 * x.s1);
     }
     return make_float2(y[0], y[1]);
 }
 
-// The lane's share of one super-block, Q6_K form: B column g = (16-value group
-// slot g/2, plane g%2); slot s of tile pair P is tile 2P + s/2, group s%2, so
-// the lane supplies group (g/2)%2 of tiles g/4 + 2i.
+// The lane's share of one super-block, Q6_K form: B column g = (16-value
+// group slot g/2, plane g%2); slot s of tile pair P is tile 2P + s/2, group
+// s%2, so the lane supplies group (g/2)%2 of tiles g/4 + 2i.  Its outputs (C
+// slot t of tile pair P) are group 4P + t, in tile 2P + t/2.
 struct XQ6 {
     uint32_t w[4];
-    float xs[4];   // per 64 values (tile pair)
-    int is16[4];   // Σ(256·hi + lo) of this lane's output groups 4P + t
+    float xs[4];   // xs of tile 2P + t/2
+    float is32[4]; // 32·Σ(256·hi + lo) of group 4P + t
 };
 __device__ __forceinline__ XQ6 load_xq6(const uint8_t* xsb, int lane, float s_in) {
     const int g = lane >> 2, t = lane & 3, m = g >> 1;
@@ -257,8 +263,8 @@ __device__ __forceinline__ XQ6 load_xq6(const uint8_t* xsb, int lane, float s_in
     for (int i = 0; i < 4; ++i) {
         const int j = (m >> 1) + 2 * i;
         x.w[i] = X[8 * j + 4 * (m & 1) + t];
-        x.xs[i] = XS[i] * s_in;
-        x.is16[i] = I16[4 * i + t];
+        x.xs[i] = XS[2 * i + (t >> 1)] * s_in;
+        x.is32[i] = 32.f * i2f_small(I16[4 * i + t]);
     }
     return x;
 }
@@ -303,9 +309,10 @@ __device__ __forceinline__ float2 q6_unit(const uint8_t* u, const XQ6& x, int la
         float acc = 0.f;
 #pragma unroll
         for (int P = 0; P < 4; ++P) {
-            const int T = C[P][2 * r] * 256 + C[P][2 * r + 1] - 32 * x.is16[P];  // Σ (q − 32)·xint
-            const int sc = (int)(int8_t)((sw[P] >> (8 * t)) & 0xFF);
-            acc = fmaf(x.xs[P], (float)sc * (float)T, acc);
+            // Σ (q − 32)·xint, exact in f32 (< 2^24)
+            const float T = fmaf(256.f, i2f_small(C[P][2 * r]), i2f_small(C[P][2 * r + 1])) - x.is32[P];
+            const float sc = i2f_small((int)(int8_t)((sw[P] >> (8 * t)) & 0xFF));
+            acc = fmaf(x.xs[P] * sc, T, acc);
         }
         y[r] = d * acc;
     }
@@ -319,7 +326,7 @@ __device__ __forceinline__ float2 q6_unit(const uint8_t* u, const XQ6& x, int la
 // then quantised into the shared XQ layout.
 template <int NIT, bool NORM>
 __device__ __forceinline__ void input_prologue_t(const GemvParams& p, uint8_t* xqs, float* red) {
-    static_assert(kCT % 16 == 0, "16 consecutive threads own one 64-value group");
+    static_assert(kCT % 8 == 0, "8 consecutive threads own one 32-value group");
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
     const int nvec = p.K / 4;
@@ -371,8 +378,9 @@ __device__ __forceinline__ void input_prologue_t(const GemvParams& p, uint8_t* x
     for (int j = 0; j < NIT; ++j) {
         const int v = j * kCT + tid;
         float amax = fmaxf(fmaxf(fabsf(a[j].x), fabsf(a[j].y)), fmaxf(fabsf(a[j].z), fabsf(a[j].w)));
-#pragma unroll
-        for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));  // 8 threads = 32 values
         // 16-bit grid of ±32639 so that hi = (q + 128) >> 8 stays within int8.
         const float inv = amax > 0.f ? 32639.f / amax : 0.f;
         const float av[4] = {a[j].x, a[j].y, a[j].z, a[j].w};
@@ -390,7 +398,7 @@ __device__ __forceinline__ void input_prologue_t(const GemvParams& p, uint8_t* x
         }
         float fs = a[j].x + a[j].y + a[j].z + a[j].w;
         is += __shfl_xor_sync(0xffffffffu, is, 1);
-        is += __shfl_xor_sync(0xffffffffu, is, 2);
+        is += __shfl_xor_sync(0xffffffffu, is, 2);  // 4 threads = 16 values
         fs += __shfl_xor_sync(0xffffffffu, fs, 1);
         fs += __shfl_xor_sync(0xffffffffu, fs, 2);
         fs += __shfl_xor_sync(0xffffffffu, fs, 4);
@@ -399,9 +407,11 @@ __device__ __forceinline__ void input_prologue_t(const GemvParams& p, uint8_t* x
             const int ko = (4 * v) & 255;
             *reinterpret_cast<uint32_t*>(sb + ko) = hw;
             *reinterpret_cast<uint32_t*>(sb + 256 + ko) = lw;
-            if ((tid & 15) == 0) reinterpret_cast<float*>(sb + kXqXs)[ko >> 6] = amax / 32639.f;
-            if ((tid & 7) == 0) reinterpret_cast<float*>(sb + kXqS32)[ko >> 5] = fs;
             if ((tid & 3) == 0) reinterpret_cast<int*>(sb + kXqI16)[ko >> 4] = is;
+            if ((tid & 7) == 0) {
+                reinterpret_cast<float*>(sb + kXqXs)[ko >> 5] = amax / 32639.f;
+                reinterpret_cast<float*>(sb + kXqS32)[ko >> 5] = fs;
+            }
         }
     }
 }
@@ -452,7 +462,7 @@ __device__ __forceinline__ float load_xq(const GemvParams& p, uint8_t* xqs) {
         // fixed order (deterministic)
         const float* pss = reinterpret_cast<const float*>(xqs + xq_bytes(p.K));
         float ss = 0.f;
-        for (int g = (tid & 31); g < p.K / 64; g += 32) ss += pss[g];
+        for (int g = (tid & 31); g < p.K / 32; g += 32) ss += pss[g];
         ss = warp_sum(ss);
         s_in = 1.f / sqrtf(ss / (float)p.K + p.eps);
     }
@@ -480,17 +490,26 @@ __device__ __forceinline__ bool consume(const GemvParams& p, int vbeg, int vend,
     while (ok && it.next(p, t)) {
         const int type = p.seg[t.seg].type;
         const int ub = unit_bytes(type);
-        // warp 0 owns the epilogue rows: lane = (tile k = lane/16, row lane%16)
+        const int nu = t.units();
+        const bool sw = t.parts == 2;
+        // the epilogue of fragment f is warp f % kCW's (the duty rotates so no
+        // warp lags behind the others); lane l owns output row 32·frag + l,
+        // i.e. row l%16 of unit l/16 (SwiGLU: of gate unit l/16 and up unit 2 + l/16)
+        const bool ew = warp == fcount % kCW;
         const int ek = lane >> 4, er = lane & 15;
-        const GemvSeg& eseg = frag_seg(p, t, ek);
-        const int erow = frag_tile(p, t, ek) * kPackTile + er;
+        const GemvSeg& eseg = p.seg[t.seg];
+        const int erow = (t.tile + ek) * kPackTile + er;
         const bool evalid = ek < t.nt && erow < eseg.rows;
-        float rpre = 0.f;
-        if (warp == 0 && p.epi == EPI_RESID && evalid) rpre = __ldcg(p.resid + erow);  // in flight during the stages
-        float y[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+        // loads the epilogue needs, in flight during the stages
+        float rpre = 0.f, qw = 1.f;
+        if (ew && p.epi == EPI_RESID && evalid) rpre = __ldcg(p.resid + erow);
+        if (ew && p.q_norm_w && evalid) qw = __ldg(p.q_norm_w + erow);
+        float y[kFragUnits][2];
+#pragma unroll
+        for (int k = 0; k < kFragUnits; ++k) y[k][0] = y[k][1] = 0.f;
         for (int st = 0; st < nst; ++st) {
             const int nbs = min(kGemvStageBlocks, nb - st * kGemvStageBlocks);
-            const int at = ring_place(head, t.nt * nbs * ub, r.bytes);
+            const int at = ring_place(head, nu * nbs * ub, r.bytes);
             const uint32_t d = consumed % kRingDesc;
             if (lane == 0) ok = mbar_wait(&r.full[d], (consumed / kRingDesc) & 1u, abort);
             ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -503,23 +522,23 @@ __device__ __forceinline__ bool consume(const GemvParams& p, int vbeg, int vend,
                 const uint8_t* u = r.buf + at + warp * ub;
                 if (type == AF_GGML_Q6_K) {
                     const XQ6 x = load_xq6(xsb, lane, s_in);
-                    const float2 v0 = q6_unit(u, x, lane);
-                    y[0][0] += v0.x;
-                    y[0][1] += v0.y;
-                    if (t.nt > 1) {
-                        const float2 v1 = q6_unit(u + nbs * ub, x, lane);
-                        y[1][0] += v1.x;
-                        y[1][1] += v1.y;
+#pragma unroll
+                    for (int k = 0; k < kFragUnits; ++k) {
+                        if (k < nu) {
+                            const float2 v = q6_unit(u + k * nbs * ub, x, lane);
+                            y[k][0] += v.x;
+                            y[k][1] += v.y;
+                        }
                     }
                 } else {
                     const XQ4 x = load_xq4(xsb, lane, s_in);
-                    const float2 v0 = q4_unit(u, x, lane);
-                    y[0][0] += v0.x;
-                    y[0][1] += v0.y;
-                    if (t.nt > 1) {
-                        const float2 v1 = q4_unit(u + nbs * ub, x, lane);
-                        y[1][0] += v1.x;
-                        y[1][1] += v1.y;
+#pragma unroll
+                    for (int k = 0; k < kFragUnits; ++k) {
+                        if (k < nu) {
+                            const float2 v = q4_unit(u + k * nbs * ub, x, lane);
+                            y[k][0] += v.x;
+                            y[k][1] += v.y;
+                        }
                     }
                 }
             }
@@ -528,32 +547,39 @@ __device__ __forceinline__ bool consume(const GemvParams& p, int vbeg, int vend,
             ++consumed;
         }
         if (!ok) break;
-        // rows g, g+8 of each tile: sum the 4 lanes of a row group, then the
+        // rows g, g+8 of each unit: sum the 4 lanes of a row group, then the
         // 8 warps in a fixed order (deterministic)
-        float* rb = red + (fcount & 1) * 2 * kCW * 16;
+        float* rb = red + (fcount & 1) * kFragUnits * kCW * 16;
 #pragma unroll
-        for (int k = 0; k < 2; ++k)
+        for (int k = 0; k < kFragUnits; ++k)
 #pragma unroll
             for (int rr = 0; rr < 2; ++rr) {
                 float v = y[k][rr];
                 v += __shfl_xor_sync(0xffffffffu, v, 1);
                 v += __shfl_xor_sync(0xffffffffu, v, 2);
-                if ((lane & 3) == 0) rb[(k * kCW + warp) * 16 + (lane >> 2) + 8 * rr] = v;
+                if ((lane & 3) == 0 && k < nu) rb[(k * kCW + warp) * 16 + (lane >> 2) + 8 * rr] = v;
             }
         bar_consumers();
         ++fcount;
-        if (warp == 0) {
-            float v = 0.f;
+        if (ew) {
+            float v = 0.f, vu = 0.f;
 #pragma unroll
             for (int w = 0; w < kCW; ++w) v += rb[(ek * kCW + w) * 16 + er];
-            if (p.epi == EPI_SWIGLU) {
-                const float u = __shfl_down_sync(0xffffffffu, v, 16);  // up row of the same row index
-                if (lane < 16 && evalid) p.seg[0].y[erow] = (v / (1.f + expf(-v))) * u;
-            } else if (evalid) {
-                if (p.epi == EPI_RESID) {
-                    p.resid[erow] = rpre + v;
+            if (sw) {
+#pragma unroll
+                for (int w = 0; w < kCW; ++w) vu += rb[((t.nt + ek) * kCW + w) * 16 + er];
+            }
+            float out = 0.f;  // this lane's output value, quantised for the next GEMV
+            if (evalid) {
+                if (sw) {
+                    out = (v / (1.f + expf(-v))) * vu;
+                    p.seg[0].y[erow] = out;
+                } else if (p.epi == EPI_RESID) {
+                    out = rpre + v;
+                    p.resid[erow] = out;
                 } else {
                     if (eseg.bias) v += eseg.bias[erow];
+                    out = v;
                     eseg.y[erow] = v;
                     if (p.epi == EPI_ARGMAX) {
                         // a lane's rows arrive in increasing order; ties keep the lowest index
@@ -565,9 +591,11 @@ __device__ __forceinline__ bool consume(const GemvParams& p, int vbeg, int vend,
                     }
                 }
             }
+            // the fragment's 32 rows are one 32-value group of q_out
+            if (p.q_out) xq_store32w(p.q_out, out, qw, p.q_norm_w != nullptr, p.seg[0].rows, evalid ? erow : -1);
         }
     }
-    if (p.epi == EPI_ARGMAX && warp == 0) {
+    if (p.epi == EPI_ARGMAX) {
         unsigned long long key = best > -INFINITY ? argmax_key(best, best_idx) : 0ull;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
@@ -577,38 +605,6 @@ __device__ __forceinline__ bool consume(const GemvParams& p, int vbeg, int vend,
         if (lane == 0 && key) atomicMax(p.argmax, key);
     }
     return ok;
-}
-
-// After the epilogue stores of virtual tiles [vbeg, vend): every 64-row
-// output group this CTA completes (per-group arrival counters) is quantised
-// into q_out for the next GEMV.  Consumer warps only; `list` is the header's
-// group list (kGroupListMax + 1 ints).
-__device__ __forceinline__ void quantise_output(const GemvParams& p, int vbeg, int vend, int* list) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int Kout = p.seg[0].rows;
-    const int rbeg = vbeg * kPackTile, rend = min(vend * kPackTile, Kout);
-    if (threadIdx.x == 0) list[0] = 0;
-    bar_consumers();  // every epilogue store of this CTA is done
-    // one thread per touched group: the arrival atomics run in parallel
-    for (int g = rbeg / 64 + threadIdx.x; rend > rbeg && g * 64 < rend; g += kCT) {
-        const int lo = max(rbeg, g * 64), hi = min(rend, g * 64 + 64);
-        __threadfence();
-        const unsigned int prev = atomicAdd(&p.q_cnt[g], (unsigned int)(hi - lo));
-        if (prev + (unsigned int)(hi - lo) == 64u) {
-            const int at = atomicAdd(&list[0], 1);
-            if (at < kGroupListMax) list[1 + at] = g;
-            else set_err(kErrBadArgs);  // more rows per CTA than the list holds
-        }
-    }
-    __threadfence();
-    bar_consumers();
-    const int n = min(list[0], kGroupListMax);
-    const float* src = p.epi == EPI_RESID ? p.resid : p.seg[0].y;
-    for (int k = warp; k < n; k += kCW) {
-        const int gg = list[1 + k];
-        xq_quantize_group(p.q_out, src, p.q_norm_w, Kout, gg);
-        if (lane == 0) p.q_cnt[gg] = 0u;
-    }
 }
 
 }  // namespace gdev

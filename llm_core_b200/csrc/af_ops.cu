@@ -147,11 +147,11 @@ __global__ void embed_kernel(float* __restrict__ x, const uint8_t* __restrict__ 
         x[v] = embed_value(W, type, nb, row_stride, *token, v);
     }
     if (xq) {
-        // quantise this block's 64-value groups for the first GEMV
+        // quantise this block's values (two 16-value groups per warp) for the first GEMV
         __threadfence();
         __syncthreads();
-        const int g = (blockIdx.x * blockDim.x) / 64 + (threadIdx.x >> 5);
-        if ((threadIdx.x >> 5) < (int)blockDim.x / 64 && g < cols / 64) xq_quantize_group(xq, x, xq_norm_w, cols, g);
+        const int g = (blockIdx.x * blockDim.x) / 32 + (threadIdx.x >> 5);
+        if (g < cols / 32) xq_quantize_group(xq, x, xq_norm_w, cols, g);
     }
 }
 

@@ -67,7 +67,7 @@ __device__ __forceinline__ void copy_params(void* dst, const void* src, int byte
 // ------------------------------------------------------------------ embedding
 
 // x = dequant(row token of the embedding) and its quantised, attn_norm-
-// weighted form for the first QKV GEMV: one warp per 64-value group.
+// weighted form for the first QKV GEMV: one warp per 32 values.
 __device__ void embed_phase(const StepParams& sp, int tok) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (blockIdx.x == 0 && threadIdx.x == 0) *sp.key = 0ull;  // argmax of this step starts empty
@@ -75,27 +75,31 @@ __device__ void embed_phase(const StepParams& sp, int tok) {
         if (blockIdx.x == 0 && threadIdx.x == 0) set_err(kErrBadToken);
         tok = 0;
     }
-    const int nb = sp.n_embd / 256, ng = sp.n_embd / 64;
+    const int nb = sp.n_embd / 256, ng = sp.n_embd / 32;
     for (int g = blockIdx.x * kCW + warp; g < ng; g += gridDim.x * kCW) {
-        const int v0 = 64 * g + 2 * lane;
-        const float a0 = embed_value(sp.tok_w, sp.tok_type, nb, sp.tok_stride, tok, v0);
-        const float a1 = embed_value(sp.tok_w, sp.tok_type, nb, sp.tok_stride, tok, v0 + 1);
-        sp.x[v0] = a0;
-        sp.x[v0 + 1] = a1;
-        if (sp.xq) xq_quantize_vals(sp.xq, a0, a1, sp.xq_norm_w, sp.n_embd, g);
+        const int v = 32 * g + lane;
+        const float a = embed_value(sp.tok_w, sp.tok_type, nb, sp.tok_stride, tok, v);
+        sp.x[v] = a;
+        if (sp.xq) xq_store32(sp.xq, a, sp.xq_norm_w, sp.n_embd, v);
     }
 }
 
 // ------------------------------------------------------------------ attention
+
+// Attention item: positions are taken in chunks of kStepAttnChunk; lane l of
+// warp w holds K and V of positions w + kCW·i (i < kAttnPer) of the chunk at
+// head dims 4l..4l+3 in registers, so the same thread needs its K rows for
+// the scores and its V rows for P·V: no shared-memory staging of the cache.
+constexpr int kAttnPer = kStepAttnChunk / kCW;
+static_assert(kStepAttnChunk % kCW == 0 && kStepAttnChunk <= 64, "chunk: whole warps, two per lane at most");
 
 // Shared scratch of one attention item (floats), inside the union area.
 struct AttnSmem {
     float* qs;    // [G][hd]
     float* ks;    // [hd]
     float* vs;    // [hd]
-    float* kt;    // [tile][hd]
-    float* vt;    // [tile][hd]
-    float* sc;    // [G][tile]
+    float* sc;    // [G][chunk] scores, then probabilities
+    float* red;   // [kCW][hd] P·V partials of the warps
     float* mrow;  // [G]
     float* lrow;  // [G]
     float* corr;  // [G]
@@ -104,24 +108,35 @@ struct AttnSmem {
         qs = reinterpret_cast<float*>(base);
         ks = qs + kStepMaxG * 128;
         vs = ks + 128;
-        kt = vs + 128;
-        vt = kt + kStepAttnTile * 128;
-        sc = vt + kStepAttnTile * 128;
-        mrow = sc + kStepMaxG * kStepAttnTile;
+        sc = vs + 128;
+        red = sc + kStepMaxG * kStepAttnChunk;
+        mrow = red + kCW * 128;
         lrow = mrow + kStepMaxG;
         corr = lrow + kStepMaxG;
         last = reinterpret_cast<int*>(corr + kStepMaxG);
     }
 };
-static_assert((kStepMaxG * 128 + 256 + 2 * kStepAttnTile * 128 + kStepMaxG * kStepAttnTile + 3 * kStepMaxG + 4) * 4 <=
-                  kStepUnion,
+static_assert((kStepMaxG * 128 + 256 + kStepMaxG * kStepAttnChunk + kCW * 128 + 3 * kStepMaxG + 4) * 4 <= kStepUnion,
               "attention scratch exceeds the union area");
 
-// Splits of each kv head's positions for this step: about one tile per split,
-// at most the configured maximum (the partial buffer's depth).
+// Per-thread K/V rows of the current chunk and the RoPE factors of the item.
+struct AttnPre {
+    float4 k[kAttnPer], v[kAttnPer];
+    float c, s;
+};
+
+// Splits of each kv head's positions for this step: about one chunk per
+// split, at most the configured maximum (the partial buffer's depth).
 __device__ __forceinline__ int attn_splits(const AttnParams& a, int pos) {
-    const int s = (pos + 1 + kStepAttnTile - 1) / kStepAttnTile;
+    const int s = (pos + 1 + kStepAttnChunk - 1) / kStepAttnChunk;
     return max(1, min(a.nsplit, s));
+}
+
+// Range of positions of split `split` of `ns` for sequence length seq.
+__device__ __forceinline__ void attn_range(int seq, int ns, int split, int& t0, int& t1) {
+    const int chunk = (seq + ns - 1) / ns;
+    t0 = min(seq, split * chunk);
+    t1 = min(seq, t0 + chunk);
 }
 
 // One warp RMS-normalises one head in shared memory (qwen3 / hunyuan Q/K norm,
@@ -137,39 +152,53 @@ __device__ __forceinline__ void rms_norm_head(float* x, const float* w, int hd, 
     __syncwarp();
 }
 
-// Issue cp.async loads of tile positions [p0, p0 + n) ∩ [0, pos) of one kv head
-// (rows older than the new token: they do not depend on this step's QKV).
-__device__ __forceinline__ void attn_tile_prefetch(const AttnParams& a, const AttnSmem& s, int kvh, int p0, int n,
-                                                   int pos) {
-    const int hd = a.head_dim, Q4 = hd / 4, kvd = a.n_kv_heads * hd;
-    for (int idx = threadIdx.x; idx < n * Q4; idx += kCT) {
-        const int j = idx / Q4, c = idx % Q4, p = p0 + j;
-        if (p >= pos) continue;
-        const size_t off = (size_t)p * kvd + (size_t)kvh * hd + 4 * c;
-        const uint32_t dk = smem_u32(s.kt + j * hd + 4 * c), dv = smem_u32(s.vt + j * hd + 4 * c);
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dk), "l"(a.kc + off) : "memory");
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dv), "l"(a.vc + off) : "memory");
+// Request this thread's K (or V) registers of chunk positions [p0, p0 + n)
+// that are older than pos (the new token's row comes from shared memory).
+__device__ __forceinline__ void attn_load_rows(const float* cache, int hd, int kvd, int kvh, int p0, int n, int pos,
+                                               float4 (&x)[kAttnPer]) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+    for (int i = 0; i < kAttnPer; ++i) {
+        const int j = warp + kCW * i, p = p0 + j;
+        x[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (j < n && p < pos && 4 * lane < hd)
+            x[i] = __ldg(reinterpret_cast<const float4*>(cache + (size_t)p * kvd + (size_t)kvh * hd + 4 * lane));
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
 
-// Range of positions of split `split` of `ns` for sequence length seq.
-__device__ __forceinline__ void attn_range(int seq, int ns, int split, int& t0, int& t1) {
-    const int chunk = (seq + ns - 1) / ns;
-    t0 = min(seq, split * chunk);
-    t1 = min(seq, t0 + chunk);
+// Before the grid wait: pull into L2 everything of an item that does not
+// depend on the QKV phase (its K/V rows older than the new token, the RoPE
+// row), one bulk prefetch per cache row; no registers are held across the
+// wait.
+__device__ __forceinline__ void attn_prefetch(const AttnParams& a, int pos, int kvh, int split, int ns) {
+    const int hd = a.head_dim, kvd = a.n_kv_heads * hd;
+    int t0, t1;
+    attn_range(pos + 1, ns, split, t0, t1);
+    const int rows = min(t1, pos) - t0;  // rows in the cache (the new token is not yet)
+    for (int i = threadIdx.x; i < 2 * rows; i += kCT) {
+        const float* base = (i & 1) ? a.vc : a.kc;
+        prefetch_l2(base + (size_t)(t0 + (i >> 1)) * kvd + (size_t)kvh * hd, (uint32_t)hd * 4);
+    }
+    if (threadIdx.x == kCT - 1) {
+        prefetch_l2(a.cos_t + (size_t)pos * (hd / 2), (uint32_t)hd * 2);
+        prefetch_l2(a.sin_t + (size_t)pos * (hd / 2), (uint32_t)hd * 2);
+    }
 }
 
 // One (kv head, split) item: llama_forward_token's attention
 // (src/models/llama_model.cpp:1236-1272) for the G query heads of kv head kvh
-// over positions [t0, t1), as an online softmax over tiles of 32 positions;
-// the un-normalised partial (o, max, sum) goes to a.part and the last split
-// of the kv head to finish merges them and quantises the output for the O
-// GEMV.  `prefetched`: tile 0 rows older than pos were already requested.
-__device__ void attn_item(const AttnParams& a, const AttnSmem& s, int pos, int kvh, int split, int ns,
-                          bool prefetched) {
+// over positions [t0, t1), as an online softmax over chunks; the
+// un-normalised partial (o, max, sum) goes to a.part and the last split of
+// the kv head to finish merges them and quantises the output for the O GEMV.
+// `r` holds the prefetched first chunk and RoPE factors.
+// GM: query heads per kv head held in registers (G <= GM; the instance is
+// chosen per model so that P·V accumulators cost 4·GM registers).
+template <int GM>
+__device__ __forceinline__ void attn_item(const AttnParams& a, const AttnSmem& s, int pos, int kvh, int split, int ns, AttnPre& r) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int hd = a.head_dim, half = hd / 2, Q4 = hd / 4;
     const int G = a.n_heads / a.n_kv_heads;
@@ -177,6 +206,13 @@ __device__ void attn_item(const AttnParams& a, const AttnSmem& s, int pos, int k
     const int seq = pos + 1;
     int t0, t1;
     attn_range(seq, ns, split, t0, t1);
+    // first chunk's K/V rows and the RoPE factors (L2-resident after the
+    // prefetch), in flight with the new token's q/k/v below.  RoPE pair i
+    // of every head this thread rotates is tid % half (kCT is a multiple of half).
+    attn_load_rows(a.kc, hd, kvd, kvh, t0, min(kStepAttnChunk, t1 - t0), pos, r.k);
+    attn_load_rows(a.vc, hd, kvd, kvh, t0, min(kStepAttnChunk, t1 - t0), pos, r.v);
+    r.c = __ldg(a.cos_t + (size_t)pos * half + tid % half);
+    r.s = __ldg(a.sin_t + (size_t)pos * half + tid % half);
 
     // ---- q (G heads), k, v of the new token (written by the QKV phase)
     for (int i = tid; i < G * hd; i += kCT) s.qs[i] = __ldcg(a.q + (size_t)kvh * G * hd + i);
@@ -197,15 +233,12 @@ __device__ void attn_item(const AttnParams& a, const AttnSmem& s, int pos, int k
         bar_consumers();
     }
     // RoPE, half-split pairs (i, i + hd/2) (apply_rope, llama_model.cpp:1046-1080)
-    const float* cr = a.cos_t + (size_t)pos * half;
-    const float* sr = a.sin_t + (size_t)pos * half;
     for (int idx = tid; idx < (G + 1) * half; idx += kCT) {
         const int g = idx / half, i = idx % half;
         float* hp = g < G ? s.qs + g * hd : s.ks;
         const float x0 = hp[i], x1 = hp[i + half];
-        const float c = __ldg(cr + i), sn = __ldg(sr + i);
-        hp[i] = x0 * c - x1 * sn;
-        hp[i + half] = x0 * sn + x1 * c;
+        hp[i] = x0 * r.c - x1 * r.s;
+        hp[i + half] = x0 * r.s + x1 * r.c;
     }
     bar_consumers();
     if (a.qk_norm_order == 2) {  // hunyuan: per-head norm after RoPE
@@ -222,86 +255,92 @@ __device__ void attn_item(const AttnParams& a, const AttnSmem& s, int pos, int k
         }
     }
 
-    // ---- tiles
-    const int npg = kCT / Q4;  // position groups of the P·V product
-    const int d4 = tid % Q4, pg = tid / Q4;
-    float4 o[kStepMaxG];
+    // ---- chunks
+    const bool dl = lane < Q4;  // this lane holds head dims 4·lane..4·lane+3
+    float4 o[GM];
 #pragma unroll
-    for (int g = 0; g < kStepMaxG; ++g) o[g] = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int p0 = t0; p0 < t1; p0 += kStepAttnTile) {
-        const int n = min(kStepAttnTile, t1 - p0);
-        if (!(prefetched && p0 == t0)) attn_tile_prefetch(a, s, kvh, p0, n, pos);
-        // the new token's row comes from shared memory, not the cache
-        if (pos >= p0 && pos < p0 + n) {
-            const int j = pos - p0;
-            for (int i = tid; i < hd; i += kCT) {
-                s.kt[j * hd + i] = s.ks[i];
-                s.vt[j * hd + i] = s.vs[i];
-            }
+    for (int g = 0; g < GM; ++g) o[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int p0 = t0; p0 < t1; p0 += kStepAttnChunk) {
+        const int n = min(kStepAttnChunk, t1 - p0);
+        if (p0 != t0) {
+            attn_load_rows(a.kc, hd, kvd, kvh, p0, n, pos, r.k);
+            attn_load_rows(a.vc, hd, kvd, kvh, p0, n, pos, r.v);
         }
-        cp_async_wait_all();
-        bar_consumers();
-        // scores: warp per position, lanes over the head dims
-        for (int j = warp; j < n; j += kCW) {
-            for (int g = 0; g < G; ++g) {
-                float dot = 0.f;
-                for (int i = lane; i < hd; i += 32) dot = fmaf(s.qs[g * hd + i], s.kt[j * hd + i], dot);
-                dot = warp_sum(dot);
-                if (lane == 0) s.sc[g * kStepAttnTile + j] = dot * a.scale;
+        // the new token's row
+#pragma unroll
+        for (int i = 0; i < kAttnPer; ++i)
+            if (p0 + warp + kCW * i == pos && dl) {
+                r.k[i] = reinterpret_cast<const float4*>(s.ks)[lane];
+                r.v[i] = reinterpret_cast<const float4*>(s.vs)[lane];
+            }
+        // scores q_g · k_j (lanes over the head dims, then a warp sum)
+#pragma unroll
+        for (int g = 0; g < GM; ++g) {
+            if (g >= G) break;
+            const float4 q = dl ? reinterpret_cast<const float4*>(s.qs + g * hd)[lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int i = 0; i < kAttnPer; ++i) {
+                float d = q.x * r.k[i].x + q.y * r.k[i].y + q.z * r.k[i].z + q.w * r.k[i].w;
+                d = warp_sum(d);
+                const int j = warp + kCW * i;
+                if (lane == 0 && j < n) s.sc[g * kStepAttnChunk + j] = d * a.scale;
             }
         }
         bar_consumers();
         // online softmax update, warp per head (max-subtracted exp, llama_model.cpp:445-451)
         static_assert(kStepMaxG <= kCW, "one warp per query head");
         if (warp < G) {
-            const float v = lane < n ? s.sc[warp * kStepAttnTile + lane] : -INFINITY;
-            const float mt = warp_max(v);
+            float* sg = s.sc + warp * kStepAttnChunk;
+            const float v0 = lane < n ? sg[lane] : -INFINITY;
+            const float v1 = lane + 32 < n ? sg[lane + 32] : -INFINITY;
             const float m_old = s.mrow[warp];
-            const float m_new = fmaxf(m_old, mt);
-            const float e = lane < n ? expf(v - m_new) : 0.f;
-            s.sc[warp * kStepAttnTile + lane] = e;
-            const float l = warp_sum(e);
+            const float m_new = fmaxf(m_old, warp_max(fmaxf(v0, v1)));
+            const float e0 = lane < n ? expf(v0 - m_new) : 0.f;
+            const float e1 = lane + 32 < n ? expf(v1 - m_new) : 0.f;
+            if (lane < n) sg[lane] = e0;
+            if (lane + 32 < n) sg[lane + 32] = e1;
+            const float l = warp_sum(e0 + e1);
             if (lane == 0) {
-                const float c = expf(m_old - m_new);  // 0 on the first tile (m_old = -inf)
+                const float c = expf(m_old - m_new);  // 0 on the first chunk (m_old = -inf)
                 s.corr[warp] = c;
                 s.lrow[warp] = s.lrow[warp] * c + l;
                 s.mrow[warp] = m_new;
             }
         }
         bar_consumers();
-        if (pg < npg) {
+        // P·V on this thread's rows
 #pragma unroll
-            for (int g = 0; g < kStepMaxG; ++g) {
-                if (g >= G) break;
-                const float c = s.corr[g];
-                o[g].x *= c;
-                o[g].y *= c;
-                o[g].z *= c;
-                o[g].w *= c;
-                for (int j = pg; j < n; j += npg) {
-                    const float e = s.sc[g * kStepAttnTile + j];
-                    const float4 v = reinterpret_cast<const float4*>(s.vt + j * hd)[d4];
-                    o[g].x = fmaf(e, v.x, o[g].x);
-                    o[g].y = fmaf(e, v.y, o[g].y);
-                    o[g].z = fmaf(e, v.z, o[g].z);
-                    o[g].w = fmaf(e, v.w, o[g].w);
-                }
+        for (int g = 0; g < GM; ++g) {
+            if (g >= G) break;
+            const float c = s.corr[g];
+            o[g].x *= c;
+            o[g].y *= c;
+            o[g].z *= c;
+            o[g].w *= c;
+#pragma unroll
+            for (int i = 0; i < kAttnPer; ++i) {
+                const int j = warp + kCW * i;
+                const float e = j < n ? s.sc[g * kStepAttnChunk + j] : 0.f;
+                o[g].x = fmaf(e, r.v[i].x, o[g].x);
+                o[g].y = fmaf(e, r.v[i].y, o[g].y);
+                o[g].z = fmaf(e, r.v[i].z, o[g].z);
+                o[g].w = fmaf(e, r.v[i].w, o[g].w);
             }
         }
-        bar_consumers();
+        bar_consumers();  // sc is rewritten by the next chunk
     }
-    // ---- reduce the position groups, write this split's partial
-    float* red = s.kt;  // [npg][hd]
+    // ---- reduce the warps, write this split's partial
 #pragma unroll
-    for (int g = 0; g < kStepMaxG; ++g) {
+    for (int g = 0; g < GM; ++g) {
         if (g >= G) break;
-        if (pg < npg) reinterpret_cast<float4*>(red + pg * hd)[d4] = o[g];
+        if (dl) reinterpret_cast<float4*>(s.red + warp * hd)[lane] = o[g];
         bar_consumers();
         const int h = kvh * G + g;
         float* dst = a.part + ((size_t)h * a.nsplit + split) * (hd + 2);
         for (int d = tid; d < hd; d += kCT) {
             float acc = 0.f;
-            for (int q = 0; q < npg; ++q) acc += red[q * hd + d];
+#pragma unroll
+            for (int w = 0; w < kCW; ++w) acc += s.red[w * hd + d];
             dst[d] = acc;
             if (d == 0) {
                 dst[hd] = s.mrow[g];
@@ -335,12 +374,29 @@ __device__ void attn_item(const AttnParams& a, const AttnSmem& s, int pos, int k
     }
     if (tid == 0) a.counter[kvh] = 0u;
     if (a.xq_out) {
-        // quantise this kv head's G*hd outputs (whole 64-value groups) for the O GEMV
+        // quantise this kv head's G*hd outputs (32-value groups) for the O GEMV
         __threadfence();
         bar_consumers();
-        const int g0 = kvh * G * hd / 64, ng = G * hd / 64;
+        const int g0 = kvh * G * hd / 32, ng = G * hd / 32;
         for (int k = warp; k < ng; k += kCW) xq_quantize_group(a.xq_out, a.out, nullptr, a.n_heads * hd, g0 + k);
     }
+}
+
+// The whole attention phase of one layer for this CTA: the prefetch of what
+// does not depend on the QKV phase, the grid wait, then the CTA's items.
+template <int GM>
+__device__ __forceinline__ bool attn_phase(const AttnParams& a, const AttnSmem& s, int pos, unsigned* bar,
+                                           unsigned target, volatile int* abort) {
+    const int ns = attn_splits(a, pos);
+    const int items = a.n_kv_heads * ns;
+    for (int item = blockIdx.x; item < items; item += gridDim.x) attn_prefetch(a, pos, item / ns, item % ns, ns);
+    if (!grid_wait(bar, target, abort)) return false;
+    for (int item = blockIdx.x; item < items; item += gridDim.x) {
+        AttnPre r;
+        attn_item<GM>(a, s, pos, item / ns, item % ns, ns, r);
+        bar_consumers();
+    }
+    return true;
 }
 
 // ------------------------------------------------------------------ kernel
@@ -393,48 +449,36 @@ __global__ void __launch_bounds__(kGemvThreads, 1) step_kernel(const __grid_cons
     const int tok = __ldcg(sp.token);
     uint32_t consumed = 0;
     int head = 0;
-    int next_attn = -1;  // phase index whose tile 0 was prefetched
     const unsigned grid = gridDim.x;
     for (int i = 0; i < sp.nph; ++i) {
         const StepPhase& ph = sp.ph[i];
         const int kind = ph.kind;
         if (kind == PH_ATTN) {
-            // KV rows older than the new token do not depend on the QKV phase:
-            // request this CTA's first tile before waiting for it.
             copy_params(ap, &ph.a, sizeof(AttnParams));
-            const int ns = attn_splits(*ap, pos);
-            if ((int)blockIdx.x < ap->n_kv_heads * ns && ap->head_dim <= 128) {
-                const int item = blockIdx.x, kvh = item / ns, split = item % ns;
-                int t0, t1;
-                attn_range(pos + 1, ns, split, t0, t1);
-                if (t1 > t0) attn_tile_prefetch(*ap, AttnSmem(uni), kvh, t0, min(kStepAttnTile, t1 - t0), pos);
-                next_attn = i;
-            }
-        }
-        if (i > 0 && !grid_wait(sp.bar, (unsigned)i * grid, abort)) break;
-        if (kind == PH_EMBED) {
-            embed_phase(sp, tok);
-        } else if (kind == PH_GEMV) {
-            copy_params(gp, &ph.g, offsetof(GemvParams, vrange));
-            const int vbeg = ph.g.vrange[blockIdx.x], vend = ph.g.vrange[blockIdx.x + 1];
-            float s_in = 1.f;
-            if (gp->xq) s_in = load_xq(*gp, uni);
-            else input_prologue(*gp, uni, red);
-            if (!consume(*gp, vbeg, vend, ring, consumed, head, uni, s_in, smem)) {
-                *abort = 1;
-                break;
-            }
-            if (gp->q_out) quantise_output(*gp, vbeg, vend, flags + 1);
-        } else {
-            const AttnParams& a = *ap;
+            const int G = ap->n_heads / ap->n_kv_heads;
             const AttnSmem s(uni);
-            const int ns = attn_splits(a, pos);
-            const int items = a.n_kv_heads * ns;
-            for (int item = blockIdx.x; item < items; item += gridDim.x) {
-                attn_item(a, s, pos, item / ns, item % ns, ns, next_attn == i && item == (int)blockIdx.x);
-                bar_consumers();
+            const unsigned target = (unsigned)i * grid;
+            bool ok;
+            if (G == 1) ok = attn_phase<1>(*ap, s, pos, sp.bar, target, abort);
+            else if (G == 2) ok = attn_phase<2>(*ap, s, pos, sp.bar, target, abort);
+            else if (G <= 4) ok = attn_phase<4>(*ap, s, pos, sp.bar, target, abort);
+            else ok = attn_phase<kStepMaxG>(*ap, s, pos, sp.bar, target, abort);
+            if (!ok) break;
+        } else {
+            if (i > 0 && !grid_wait(sp.bar, (unsigned)i * grid, abort)) break;
+            if (kind == PH_EMBED) {
+                embed_phase(sp, tok);
+            } else {
+                copy_params(gp, &ph.g, offsetof(GemvParams, vrange));
+                const int vbeg = ph.g.vrange[blockIdx.x], vend = ph.g.vrange[blockIdx.x + 1];
+                float s_in = 1.f;
+                if (gp->xq) s_in = load_xq(*gp, uni);
+                else input_prologue(*gp, uni, red);
+                if (!consume(*gp, vbeg, vend, ring, consumed, head, uni, s_in, smem)) {
+                    *abort = 1;
+                    break;
+                }
             }
-            cp_async_wait_all();  // a prefetch whose item did not run (none in practice)
         }
         // arrive: every store of this phase by this CTA happens before the count
         bar_consumers();

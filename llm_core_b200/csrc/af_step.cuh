@@ -9,14 +9,15 @@
 // for a phase boundary; the consumer warps wait for the previous phase on a
 // grid-wide arrival counter (bounded spin) and then run the phase:
 //
-//   EMBED  token row dequant → x
+//   EMBED  token row dequant → x and its quantised form
 //   GEMV   QKV(+bias) | O(+resid) | gate/up SwiGLU | down(+resid) | LM head+argmax
 //   ATTN   RoPE, Q/K norm, KV store, split attention
 //
-// Every GEMV phase reads its f32 input (the previous phase's output, through
-// L2) and quantises it in shared memory itself, RMSNorm included, so a phase
-// ends with its epilogue stores: no cross-CTA quantisation pass, counters or
-// fences between phases other than the arrival itself.
+// Every phase writes the next GEMV's input already quantised: the epilogue
+// that finishes a 16-row tile quantises it (16-value groups, RMSNorm-weighted
+// where the next GEMV normalises), so a phase ends with its epilogue stores
+// and the next one copies its input with one L2 read: no cross-CTA pass,
+// counters or fences between phases other than the arrival itself.
 //
 // and CTA 0, once every CTA has finished the last phase, turns the argmax
 // into the next token and advances the position.
@@ -29,7 +30,7 @@ namespace af {
 enum StepPhaseKind : int { PH_EMBED = 0, PH_GEMV = 1, PH_ATTN = 2 };
 
 constexpr int kStepMaxG = 8;            // query heads per kv head
-constexpr int kStepAttnTile = 32;       // KV positions per attention tile
+constexpr int kStepAttnChunk = 64;      // KV positions per attention chunk
 constexpr int kStepHdr = kGemvSmemHdr;  // mbarriers, flags, phase parameter copies, reduction scratch
 constexpr int kStepUnion = 40 * 1024;   // XQ input of a GEMV phase / attention scratch
 constexpr int kStepSmem = 227 * 1024;
