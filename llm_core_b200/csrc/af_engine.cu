@@ -402,7 +402,7 @@ cudaError_t enqueue_step(af_engine* e, Prof* prof = nullptr) {
     ENG_TRY(finalize_launch(e->key, &e->tokpos[0], &e->tokpos[1], e->hist, e->stream, e->pdl));
     ++nk;
     AF_MARK(AF_PROF_FINAL, 16.0);
-    e->kernels_per_step = nk;
+    if (!prof) e->kernels_per_step = nk;
     return cudaSuccess;
 #undef AF_MARK
 }

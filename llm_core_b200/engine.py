@@ -41,6 +41,43 @@ def nccl_unique_id() -> bytes:
     return buf.raw
 
 
+def block_split(n: int, r: int, t: int) -> tuple[int, int]:
+    """[lo, hi) of n items for rank r of t, the remainder to the low ranks —
+    the engine's split of FFN super-blocks and vocabulary rows."""
+    base, rem = divmod(n, t)
+    lo = r * base + min(r, rem)
+    return lo, lo + base + (1 if r < rem else 0)
+
+
+@dataclass
+class TpShard:
+    """What tensor-parallel rank `rank` of `size` holds (af_engine_create's
+    geometry): query / kv heads [h0, h1) / [kv0, kv1) (column-parallel QKV,
+    row-parallel attn_output over the same heads), FFN values [f0, f1)
+    (column-parallel gate/up, row-parallel down over whole 256-value
+    super-blocks) and vocabulary rows [v0, v1) of the LM head."""
+    h0: int
+    h1: int
+    kv0: int
+    kv1: int
+    f0: int
+    f1: int
+    v0: int
+    v1: int
+
+
+def tp_shard(cfg: ModelConfig, rank: int, size: int) -> TpShard:
+    """Shard of one rank; raises ValueError for shapes the engine rejects."""
+    if size < 1 or not 0 <= rank < size:
+        raise ValueError("bad tp rank/size")
+    if size > 1 and (cfg.n_kv_head % size or (cfg.n_embd // size) % 256):
+        raise ValueError("tensor parallel needs n_kv_head and n_embd/256 divisible by tp_size")
+    hl, kvl = cfg.n_head // size, cfg.n_kv_head // size
+    f0, f1 = block_split(cfg.ffn // 256, rank, size)
+    v0, v1 = block_split(cfg.vocab, rank, size)
+    return TpShard(rank * hl, (rank + 1) * hl, rank * kvl, (rank + 1) * kvl, f0 * 256, f1 * 256, v0, v1)
+
+
 def read_config(path: str, max_context_len: int = 4096) -> ModelConfig:
     lib = _lib.load()
     cfg = ModelConfig()

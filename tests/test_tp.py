@@ -1,0 +1,103 @@
+"""Tensor parallelism: host-side shard plumbing on CPU (gloo, world size 2)
+and TP=2 parity against one GPU (skipped with fewer than 2 GPUs)."""
+import os
+import socket
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+from helpers import LOGITS_TOL, model_path, rel_l2
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _gloo_rank(rank, world, port, q):
+    import torch.distributed as dist
+    from llm_core_b200 import gguf
+    from llm_core_b200.engine import tp_shard
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    from llm_core_b200._lib import ModelConfig
+    p = gguf.PRESETS["llama2-7b"]
+    c = ModelConfig()
+    c.n_layer, c.n_embd, c.n_head, c.n_kv_head, c.ffn, c.vocab = p.n_layer, p.n_embd, p.n_head, p.n_kv_head, p.ffn, p.vocab
+    shard = tp_shard(c, rank, world)
+    # the NCCL id travels as an opaque byte string from rank 0
+    obj = [bytes(range(128)) if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0)
+    allsh = [None] * world
+    dist.all_gather_object(allsh, shard)
+    q.put((rank, obj[0], allsh))
+    dist.destroy_process_group()
+
+
+def test_tp_shards_cover_the_model_over_gloo():
+    """Two gloo ranks compute their shards and exchange them: heads, kv heads,
+    FFN super-blocks and vocabulary rows are covered exactly once."""
+    import torch.multiprocessing as mp
+    from llm_core_b200 import gguf
+    world, port = 2, _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_gloo_rank, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    cfg = gguf.PRESETS["llama2-7b"]
+    for rank, nid, shards in res:
+        assert nid == bytes(range(128))
+        shards = sorted(shards, key=lambda s: s.h0)
+        assert shards[0].h0 == 0 and shards[-1].h1 == cfg.n_head
+        assert shards[0].f0 == 0 and shards[-1].f1 == cfg.ffn
+        assert shards[0].v0 == 0 and shards[-1].v1 == cfg.vocab
+        for a, b in zip(shards, shards[1:]):
+            assert a.h1 == b.h0 and a.kv1 == b.kv0 and a.f1 == b.f0 and a.v1 == b.v0
+        # ffn_down K = 11008 = 43 super-blocks splits 22 / 21
+        assert [(s.f1 - s.f0) // 256 for s in shards] == [22, 21]
+
+
+def test_tp_shard_rejects_unsupported_shapes():
+    from llm_core_b200._lib import ModelConfig
+    from llm_core_b200.engine import tp_shard
+    c = ModelConfig()
+    c.n_layer, c.n_embd, c.n_head, c.n_kv_head, c.ffn, c.vocab = 2, 256, 4, 2, 512, 512
+    with pytest.raises(ValueError):
+        tp_shard(c, 0, 2)  # n_embd / 2 = 128 is not a whole super-block
+    assert tp_shard(c, 0, 1).h1 == 4
+
+
+@pytest.mark.gpu
+def test_tp2_matches_single_gpu():
+    """TP=2 (torchrun, NCCL) prefill logits and greedy continuation equal the
+    single-GPU engine's on the same GGUF."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from llm_core_b200.engine import LlamaCudaModel
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import tp_worker
+    path = model_path("small", 5)
+    out = os.path.join(os.environ.get("TMPDIR", "/tmp"), f"af_tp2_{os.getpid()}.npz")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nproc-per-node", "2", "--master-addr", "127.0.0.1",
+           "--master-port", str(_free_port()), os.path.join(ROOT, "tests", "tp_worker.py"), path, out]
+    r = subprocess.run(cmd, cwd=ROOT, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+    z = np.load(out)
+    m = LlamaCudaModel(path)
+    nxt, lg = m.prefill(tp_worker.PROMPT, 0)
+    ids = m.decode_greedy(nxt, len(tp_worker.PROMPT), tp_worker.STEPS)
+    m.close()
+    assert rel_l2(z["logits"], lg) < LOGITS_TOL
+    assert int(z["first"]) == nxt
+    agree = np.mean(z["ids"] == ids)
+    assert agree >= 0.9, agree
