@@ -100,6 +100,8 @@ struct af_engine {
     // persistent step kernel (single GPU): phase table in device memory
     bool use_step = false;
     StepPhase* d_phases = nullptr;
+    uint8_t* xchg = nullptr;                 // this rank's exchange area (tensor parallel)
+    std::vector<void*> peer_maps;            // IPC mappings of the other ranks' areas
     unsigned int* step_bar = nullptr;
     StepParams step{};
 
@@ -407,20 +409,79 @@ cudaError_t enqueue_step(af_engine* e, Prof* prof = nullptr) {
 #undef AF_MARK
 }
 
+// Tensor-parallel exchange areas: each rank allocates and zeroes its own,
+// the CUDA IPC handles travel over the NCCL communicator (all-gather), and
+// every rank maps the others' areas, so the step kernel reaches the peers'
+// partial sums, counters and argmax slots with plain loads and system-scope
+// reductions over NVLink.
+cudaError_t setup_exchange(af_engine* e) {
+    const int E = e->cfg.n_embd;
+    const size_t bytes = step_xchg_bytes(E);
+    e->xchg = static_cast<uint8_t*>(e->dalloc(bytes));
+    ENG_TRY(cudaMemset(e->xchg, 0, bytes));
+    unsigned long long* epoch = static_cast<unsigned long long*>(e->dalloc(64));
+    ENG_TRY(cudaMemset(epoch, 0, 64));
+    ENG_TRY(cudaDeviceSynchronize());
+    cudaIpcMemHandle_t mine;
+    ENG_TRY(cudaIpcGetMemHandle(&mine, e->xchg));
+    const size_t hs = sizeof(cudaIpcMemHandle_t);
+    uint8_t* d_h = nullptr;
+    ENG_TRY(cudaMalloc(&d_h, hs * (e->tp + 1)));
+    ENG_TRY(cudaMemcpy(d_h + hs * e->tp, &mine, hs, cudaMemcpyHostToDevice));
+    NCCL_TRY(ncclAllGather(d_h + hs * e->tp, d_h, hs, ncclUint8, e->comm, e->stream));
+    std::vector<cudaIpcMemHandle_t> all(e->tp);
+    ENG_TRY(cudaStreamSynchronize(e->stream));
+    ENG_TRY(cudaMemcpy(all.data(), d_h, hs * e->tp, cudaMemcpyDeviceToHost));
+    cudaFree(d_h);
+    StepParams& sp = e->step;
+    for (int r = 0; r < e->tp; ++r) {
+        uint8_t* base = e->xchg;
+        if (r != e->rank) {
+            void* p = nullptr;
+            ENG_TRY(cudaIpcOpenMemHandle(&p, all[r], cudaIpcMemLazyEnablePeerAccess));
+            e->peer_maps.push_back(p);
+            base = static_cast<uint8_t*>(p);
+        }
+        sp.xbar[r] = reinterpret_cast<unsigned long long*>(base);
+        sp.xkey[r] = reinterpret_cast<unsigned long long*>(base + 128);
+        sp.xpart[r] = reinterpret_cast<float*>(base + 256);
+    }
+    sp.epoch = epoch;
+    // every rank has mapped every area before any step runs
+    int* dd = static_cast<int*>(e->dalloc(16));
+    ENG_TRY(cudaMemset(dd, 0, 16));
+    NCCL_TRY(ncclAllReduce(dd, dd, 1, ncclInt32, ncclSum, e->comm, e->stream));
+    ENG_TRY(cudaStreamSynchronize(e->stream));
+    return cudaSuccess;
+}
+
 // Phase table of the persistent step kernel (single GPU, quantised inputs
 // handed from phase to phase), mirroring enqueue_step's kernel sequence.
 cudaError_t build_step(af_engine* e) {
     const auto& c = e->cfg;
     const int E = c.n_embd;
     ENG_TRY(step_init());
+    const bool tp = e->tp > 1;
+    auto allreduce = [&](int k, const float* norm_w, uint8_t* xq) {
+        StepPhase r = {};
+        r.kind = PH_ALLREDUCE;
+        r.x.k = k;
+        r.x.resid = e->x[0];
+        r.x.xq = xq;
+        r.x.norm_w = norm_w;
+        r.x.n = E;
+        return r;
+    };
     std::vector<StepPhase> ph;
     StepPhase embed = {};
     embed.kind = PH_EMBED;
+    embed.x.k = -1;
     ph.push_back(embed);
     for (int l = 0; l < c.n_layer; ++l) {
         const LayerW& L = e->layers[l];
         StepPhase q = {};
         q.kind = PH_GEMV;
+        q.x.k = -1;
         q.g = base_params(e, E);
         q.g.seg[0] = seg_of(L.wq, e->q, L.bq);
         q.g.seg[1] = seg_of(L.wk, e->k, L.bk);
@@ -434,6 +495,7 @@ cudaError_t build_step(af_engine* e) {
 
         StepPhase at = {};
         at.kind = PH_ATTN;
+        at.x.k = -1;
         AttnParams& a = at.a;
         a.q = e->q;
         a.k = e->k;
@@ -462,19 +524,28 @@ cudaError_t build_step(af_engine* e) {
 
         StepPhase o = {};
         o.kind = PH_GEMV;
+        o.x.k = -1;
         o.g = base_params(e, e->Hl * e->hd);
         o.g.seg[0] = seg_of(L.wo, e->ypart, nullptr);
         o.g.nseg = 1;
-        o.g.epi = EPI_RESID;
-        o.g.resid = e->x[0];
         o.g.xq = e->xq_o;
-        o.g.q_out = e->xq_gu;
-        o.g.q_norm_w = L.ffn_norm;
+        if (tp) {  // row-parallel: partial sums into the exchange buffer, then the all-reduce
+            o.g.epi = EPI_STORE;
+            o.x.k = 2 * l;
+            o.x.n = E;
+        } else {
+            o.g.epi = EPI_RESID;
+            o.g.resid = e->x[0];
+            o.g.q_out = e->xq_gu;
+            o.g.q_norm_w = L.ffn_norm;
+        }
         gemv_configure(o.g, e->sms);
         ph.push_back(o);
+        if (tp) ph.push_back(allreduce(2 * l, L.ffn_norm, e->xq_gu));
 
         StepPhase gu = {};
         gu.kind = PH_GEMV;
+        gu.x.k = -1;
         gu.g = base_params(e, E);
         gu.g.seg[0] = seg_of(L.wg, e->h, nullptr);
         gu.g.seg[1] = seg_of(L.wu, nullptr, nullptr);
@@ -488,19 +559,29 @@ cudaError_t build_step(af_engine* e) {
 
         StepPhase d = {};
         d.kind = PH_GEMV;
+        d.x.k = -1;
         d.g = base_params(e, e->Fl);
         d.g.seg[0] = seg_of(L.wd, e->ypart, nullptr);
         d.g.nseg = 1;
-        d.g.epi = EPI_RESID;
-        d.g.resid = e->x[0];
         d.g.xq = e->xq_d;
-        d.g.q_out = e->xq_a;
-        d.g.q_norm_w = l + 1 < c.n_layer ? e->layers[l + 1].attn_norm : e->out_norm;
+        const float* next_norm = l + 1 < c.n_layer ? e->layers[l + 1].attn_norm : e->out_norm;
+        if (tp) {
+            d.g.epi = EPI_STORE;
+            d.x.k = 2 * l + 1;
+            d.x.n = E;
+        } else {
+            d.g.epi = EPI_RESID;
+            d.g.resid = e->x[0];
+            d.g.q_out = e->xq_a;
+            d.g.q_norm_w = next_norm;
+        }
         gemv_configure(d.g, e->sms);
         ph.push_back(d);
+        if (tp) ph.push_back(allreduce(2 * l + 1, next_norm, e->xq_a));
     }
     StepPhase lm = {};
     lm.kind = PH_GEMV;
+    lm.x.k = -1;
     lm.g = base_params(e, E);
     lm.g.seg[0] = seg_of(e->output, e->logits, nullptr);
     lm.g.nseg = 1;
@@ -534,6 +615,10 @@ cudaError_t build_step(af_engine* e) {
     sp.pos = &e->tokpos[1];
     sp.hist = e->hist;
     sp.ring_bytes = kStepSmem - kStepHdr - kStepUnion;
+    sp.tp = e->tp;
+    sp.rank = e->rank;
+    sp.n_xchg = 2 * c.n_layer + 1;
+    if (tp) ENG_TRY(setup_exchange(e));
     return cudaSuccess;
 }
 
@@ -617,6 +702,7 @@ cudaError_t af_engine_destroy(af_engine* e) {
     cudaSetDevice(e->device);
     if (e->gexec) cudaGraphExecDestroy(e->gexec);
     if (e->graph) cudaGraphDestroy(e->graph);
+    for (void* p : e->peer_maps) cudaIpcCloseMemHandle(p);
     for (void* p : e->allocs) cudaFree(p);
     if (e->h_tokpos) cudaFreeHost(e->h_tokpos);
     if (e->comm) ncclCommDestroy(e->comm);
@@ -820,7 +906,7 @@ cudaError_t af_engine_finalize(af_engine* e) {
         ENG_TRY(gemv_init());
         ENG_TRY(attention_init());
         const char* sv = std::getenv("AF_STEP_KERNEL");
-        e->use_step = e->tp == 1 && (!sv || std::atoi(sv) != 0) &&
+        e->use_step = (!sv || std::atoi(sv) != 0) && e->tp <= kStepMaxRanks && c.n_embd % 32 == 0 &&
                       step_supported(e->Hl, e->KVl, e->hd, c.n_embd, e->Fl);
         if (e->use_step) ENG_TRY(build_step(e));
         ENG_TRY(cudaDeviceSynchronize());

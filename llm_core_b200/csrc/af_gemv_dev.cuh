@@ -19,7 +19,8 @@ namespace gdev {
 
 constexpr int kCW = kGemvConsumerWarps;
 constexpr int kCT = kCW * 32;
-constexpr int kRingDesc = 8;  // entries in flight at most
+constexpr int kRingDesc = 8;  // entries in flight at most (a power of two)
+static_assert((kRingDesc & (kRingDesc - 1)) == 0, "ring descriptors: power of two");
 
 // Shared-memory header of the GEMV kernels (kGemvSmemHdr bytes).
 constexpr int kHdrFlags = 256;    // int[0] abort
@@ -91,7 +92,10 @@ struct Ring {
 
 // ---------------------------------------------------------------- producer
 
-// Single-thread producer state; persists across the phases of a step.
+// Single-thread producer state; persists across the phases of a step.  The
+// in-flight table is indexed with compile-time slots only, so it stays in
+// registers (a dynamically indexed table would live in local memory and put
+// an L1 round trip on every check of the producer's serial loop).
 struct Producer {
     uint32_t issued = 0, released = 0;
     int head = 0;
@@ -111,18 +115,25 @@ struct Producer {
         int h = head;
         at = ring_place(h, bytes, r.bytes);
         for (;;) {
-            if (issued == released) break;
-            bool clash = issued - released >= (uint32_t)kRingDesc;
-            for (uint32_t i = released; !clash && i < issued; ++i) {
-                const int o = off[i % kRingDesc], s = size[i % kRingDesc];
-                clash = at < o + s && o < at + bytes;
+            const uint32_t n = issued - released;
+            if (n == 0) break;
+            bool clash = n >= (uint32_t)kRingDesc;
+#pragma unroll
+            for (int d = 0; d < kRingDesc; ++d) {
+                const bool live = ((uint32_t)(d - (int)released) & (kRingDesc - 1)) < n;
+                clash |= live && at < off[d] + size[d] && off[d] < at + bytes;
             }
             if (!clash) break;
             if (!release_oldest(r, abort)) return false;
         }
         head = h;
-        off[issued % kRingDesc] = at;
-        size[issued % kRingDesc] = bytes;
+        const int slot = issued % kRingDesc;
+#pragma unroll
+        for (int d = 0; d < kRingDesc; ++d)
+            if (d == slot) {
+                off[d] = at;
+                size[d] = bytes;
+            }
         return true;
     }
 
@@ -185,9 +196,9 @@ __device__ __forceinline__ float i2f_small(int v) {
 // plane's words of sub-blocks g/2 and 4 + g/2.  Its outputs (C slot t of the
 // two accumulators) are sub-blocks t and 4 + t.
 struct XQ4 {
-    uint32_t a0, a1, b0, b1;
-    float xs0, xs1;  // xs of sub-blocks t and 4+t (1/16 folded in for odd t: high nibbles)
-    float s0, s1;    // Σx of sub-blocks t and 4+t
+    uint32_t b[8][2];  // B operands of tiles 0..7 (this lane's word where its column is the tile's, else 0)
+    float xs0, xs1;    // xs of sub-blocks t and 4+t (1/16 folded in for odd t: high nibbles)
+    float s0, s1;      // Σx of sub-blocks t and 4+t
 };
 __device__ __forceinline__ XQ4 load_xq4(const uint8_t* xsb, int lane, float s_in) {
     const int g = lane >> 2, t = lane & 3, m = g >> 1;
@@ -195,10 +206,14 @@ __device__ __forceinline__ XQ4 load_xq4(const uint8_t* xsb, int lane, float s_in
     const float* XS = reinterpret_cast<const float*>(xsb + kXqXs);
     const float* S32 = reinterpret_cast<const float*>(xsb + kXqS32);
     XQ4 x;
-    x.a0 = X[8 * m + t];
-    x.a1 = X[8 * m + 4 + t];
-    x.b0 = X[8 * (m + 4) + t];
-    x.b1 = X[8 * (m + 4) + 4 + t];
+    const uint32_t a0 = X[8 * m + t], a1 = X[8 * m + 4 + t];
+    const uint32_t c0 = X[8 * (m + 4) + t], c1 = X[8 * (m + 4) + 4 + t];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const bool sel = (j & 3) == m;
+        x.b[j][0] = sel ? (j < 4 ? a0 : c0) : 0u;
+        x.b[j][1] = sel ? (j < 4 ? a1 : c1) : 0u;
+    }
     const float f = (t & 1) ? s_in * 0.0625f : s_in;
     x.xs0 = XS[t] * f;
     x.xs1 = XS[4 + t] * f;
@@ -211,7 +226,7 @@ __device__ __forceinline__ XQ4 load_xq4(const uint8_t* xsb, int lane, float s_in
 // g and g+8 from its sub-blocks t and 4+t.  Block math of q4k_dot_row
 // (src/models/llama_model.cpp:476-504) / get_scale_min_k4 (gemv_q4k_avx2.cpp:34-43).
 __device__ __forceinline__ float2 q4_unit(const uint8_t* u, const XQ4& x, int lane) {
-    const int g = lane >> 2, t = lane & 3, m = g >> 1;
+    const int g = lane >> 2, t = lane & 3;
     uint4 a[4];
 #pragma unroll
     for (int c = 0; c < 4; ++c) a[c] = lds128(u + c * 512 + lane * 16);
@@ -220,24 +235,21 @@ __device__ __forceinline__ float2 q4_unit(const uint8_t* u, const XQ4& x, int la
     for (int j = 0; j < 8; ++j) {
         const uint32_t M = (j & 1) ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
         const uint4 q = a[j >> 1];
-        const bool sel = (j & 3) == m;
-        const uint32_t b0 = sel ? (j < 4 ? x.a0 : x.b0) : 0u;
-        const uint32_t b1 = sel ? (j < 4 ? x.a1 : x.b1) : 0u;
-        if (j < 4) mma_u8s8(C0, q.x & M, q.y & M, q.z & M, q.w & M, b0, b1);
-        else mma_u8s8(C1, q.x & M, q.y & M, q.z & M, q.w & M, b0, b1);
+        if (j < 4) mma_u8s8(C0, q.x & M, q.y & M, q.z & M, q.w & M, x.b[j][0], x.b[j][1]);
+        else mma_u8s8(C1, q.x & M, q.y & M, q.z & M, q.w & M, x.b[j][0], x.b[j][1]);
     }
     const int sh = 8 * t;
     float y[2];
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
         const uint4 h = lds128(u + kQ4Hdr + (g + 8 * r) * 16);
-        // exact integer dots Σ q·(256·hi + lo) of sub-blocks t and 4+t, as f32
-        const float T0 = fmaf(256.f, i2f_small(C0[2 * r]), i2f_small(C0[2 * r + 1]));
-        const float T1 = fmaf(256.f, i2f_small(C1[2 * r]), i2f_small(C1[2 * r + 1]));
+        // exact integer dots Σ q·(256·hi + lo) of sub-blocks t and 4+t (|T| < 2^28)
+        const float T0 = __int2float_rn(C0[2 * r] * 256 + C0[2 * r + 1]);
+        const float T1 = __int2float_rn(C1[2 * r] * 256 + C1[2 * r + 1]);
         const uint32_t w0 = h.y >> sh, w1 = h.z >> sh, w2 = h.w >> sh;
-        const float sc0 = i2f_small(w0 & 63), m0 = i2f_small(w1 & 63);
-        const float sc1 = i2f_small((w2 & 0xF) | ((w0 >> 2) & 0x30));
-        const float m1 = i2f_small(((w2 >> 4) & 0xF) | ((w1 >> 2) & 0x30));
+        const float sc0 = __int2float_rn(w0 & 63), m0 = __int2float_rn(w1 & 63);
+        const float sc1 = __int2float_rn((w2 & 0xF) | ((w0 >> 2) & 0x30));
+        const float m1 = __int2float_rn(((w2 >> 4) & 0xF) | ((w1 >> 2) & 0x30));
         const float d = half_bits_to_float(h.x & 0xFFFFu), dmin = half_bits_to_float(h.x >> 16);
         y[r] = d * fmaf(x.xs0 * sc0, T0, x.xs1 * sc1 * T1) - dmin * fmaf(m0, x.s0, m1 * x.s1);
     }

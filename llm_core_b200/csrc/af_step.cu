@@ -57,6 +57,52 @@ __device__ bool grid_wait(unsigned* bar, unsigned target, volatile int* flags) {
     return flags[0] == 0;
 }
 
+// ---- tensor-parallel exchanges (system scope: the counters and buffers of
+// the other ranks are peer memory mapped into this process)
+__device__ __forceinline__ void red_release_sys(unsigned long long* p, unsigned long long v) {
+    asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Thread 0 spins (bounded) until this rank's exchange counter reaches
+// `target`; the consumer barrier publishes the result.
+__device__ bool xchg_wait(const unsigned long long* bar, unsigned long long target, volatile int* flags) {
+    if (threadIdx.x == 0) {
+        bool ok = false;
+        for (uint32_t i = 0; i < kGridSpinLimit; ++i) {
+            if (ld_acquire_sys(bar) >= target) {
+                ok = true;
+                break;
+            }
+            if ((i & 63) == 63 && flags[0]) break;
+        }
+        if (!ok) {
+            if (!flags[0]) set_err(kErrMbarTimeout);
+            flags[0] = 1;
+        }
+    }
+    bar_consumers();
+    return flags[0] == 0;
+}
+
+// All-reduce of exchange k: residual += Σ_r partial_r (ranks in order, so
+// every rank computes the same sum), and the quantised input of the next GEMV
+// (one warp per 32-value group).
+__device__ void allreduce_phase(const StepParams& sp, const XchgParams& x, int buf) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int g = blockIdx.x * kCW + warp; g < x.n / 32; g += gridDim.x * kCW) {
+        const int idx = 32 * g + lane;
+        float v = __ldcg(x.resid + idx);
+        for (int r = 0; r < sp.tp; ++r) v += __ldcv(sp.xpart[r] + (size_t)buf * x.n + idx);
+        x.resid[idx] = v;
+        xq_store32(x.xq, v, x.norm_w, x.n, idx);
+    }
+}
+
 // Copy `bytes` (multiple of 4) of a parameter block into shared memory.
 __device__ __forceinline__ void copy_params(void* dst, const void* src, int bytes) {
     for (int i = threadIdx.x; i < bytes / 4; i += kCT)
@@ -447,6 +493,12 @@ __global__ void __launch_bounds__(kGemvThreads, 1) step_kernel(const __grid_cons
     // ---- consumers: the phases, separated by grid-wide arrivals
     const int pos = __ldcg(sp.pos);
     const int tok = __ldcg(sp.token);
+    const unsigned long long epoch = sp.tp > 1 ? __ldcg(sp.epoch) : 0ull;
+    // exchange counter target after exchange k of this step: every CTA of
+    // every rank counts once per exchange
+    auto xtarget = [&](int k) {
+        return (unsigned long long)sp.tp * gridDim.x * (epoch * (unsigned long long)sp.n_xchg + (unsigned long long)k + 1ull);
+    };
     uint32_t consumed = 0;
     int head = 0;
     const unsigned grid = gridDim.x;
@@ -464,12 +516,22 @@ __global__ void __launch_bounds__(kGemvThreads, 1) step_kernel(const __grid_cons
             else if (G <= 4) ok = attn_phase<4>(*ap, s, pos, sp.bar, target, abort);
             else ok = attn_phase<kStepMaxG>(*ap, s, pos, sp.bar, target, abort);
             if (!ok) break;
+        } else if (kind == PH_ALLREDUCE) {
+            // every rank's partial of exchange k is in (its own CTAs included)
+            const int k = ph.x.k;
+            if (!xchg_wait(sp.xbar[sp.rank], xtarget(k), abort)) break;
+            allreduce_phase(sp, ph.x, (int)((epoch * sp.n_xchg + k) & 1ull));
         } else {
             if (i > 0 && !grid_wait(sp.bar, (unsigned)i * grid, abort)) break;
             if (kind == PH_EMBED) {
                 embed_phase(sp, tok);
             } else {
                 copy_params(gp, &ph.g, offsetof(GemvParams, vrange));
+                if (ph.x.k >= 0) {  // row-parallel partial sums into exchange buffer (epoch·n + k) % 2
+                    if (threadIdx.x == 0)
+                        gp->seg[0].y = sp.xpart[sp.rank] + ((epoch * sp.n_xchg + ph.x.k) & 1ull) * ph.x.n;
+                    bar_consumers();
+                }
                 const int vbeg = ph.g.vrange[blockIdx.x], vend = ph.g.vrange[blockIdx.x + 1];
                 float s_in = 1.f;
                 if (gp->xq) s_in = load_xq(*gp, uni);
@@ -482,7 +544,11 @@ __global__ void __launch_bounds__(kGemvThreads, 1) step_kernel(const __grid_cons
         }
         // arrive: every store of this phase by this CTA happens before the count
         bar_consumers();
-        if (threadIdx.x == 0) grid_arrive(sp.bar);
+        if (threadIdx.x == 0) {
+            grid_arrive(sp.bar);
+            if (kind == PH_GEMV && ph.x.k >= 0)  // this CTA's partial rows are in: tell every rank
+                for (int r = 0; r < sp.tp; ++r) red_release_sys(sp.xbar[r], 1ull);
+        }
     }
     // CTA 0 turns the step's argmax into the next token once every CTA has
     // finished the LM head, and advances the position.
@@ -495,7 +561,28 @@ __global__ void __launch_bounds__(kGemvThreads, 1) step_kernel(const __grid_cons
             set_err(kErrMbarTimeout);
             return;
         }
-        const unsigned long long k = __ldcg(sp.key);
+        unsigned long long k = __ldcg(sp.key);
+        if (sp.tp > 1) {
+            // argmax over the ranks' vocabulary shards: publish this rank's key
+            // in every rank's key slot, count it as the last exchange of the step
+            for (int r = 0; r < sp.tp; ++r) {
+                sp.xkey[r][sp.rank] = k;
+                red_release_sys(sp.xbar[r], (unsigned long long)grid);
+            }
+            const unsigned long long target = xtarget(sp.n_xchg - 1);
+            uint32_t it2 = 0;
+            while (ld_acquire_sys(sp.xbar[sp.rank]) < target && ++it2 < kGridSpinLimit) {
+            }
+            if (it2 >= kGridSpinLimit) {
+                set_err(kErrMbarTimeout);
+                return;
+            }
+            for (int r = 0; r < sp.tp; ++r) {
+                const unsigned long long kr = __ldcv(sp.xkey[sp.rank] + r);
+                k = kr > k ? kr : k;
+            }
+            *sp.epoch = epoch + 1ull;
+        }
         int id = (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
         if (k == 0ull || id < 0 || id >= sp.vocab) {  // no finite logit reached the argmax
             set_err(kErrBadToken);

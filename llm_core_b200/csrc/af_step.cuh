@@ -27,7 +27,9 @@
 
 namespace af {
 
-enum StepPhaseKind : int { PH_EMBED = 0, PH_GEMV = 1, PH_ATTN = 2 };
+enum StepPhaseKind : int { PH_EMBED = 0, PH_GEMV = 1, PH_ATTN = 2, PH_ALLREDUCE = 3 };
+
+constexpr int kStepMaxRanks = 8;
 
 constexpr int kStepMaxG = 8;            // query heads per kv head
 constexpr int kStepAttnChunk = 64;      // KV positions per attention chunk
@@ -35,10 +37,24 @@ constexpr int kStepHdr = kGemvSmemHdr;  // mbarriers, flags, phase parameter cop
 constexpr int kStepUnion = 40 * 1024;   // XQ input of a GEMV phase / attention scratch
 constexpr int kStepSmem = 227 * 1024;
 
+// Tensor-parallel exchange k of a step (the row-parallel O / down GEMVs):
+// the GEMV stores its partial sums in this rank's exchange buffer k % 2 and
+// every CTA counts its arrival on every rank's exchange counter; the
+// following PH_ALLREDUCE phase adds the ranks' partials (in rank order) to
+// the residual and quantises it for the next GEMV.
+struct XchgParams {
+    int k;                 // exchange index within the step (-1: none)
+    float* resid;          // PH_ALLREDUCE: residual stream [n]
+    uint8_t* xq;           // PH_ALLREDUCE: quantised input of the next GEMV
+    const float* norm_w;   // PH_ALLREDUCE: its RMSNorm weights
+    int n;                 // values (n_embd)
+};
+
 struct StepPhase {
     int kind;
     GemvParams g;  // PH_GEMV
     AttnParams a;  // PH_ATTN (nsplit = splits per kv head)
+    XchgParams x;  // PH_GEMV of a row-parallel GEMV, PH_ALLREDUCE
 };
 
 struct StepParams {
@@ -57,9 +73,22 @@ struct StepParams {
     int* pos;
     int* hist;
     int ring_bytes;
+    // tensor parallel (tp > 1): per rank r, its exchange area mapped into
+    // this process (IPC): partial sums [2][n_embd] f32, arrival counter
+    // (u64, monotonic over the engine's life), argmax keys [kStepMaxRanks]
+    int tp, rank;
+    int n_xchg;                      // exchanges per step (2·layers + 1, the last one the argmax)
+    float* xpart[kStepMaxRanks];
+    unsigned long long* xbar[kStepMaxRanks];
+    unsigned long long* xkey[kStepMaxRanks];
+    unsigned long long* epoch;       // steps run by this engine (this rank's memory)
 };
 
+// Bytes of one rank's exchange area for n_embd values.
+inline size_t step_xchg_bytes(int n_embd) { return 256 + 64 + (size_t)2 * n_embd * sizeof(float); }
+
 // Whether a model shape runs on the step kernel (else: separate kernels).
+// Tensor-parallel ranks need n_embd a multiple of 32 as well (checked by the engine).
 bool step_supported(int n_heads, int n_kv_heads, int head_dim, int n_embd, int ffn);
 cudaError_t step_init();
 // Zero the arrival counter and launch the cooperative step grid on `st`.
