@@ -412,8 +412,7 @@ cudaError_t enqueue_step(af_engine* e, Prof* prof = nullptr) {
 // Tensor-parallel exchange areas: each rank allocates and zeroes its own,
 // the CUDA IPC handles travel over the NCCL communicator (all-gather), and
 // every rank maps the others' areas, so the step kernel reaches the peers'
-// partial sums, counters and argmax slots with plain loads and system-scope
-// reductions over NVLink.
+// receive slots (tagged stores), argmax slots and counters over NVLink.
 cudaError_t setup_exchange(af_engine* e) {
     const int E = e->cfg.n_embd;
     const size_t bytes = step_xchg_bytes(E);
@@ -444,7 +443,7 @@ cudaError_t setup_exchange(af_engine* e) {
         }
         sp.xbar[r] = reinterpret_cast<unsigned long long*>(base);
         sp.xkey[r] = reinterpret_cast<unsigned long long*>(base + 128);
-        sp.xpart[r] = reinterpret_cast<float*>(base + 256);
+        sp.xrecv[r] = reinterpret_cast<unsigned long long*>(base + 256);
     }
     sp.epoch = epoch;
     // every rank has mapped every area before any step runs
@@ -462,26 +461,26 @@ cudaError_t build_step(af_engine* e) {
     const int E = c.n_embd;
     ENG_TRY(step_init());
     const bool tp = e->tp > 1;
-    auto allreduce = [&](int k, const float* norm_w, uint8_t* xq) {
-        StepPhase r = {};
-        r.kind = PH_ALLREDUCE;
-        r.x.k = k;
-        r.x.resid = e->x[0];
-        r.x.xq = xq;
-        r.x.norm_w = norm_w;
-        r.x.n = E;
-        return r;
+    auto none = [](StepPhase& p) { p.x.k_out = p.x.k_in = -1; };
+    // exchange k: input of the next normalised GEMV (norm weights norm_w);
+    // the residual ping-pongs x[k % 2] -> x[(k + 1) % 2]
+    auto xin = [&](StepPhase& p, int k, const float* norm_w) {
+        p.x.k_in = k;
+        p.x.resid_in = e->x[k & 1];
+        p.x.resid_out = e->x[(k + 1) & 1];
+        p.x.norm_w = norm_w;
+        p.x.n = E;
     };
     std::vector<StepPhase> ph;
     StepPhase embed = {};
     embed.kind = PH_EMBED;
-    embed.x.k = -1;
+    none(embed);
     ph.push_back(embed);
     for (int l = 0; l < c.n_layer; ++l) {
         const LayerW& L = e->layers[l];
         StepPhase q = {};
         q.kind = PH_GEMV;
-        q.x.k = -1;
+        none(q);
         q.g = base_params(e, E);
         q.g.seg[0] = seg_of(L.wq, e->q, L.bq);
         q.g.seg[1] = seg_of(L.wk, e->k, L.bk);
@@ -490,12 +489,13 @@ cudaError_t build_step(af_engine* e) {
         q.g.xq = e->xq_a;
         q.g.xq_norm = 1;
         q.g.epi = EPI_STORE;
+        if (tp && l > 0) xin(q, 2 * l - 1, L.attn_norm);
         gemv_configure(q.g, e->sms);
         ph.push_back(q);
 
         StepPhase at = {};
         at.kind = PH_ATTN;
-        at.x.k = -1;
+        none(at);
         AttnParams& a = at.a;
         a.q = e->q;
         a.k = e->k;
@@ -524,14 +524,14 @@ cudaError_t build_step(af_engine* e) {
 
         StepPhase o = {};
         o.kind = PH_GEMV;
-        o.x.k = -1;
+        none(o);
         o.g = base_params(e, e->Hl * e->hd);
         o.g.seg[0] = seg_of(L.wo, e->ypart, nullptr);
         o.g.nseg = 1;
         o.g.xq = e->xq_o;
         if (tp) {  // row-parallel: partial sums into the exchange buffer, then the all-reduce
             o.g.epi = EPI_STORE;
-            o.x.k = 2 * l;
+            o.x.k_out = 2 * l;
             o.x.n = E;
         } else {
             o.g.epi = EPI_RESID;
@@ -541,11 +541,10 @@ cudaError_t build_step(af_engine* e) {
         }
         gemv_configure(o.g, e->sms);
         ph.push_back(o);
-        if (tp) ph.push_back(allreduce(2 * l, L.ffn_norm, e->xq_gu));
 
         StepPhase gu = {};
         gu.kind = PH_GEMV;
-        gu.x.k = -1;
+        none(gu);
         gu.g = base_params(e, E);
         gu.g.seg[0] = seg_of(L.wg, e->h, nullptr);
         gu.g.seg[1] = seg_of(L.wu, nullptr, nullptr);
@@ -554,12 +553,13 @@ cudaError_t build_step(af_engine* e) {
         gu.g.xq = e->xq_gu;
         gu.g.xq_norm = 1;
         gu.g.q_out = e->xq_d;
+        if (tp) xin(gu, 2 * l, L.ffn_norm);
         gemv_configure(gu.g, e->sms);
         ph.push_back(gu);
 
         StepPhase d = {};
         d.kind = PH_GEMV;
-        d.x.k = -1;
+        none(d);
         d.g = base_params(e, e->Fl);
         d.g.seg[0] = seg_of(L.wd, e->ypart, nullptr);
         d.g.nseg = 1;
@@ -567,7 +567,7 @@ cudaError_t build_step(af_engine* e) {
         const float* next_norm = l + 1 < c.n_layer ? e->layers[l + 1].attn_norm : e->out_norm;
         if (tp) {
             d.g.epi = EPI_STORE;
-            d.x.k = 2 * l + 1;
+            d.x.k_out = 2 * l + 1;
             d.x.n = E;
         } else {
             d.g.epi = EPI_RESID;
@@ -577,11 +577,10 @@ cudaError_t build_step(af_engine* e) {
         }
         gemv_configure(d.g, e->sms);
         ph.push_back(d);
-        if (tp) ph.push_back(allreduce(2 * l + 1, next_norm, e->xq_a));
     }
     StepPhase lm = {};
     lm.kind = PH_GEMV;
-    lm.x.k = -1;
+    none(lm);
     lm.g = base_params(e, E);
     lm.g.seg[0] = seg_of(e->output, e->logits, nullptr);
     lm.g.nseg = 1;
@@ -590,6 +589,7 @@ cudaError_t build_step(af_engine* e) {
     lm.g.epi = EPI_ARGMAX;
     lm.g.argmax = e->key;
     lm.g.argmax_base = e->V0;
+    if (tp) xin(lm, 2 * c.n_layer - 1, e->out_norm);
     gemv_configure(lm.g, e->sms);
     ph.push_back(lm);
 
@@ -617,7 +617,7 @@ cudaError_t build_step(af_engine* e) {
     sp.ring_bytes = kStepSmem - kStepHdr - kStepUnion;
     sp.tp = e->tp;
     sp.rank = e->rank;
-    sp.n_xchg = 2 * c.n_layer + 1;
+    sp.n_buf = 2 * c.n_layer;
     if (tp) ENG_TRY(setup_exchange(e));
     return cudaSuccess;
 }
@@ -906,7 +906,9 @@ cudaError_t af_engine_finalize(af_engine* e) {
         ENG_TRY(gemv_init());
         ENG_TRY(attention_init());
         const char* sv = std::getenv("AF_STEP_KERNEL");
+        // tensor-parallel exchanges hold at most 8 float4 chunks per consumer thread
         e->use_step = (!sv || std::atoi(sv) != 0) && e->tp <= kStepMaxRanks && c.n_embd % 32 == 0 &&
+                      (e->tp == 1 || c.n_embd <= 8192) &&
                       step_supported(e->Hl, e->KVl, e->hd, c.n_embd, e->Fl);
         if (e->use_step) ENG_TRY(build_step(e));
         ENG_TRY(cudaDeviceSynchronize());

@@ -8,48 +8,6 @@ namespace af {
 
 __device__ int g_err = 0;
 
-// Quantise value v (index idx = 32·g + lane) into the XQ layout.  The 16-bit
-// split matches the consumers' integer form: q = rint(v·32639/amax),
-// hi = (q + 128) >> 8, lo = q − 256·hi.
-__device__ void xq_store32(uint8_t* xq, float v, const float* norm_w, int K, int idx) {
-    const bool in = idx >= 0 && idx < K;
-    xq_store32w(xq, v, norm_w && in ? __ldg(norm_w + idx) : 1.f, norm_w != nullptr, K, idx);
-}
-
-__device__ void xq_store32w(uint8_t* xq, float v, float wgt, bool norm, int K, int idx) {
-    const int lane = threadIdx.x & 31;
-    const bool in = idx >= 0 && idx < K;
-    if (!in) v = 0.f;
-    const float a = v * wgt;
-    const float amax = warp_max(fabsf(a));
-    const float inv = amax > 0.f ? 32639.f / amax : 0.f;
-    const int q = max(-32639, min(32639, __float2int_rn(a * inv)));
-    const int hi = (q + 128) >> 8, lo = q - 256 * hi;
-    int is = q;
-#pragma unroll
-    for (int o = 1; o < 16; o <<= 1) is += __shfl_xor_sync(0xffffffffu, is, o);  // per 16
-    const float fs = warp_sum(a);
-    const float ss = norm ? warp_sum(v * v) : 0.f;
-    if (!in) return;
-    uint8_t* sb = xq + (idx >> 8) * kXqSb;
-    const int ko = idx & 255;
-    sb[ko] = (uint8_t)(hi & 0xFF);
-    sb[256 + ko] = (uint8_t)(lo & 0xFF);
-    if ((lane & 15) == 0) reinterpret_cast<int*>(sb + kXqI16)[ko >> 4] = is;
-    if (lane == 0) {
-        reinterpret_cast<float*>(sb + kXqXs)[ko >> 5] = amax / 32639.f;
-        reinterpret_cast<float*>(sb + kXqS32)[ko >> 5] = fs;
-        if (norm) reinterpret_cast<float*>(xq + xq_bytes(K))[idx >> 5] = ss;
-    }
-}
-
-// One warp quantises values [32·g, 32·g + 32) of src (global f32, written by
-// other CTAs: read through L2).
-__device__ void xq_quantize_group(uint8_t* xq, const float* src, const float* norm_w, int K, int g) {
-    const int idx = 32 * g + (threadIdx.x & 31);
-    xq_store32(xq, idx < K ? __ldcg(src + idx) : 0.f, norm_w, K, idx);
-}
-
 namespace {
 
 using namespace gdev;

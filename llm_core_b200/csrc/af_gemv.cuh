@@ -60,6 +60,7 @@ constexpr int kGemvStageBlocks = 8;  // super-blocks per K stage (one per consum
 constexpr int kGemvMaxK = 12288;     // input length quantised by the f32 prologue
 constexpr int kGemvMaxGrid = 296;
 constexpr int kGemvSmemHdr = 6144;   // mbarriers, abort flag, phase parameters, reduction scratch
+constexpr int kGemvMaxRanks = 8;     // tensor-parallel ranks a plain-store epilogue can send to
 
 static_assert(kGemvStageBlocks == kGemvConsumerWarps, "one super-block per consumer warp");
 
@@ -111,6 +112,13 @@ struct GemvParams {
     // the per-16 sums of squares for that GEMV's RMSNorm
     uint8_t* q_out;
     const float* q_norm_w;
+    // tensor-parallel partial sums (xsend_n > 0, EPI_STORE): instead of y, the
+    // epilogue stores each value v of row i as the 64-bit word
+    // (xtag << 32) | bits(v) at xsend[r][i] for every rank r < xsend_n; the
+    // tag makes the word its own arrival flag (no fence, no counter)
+    unsigned long long* xsend[kGemvMaxRanks];
+    int xsend_n;
+    uint32_t xtag;
     int ring_bytes;        // weight ring in shared memory (multiple of 16)
     int grid;
     int vrange[kGemvMaxGrid + 1];  // CTA i owns fragments [vrange[i], vrange[i+1])
@@ -152,13 +160,50 @@ cudaError_t gemv_launch(const GemvParams& p, cudaStream_t stream, bool pdl);
 cudaError_t xq_quantize_launch(uint8_t* xq, const float* x, const float* norm_w, int K, cudaStream_t st, bool pdl);
 
 // Quantise value v (this lane's; the warp's 32 lanes hold one 32-value group,
-// indices idx = 32·g + lane) into the XQ buffer.  With norm_w the weighted
-// value w·v is quantised and Σv² of the group stored after the layout.  All
-// 32 lanes must call (lanes past the vector pass any v; they store nothing).
-__device__ void xq_store32(uint8_t* xq, float v, const float* norm_w, int K, int idx);
-// Same with the lane's RMSNorm weight already loaded (norm: store Σv²).
-__device__ void xq_store32w(uint8_t* xq, float v, float wgt, bool norm, int K, int idx);
-// One warp quantises values [32·g, 32·g + 32) of src (global f32).
-__device__ void xq_quantize_group(uint8_t* xq, const float* src, const float* norm_w, int K, int g);
+// indices idx = 32·g + lane) into the XQ buffer, with the lane's RMSNorm
+// weight already loaded (norm: the weighted value w·v is quantised and Σv²
+// of the group stored after the layout).  All 32 lanes must call (lanes
+// past the vector pass any v; they store nothing).  The 16-bit split matches
+// the consumers' integer form: q = rint(v·32639/amax), hi = (q + 128) >> 8,
+// lo = q − 256·hi.  Inline: it runs in the epilogues of the hot loops.
+__device__ __forceinline__ void xq_store32w(uint8_t* xq, float v, float wgt, bool norm, int K, int idx) {
+    const int lane = threadIdx.x & 31;
+    const bool in = idx >= 0 && idx < K;
+    if (!in) v = 0.f;
+    const float a = v * wgt;
+    const float amax = warp_max(fabsf(a));
+    const float inv = amax > 0.f ? 32639.f / amax : 0.f;
+    const int q = max(-32639, min(32639, __float2int_rn(a * inv)));
+    const int hi = (q + 128) >> 8, lo = q - 256 * hi;
+    int is = q;
+#pragma unroll
+    for (int o = 1; o < 16; o <<= 1) is += __shfl_xor_sync(0xffffffffu, is, o);  // per 16
+    const float fs = warp_sum(a);
+    const float ss = norm ? warp_sum(v * v) : 0.f;
+    if (!in) return;
+    uint8_t* sb = xq + (idx >> 8) * kXqSb;
+    const int ko = idx & 255;
+    sb[ko] = (uint8_t)(hi & 0xFF);
+    sb[256 + ko] = (uint8_t)(lo & 0xFF);
+    if ((lane & 15) == 0) reinterpret_cast<int*>(sb + kXqI16)[ko >> 4] = is;
+    if (lane == 0) {
+        reinterpret_cast<float*>(sb + kXqXs)[ko >> 5] = amax / 32639.f;
+        reinterpret_cast<float*>(sb + kXqS32)[ko >> 5] = fs;
+        if (norm) reinterpret_cast<float*>(xq + xq_bytes(K))[idx >> 5] = ss;
+    }
+}
+
+// Same, loading the weight from norm_w (nullptr: no norm).
+__device__ __forceinline__ void xq_store32(uint8_t* xq, float v, const float* norm_w, int K, int idx) {
+    const bool in = idx >= 0 && idx < K;
+    xq_store32w(xq, v, norm_w && in ? __ldg(norm_w + idx) : 1.f, norm_w != nullptr, K, idx);
+}
+
+// One warp quantises values [32·g, 32·g + 32) of src (global f32, written by
+// other CTAs: read through L2).
+__device__ __forceinline__ void xq_quantize_group(uint8_t* xq, const float* src, const float* norm_w, int K, int g) {
+    const int idx = 32 * g + (threadIdx.x & 31);
+    xq_store32(xq, idx < K ? __ldcg(src + idx) : 0.f, norm_w, K, idx);
+}
 
 }  // namespace af

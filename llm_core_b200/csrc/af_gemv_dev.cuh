@@ -333,38 +333,16 @@ __device__ __forceinline__ float2 q6_unit(const uint8_t* u, const XQ6& x, int la
 
 // ---------------------------------------------------------------- input
 
-// f32-input prologue: x (+ pending residual, optionally RMS-normalised)
-// loaded with all NIT float4 loads per thread in flight (norm weights too),
-// then quantised into the shared XQ layout.
+// Quantise NIT float4 chunks per thread (chunk j of thread t holds values
+// 4·(j·kCT + t) .. +3; chunks at or past nvec are zero) into the shared XQ
+// layout, RMS-normalising first (weights w) when NORM.  `red` is kCW floats
+// of shared scratch.
 template <int NIT, bool NORM>
-__device__ __forceinline__ void input_prologue_t(const GemvParams& p, uint8_t* xqs, float* red) {
+__device__ __forceinline__ void quantise_f4(float4 (&a)[NIT], const float4 (&w)[NORM ? NIT : 1], int nvec, float eps,
+                                            uint8_t* xqs, float* red) {
     static_assert(kCT % 8 == 0, "8 consecutive threads own one 32-value group");
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
-    const int nvec = p.K / 4;
-    float4 a[NIT], w[NORM ? NIT : 1];
-#pragma unroll
-    for (int j = 0; j < NIT; ++j) {
-        const int v = j * kCT + tid;
-        const int vc = v < nvec ? v : 0;
-        a[j] = __ldcg(reinterpret_cast<const float4*>(p.x) + vc);
-        if (p.x_add) {
-            const float4 b = __ldcg(reinterpret_cast<const float4*>(p.x_add) + vc);
-            a[j].x += b.x;
-            a[j].y += b.y;
-            a[j].z += b.z;
-            a[j].w += b.w;
-        }
-        if (NORM) w[NORM ? j : 0] = __ldg(reinterpret_cast<const float4*>(p.norm_w) + vc);
-        if (v >= nvec) a[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-    if (p.x_store && blockIdx.x == 0) {
-#pragma unroll
-        for (int j = 0; j < NIT; ++j) {
-            const int v = j * kCT + tid;
-            if (v < nvec) reinterpret_cast<float4*>(p.x_store)[v] = a[j];
-        }
-    }
     if (NORM) {
         float ss = 0.f;
 #pragma unroll
@@ -376,7 +354,7 @@ __device__ __forceinline__ void input_prologue_t(const GemvParams& p, uint8_t* x
 #pragma unroll
         for (int k = 0; k < kCW; ++k) tot += red[k];
         // rms_norm_out (src/models/llama_model.cpp:393-419): 1/sqrt(ss/n + eps)
-        const float inv_rms = 1.f / sqrtf(tot / (float)p.K + p.eps);
+        const float inv_rms = 1.f / sqrtf(tot / (float)(4 * nvec) + eps);
 #pragma unroll
         for (int j = 0; j < NIT; ++j) {
             const float4 wj = w[NORM ? j : 0];
@@ -428,6 +406,39 @@ __device__ __forceinline__ void input_prologue_t(const GemvParams& p, uint8_t* x
     }
 }
 
+// f32-input prologue: x (+ pending residual, optionally RMS-normalised)
+// loaded with all NIT float4 loads per thread in flight (norm weights too),
+// then quantised into the shared XQ layout.
+template <int NIT, bool NORM>
+__device__ __forceinline__ void input_prologue_t(const GemvParams& p, uint8_t* xqs, float* red) {
+    const int tid = threadIdx.x;
+    const int nvec = p.K / 4;
+    float4 a[NIT], w[NORM ? NIT : 1];
+#pragma unroll
+    for (int j = 0; j < NIT; ++j) {
+        const int v = j * kCT + tid;
+        const int vc = v < nvec ? v : 0;
+        a[j] = __ldcg(reinterpret_cast<const float4*>(p.x) + vc);
+        if (p.x_add) {
+            const float4 b = __ldcg(reinterpret_cast<const float4*>(p.x_add) + vc);
+            a[j].x += b.x;
+            a[j].y += b.y;
+            a[j].z += b.z;
+            a[j].w += b.w;
+        }
+        if (NORM) w[NORM ? j : 0] = __ldg(reinterpret_cast<const float4*>(p.norm_w) + vc);
+        if (v >= nvec) a[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    if (p.x_store && blockIdx.x == 0) {
+#pragma unroll
+        for (int j = 0; j < NIT; ++j) {
+            const int v = j * kCT + tid;
+            if (v < nvec) reinterpret_cast<float4*>(p.x_store)[v] = a[j];
+        }
+    }
+    quantise_f4<NIT, NORM>(a, w, nvec, p.eps, xqs, red);
+}
+
 // Quantise the f32 input of p into the shared XQ layout (all consumer warps;
 // `red` is kCW floats of shared scratch).  Ends with a consumer barrier.
 __device__ __forceinline__ void input_prologue(const GemvParams& p, uint8_t* xqs, float* red) {
@@ -446,6 +457,17 @@ __device__ __forceinline__ void input_prologue(const GemvParams& p, uint8_t* xqs
     }
 #undef AF_PRO
     bar_consumers();
+}
+
+// RMSNorm scale 1/sqrt(Σx²/K + eps) of a quantised input in shared memory,
+// from the per-32 sums of squares stored after the layout, added in a fixed
+// order (deterministic; every lane returns the same value).
+__device__ __forceinline__ float xq_norm_scale(const uint8_t* xqs, int K, float eps) {
+    const float* pss = reinterpret_cast<const float*>(xqs + xq_bytes(K));
+    float ss = 0.f;
+    for (int g = (threadIdx.x & 31); g < K / 32; g += 32) ss += pss[g];
+    ss = warp_sum(ss);
+    return 1.f / sqrtf(ss / (float)K + eps);
 }
 
 // Copy the quantised input (XQ layout, written by other CTAs or an earlier
@@ -468,17 +490,7 @@ __device__ __forceinline__ float load_xq(const GemvParams& p, uint8_t* xqs) {
             if (i0 + u * kCT < n16) dst[i0 + u * kCT] = v[u];
     }
     bar_consumers();
-    float s_in = 1.f;
-    if (p.xq_norm) {
-        // s = 1/sqrt(Σx²/K + eps) from the producers' per-group sums, in a
-        // fixed order (deterministic)
-        const float* pss = reinterpret_cast<const float*>(xqs + xq_bytes(p.K));
-        float ss = 0.f;
-        for (int g = (tid & 31); g < p.K / 32; g += 32) ss += pss[g];
-        ss = warp_sum(ss);
-        s_in = 1.f / sqrtf(ss / (float)p.K + p.eps);
-    }
-    return s_in;
+    return p.xq_norm ? xq_norm_scale(xqs, p.K, p.eps) : 1.f;
 }
 
 // ---------------------------------------------------------------- consumers
@@ -592,7 +604,12 @@ __device__ __forceinline__ bool consume(const GemvParams& p, int vbeg, int vend,
                 } else {
                     if (eseg.bias) v += eseg.bias[erow];
                     out = v;
-                    eseg.y[erow] = v;
+                    if (p.xsend_n) {
+                        const unsigned long long wv = ((unsigned long long)p.xtag << 32) | __float_as_uint(v);
+                        for (int rk = 0; rk < p.xsend_n; ++rk) st_relaxed_sys(p.xsend[rk] + erow, wv);
+                    } else {
+                        eseg.y[erow] = v;
+                    }
                     if (p.epi == EPI_ARGMAX) {
                         // a lane's rows arrive in increasing order; ties keep the lowest index
                         const uint32_t gi = (uint32_t)(p.argmax_base + erow);

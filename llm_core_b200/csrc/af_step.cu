@@ -68,38 +68,112 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
     return v;
 }
 
-// Thread 0 spins (bounded) until this rank's exchange counter reaches
-// `target`; the consumer barrier publishes the result.
-__device__ bool xchg_wait(const unsigned long long* bar, unsigned long long target, volatile int* flags) {
-    if (threadIdx.x == 0) {
-        bool ok = false;
-        for (uint32_t i = 0; i < kGridSpinLimit; ++i) {
-            if (ld_acquire_sys(bar) >= target) {
-                ok = true;
-                break;
-            }
-            if ((i & 63) == 63 && flags[0]) break;
-        }
-        if (!ok) {
-            if (!flags[0]) set_err(kErrMbarTimeout);
-            flags[0] = 1;
-        }
-    }
-    bar_consumers();
-    return flags[0] == 0;
+__device__ __forceinline__ ulonglong2 ld_relaxed_sys2(const unsigned long long* p) {
+    ulonglong2 v;
+    asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
+    return v;
 }
 
-// All-reduce of exchange k: residual += Σ_r partial_r (ranks in order, so
-// every rank computes the same sum), and the quantised input of the next GEMV
-// (one warp per 32-value group).
-__device__ void allreduce_phase(const StepParams& sp, const XchgParams& x, int buf) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int g = blockIdx.x * kCW + warp; g < x.n / 32; g += gridDim.x * kCW) {
-        const int idx = 32 * g + lane;
-        float v = __ldcg(x.resid + idx);
-        for (int r = 0; r < sp.tp; ++r) v += __ldcv(sp.xpart[r] + (size_t)buf * x.n + idx);
-        x.resid[idx] = v;
-        xq_store32(x.xq, v, x.norm_w, x.n, idx);
+// Input of a GEMV fed by tensor-parallel exchange `seq` (sequence number
+// over the engine's life).  Thread t owns the float4 chunks j·kCT + t of the
+// vector: it loads the residual chunks, then, RP ranks per pass, issues all
+// its tagged-word loads of those ranks at once (16-byte vectors), re-polls
+// the words whose tag is not yet this exchange's (bounded; every missing word
+// per round trip), and adds the partials in rank order.  The sum goes to
+// resid_out for the 32-value groups this CTA owns (group g: CTA g % grid) and
+// is RMS-normalised and quantised into the shared XQ layout like an f32
+// input.  False on a timeout or an abort.
+template <int NIT>
+__device__ bool xchg_input_t(const StepParams& sp, const XchgParams& x, unsigned long long seq, uint8_t* xqs,
+                             float eps, volatile int* flags, float* red) {
+    constexpr int RP = NIT <= 4 ? 2 : 1;  // ranks per pass: ≤ 16 vector loads in flight per thread
+    const int tid = threadIdx.x;
+    const int nvec = x.n / 4;
+    const uint32_t tag = (uint32_t)(seq + 1ull);
+    const unsigned long long* area = sp.xrecv[sp.rank] + (size_t)(seq & 1ull) * kStepMaxRanks * x.n;
+    float4 a[NIT], w[NIT];
+#pragma unroll
+    for (int j = 0; j < NIT; ++j) {
+        const int v = j * kCT + tid;
+        a[j] = v < nvec ? __ldcg(reinterpret_cast<const float4*>(x.resid_in) + v) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    bool ok = true;
+    for (int r0 = 0; r0 < sp.tp && ok; r0 += RP) {
+        ulonglong2 t[NIT][RP][2];
+        auto word = [&](int j, int rr) { return area + (size_t)(r0 + rr) * x.n + 4 * (j * kCT + tid); };
+        auto live = [&](int j, int rr) { return j * kCT + tid < nvec && r0 + rr < sp.tp; };
+        auto have = [&](const ulonglong2& u) {
+            return (uint32_t)(u.x >> 32) == tag && (uint32_t)(u.y >> 32) == tag;
+        };
+#pragma unroll
+        for (int j = 0; j < NIT; ++j)
+#pragma unroll
+            for (int rr = 0; rr < RP; ++rr) {
+                if (live(j, rr)) {
+                    t[j][rr][0] = ld_relaxed_sys2(word(j, rr));
+                    t[j][rr][1] = ld_relaxed_sys2(word(j, rr) + 2);
+                } else {
+                    t[j][rr][0] = t[j][rr][1] = make_ulonglong2((unsigned long long)tag << 32, (unsigned long long)tag << 32);
+                }
+            }
+        for (uint32_t it = 0;; ++it) {
+            bool all = true;
+#pragma unroll
+            for (int j = 0; j < NIT; ++j)
+#pragma unroll
+                for (int rr = 0; rr < RP; ++rr) all &= have(t[j][rr][0]) && have(t[j][rr][1]);
+            if (all) break;
+            if (it >= kGridSpinLimit || ((it & 15u) == 15u && flags[0])) {
+                ok = false;
+                break;
+            }
+#pragma unroll
+            for (int j = 0; j < NIT; ++j)
+#pragma unroll
+                for (int rr = 0; rr < RP; ++rr)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h)
+                        if (!have(t[j][rr][h])) t[j][rr][h] = ld_relaxed_sys2(word(j, rr) + 2 * h);
+        }
+#pragma unroll
+        for (int j = 0; j < NIT; ++j)
+#pragma unroll
+            for (int rr = 0; rr < RP; ++rr)
+                if (r0 + rr < sp.tp) {
+                    a[j].x += __uint_as_float((uint32_t)t[j][rr][0].x);
+                    a[j].y += __uint_as_float((uint32_t)t[j][rr][0].y);
+                    a[j].z += __uint_as_float((uint32_t)t[j][rr][1].x);
+                    a[j].w += __uint_as_float((uint32_t)t[j][rr][1].y);
+                }
+    }
+    if (!ok) {
+        if (!flags[0]) set_err(kErrMbarTimeout);
+        flags[0] = 1;
+    }
+    bar_consumers();
+    if (flags[0]) return false;
+#pragma unroll
+    for (int j = 0; j < NIT; ++j) {
+        const int v = j * kCT + tid;
+        if (v < nvec && (v >> 3) % (int)gridDim.x == (int)blockIdx.x) reinterpret_cast<float4*>(x.resid_out)[v] = a[j];
+        w[j] = v < nvec ? __ldg(reinterpret_cast<const float4*>(x.norm_w) + v) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    quantise_f4<NIT, true>(a, w, nvec, eps, xqs, red);
+    bar_consumers();
+    return true;
+}
+
+__device__ bool xchg_input(const StepParams& sp, const XchgParams& x, unsigned long long seq, uint8_t* xqs,
+                           float eps, volatile int* flags, float* red) {
+    switch ((x.n / 4 + kCT - 1) / kCT) {
+        case 1: return xchg_input_t<1>(sp, x, seq, xqs, eps, flags, red);
+        case 2: return xchg_input_t<2>(sp, x, seq, xqs, eps, flags, red);
+        case 3: return xchg_input_t<3>(sp, x, seq, xqs, eps, flags, red);
+        case 4: return xchg_input_t<4>(sp, x, seq, xqs, eps, flags, red);
+        case 5: return xchg_input_t<5>(sp, x, seq, xqs, eps, flags, red);
+        case 6: return xchg_input_t<6>(sp, x, seq, xqs, eps, flags, red);
+        case 7: return xchg_input_t<7>(sp, x, seq, xqs, eps, flags, red);
+        default: return xchg_input_t<8>(sp, x, seq, xqs, eps, flags, red);
     }
 }
 
@@ -494,11 +568,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) step_kernel(const __grid_cons
     const int pos = __ldcg(sp.pos);
     const int tok = __ldcg(sp.token);
     const unsigned long long epoch = sp.tp > 1 ? __ldcg(sp.epoch) : 0ull;
-    // exchange counter target after exchange k of this step: every CTA of
-    // every rank counts once per exchange
-    auto xtarget = [&](int k) {
-        return (unsigned long long)sp.tp * gridDim.x * (epoch * (unsigned long long)sp.n_xchg + (unsigned long long)k + 1ull);
-    };
+    // sequence number of partial-sum exchange k of this step
+    auto xseq = [&](int k) { return epoch * (unsigned long long)sp.n_buf + (unsigned long long)k; };
     uint32_t consumed = 0;
     int head = 0;
     const unsigned grid = gridDim.x;
@@ -516,26 +587,35 @@ __global__ void __launch_bounds__(kGemvThreads, 1) step_kernel(const __grid_cons
             else if (G <= 4) ok = attn_phase<4>(*ap, s, pos, sp.bar, target, abort);
             else ok = attn_phase<kStepMaxG>(*ap, s, pos, sp.bar, target, abort);
             if (!ok) break;
-        } else if (kind == PH_ALLREDUCE) {
-            // every rank's partial of exchange k is in (its own CTAs included)
-            const int k = ph.x.k;
-            if (!xchg_wait(sp.xbar[sp.rank], xtarget(k), abort)) break;
-            allreduce_phase(sp, ph.x, (int)((epoch * sp.n_xchg + k) & 1ull));
         } else {
-            if (i > 0 && !grid_wait(sp.bar, (unsigned)i * grid, abort)) break;
+            // a GEMV fed by an exchange waits for the tagged partials instead
+            // of the grid (the tags arrive only after every rank's producing
+            // phase, and everything else it reads is older)
+            const bool xin = kind == PH_GEMV && ph.x.k_in >= 0;
+            if (i > 0 && !xin && !grid_wait(sp.bar, (unsigned)i * grid, abort)) break;
             if (kind == PH_EMBED) {
                 embed_phase(sp, tok);
             } else {
                 copy_params(gp, &ph.g, offsetof(GemvParams, vrange));
-                if (ph.x.k >= 0) {  // row-parallel partial sums into exchange buffer (epoch·n + k) % 2
-                    if (threadIdx.x == 0)
-                        gp->seg[0].y = sp.xpart[sp.rank] + ((epoch * sp.n_xchg + ph.x.k) & 1ull) * ph.x.n;
+                if (ph.x.k_out >= 0) {  // row-parallel partial sums, sent to every rank
+                    if (threadIdx.x == 0) {
+                        const unsigned long long q = xseq(ph.x.k_out);
+                        for (int r = 0; r < sp.tp; ++r)
+                            gp->xsend[r] = sp.xrecv[r] + ((size_t)(q & 1ull) * kStepMaxRanks + sp.rank) * ph.x.n;
+                        gp->xsend_n = sp.tp;
+                        gp->xtag = (uint32_t)(q + 1ull);
+                    }
                     bar_consumers();
                 }
                 const int vbeg = ph.g.vrange[blockIdx.x], vend = ph.g.vrange[blockIdx.x + 1];
                 float s_in = 1.f;
-                if (gp->xq) s_in = load_xq(*gp, uni);
-                else input_prologue(*gp, uni, red);
+                if (xin) {
+                    if (!xchg_input(sp, ph.x, xseq(ph.x.k_in), uni, gp->eps, abort, red)) break;
+                } else if (gp->xq) {
+                    s_in = load_xq(*gp, uni);
+                } else {
+                    input_prologue(*gp, uni, red);
+                }
                 if (!consume(*gp, vbeg, vend, ring, consumed, head, uni, s_in, smem)) {
                     *abort = 1;
                     break;
@@ -544,11 +624,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) step_kernel(const __grid_cons
         }
         // arrive: every store of this phase by this CTA happens before the count
         bar_consumers();
-        if (threadIdx.x == 0) {
-            grid_arrive(sp.bar);
-            if (kind == PH_GEMV && ph.x.k >= 0)  // this CTA's partial rows are in: tell every rank
-                for (int r = 0; r < sp.tp; ++r) red_release_sys(sp.xbar[r], 1ull);
-        }
+        if (threadIdx.x == 0) grid_arrive(sp.bar);
     }
     // CTA 0 turns the step's argmax into the next token once every CTA has
     // finished the LM head, and advances the position.
@@ -564,12 +640,12 @@ __global__ void __launch_bounds__(kGemvThreads, 1) step_kernel(const __grid_cons
         unsigned long long k = __ldcg(sp.key);
         if (sp.tp > 1) {
             // argmax over the ranks' vocabulary shards: publish this rank's key
-            // in every rank's key slot, count it as the last exchange of the step
+            // in every rank's key slot and count one arrival per rank and step
             for (int r = 0; r < sp.tp; ++r) {
                 sp.xkey[r][sp.rank] = k;
-                red_release_sys(sp.xbar[r], (unsigned long long)grid);
+                red_release_sys(sp.xbar[r], 1ull);
             }
-            const unsigned long long target = xtarget(sp.n_xchg - 1);
+            const unsigned long long target = (unsigned long long)sp.tp * (epoch + 1ull);
             uint32_t it2 = 0;
             while (ld_acquire_sys(sp.xbar[sp.rank]) < target && ++it2 < kGridSpinLimit) {
             }

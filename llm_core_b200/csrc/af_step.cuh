@@ -27,9 +27,9 @@
 
 namespace af {
 
-enum StepPhaseKind : int { PH_EMBED = 0, PH_GEMV = 1, PH_ATTN = 2, PH_ALLREDUCE = 3 };
+enum StepPhaseKind : int { PH_EMBED = 0, PH_GEMV = 1, PH_ATTN = 2 };
 
-constexpr int kStepMaxRanks = 8;
+constexpr int kStepMaxRanks = kGemvMaxRanks;
 
 constexpr int kStepMaxG = 8;            // query heads per kv head
 constexpr int kStepAttnChunk = 64;      // KV positions per attention chunk
@@ -37,16 +37,21 @@ constexpr int kStepHdr = kGemvSmemHdr;  // mbarriers, flags, phase parameter cop
 constexpr int kStepUnion = 40 * 1024;   // XQ input of a GEMV phase / attention scratch
 constexpr int kStepSmem = 227 * 1024;
 
-// Tensor-parallel exchange k of a step (the row-parallel O / down GEMVs):
-// the GEMV stores its partial sums in this rank's exchange buffer k % 2 and
-// every CTA counts its arrival on every rank's exchange counter; the
-// following PH_ALLREDUCE phase adds the ranks' partials (in rank order) to
-// the residual and quantises it for the next GEMV.
+// Tensor-parallel exchanges (the outputs of the row-parallel O and down
+// GEMVs, 2 per layer): the producing GEMV (k_out = k) sends each partial
+// value tagged with the exchange's sequence number straight into every rank's
+// receive area (slot [seq % 2][this rank]), and the GEMV that consumes the
+// sum (k_in = k) waits for the tags instead of a grid barrier: each of its
+// CTAs reads all ranks' partials, adds them in rank order to the residual
+// (resid_in → resid_out, ping-pong so that no CTA overwrites what another
+// still reads) and quantises the RMSNorm-weighted sum into its own shared
+// memory.  No fence, counter or separate reduction phase.
 struct XchgParams {
-    int k;                 // exchange index within the step (-1: none)
-    float* resid;          // PH_ALLREDUCE: residual stream [n]
-    uint8_t* xq;           // PH_ALLREDUCE: quantised input of the next GEMV
-    const float* norm_w;   // PH_ALLREDUCE: its RMSNorm weights
+    int k_out;             // exchange this GEMV's partial sums feed (-1: none)
+    int k_in;              // exchange whose sum is this GEMV's input (-1: none)
+    const float* resid_in; // residual stream before the exchange [n]
+    float* resid_out;      // after it (CTA g % grid writes group g)
+    const float* norm_w;   // RMSNorm weights of the consuming GEMV
     int n;                 // values (n_embd)
 };
 
@@ -54,7 +59,7 @@ struct StepPhase {
     int kind;
     GemvParams g;  // PH_GEMV
     AttnParams a;  // PH_ATTN (nsplit = splits per kv head)
-    XchgParams x;  // PH_GEMV of a row-parallel GEMV, PH_ALLREDUCE
+    XchgParams x;  // PH_GEMV: tensor-parallel exchanges
 };
 
 struct StepParams {
@@ -74,18 +79,19 @@ struct StepParams {
     int* hist;
     int ring_bytes;
     // tensor parallel (tp > 1): per rank r, its exchange area mapped into
-    // this process (IPC): partial sums [2][n_embd] f32, arrival counter
-    // (u64, monotonic over the engine's life), argmax keys [kStepMaxRanks]
+    // this process (IPC): argmax arrival counter (u64, monotonic over the
+    // engine's life), argmax keys [kStepMaxRanks], receive slots
+    // [2][kStepMaxRanks][n_embd] of tagged partial sums
     int tp, rank;
-    int n_xchg;                      // exchanges per step (2·layers + 1, the last one the argmax)
-    float* xpart[kStepMaxRanks];
+    int n_buf;                       // partial-sum exchanges per step (2·layers)
+    unsigned long long* xrecv[kStepMaxRanks];
     unsigned long long* xbar[kStepMaxRanks];
     unsigned long long* xkey[kStepMaxRanks];
     unsigned long long* epoch;       // steps run by this engine (this rank's memory)
 };
 
 // Bytes of one rank's exchange area for n_embd values.
-inline size_t step_xchg_bytes(int n_embd) { return 256 + 64 + (size_t)2 * n_embd * sizeof(float); }
+inline size_t step_xchg_bytes(int n_embd) { return 256 + (size_t)2 * kStepMaxRanks * n_embd * sizeof(unsigned long long); }
 
 // Whether a model shape runs on the step kernel (else: separate kernels).
 // Tensor-parallel ranks need n_embd a multiple of 32 as well (checked by the engine).
