@@ -77,18 +77,19 @@ def test_tp_shard_rejects_unsupported_shapes():
 
 
 @pytest.mark.gpu
-def test_tp2_matches_single_gpu():
-    """TP=2 (torchrun, NCCL) prefill logits and greedy continuation equal the
-    single-GPU engine's on the same GGUF."""
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_matches_single_gpu(world):
+    """TP=2 / TP=4 (torchrun, NCCL) prefill logits and greedy continuation
+    equal the single-GPU engine's on the same GGUF."""
     import torch
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     from llm_core_b200.engine import LlamaCudaModel
     sys.path.insert(0, os.path.join(ROOT, "tests"))
     import tp_worker
     path = model_path("small", 5)
-    out = os.path.join(os.environ.get("TMPDIR", "/tmp"), f"af_tp2_{os.getpid()}.npz")
-    cmd = [sys.executable, "-m", "torch.distributed.run", "--nproc-per-node", "2", "--master-addr", "127.0.0.1",
+    out = os.path.join(os.environ.get("TMPDIR", "/tmp"), f"af_tp{world}_{os.getpid()}.npz")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nproc-per-node", str(world), "--master-addr", "127.0.0.1",
            "--master-port", str(_free_port()), os.path.join(ROOT, "tests", "tp_worker.py"), path, out]
     r = subprocess.run(cmd, cwd=ROOT, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
