@@ -244,7 +244,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
     }
     if (tid == 0) p.counter[kvh] = 0u;
     if (p.xq_out) {
-        // quantise this kv head's G*hd outputs (whole 16-value groups) for the O projection
+        // quantise this kv head's G*hd outputs (whole 32-value groups) for the O projection
         __threadfence();
         __syncthreads();
         const int g0 = kvh * G * hd / 32, ng = G * hd / 32;  // 32-value warp groups

@@ -94,7 +94,7 @@ struct GemvParams {
     int nseg;
     int K;                 // input length, multiple of 256
     // input, quantised form: XQ layout of xq_bytes(K) bytes, and with xq_norm
-    // the per-64 sums of squares after it (RMSNorm input)
+    // the per-32 sums of squares after it (RMSNorm input)
     const uint8_t* xq;
     int xq_norm;
     // input, f32 form (prologue): x (+ x_add, stored to x_store) [+ RMSNorm]
@@ -109,7 +109,7 @@ struct GemvParams {
     int argmax_base;       // global index of row 0 (vocab shard offset)
     // optional: quantise the output vector (resid for EPI_RESID, y_0 otherwise)
     // into q_out (XQ of the next GEMV), weighted by q_norm_w when set, with
-    // the per-16 sums of squares for that GEMV's RMSNorm
+    // the per-32 sums of squares for that GEMV's RMSNorm
     uint8_t* q_out;
     const float* q_norm_w;
     // tensor-parallel partial sums (xsend_n > 0, EPI_STORE): instead of y, the

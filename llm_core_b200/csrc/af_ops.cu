@@ -147,7 +147,7 @@ __global__ void embed_kernel(float* __restrict__ x, const uint8_t* __restrict__ 
         x[v] = embed_value(W, type, nb, row_stride, *token, v);
     }
     if (xq) {
-        // quantise this block's values (two 16-value groups per warp) for the first GEMV
+        // quantise this block's values (one 32-value group per warp) for the first GEMV
         __threadfence();
         __syncthreads();
         const int g = (blockIdx.x * blockDim.x) / 32 + (threadIdx.x >> 5);

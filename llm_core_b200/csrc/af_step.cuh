@@ -14,13 +14,14 @@
 //   ATTN   RoPE, Q/K norm, KV store, split attention
 //
 // Every phase writes the next GEMV's input already quantised: the epilogue
-// that finishes a 16-row tile quantises it (16-value groups, RMSNorm-weighted
-// where the next GEMV normalises), so a phase ends with its epilogue stores
-// and the next one copies its input with one L2 read: no cross-CTA pass,
-// counters or fences between phases other than the arrival itself.
-//
-// and CTA 0, once every CTA has finished the last phase, turns the argmax
-// into the next token and advances the position.
+// that finishes a 32-row fragment quantises it (one 32-value group,
+// RMSNorm-weighted where the next GEMV normalises), so a phase ends with its
+// epilogue stores and the next one copies its input with one L2 read: no
+// cross-CTA pass, counters or fences between phases other than the arrival
+// itself.  Under tensor parallelism the row-parallel GEMVs send tagged partial
+// sums to every rank instead, and the GEMV after them reduces its input
+// itself (XchgParams).  CTA 0, once every CTA has finished the last phase,
+// turns the argmax into the next token and advances the position.
 #pragma once
 #include "af_gemv.cuh"
 #include "af_ops.cuh"
