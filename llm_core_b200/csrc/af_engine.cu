@@ -421,6 +421,8 @@ cudaError_t setup_exchange(af_engine* e) {
     unsigned long long* epoch = static_cast<unsigned long long*>(e->dalloc(64));
     ENG_TRY(cudaMemset(epoch, 0, 64));
     ENG_TRY(cudaDeviceSynchronize());
+    StepParams& sp = e->step;
+    sp.epoch = epoch;
     cudaIpcMemHandle_t mine;
     ENG_TRY(cudaIpcGetMemHandle(&mine, e->xchg));
     const size_t hs = sizeof(cudaIpcMemHandle_t);
@@ -432,7 +434,6 @@ cudaError_t setup_exchange(af_engine* e) {
     ENG_TRY(cudaStreamSynchronize(e->stream));
     ENG_TRY(cudaMemcpy(all.data(), d_h, hs * e->tp, cudaMemcpyDeviceToHost));
     cudaFree(d_h);
-    StepParams& sp = e->step;
     for (int r = 0; r < e->tp; ++r) {
         uint8_t* base = e->xchg;
         if (r != e->rank) {
@@ -445,7 +446,6 @@ cudaError_t setup_exchange(af_engine* e) {
         sp.xkey[r] = reinterpret_cast<unsigned long long*>(base + 128);
         sp.xrecv[r] = reinterpret_cast<unsigned long long*>(base + 256);
     }
-    sp.epoch = epoch;
     // every rank has mapped every area before any step runs
     int* dd = static_cast<int*>(e->dalloc(16));
     ENG_TRY(cudaMemset(dd, 0, 16));
@@ -617,7 +617,7 @@ cudaError_t build_step(af_engine* e) {
     sp.ring_bytes = kStepSmem - kStepHdr - kStepUnion;
     sp.tp = e->tp;
     sp.rank = e->rank;
-    sp.n_buf = 2 * c.n_layer;
+    sp.n_buf = tp ? 2 * c.n_layer : 0;
     if (tp) ENG_TRY(setup_exchange(e));
     return cudaSuccess;
 }

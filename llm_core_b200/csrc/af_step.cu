@@ -567,7 +567,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) step_kernel(const __grid_cons
     // ---- consumers: the phases, separated by grid-wide arrivals
     const int pos = __ldcg(sp.pos);
     const int tok = __ldcg(sp.token);
-    const unsigned long long epoch = sp.tp > 1 ? __ldcg(sp.epoch) : 0ull;
+    const unsigned long long epoch = sp.n_buf > 0 ? __ldcg(sp.epoch) : 0ull;
     // sequence number of partial-sum exchange k of this step
     auto xseq = [&](int k) { return epoch * (unsigned long long)sp.n_buf + (unsigned long long)k; };
     uint32_t consumed = 0;
@@ -657,8 +657,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) step_kernel(const __grid_cons
                 const unsigned long long kr = __ldcv(sp.xkey[sp.rank] + r);
                 k = kr > k ? kr : k;
             }
-            *sp.epoch = epoch + 1ull;
         }
+        if (sp.n_buf > 0) *sp.epoch = epoch + 1ull;
         int id = (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
         if (k == 0ull || id < 0 || id >= sp.vocab) {  // no finite logit reached the argmax
             set_err(kErrBadToken);
