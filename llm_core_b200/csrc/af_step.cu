@@ -91,11 +91,14 @@ __device__ bool xchg_input_t(const StepParams& sp, const XchgParams& x, unsigned
     const int nvec = x.n / 4;
     const uint32_t tag = (uint32_t)(seq + 1ull);
     const unsigned long long* area = sp.xrecv[sp.rank] + (size_t)(seq & 1ull) * kStepMaxRanks * x.n;
+    constexpr bool kEarlyW = NIT <= 4;  // norm weights in flight with the polls when registers allow
     float4 a[NIT], w[NIT];
 #pragma unroll
     for (int j = 0; j < NIT; ++j) {
         const int v = j * kCT + tid;
         a[j] = v < nvec ? __ldcg(reinterpret_cast<const float4*>(x.resid_in) + v) : make_float4(0.f, 0.f, 0.f, 0.f);
+        if (kEarlyW)
+            w[j] = v < nvec ? __ldg(reinterpret_cast<const float4*>(x.norm_w) + v) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     bool ok = true;
     for (int r0 = 0; r0 < sp.tp && ok; r0 += RP) {
@@ -156,7 +159,8 @@ __device__ bool xchg_input_t(const StepParams& sp, const XchgParams& x, unsigned
     for (int j = 0; j < NIT; ++j) {
         const int v = j * kCT + tid;
         if (v < nvec && (v >> 3) % (int)gridDim.x == (int)blockIdx.x) reinterpret_cast<float4*>(x.resid_out)[v] = a[j];
-        w[j] = v < nvec ? __ldg(reinterpret_cast<const float4*>(x.norm_w) + v) : make_float4(0.f, 0.f, 0.f, 0.f);
+        if (!kEarlyW)
+            w[j] = v < nvec ? __ldg(reinterpret_cast<const float4*>(x.norm_w) + v) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     quantise_f4<NIT, true>(a, w, nvec, eps, xqs, red);
     bar_consumers();
