@@ -5,14 +5,17 @@
 A step is one decode token (all 32 layers + LM head + argmax) of a random-init
 Llama-2-7B Q4_K_M GGUF (seeded; weights 4.07 GB/token >> 126 MB L2, so no L2
 flush is needed between steps), after a 128-token uniform-random prompt.
-N > 1 is tensor parallel over NCCL (strong scaling: one token stream per job).
+N > 1 is tensor parallel (strong scaling: one token stream per job); the ranks
+exchange partial sums inside the step kernel over NVLink peer memory.
 
 value   = tokens/s of the job, device-timed with CUDA events on the engine's
           stream over K device-fed graph launches (max over ranks).
-e2e     = the same through the public per-step API (af_engine_step): each step
-          copies the token id host->device and reads the next id back.
-roofline: dominant kernel = the dequant GEMVs; algorithmic bytes (weights +
-          x + y) per launch / event-bracketed launch time, vs measured HBM peak.
+e2e     = the same through the public per-step API (af_engine_step) over the
+          same positions: each step copies the token id host->device and reads
+          the next id back (host wall clock, max over ranks).
+roofline: dominant kernel = the persistent step kernel (one launch per token);
+          algorithmic bytes (weights + KV rows read) per launch / its
+          event-timed duration, vs the measured HBM copy peak.
 cpu_baseline: the reference's own CPU decode (oracle/_ref, compiled from the
           unmodified sources), production Q8_0 path, all host threads, on a
           bounded sample of decode steps.
@@ -246,20 +249,22 @@ def run_b200(args):
     pos += args.steps
     ms_step = ms / args.steps
     value = 1000.0 / ms_step
-    # e2e through the per-step public API (host token in, host id out)
-    n_e2e = min(args.steps, 4096 - pos - 8)
+    # e2e through the per-step public API (host token in, host id out), over
+    # the same positions as the timed region (the KV rows there are simply
+    # rewritten), so both numbers see the same attention context
+    pos_e2e = pos - args.steps
+    n_e2e = args.steps
     if dist is not None:
         dist.barrier()
     t0 = time.perf_counter()
     t = tok
     for i in range(n_e2e):
-        t, _ = m.step(t, pos + i, want_logits=False)
+        t, _ = m.step(t, pos_e2e + i, want_logits=False)
     e2e_s = time.perf_counter() - t0
     if dist is not None:
         tt = torch.tensor([e2e_s], device="cuda")
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         e2e_s = float(tt.item())
-    pos += n_e2e
     e2e = n_e2e / e2e_s
     # Roofline of the dominant kernel.  With the persistent step kernel (one
     # launch per token) that kernel is the whole step: its algorithmic bytes
