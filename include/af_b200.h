@@ -76,6 +76,17 @@ cudaError_t af_weight_unpack(void* d_dst, const void* d_src, int ggml_type, int 
 cudaError_t af_gemv_f32(float* d_y, const void* d_w, int ggml_type, const float* d_x, int rows,
                         int cols, cudaStream_t stream);
 
+/* Prefill dequant-GEMM: y[n_tokens][rows] = x[n_tokens][cols] · Wᵀ with W
+ * packed (af_weight_pack) and f32 x, on the tcgen05 tensor cores (W
+ * dequantised to bf16 in shared memory, x split into bf16 hi + lo, f32
+ * accumulation in tensor memory; ~1e-3 relative error from the bf16 weights).
+ * The linear layers of the reference's batched prompt pass llama_forward_batch
+ * (src/models/llama_model.cpp:1339-1462), whose Q4_K × Q8_0 GEMM is
+ * gemm_q4k_q8_avx2_range (src/backend/cpu_x86/kernels/gemv_q4k_q8_avx2.cpp:257-346).
+ * cols % 256 == 0; x and W 16-byte aligned. */
+cudaError_t af_prefill_gemm_f32(float* d_y, const void* d_w, int ggml_type, const float* d_x, int rows,
+                                int cols, int n_tokens, cudaStream_t stream);
+
 /* The fused GEMV the decode step is built from: up to three matrices sharing
  * one input (e.g. attn_q/attn_k/attn_v), an optional residual add into the
  * input (x + x_add, stored to x_store), an optional RMSNorm of the input
