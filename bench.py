@@ -385,6 +385,51 @@ def run_gemv_sweep(args):
     return 0
 
 
+def run_prefill_sweep(args):
+    """Prefill dequant-GEMM (tcgen05) at the Llama-2-7B linear-layer shapes for
+    a 512-token prompt: one JSON line per shape,
+    device-timed with CUDA events.  `tflops` counts the algorithmic 2·M·K·T;
+    the kernel issues twice that on the tensor pipe (x as bf16 hi + lo)."""
+    import torch
+    from llm_core_b200 import _lib, gguf
+    lib = _lib.load()
+    pj = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    peak = float(json.load(open(pj))["bf16_tflops"]) if os.path.exists(pj) else 1590.0
+    kind = "measured" if os.path.exists(pj) else "fallback"
+    T = 512
+    shapes = [(12288, 4096), (4096, 4096), (11008, 4096), (4096, 11008), (32000, 4096)]
+    if args.shapes:
+        shapes = [tuple(int(v) for v in s.split("x")) for s in args.shapes.split(",")]
+    rng = np.random.default_rng(0)
+    t = gguf.GGML_Q4_K
+    for (m, k) in shapes:
+        host = gguf.random_q4k(rng, m * k // 256).reshape(-1)
+        src = torch.from_numpy(host).cuda()
+        w = torch.empty(lib.af_weight_bytes(t, m, k), dtype=torch.uint8, device="cuda")
+        assert lib.af_weight_pack(w.data_ptr(), src.data_ptr(), t, m, k, None) == 0
+        x = torch.randn(T, k, device="cuda")
+        y = torch.empty(T, m, device="cuda")
+        st = torch.cuda.current_stream().cuda_stream
+        for _ in range(3):
+            assert lib.af_prefill_gemm_f32(y.data_ptr(), w.data_ptr(), t, x.data_ptr(), m, k, T, st) == 0
+        n = max(3, min(args.steps, 20))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(n):
+            lib.af_prefill_gemm_f32(y.data_ptr(), w.data_ptr(), t, x.data_ptr(), m, k, T, st)
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1000 / n
+        tf = 2.0 * m * k * T / (us * 1e-6) / 1e12
+        print(json.dumps({"kernel": "prefill_gemm_kernel", "type": "Q4_K", "M": m, "K": k, "tokens": T,
+                          "us": round(us, 1), "tflops": round(tf, 1), "tensor_tflops": round(2 * tf, 1),
+                          "frac": round(tf / peak, 4), "peak": f"{peak} ({kind}, bf16 burst)"}))
+        del w, src, x, y
+        torch.cuda.empty_cache()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -395,11 +440,14 @@ def main():
     ap.add_argument("--cpu-steps", type=int, default=12)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--gemv-sweep", action="store_true", help="standalone GEMV sweep (not the headline line)")
+    ap.add_argument("--prefill-sweep", action="store_true", help="prefill GEMM at the 7B shapes, 512 tokens")
     ap.add_argument("--shapes", default="", help="sweep shapes, e.g. 4096x4096,32000x4096")
     ap.add_argument("--types", default="both", help="12 (Q4_K), 14 (Q6_K) or both")
     args = ap.parse_args()
     if args.gemv_sweep:
         return run_gemv_sweep(args)
+    if args.prefill_sweep:
+        return run_prefill_sweep(args)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
