@@ -388,8 +388,8 @@ def run_gemv_sweep(args):
 def run_prefill_sweep(args):
     """Prefill dequant-GEMM (tcgen05) at the Llama-2-7B linear-layer shapes for
     a 512-token prompt: one JSON line per shape,
-    device-timed with CUDA events.  `tflops` counts the algorithmic 2·M·K·T;
-    the kernel issues twice that on the tensor pipe (x as bf16 hi + lo)."""
+    device-timed with CUDA events (the per-call staging of X included).
+    `tflops` counts the algorithmic 2·M·K·T."""
     import torch
     from llm_core_b200 import _lib, gguf
     lib = _lib.load()
@@ -423,8 +423,8 @@ def run_prefill_sweep(args):
         us = e0.elapsed_time(e1) * 1000 / n
         tf = 2.0 * m * k * T / (us * 1e-6) / 1e12
         print(json.dumps({"kernel": "prefill_gemm_kernel", "type": "Q4_K", "M": m, "K": k, "tokens": T,
-                          "us": round(us, 1), "tflops": round(tf, 1), "tensor_tflops": round(2 * tf, 1),
-                          "frac": round(tf / peak, 4), "peak": f"{peak} ({kind}, bf16 burst)"}))
+                          "us": round(us, 1), "tflops": round(tf, 1),
+                          "frac": round(tf / peak, 4), "peak": f"{peak} ({kind}, bf16 burst; f16 operands run at the same rate)"}))
         del w, src, x, y
         torch.cuda.empty_cache()
     return 0

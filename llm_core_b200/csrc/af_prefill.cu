@@ -7,51 +7,59 @@
 // (src/models/llama_model.cpp:1339-1462) with its 4-row × 8-token Q8 GEMM
 // tiles (gemm_q4k_q8_avx2_range, src/backend/cpu_x86/kernels/gemv_q4k_q8_avx2.cpp:257-346).
 // Unlike decode, prefill is a dense contraction (2·rows·cols·T flops against
-// rows·cols·0.56 weight bytes), so it belongs on the tensor cores:
+// rows·cols·0.56 weight bytes), so it belongs on the tensor cores.
 //
-//  * CTA tile: 128 weight rows × 128 tokens; the f32 accumulators live in
-//    tensor memory (128 lanes × 128 columns), never in registers.
-//  * K advances in stages of 64 values.  All 256 threads build a stage in
-//    shared memory: the weight rows dequantised to bf16 (w = d·sc·q − dmin·m
-//    for Q4_K, d·sc·(q − 32) for Q6_K, as the reference dequantises) and the
-//    activations split into two bf16 planes, x ≈ hi + lo (the split keeps the
-//    activation error near 2⁻¹⁶, so the bf16 rounding of the weights is the
-//    only error that matters: ~1e-3 relative).
+//  * X is staged once per call (prefill_pack_x): every token is scaled by a
+//    power of two that puts its largest |x| in [2^14, 2^15) (exact, undone in
+//    the epilogue; no f16 overflow whatever the activation range), converted
+//    to f16 and laid out per (128-token tile, 64-value stage) exactly as the
+//    tensor core reads it from shared memory, so one bulk copy moves a stage.
+//  * CTA tile: 128 weight rows × 128 tokens, f32 accumulators in tensor
+//    memory (128 lanes × 128 columns).  Two stages of shared memory per CTA,
+//    two CTAs per SM.
+//  * Warp roles (10 warps): a loader thread issues, per stage, the bulk copies
+//    (TMA engine, no tensor map, no multicast) of the X tile and of the raw
+//    Q4_K / Q6_K bytes of the CTA's 8 weight units; 8 builder warps dequantise
+//    one 16-row unit each from the raw bytes into the f16 A tile
+//    (w = d·sc·q − dmin·m for Q4_K, d·sc·(q − 32) for Q6_K, as the reference
+//    dequantises); one thread issues the stage's 4 tcgen05.mma (kind::f16,
+//    f16 × f16 → f32, M = N = 128, K = 16) and commits them to the stage's
+//    "empty" barrier, which frees the buffers for the loader.
+//  * f16 operands (11-bit significands) keep the GEMM at ~4e-4 relative error
+//    with one MMA per K-step; bf16 would need a hi/lo split of x (twice the
+//    tensor work) to stay inside the GEMV tolerance.
 //  * Both operands are K-major in the no-swizzle canonical layout: 16-byte
 //    core-matrix rows, 8-row groups 128 B apart (SBO), the two 16-byte K
 //    halves of one MMA K-step 2 KiB apart (LBO).
-//  * One elected thread issues 8 tcgen05.mma (kind::f16, bf16 × bf16 → f32,
-//    M = 128, N = 128, K = 16: four K-steps × hi/lo) per stage and commits
-//    them to the stage's mbarrier; the stage's buffer is rebuilt only after
-//    that commit lands (two buffers, so building stage s + 1 overlaps the
-//    tensor work of stage s).
-//  * Epilogue: warps 0-3 read their 32 TMEM lanes (tcgen05.ld 32x32b) and
-//    store token-major rows of Y (consecutive lanes = consecutive rows).
+//  * Epilogue: warps 0-3 read their 32 TMEM lanes (tcgen05.ld 32x32b), undo
+//    the token scale and store token-major rows of Y.
 //  Every wait is bounded; on a timeout the kernel records an error, stops
 //  issuing, and still frees its tensor memory.
-#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include <cstdint>
+#include <mutex>
 
 #include "af_ops.cuh"
 
 namespace af {
 namespace {
 
-constexpr int kPfM = 128;       // weight rows per CTA tile (MMA M)
-constexpr int kPfN = 128;       // tokens per CTA tile (MMA N, TMEM columns)
-constexpr int kPfK = 64;        // K values per stage
-constexpr int kPfThreads = 256;
-constexpr int kPfPlane = kPfM * kPfK * 2;  // bytes of one bf16 operand plane of a stage (16 KiB)
-constexpr int kPfStage = 3 * kPfPlane;     // A, B hi, B lo
-constexpr int kPfHdr = 1024;               // mbarriers + TMEM address
-constexpr int kPfSmem = kPfHdr + 2 * kPfStage;
-static_assert(kPfM == kPfN, "A and B planes share the stage geometry");
-
-__device__ __forceinline__ uint32_t bf16_bits(float f) {
-    return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(f));
-}
-__device__ __forceinline__ float bf16_val(uint32_t b) { return __uint_as_float(b << 16); }
+constexpr int kPfM = 128;        // weight rows per CTA tile (MMA M): 8 units
+constexpr int kPfN = 128;        // tokens per CTA tile (MMA N, TMEM columns)
+constexpr int kPfK = 64;         // K values per stage
+constexpr int kPfS = 2;          // stages in flight per CTA (two CTAs per SM)
+constexpr int kPfBuilders = 8;   // one 16-row unit per builder warp
+constexpr int kPfMmaWarp = 8, kPfLoadWarp = 9;
+constexpr int kPfThreads = 320;
+constexpr int kPfPlane = kPfM * kPfK * 2;  // one f16 operand tile of a stage (16 KiB)
+constexpr int kPfRawUnit = 1344;           // raw bytes of one unit per stage (Q6_K: 512 + 512 + 256 + 32)
+constexpr int kPfStage = 2 * kPfPlane + kPfBuilders * kPfRawUnit + 512;  // A, B, raw; 1 KiB multiple
+constexpr int kPfHdr = 1024;
+constexpr int kPfSmem = kPfHdr + kPfS * kPfStage;
+static_assert(kPfM == kPfN, "A and B tiles share the stage geometry");
+static_assert(kPfStage % 1024 == 0, "stage alignment");
+static_assert(2 * kPfSmem <= 227 * 1024, "two CTAs per SM");
 
 // Shared-memory matrix descriptor: K-major, no swizzle; start, LBO, SBO in
 // 16-byte units, descriptor version 1 (sm_100).
@@ -60,10 +68,9 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
            ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46);
 }
 
-// Instruction descriptor of kind::f16: f32 accumulate, bf16 A and B, both
-// K-major, N >> 3 at bit 17, M >> 4 at bit 24.
-constexpr uint32_t kPfIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kPfN >> 3) << 17) |
-                              ((uint32_t)(kPfM >> 4) << 24);
+// Instruction descriptor of kind::f16: f32 accumulate (bits 4-5 = 1), f16 A
+// and B (formats 0), both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
+constexpr uint32_t kPfIdesc = (1u << 4) | ((uint32_t)(kPfN >> 3) << 17) | ((uint32_t)(kPfM >> 4) << 24);
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -96,74 +103,127 @@ __device__ __forceinline__ void tc_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// Eight consecutive dequantised values k0 .. k0+7 (k0 % 8 == 0) of packed row
-// m (the reference's dequantisation: dequant_q4k_row / q6k_row_to_f32,
-// src/models/llama_model.cpp:476-504, 560-592).
-__device__ __forceinline__ void dequant8(const uint8_t* __restrict__ W, int type, int row_stride, int m, int k0,
-                                         float (&w)[8]) {
-    const int b = k0 >> 8, k = k0 & 255, r = m & (kPackTile - 1);
-    const uint8_t* unit = W + (size_t)(m / kPackTile) * kPackTile * row_stride + (size_t)b * unit_bytes(type);
-    const int l0 = k & 31;  // multiple of 8: words l0/4 and l0/4 + 1 of the 32-value chunk
-    if (type == AF_GGML_Q6_K) {
-        const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(unit + kQ6D + 2 * r));
-        const int sc = (int8_t)unit[kQ6Sc + 16 * r + (k >> 4)];
-        const int P = k >> 6, hiq = (k & 63) >= 32, Q = k >> 7, s = (k & 127) >> 5;
+__device__ __forceinline__ uint64_t policy_evict_last() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+__device__ __forceinline__ uint32_t h2bits(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Store 4 f16 values of A tile row `row` starting at K index k (k % 4 == 0).
+__device__ __forceinline__ void st_a4(uint8_t* A, int row, int k, float a, float b, float c, float d) {
+    *reinterpret_cast<uint2*>(A + (k >> 3) * (kPfM * 16) + row * 16 + (k & 7) * 2) = make_uint2(h2bits(a, b), h2bits(c, d));
+}
+
+// Builder lane's share of a Q4_K unit stage (chunk c of the super-block): the
+// raw 16-byte fragment word group of lane L holds rows g, g+8 × words t, t+4
+// (see af_gemv.cuh); low nibbles are sub-block 2c, high nibbles 2c + 1.
+__device__ __forceinline__ void build_q4(uint8_t* A, const uint8_t* raw, int row0, int c, int lane) {
+    const int g = lane >> 2, t = lane & 3;
+    const uint4 qv = *reinterpret_cast<const uint4*>(raw + lane * 16);
+    const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};  // e = 0..3
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int wd = (l0 >> 2) + h;
-            const uint32_t lo = *reinterpret_cast<const uint32_t*>(unit + P * 512 + packed_frag_off(r, wd, 0));
-            const uint32_t hi = *reinterpret_cast<const uint32_t*>(unit + kQ6Hi + Q * 512 + packed_frag_off(r, wd, 0));
+    for (int h = 0; h < 2; ++h) {  // row g (h = 0) or g + 8
+        const int r = g + 8 * h;
+        const uint8_t* hdr = raw + 512 + 16 * r;
+        const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(hdr));
+        const float dmin = half_bits_to_float(*reinterpret_cast<const uint16_t*>(hdr + 2));
+        const uint8_t* sc = hdr + 4;
+        float ds[2], dm[2];
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            const int j = 2 * c + q;
+            int sv, mv;
+            if (j < 4) {
+                sv = sc[j] & 63;
+                mv = sc[j + 4] & 63;
+            } else {
+                sv = (sc[j + 4] & 0xF) | ((sc[j - 4] >> 6) << 4);
+                mv = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
+            }
+            ds[q] = d * sv;
+            dm[q] = dmin * mv;
+        }
+#pragma unroll
+        for (int ww = 0; ww < 2; ++ww) {  // word t (ww = 0) or t + 4
+            const uint32_t wd = qw[h + 2 * ww];
+            const int k = 4 * (t + 4 * ww);
+            float lo[4], hi[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                const int lb = (lo >> (8 * i)) & 0xFF, hb = (hi >> (8 * i)) & 0xFF;
-                const int q = ((hiq ? lb >> 4 : lb) & 0xF) | (((hb >> (2 * s)) & 3) << 4);
-                w[4 * h + i] = d * sc * (q - 32);
+                const int qb = (wd >> (8 * i)) & 0xFF;
+                lo[i] = ds[0] * (qb & 0xF) - dm[0];
+                hi[i] = ds[1] * (qb >> 4) - dm[1];
             }
-        }
-        return;
-    }
-    const uint8_t* hdr = unit + kQ4Hdr + 16 * r;
-    const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(hdr));
-    const float dmin = half_bits_to_float(*reinterpret_cast<const uint16_t*>(hdr + 2));
-    const uint8_t* sc = hdr + 4;
-    const int chunk = k >> 6, rr = k & 63, j = chunk * 2 + (rr >> 5);
-    int s, mn;
-    if (j < 4) {
-        s = sc[j] & 63;
-        mn = sc[j + 4] & 63;
-    } else {
-        s = (sc[j + 4] & 0xF) | ((sc[j - 4] >> 6) << 4);
-        mn = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
-    }
-    const float ds = d * s, dm = dmin * mn;
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        const uint32_t qw = *reinterpret_cast<const uint32_t*>(unit + chunk * 512 + packed_frag_off(r, (l0 >> 2) + h, 0));
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int qb = (qw >> (8 * i)) & 0xFF;
-            const int q = rr < 32 ? (qb & 0xF) : (qb >> 4);
-            w[4 * h + i] = ds * q - dm;
+            st_a4(A, row0 + r, k, lo[0], lo[1], lo[2], lo[3]);
+            st_a4(A, row0 + r, 32 + k, hi[0], hi[1], hi[2], hi[3]);
         }
     }
 }
 
-__global__ void __launch_bounds__(kPfThreads, 1)
-    prefill_gemm_kernel(float* __restrict__ Y, const uint8_t* __restrict__ W, int type, const float* __restrict__ X,
-                        int rows, int cols, int T) {
+// Q6_K unit stage P = c of the super-block: raw [0,512) low nibbles of the
+// 64-value block, [512,1024) the high 2-bit fields of its 128-value quad,
+// [1024,1280) the 16 rows' scales, [1280,1312) the rows' d.
+__device__ __forceinline__ void build_q6(uint8_t* A, const uint8_t* raw, int row0, int c, int lane) {
+    const int g = lane >> 2, t = lane & 3;
+    const uint4 lv = *reinterpret_cast<const uint4*>(raw + lane * 16);
+    const uint4 hv = *reinterpret_cast<const uint4*>(raw + 512 + lane * 16);
+    const uint32_t lw[4] = {lv.x, lv.y, lv.z, lv.w}, hw[4] = {hv.x, hv.y, hv.z, hv.w};
+    const int s0 = 2 * (c & 1);  // 32-value group of the low nibbles within the quad (high: s0 + 1)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int r = g + 8 * h;
+        const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(raw + 1280 + 2 * r));
+        const int8_t* scr = reinterpret_cast<const int8_t*>(raw + 1024 + 16 * r + 4 * c);
+#pragma unroll
+        for (int ww = 0; ww < 2; ++ww) {
+            const uint32_t lo_w = lw[h + 2 * ww], hi_w = hw[h + 2 * ww];
+            const int k = 4 * (t + 4 * ww);  // 0..31
+            const int sc_lo = scr[k >> 4], sc_hi = scr[2 + (k >> 4)];
+            float lo[4], hi[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int lb = (lo_w >> (8 * i)) & 0xFF, hb = (hi_w >> (8 * i)) & 0xFF;
+                const int q0 = (lb & 0xF) | (((hb >> (2 * s0)) & 3) << 4);
+                const int q1 = (lb >> 4) | (((hb >> (2 * s0 + 2)) & 3) << 4);
+                lo[i] = d * sc_lo * (q0 - 32);
+                hi[i] = d * sc_hi * (q1 - 32);
+            }
+            st_a4(A, row0 + r, k, lo[0], lo[1], lo[2], lo[3]);
+            st_a4(A, row0 + r, 32 + k, hi[0], hi[1], hi[2], hi[3]);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kPfThreads, 2)
+    prefill_gemm_kernel(float* __restrict__ Y, const uint8_t* __restrict__ W, int type, const uint8_t* __restrict__ Xp,
+                        const int* __restrict__ xexp, int rows, int cols, int T) {
     extern __shared__ __align__(1024) uint8_t smem[];
-    uint64_t* done = reinterpret_cast<uint64_t*>(smem);          // [2] MMA completion per buffer
-    uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + 64);    // TMEM base address
-    volatile int* flag = reinterpret_cast<volatile int*>(smem + 128);
+    uint64_t* full_b = reinterpret_cast<uint64_t*>(smem);        // [kPfS] loader bulk copies (tx)
+    uint64_t* full_a = full_b + kPfS;                             // [kPfS] builder warps
+    uint64_t* empty = full_a + kPfS;                              // [kPfS] MMA completion
+    uint64_t* accf = empty + kPfS;                                // accumulators final
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + 256);
+    volatile int* flag = reinterpret_cast<volatile int*>(smem + 320);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int m0 = blockIdx.x * kPfM, n0 = blockIdx.y * kPfN;
+    const int m0 = blockIdx.x * kPfM, nt = blockIdx.y, n0 = nt * kPfN;
     const int tiles = (rows + kPackTile - 1) / kPackTile;
     const int row_stride = dev_row_stride(type, cols);
+    const int ub = unit_bytes(type);
     const int nst = cols / kPfK;
+    const bool q6 = type == AF_GGML_Q6_K;
 
     if (tid == 0) {
-        mbar_init(&done[0], 1);
-        mbar_init(&done[1], 1);
+        for (int i = 0; i < kPfS; ++i) {
+            mbar_init(&full_b[i], 1);
+            mbar_init(&full_a[i], kPfBuilders);
+            mbar_init(&empty[i], 1);
+        }
+        mbar_init(accf, 1);
         *flag = 0;
         fence_mbar_init();
     }
@@ -178,92 +238,98 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     tc_fence_after();
     const uint32_t tmem = *tslot;
 
-    for (int s = 0; s < nst; ++s) {
-        const int buf = s & 1;
-        uint8_t* A = smem + kPfHdr + buf * kPfStage;
-        uint8_t* Bh = A + kPfPlane;
-        uint8_t* Bl = Bh + kPfPlane;
-        if (s >= 2) {  // the MMAs that read this buffer (stage s - 2) have completed
-            if (!mbar_wait(&done[buf], (uint32_t)((s - 2) >> 1) & 1u, flag)) {
-                if (tid == 0 && !*flag) set_err(kErrMbarTimeout);
-                *flag = 1;
-            }
-            tc_fence_after();
-        }
-        __syncthreads();
-        if (*flag) break;
-        const int kb = s * kPfK;
-        // A: 128 rows × 8 sixteen-byte chunks; B: 128 tokens × 8 chunks (hi and lo planes)
-        for (int it = tid; it < kPfM * (kPfK / 8); it += kPfThreads) {
-            const int row = it & (kPfM - 1), c8 = it / kPfM;
-            const int m = m0 + row;
-            uint4 pk = make_uint4(0u, 0u, 0u, 0u);
-            if (m < tiles * kPackTile) {
-                float w[8];
-                dequant8(W, type, row_stride, m, kb + 8 * c8, w);
-                pk.x = bf16_bits(w[0]) | (bf16_bits(w[1]) << 16);
-                pk.y = bf16_bits(w[2]) | (bf16_bits(w[3]) << 16);
-                pk.z = bf16_bits(w[4]) | (bf16_bits(w[5]) << 16);
-                pk.w = bf16_bits(w[6]) | (bf16_bits(w[7]) << 16);
-            }
-            *reinterpret_cast<uint4*>(A + c8 * (kPfM * 16) + row * 16) = pk;
-        }
-        for (int it = tid; it < kPfN * (kPfK / 8); it += kPfThreads) {
-            const int tok = it & (kPfN - 1), c8 = it / kPfN;
-            const int n = n0 + tok;
-            uint4 ph = make_uint4(0u, 0u, 0u, 0u), pl = ph;
-            if (n < T) {
-                const float4* src = reinterpret_cast<const float4*>(X + (size_t)n * cols + kb + 8 * c8);
-                const float4 a = __ldg(src), b = __ldg(src + 1);
-                const float x[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-                uint32_t h[8], l[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    h[i] = bf16_bits(x[i]);
-                    l[i] = bf16_bits(x[i] - bf16_val(h[i]));
+    if (warp == kPfLoadWarp) {
+        if (lane == 0) {
+            const uint64_t pol_x = policy_evict_last(), pol_w = policy_evict_first();
+            for (int j = 0; j < nst && !*flag; ++j) {
+                const int slot = j % kPfS;
+                if (j >= kPfS && !mbar_wait(&empty[slot], (uint32_t)((j / kPfS) - 1) & 1u, flag)) {
+                    *flag = 1;
+                    break;
                 }
-                ph = make_uint4(h[0] | (h[1] << 16), h[2] | (h[3] << 16), h[4] | (h[5] << 16), h[6] | (h[7] << 16));
-                pl = make_uint4(l[0] | (l[1] << 16), l[2] | (l[3] << 16), l[4] | (l[5] << 16), l[6] | (l[7] << 16));
+                uint8_t* st = smem + kPfHdr + slot * kPfStage;
+                uint8_t* raw = st + 2 * kPfPlane;
+                const int b = j >> 2, c = j & 3;
+                const int nu = max(0, min(kPfBuilders, tiles - m0 / kPackTile));
+                mbar_arrive_expect_tx(&full_b[slot], (uint32_t)(kPfPlane + nu * (q6 ? 1312 : 768)));
+                bulk_g2s(st + kPfPlane, Xp + ((size_t)nt * nst + j) * kPfPlane, kPfPlane, &full_b[slot], pol_x);
+                for (int u = 0; u < nu; ++u) {
+                    const uint8_t* unit = W + (size_t)(m0 / kPackTile + u) * kPackTile * row_stride + (size_t)b * ub;
+                    uint8_t* ru = raw + u * kPfRawUnit;
+                    bulk_g2s(ru, unit + c * 512, 512, &full_b[slot], pol_w);
+                    if (q6) {
+                        bulk_g2s(ru + 512, unit + kQ6Hi + (c >> 1) * 512, 512, &full_b[slot], pol_w);
+                        bulk_g2s(ru + 1024, unit + kQ6Sc, 256, &full_b[slot], pol_w);
+                        bulk_g2s(ru + 1280, unit + kQ6D, 32, &full_b[slot], pol_w);
+                    } else {
+                        bulk_g2s(ru + 512, unit + kQ4Hdr, 256, &full_b[slot], pol_w);
+                    }
+                }
             }
-            *reinterpret_cast<uint4*>(Bh + c8 * (kPfN * 16) + tok * 16) = ph;
-            *reinterpret_cast<uint4*>(Bl + c8 * (kPfN * 16) + tok * 16) = pl;
         }
-        fence_proxy_async_smem();  // generic-proxy stores → visible to the tensor core
-        __syncthreads();
-        if (tid == 0) {
+    } else if (warp == kPfMmaWarp) {
+        if (lane == 0) {
+            for (int j = 0; j < nst; ++j) {
+                const int slot = j % kPfS;
+                const uint32_t par = (uint32_t)(j / kPfS) & 1u;
+                if (!mbar_wait(&full_b[slot], par, flag) || !mbar_wait(&full_a[slot], par, flag)) {
+                    *flag = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a0 = smem_u32(smem + kPfHdr + slot * kPfStage), b0 = a0 + kPfPlane;
+#pragma unroll
+                for (int ks = 0; ks < kPfK / 16; ++ks) {
+                    const uint32_t off = (uint32_t)ks * 2 * (kPfM * 16);
+                    tc_mma(tmem, smem_desc(a0 + off, kPfM * 16, 128), smem_desc(b0 + off, kPfN * 16, 128),
+                           (j > 0 || ks > 0) ? 1u : 0u);
+                }
+                tc_commit(&empty[slot]);
+            }
+            tc_commit(accf);  // arrives once every MMA issued above has completed
+        }
+    } else {  // builder warps: unit `warp` of every stage
+        const int mt = m0 / kPackTile + warp;
+        for (int j = 0; j < nst; ++j) {
+            const int slot = j % kPfS;
+            if (!mbar_wait(&full_b[slot], (uint32_t)(j / kPfS) & 1u, flag)) {
+                *flag = 1;
+                break;
+            }
+            uint8_t* A = smem + kPfHdr + slot * kPfStage;
+            const uint8_t* raw = A + 2 * kPfPlane + warp * kPfRawUnit;
+            if (mt < tiles) {
+                if (q6) build_q6(A, raw, warp * kPackTile, j & 3, lane);
+                else build_q4(A, raw, warp * kPackTile, j & 3, lane);
+            } else {  // rows past the matrix: zeros
+                for (int i = lane; i < kPackTile * (kPfK / 8); i += 32) {
+                    const int r = i & 15, c8 = i >> 4;
+                    *reinterpret_cast<uint4*>(A + c8 * (kPfM * 16) + (warp * kPackTile + r) * 16) = make_uint4(0u, 0u, 0u, 0u);
+                }
+            }
+            fence_proxy_async_smem();  // generic-proxy stores → visible to the tensor core
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&full_a[slot]);
+        }
+        // epilogue: warps 0-3 own TMEM lanes 32·warp .. 32·warp + 31
+        if (warp < 4) {
+            if (!*flag && !mbar_wait(accf, 0u, flag)) *flag = 1;
             tc_fence_after();
-            const uint32_t a0 = smem_u32(A), h0 = smem_u32(Bh), l0 = smem_u32(Bl);
-#pragma unroll
-            for (int ks = 0; ks < kPfK / 16; ++ks) {
-                const uint32_t off = (uint32_t)ks * 2 * (kPfM * 16);
-                const uint64_t ad = smem_desc(a0 + off, kPfM * 16, 128);
-                tc_mma(tmem, ad, smem_desc(h0 + off, kPfN * 16, 128), (s > 0 || ks > 0) ? 1u : 0u);
-                tc_mma(tmem, ad, smem_desc(l0 + off, kPfN * 16, 128), 1u);
-            }
-            tc_commit(&done[buf]);
-        }
-    }
-    // the last commit covers every MMA issued before it
-    if (!*flag && nst > 0) {
-        const int last = nst - 1;
-        if (!mbar_wait(&done[last & 1], (uint32_t)(last >> 1) & 1u, flag)) {
-            if (tid == 0 && !*flag) set_err(kErrMbarTimeout);
-            *flag = 1;
-        }
-    }
-    tc_fence_after();
-    __syncthreads();
-    if (!*flag && warp < 4) {
-        const int row = warp * 32 + lane;
-        const int m = m0 + row;
+            if (!*flag) {
+                const int row = warp * 32 + lane;
+                const int m = m0 + row;
 #pragma unroll 1
-        for (int c = 0; c < kPfN; c += 16) {
-            float v[16];
-            tc_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c, v);
-            if (m < rows) {
+                for (int c0 = 0; c0 < kPfN; c0 += 16) {
+                    float v[16];
+                    tc_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
+                    if (m < rows) {
 #pragma unroll
-                for (int i = 0; i < 16; ++i)
-                    if (n0 + c + i < T) Y[(size_t)(n0 + c + i) * rows + m] = v[i];
+                        for (int i = 0; i < 16; ++i) {
+                            const int n = n0 + c0 + i;
+                            if (n < T) Y[(size_t)n * rows + m] = ldexpf(v[i], -xexp[n]);
+                        }
+                    }
+                }
             }
         }
     }
@@ -276,19 +342,94 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     }
 }
 
+// Per-token power-of-two exponent e with max|x|·2^e in [2^14, 2^15) (0 for
+// an all-zero row): one warp per token.
+__global__ void prefill_xexp_kernel(const float* __restrict__ X, int* __restrict__ xexp, int cols, int T) {
+    const int n = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (n >= T) return;
+    float m = 0.f;
+    for (int k = lane * 4; k < cols; k += 128) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(X + (size_t)n * cols + k));
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
+    m = warp_max(m);
+    if (lane == 0) {
+        int e = 0;
+        if (m > 0.f && isfinite(m)) {
+            const int E = (int)((__float_as_uint(m) >> 23) & 0xFF) - 127;  // m in [2^E, 2^(E+1)) (normal m)
+            e = max(-120, min(120, 14 - E));
+        }
+        xexp[n] = e;
+    }
+}
+
+// X f32 [T][cols] → f16 tiles: for token tile nt and stage s, 16 KiB at
+// ((nt·nst + s)·16384) holding [8-value chunk c8][token][8 × f16], the
+// K-major no-swizzle layout of one MMA B operand stage; tokens ≥ T are zero.
+__global__ void prefill_pack_x_kernel(const float* __restrict__ X, const int* __restrict__ xexp, uint8_t* __restrict__ Xp,
+                                      int cols, int T, int ntok) {
+    const int kc = cols / 8;
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)ntok * kc) return;
+    const int n = (int)(i / kc), k0 = (int)(i % kc) * 8;
+    uint4 o = make_uint4(0u, 0u, 0u, 0u);
+    if (n < T) {
+        const float* src = X + (size_t)n * cols + k0;
+        const float4 a = __ldg(reinterpret_cast<const float4*>(src)), b = __ldg(reinterpret_cast<const float4*>(src) + 1);
+        const int e = xexp[n];
+        o = make_uint4(h2bits(ldexpf(a.x, e), ldexpf(a.y, e)), h2bits(ldexpf(a.z, e), ldexpf(a.w, e)),
+                       h2bits(ldexpf(b.x, e), ldexpf(b.y, e)), h2bits(ldexpf(b.z, e), ldexpf(b.w, e)));
+    }
+    const int nst = cols / kPfK, s = k0 / kPfK, c8 = (k0 % kPfK) / 8;
+    *reinterpret_cast<uint4*>(Xp + ((size_t)(n / kPfN) * nst + s) * kPfPlane + c8 * (kPfN * 16) + (n % kPfN) * 16) = o;
+}
+
+// Staging buffers of X, grown on demand (cudaMalloc: not during stream capture).
+struct PrefillScratch {
+    std::mutex mu;
+    int dev = -1;
+    uint8_t* xp = nullptr;
+    size_t xp_bytes = 0;
+    int* xexp = nullptr;
+    size_t xexp_n = 0;
+};
+PrefillScratch g_pf;
+
 }  // namespace
 
 cudaError_t prefill_gemm_launch(float* y, const uint8_t* w, int type, const float* x, int rows, int cols, int T,
                                 cudaStream_t st) {
-    static int attr_dev = -1;
     int dev = 0;
     AF_CUDA_TRY(cudaGetDevice(&dev));
-    if (attr_dev != dev) {
+    std::lock_guard<std::mutex> lock(g_pf.mu);
+    const int ntile = (T + kPfN - 1) / kPfN;
+    const size_t xp_bytes = (size_t)ntile * (cols / kPfK) * kPfPlane;
+    if (g_pf.dev != dev) {
         AF_CUDA_TRY(cudaFuncSetAttribute(prefill_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmem));
-        attr_dev = dev;
+        g_pf.dev = dev;
+        g_pf.xp = nullptr;  // buffers of another device are not reused (they leak with the process)
+        g_pf.xp_bytes = 0;
+        g_pf.xexp = nullptr;
+        g_pf.xexp_n = 0;
     }
-    const dim3 grid((rows + kPfM - 1) / kPfM, (T + kPfN - 1) / kPfN);
-    prefill_gemm_kernel<<<grid, kPfThreads, kPfSmem, st>>>(y, w, type, x, rows, cols, T);
+    if (g_pf.xp_bytes < xp_bytes) {
+        if (g_pf.xp) AF_CUDA_TRY(cudaFree(g_pf.xp));
+        g_pf.xp = nullptr;
+        AF_CUDA_TRY(cudaMalloc(&g_pf.xp, xp_bytes));
+        g_pf.xp_bytes = xp_bytes;
+    }
+    if (g_pf.xexp_n < (size_t)T) {
+        if (g_pf.xexp) AF_CUDA_TRY(cudaFree(g_pf.xexp));
+        g_pf.xexp = nullptr;
+        AF_CUDA_TRY(cudaMalloc(&g_pf.xexp, (size_t)T * sizeof(int)));
+        g_pf.xexp_n = (size_t)T;
+    }
+    prefill_xexp_kernel<<<(T + 7) / 8, 256, 0, st>>>(x, g_pf.xexp, cols, T);
+    const long long items = (long long)ntile * kPfN * (cols / 8);
+    prefill_pack_x_kernel<<<(unsigned)((items + 255) / 256), 256, 0, st>>>(x, g_pf.xexp, g_pf.xp, cols, T,
+                                                                            ntile * kPfN);
+    const dim3 grid((rows + kPfM - 1) / kPfM, ntile);
+    prefill_gemm_kernel<<<grid, kPfThreads, kPfSmem, st>>>(y, w, type, g_pf.xp, g_pf.xexp, rows, cols, T);
     return cudaGetLastError();
 }
 

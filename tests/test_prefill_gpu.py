@@ -3,8 +3,9 @@ oracle: every token's row of Y must equal the reference-order F32 GEMV of
 that token (oracle/af_oracle.c, pinned to gemv_q4k_avx2_range /
 gemv_q6k_avx2_range).
 
-Tolerance: 2e-3 relative L2 (the GEMV bar); the GEMM rounds the dequantised
-weights to bf16 (≈8e-4 relative rms) and splits x into bf16 hi + lo."""
+Tolerance: 2e-3 relative L2 (the GEMV bar), and 1e-3 as a tighter check: the
+GEMM rounds the dequantised weights and the (power-of-two scaled) activations
+to f16, ≈2e-4 relative rms together."""
 import ctypes
 
 import numpy as np
@@ -51,10 +52,24 @@ def test_prefill_gemm_matches_oracle(gpu, t, rows, cols, T):
     ref = oracle_rows(W, t, X, rows)
     assert np.isfinite(y).all()
     err = rel_l2(y, ref)
-    assert err < GEMV_TOL, err
+    assert err < GEMV_TOL and err < 1e-3, err
     # every token on its own, so a slip in one tile cannot hide in the total
     worst = max(rel_l2(y[n], ref[n]) for n in range(T))
     assert worst < 2 * GEMV_TOL, worst
+
+
+def test_prefill_gemm_activation_range(gpu):
+    """Per-token scales: tokens of very different magnitude (1e-6 .. 1e6, f16
+    alone would underflow or overflow) keep the same relative accuracy."""
+    rng = np.random.default_rng(11)
+    rows, cols = 256, 1024
+    W = gguf.random_q4k(rng, rows * cols // 256).reshape(-1)
+    X = rng.standard_normal((6, cols)).astype(np.float32)
+    X *= np.array([1e-6, 1e-3, 1.0, 1e3, 1e5, 1e6], np.float32)[:, None]
+    y = run_prefill(gpu, W, gguf.GGML_Q4_K, X, rows)
+    ref = oracle_rows(W, gguf.GGML_Q4_K, X, rows)
+    for n in range(X.shape[0]):
+        assert rel_l2(y[n], ref[n]) < 1e-3, n
 
 
 def test_prefill_gemm_zero_input(gpu):
