@@ -15,8 +15,9 @@
 //    to f16 and laid out per (128-token tile, 64-value stage) exactly as the
 //    tensor core reads it from shared memory, so one bulk copy moves a stage.
 //  * CTA tile: 128 weight rows × 128 tokens, f32 accumulators in tensor
-//    memory (128 lanes × 128 columns).  Two stages of shared memory per CTA,
-//    two CTAs per SM.
+//    memory (128 lanes × 128 columns).  Two stages of shared memory per CTA
+//    and two CTAs per SM when the grid has more CTAs than SMs, else four
+//    stages and one CTA per SM.
 //  * Warp roles (10 warps): a loader thread issues, per stage, the bulk copies
 //    (TMA engine, no tensor map, no multicast) of the X tile and of the raw
 //    Q4_K / Q6_K bytes of the CTA's 8 weight units; 8 builder warps dequantise
@@ -48,7 +49,6 @@ namespace {
 constexpr int kPfM = 128;        // weight rows per CTA tile (MMA M): 8 units
 constexpr int kPfN = 128;        // tokens per CTA tile (MMA N, TMEM columns)
 constexpr int kPfK = 64;         // K values per stage
-constexpr int kPfS = 2;          // stages in flight per CTA (two CTAs per SM)
 constexpr int kPfBuilders = 8;   // one 16-row unit per builder warp
 constexpr int kPfMmaWarp = 8, kPfLoadWarp = 9;
 constexpr int kPfThreads = 320;
@@ -56,10 +56,13 @@ constexpr int kPfPlane = kPfM * kPfK * 2;  // one f16 operand tile of a stage (1
 constexpr int kPfRawUnit = 1344;           // raw bytes of one unit per stage (Q6_K: 512 + 512 + 256 + 32)
 constexpr int kPfStage = 2 * kPfPlane + kPfBuilders * kPfRawUnit + 512;  // A, B, raw; 1 KiB multiple
 constexpr int kPfHdr = 1024;
-constexpr int kPfSmem = kPfHdr + kPfS * kPfStage;
+// stages in flight: 2 per CTA with two CTAs per SM (grids of more than one
+// CTA per SM), 4 with one (smaller grids)
+template <int S>
+constexpr int pf_smem() { return kPfHdr + S * kPfStage; }
 static_assert(kPfM == kPfN, "A and B tiles share the stage geometry");
 static_assert(kPfStage % 1024 == 0, "stage alignment");
-static_assert(2 * kPfSmem <= 227 * 1024, "two CTAs per SM");
+static_assert(2 * pf_smem<2>() <= 227 * 1024 && pf_smem<4>() <= 227 * 1024, "stage budget");
 
 // Shared-memory matrix descriptor: K-major, no swizzle; start, LBO, SBO in
 // 16-byte units, descriptor version 1 (sm_100).
@@ -199,7 +202,8 @@ __device__ __forceinline__ void build_q6(uint8_t* A, const uint8_t* raw, int row
     }
 }
 
-__global__ void __launch_bounds__(kPfThreads, 2)
+template <int kPfS>
+__global__ void __launch_bounds__(kPfThreads, 1)
     prefill_gemm_kernel(float* __restrict__ Y, const uint8_t* __restrict__ W, int type, const uint8_t* __restrict__ Xp,
                         const int* __restrict__ xexp, int rows, int cols, int T) {
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -405,7 +409,8 @@ cudaError_t prefill_gemm_launch(float* y, const uint8_t* w, int type, const floa
     const int ntile = (T + kPfN - 1) / kPfN;
     const size_t xp_bytes = (size_t)ntile * (cols / kPfK) * kPfPlane;
     if (g_pf.dev != dev) {
-        AF_CUDA_TRY(cudaFuncSetAttribute(prefill_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmem));
+        AF_CUDA_TRY(cudaFuncSetAttribute(prefill_gemm_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, pf_smem<2>()));
+        AF_CUDA_TRY(cudaFuncSetAttribute(prefill_gemm_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, pf_smem<4>()));
         g_pf.dev = dev;
         g_pf.xp = nullptr;  // buffers of another device are not reused (they leak with the process)
         g_pf.xp_bytes = 0;
@@ -429,7 +434,10 @@ cudaError_t prefill_gemm_launch(float* y, const uint8_t* w, int type, const floa
     prefill_pack_x_kernel<<<(unsigned)((items + 255) / 256), 256, 0, st>>>(x, g_pf.xexp, g_pf.xp, cols, T,
                                                                             ntile * kPfN);
     const dim3 grid((rows + kPfM - 1) / kPfM, ntile);
-    prefill_gemm_kernel<<<grid, kPfThreads, kPfSmem, st>>>(y, w, type, g_pf.xp, g_pf.xexp, rows, cols, T);
+    if ((int)(grid.x * grid.y) > num_sms())
+        prefill_gemm_kernel<2><<<grid, kPfThreads, pf_smem<2>(), st>>>(y, w, type, g_pf.xp, g_pf.xexp, rows, cols, T);
+    else
+        prefill_gemm_kernel<4><<<grid, kPfThreads, pf_smem<4>(), st>>>(y, w, type, g_pf.xp, g_pf.xexp, rows, cols, T);
     return cudaGetLastError();
 }
 

@@ -42,8 +42,10 @@ def oracle_rows(W, t, X, rows):
 
 @pytest.mark.parametrize("t", [gguf.GGML_Q4_K, gguf.GGML_Q6_K])
 @pytest.mark.parametrize("rows,cols,T", [(128, 256, 128), (256, 2048, 64), (300, 768, 130), (37, 512, 1),
-                                         (1024, 4096, 200)])
+                                         (1024, 4096, 200), (4096, 512, 1200)])
 def test_prefill_gemm_matches_oracle(gpu, t, rows, cols, T):
+    """(4096, 512, 1200) is a grid of 320 CTAs: the two-CTAs-per-SM variant;
+    the others run one CTA per SM with four stages."""
     rng = np.random.default_rng(7000 + rows + cols + T + t)
     gen = gguf.random_q4k if t == gguf.GGML_Q4_K else gguf.random_q6k
     W = gen(rng, rows * cols // 256).reshape(-1)
