@@ -15,13 +15,15 @@
 //    to f16 and laid out per (128-token tile, 64-value stage) exactly as the
 //    tensor core reads it from shared memory, so one bulk copy moves a stage.
 //  * CTA tile: 128 weight rows × 128 tokens, f32 accumulators in tensor
-//    memory (128 lanes × 128 columns).  Two stages of shared memory per CTA
-//    and two CTAs per SM when the grid has more CTAs than SMs, else four
-//    stages and one CTA per SM.
-//  * Warp roles (10 warps): a loader thread issues, per stage, the bulk copies
-//    (TMA engine, no tensor map, no multicast) of the X tile and of the raw
-//    Q4_K / Q6_K bytes of the CTA's 8 weight units; 8 builder warps dequantise
-//    one 16-row unit each from the raw bytes into the f16 A tile
+//    memory (128 lanes × 128 columns).  Four A/B stages and a two-super-block
+//    ring of raw weight units per CTA, one CTA per SM.
+//  * Warp roles (18 warps): a loader thread issues the bulk copies (TMA
+//    engine, no tensor map, no multicast): per 256-value super-block one copy
+//    of each of the CTA's 8 packed weight units (contiguous in the packed
+//    layout; a ring of two super-blocks), per 64-value stage one X tile (small
+//    copies cost the TMA engine a fixed time each, so they are made few and
+//    large); 16 builder warps dequantise half a 16-row unit each from shared
+//    memory into the f16 A tile
 //    (w = d·sc·q − dmin·m for Q4_K, d·sc·(q − 32) for Q6_K, as the reference
 //    dequantises); one thread issues the stage's 4 tcgen05.mma (kind::f16,
 //    f16 × f16 → f32, M = N = 128, K = 16) and commits them to the stage's
@@ -49,20 +51,22 @@ namespace {
 constexpr int kPfM = 128;        // weight rows per CTA tile (MMA M): 8 units
 constexpr int kPfN = 128;        // tokens per CTA tile (MMA N, TMEM columns)
 constexpr int kPfK = 64;         // K values per stage
-constexpr int kPfBuilders = 8;   // one 16-row unit per builder warp
-constexpr int kPfMmaWarp = 8, kPfLoadWarp = 9;
-constexpr int kPfThreads = 320;
+constexpr int kPfUnits = 8;      // 16-row units per CTA tile
+constexpr int kPfBuilders = 16;  // builder warps: rows g (even warp) or g + 8 (odd warp) of one unit
+constexpr int kPfMmaWarp = kPfBuilders, kPfLoadWarp = kPfBuilders + 1;
+constexpr int kPfThreads = (kPfBuilders + 2) * 32;
 constexpr int kPfPlane = kPfM * kPfK * 2;  // one f16 operand tile of a stage (16 KiB)
-constexpr int kPfRawUnit = 1344;           // raw bytes of one unit per stage (Q6_K: 512 + 512 + 256 + 32)
-constexpr int kPfStage = 2 * kPfPlane + kPfBuilders * kPfRawUnit + 512;  // A, B, raw; 1 KiB multiple
+constexpr int kPfStage = 2 * kPfPlane;     // A, B
+constexpr int kPfRawSlot = (kPfUnits * 3360 + 1023) / 1024 * 1024;  // one super-block of the CTA's 8 units (Q6_K size)
+constexpr int kPfRawSlots = 2;
 constexpr int kPfHdr = 1024;
-// stages in flight: 2 per CTA with two CTAs per SM (grids of more than one
-// CTA per SM), 4 with one (smaller grids)
+// A/B stages in flight (one CTA per SM), plus the raw weight ring
+constexpr int kPfStages = 4;
 template <int S>
-constexpr int pf_smem() { return kPfHdr + S * kPfStage; }
+constexpr int pf_smem() { return kPfHdr + kPfRawSlots * kPfRawSlot + S * kPfStage; }
 static_assert(kPfM == kPfN, "A and B tiles share the stage geometry");
-static_assert(kPfStage % 1024 == 0, "stage alignment");
-static_assert(2 * pf_smem<2>() <= 227 * 1024 && pf_smem<4>() <= 227 * 1024, "stage budget");
+static_assert(kPfStage % 1024 == 0 && kPfRawSlot % 1024 == 0, "stage alignment");
+static_assert(pf_smem<kPfStages>() <= 227 * 1024, "stage budget");
 
 // Shared-memory matrix descriptor: K-major, no swizzle; start, LBO, SBO in
 // 16-byte units, descriptor version 1 (sm_100).
@@ -122,17 +126,17 @@ __device__ __forceinline__ void st_a4(uint8_t* A, int row, int k, float a, float
     *reinterpret_cast<uint2*>(A + (k >> 3) * (kPfM * 16) + row * 16 + (k & 7) * 2) = make_uint2(h2bits(a, b), h2bits(c, d));
 }
 
-// Builder lane's share of a Q4_K unit stage (chunk c of the super-block): the
-// raw 16-byte fragment word group of lane L holds rows g, g+8 × words t, t+4
-// (see af_gemv.cuh); low nibbles are sub-block 2c, high nibbles 2c + 1.
-__device__ __forceinline__ void build_q4(uint8_t* A, const uint8_t* raw, int row0, int c, int lane) {
+// Builder lane's share of a Q4_K unit stage (chunk c of the super-block; a
+// whole packed unit in shared memory): the 16-byte fragment word group of
+// lane L holds rows g, g+8 × words t, t+4 (see af_gemv.cuh); low nibbles are
+// sub-block 2c, high nibbles 2c + 1.
+__device__ __forceinline__ void build_q4(uint8_t* A, const uint8_t* unit, int row0, int c, int lane, int h) {
     const int g = lane >> 2, t = lane & 3;
-    const uint4 qv = *reinterpret_cast<const uint4*>(raw + lane * 16);
-    const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};  // e = 0..3
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {  // row g (h = 0) or g + 8
+    const uint4 qv = *reinterpret_cast<const uint4*>(unit + c * 512 + lane * 16);
+    const uint32_t qw0 = h ? qv.y : qv.x, qw1 = h ? qv.w : qv.z;  // words t, t + 4 of row g + 8h
+    {  // row g (h = 0) or g + 8
         const int r = g + 8 * h;
-        const uint8_t* hdr = raw + 512 + 16 * r;
+        const uint8_t* hdr = unit + kQ4Hdr + 16 * r;
         const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(hdr));
         const float dmin = half_bits_to_float(*reinterpret_cast<const uint16_t*>(hdr + 2));
         const uint8_t* sc = hdr + 4;
@@ -153,7 +157,7 @@ __device__ __forceinline__ void build_q4(uint8_t* A, const uint8_t* raw, int row
         }
 #pragma unroll
         for (int ww = 0; ww < 2; ++ww) {  // word t (ww = 0) or t + 4
-            const uint32_t wd = qw[h + 2 * ww];
+            const uint32_t wd = ww ? qw1 : qw0;
             const int k = 4 * (t + 4 * ww);
             float lo[4], hi[4];
 #pragma unroll
@@ -168,23 +172,22 @@ __device__ __forceinline__ void build_q4(uint8_t* A, const uint8_t* raw, int row
     }
 }
 
-// Q6_K unit stage P = c of the super-block: raw [0,512) low nibbles of the
-// 64-value block, [512,1024) the high 2-bit fields of its 128-value quad,
-// [1024,1280) the 16 rows' scales, [1280,1312) the rows' d.
-__device__ __forceinline__ void build_q6(uint8_t* A, const uint8_t* raw, int row0, int c, int lane) {
+// Q6_K unit stage P = c of the super-block (a whole packed unit in shared
+// memory): low nibbles of the 64-value block P, the high 2-bit fields of its
+// 128-value quad, the 16 rows' scales and d.
+__device__ __forceinline__ void build_q6(uint8_t* A, const uint8_t* unit, int row0, int c, int lane, int h) {
     const int g = lane >> 2, t = lane & 3;
-    const uint4 lv = *reinterpret_cast<const uint4*>(raw + lane * 16);
-    const uint4 hv = *reinterpret_cast<const uint4*>(raw + 512 + lane * 16);
-    const uint32_t lw[4] = {lv.x, lv.y, lv.z, lv.w}, hw[4] = {hv.x, hv.y, hv.z, hv.w};
+    const uint4 lv = *reinterpret_cast<const uint4*>(unit + c * 512 + lane * 16);
+    const uint4 hv = *reinterpret_cast<const uint4*>(unit + kQ6Hi + (c >> 1) * 512 + lane * 16);
+    const uint32_t lw0 = h ? lv.y : lv.x, lw1 = h ? lv.w : lv.z, hw0 = h ? hv.y : hv.x, hw1 = h ? hv.w : hv.z;
     const int s0 = 2 * (c & 1);  // 32-value group of the low nibbles within the quad (high: s0 + 1)
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
+    {
         const int r = g + 8 * h;
-        const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(raw + 1280 + 2 * r));
-        const int8_t* scr = reinterpret_cast<const int8_t*>(raw + 1024 + 16 * r + 4 * c);
+        const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(unit + kQ6D + 2 * r));
+        const int8_t* scr = reinterpret_cast<const int8_t*>(unit + kQ6Sc + 16 * r + 4 * c);
 #pragma unroll
         for (int ww = 0; ww < 2; ++ww) {
-            const uint32_t lo_w = lw[h + 2 * ww], hi_w = hw[h + 2 * ww];
+            const uint32_t lo_w = ww ? lw1 : lw0, hi_w = ww ? hw1 : hw0;
             const int k = 4 * (t + 4 * ww);  // 0..31
             const int sc_lo = scr[k >> 4], sc_hi = scr[2 + (k >> 4)];
             float lo[4], hi[4];
@@ -207,12 +210,16 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     prefill_gemm_kernel(float* __restrict__ Y, const uint8_t* __restrict__ W, int type, const uint8_t* __restrict__ Xp,
                         const int* __restrict__ xexp, int rows, int cols, int T) {
     extern __shared__ __align__(1024) uint8_t smem[];
-    uint64_t* full_b = reinterpret_cast<uint64_t*>(smem);        // [kPfS] loader bulk copies (tx)
+    uint64_t* full_b = reinterpret_cast<uint64_t*>(smem);        // [kPfS] X tile copy (tx)
     uint64_t* full_a = full_b + kPfS;                             // [kPfS] builder warps
     uint64_t* empty = full_a + kPfS;                              // [kPfS] MMA completion
     uint64_t* accf = empty + kPfS;                                // accumulators final
+    uint64_t* raw_full = accf + 1;                                // [kPfRawSlots] unit copies (tx)
+    uint64_t* raw_empty = raw_full + kPfRawSlots;                 // [kPfRawSlots] builder warps
     uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + 256);
     volatile int* flag = reinterpret_cast<volatile int*>(smem + 320);
+    uint8_t* rawbase = smem + kPfHdr;
+    uint8_t* stbase = rawbase + kPfRawSlots * kPfRawSlot;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int m0 = blockIdx.x * kPfM, nt = blockIdx.y, n0 = nt * kPfN;
     const int tiles = (rows + kPackTile - 1) / kPackTile;
@@ -226,6 +233,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             mbar_init(&full_b[i], 1);
             mbar_init(&full_a[i], kPfBuilders);
             mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < kPfRawSlots; ++i) {
+            mbar_init(&raw_full[i], 1);
+            mbar_init(&raw_empty[i], kPfBuilders);
         }
         mbar_init(accf, 1);
         *flag = 0;
@@ -243,32 +254,33 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     const uint32_t tmem = *tslot;
 
     if (warp == kPfLoadWarp) {
+        // one thread: per super-block one copy of each of the CTA's units
+        // (contiguous in the packed layout), per 64-value stage one X tile
         if (lane == 0) {
             const uint64_t pol_x = policy_evict_last(), pol_w = policy_evict_first();
+            const int nu = max(0, min(kPfUnits, tiles - m0 / kPackTile));
             for (int j = 0; j < nst && !*flag; ++j) {
+                if ((j & 3) == 0) {
+                    const int sb = j >> 2, rs = sb % kPfRawSlots;
+                    if (sb >= kPfRawSlots &&
+                        !mbar_wait(&raw_empty[rs], (uint32_t)((sb / kPfRawSlots) - 1) & 1u, flag)) {
+                        *flag = 1;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&raw_full[rs], (uint32_t)(nu * ub));
+                    for (int u = 0; u < nu; ++u)
+                        bulk_g2s(rawbase + rs * kPfRawSlot + u * ub,
+                                 W + (size_t)(m0 / kPackTile + u) * kPackTile * row_stride + (size_t)sb * ub,
+                                 (uint32_t)ub, &raw_full[rs], pol_w);
+                }
                 const int slot = j % kPfS;
                 if (j >= kPfS && !mbar_wait(&empty[slot], (uint32_t)((j / kPfS) - 1) & 1u, flag)) {
                     *flag = 1;
                     break;
                 }
-                uint8_t* st = smem + kPfHdr + slot * kPfStage;
-                uint8_t* raw = st + 2 * kPfPlane;
-                const int b = j >> 2, c = j & 3;
-                const int nu = max(0, min(kPfBuilders, tiles - m0 / kPackTile));
-                mbar_arrive_expect_tx(&full_b[slot], (uint32_t)(kPfPlane + nu * (q6 ? 1312 : 768)));
-                bulk_g2s(st + kPfPlane, Xp + ((size_t)nt * nst + j) * kPfPlane, kPfPlane, &full_b[slot], pol_x);
-                for (int u = 0; u < nu; ++u) {
-                    const uint8_t* unit = W + (size_t)(m0 / kPackTile + u) * kPackTile * row_stride + (size_t)b * ub;
-                    uint8_t* ru = raw + u * kPfRawUnit;
-                    bulk_g2s(ru, unit + c * 512, 512, &full_b[slot], pol_w);
-                    if (q6) {
-                        bulk_g2s(ru + 512, unit + kQ6Hi + (c >> 1) * 512, 512, &full_b[slot], pol_w);
-                        bulk_g2s(ru + 1024, unit + kQ6Sc, 256, &full_b[slot], pol_w);
-                        bulk_g2s(ru + 1280, unit + kQ6D, 32, &full_b[slot], pol_w);
-                    } else {
-                        bulk_g2s(ru + 512, unit + kQ4Hdr, 256, &full_b[slot], pol_w);
-                    }
-                }
+                mbar_arrive_expect_tx(&full_b[slot], (uint32_t)kPfPlane);
+                bulk_g2s(stbase + slot * kPfStage + kPfPlane, Xp + ((size_t)nt * nst + j) * kPfPlane, kPfPlane,
+                         &full_b[slot], pol_x);
             }
         }
     } else if (warp == kPfMmaWarp) {
@@ -281,7 +293,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                const uint32_t a0 = smem_u32(smem + kPfHdr + slot * kPfStage), b0 = a0 + kPfPlane;
+                const uint32_t a0 = smem_u32(stbase + slot * kPfStage), b0 = a0 + kPfPlane;
 #pragma unroll
                 for (int ks = 0; ks < kPfK / 16; ++ks) {
                     const uint32_t off = (uint32_t)ks * 2 * (kPfM * 16);
@@ -292,28 +304,36 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             }
             tc_commit(accf);  // arrives once every MMA issued above has completed
         }
-    } else {  // builder warps: unit `warp` of every stage
-        const int mt = m0 / kPackTile + warp;
+    } else {  // builder warps: half (rows g or g + 8 of each lane group) of unit warp / 2 of every stage
+        const int un = warp >> 1, h = warp & 1;
+        const int mt = m0 / kPackTile + un;
         for (int j = 0; j < nst; ++j) {
-            const int slot = j % kPfS;
-            if (!mbar_wait(&full_b[slot], (uint32_t)(j / kPfS) & 1u, flag)) {
+            const int slot = j % kPfS, sb = j >> 2, rs = sb % kPfRawSlots, c = j & 3;
+            // the stage's X tile has landed (so its A slot is free: the loader
+            // copied it only after the MMAs that read the slot completed), and
+            // at a super-block's first stage, its raw units
+            if ((c == 0 && !mbar_wait(&raw_full[rs], (uint32_t)(sb / kPfRawSlots) & 1u, flag)) ||
+                !mbar_wait(&full_b[slot], (uint32_t)(j / kPfS) & 1u, flag)) {
                 *flag = 1;
                 break;
             }
-            uint8_t* A = smem + kPfHdr + slot * kPfStage;
-            const uint8_t* raw = A + 2 * kPfPlane + warp * kPfRawUnit;
+            uint8_t* A = stbase + slot * kPfStage;
+            const uint8_t* unit = rawbase + rs * kPfRawSlot + un * ub;
             if (mt < tiles) {
-                if (q6) build_q6(A, raw, warp * kPackTile, j & 3, lane);
-                else build_q4(A, raw, warp * kPackTile, j & 3, lane);
-            } else {  // rows past the matrix: zeros
-                for (int i = lane; i < kPackTile * (kPfK / 8); i += 32) {
-                    const int r = i & 15, c8 = i >> 4;
-                    *reinterpret_cast<uint4*>(A + c8 * (kPfM * 16) + (warp * kPackTile + r) * 16) = make_uint4(0u, 0u, 0u, 0u);
+                if (q6) build_q6(A, unit, un * kPackTile, c, lane, h);
+                else build_q4(A, unit, un * kPackTile, c, lane, h);
+            } else {  // rows past the matrix: zeros (this warp's 8 rows)
+                for (int i = lane; i < 8 * (kPfK / 8); i += 32) {
+                    const int r = (i & 7) + 8 * h, c8 = i >> 3;
+                    *reinterpret_cast<uint4*>(A + c8 * (kPfM * 16) + (un * kPackTile + r) * 16) = make_uint4(0u, 0u, 0u, 0u);
                 }
             }
             fence_proxy_async_smem();  // generic-proxy stores → visible to the tensor core
             __syncwarp();
-            if (lane == 0) mbar_arrive(&full_a[slot]);
+            if (lane == 0) {
+                mbar_arrive(&full_a[slot]);
+                if (c == 3 || j == nst - 1) mbar_arrive(&raw_empty[rs]);  // done with this super-block's units
+            }
         }
         // epilogue: warps 0-3 own TMEM lanes 32·warp .. 32·warp + 31
         if (warp < 4) {
@@ -409,8 +429,8 @@ cudaError_t prefill_gemm_launch(float* y, const uint8_t* w, int type, const floa
     const int ntile = (T + kPfN - 1) / kPfN;
     const size_t xp_bytes = (size_t)ntile * (cols / kPfK) * kPfPlane;
     if (g_pf.dev != dev) {
-        AF_CUDA_TRY(cudaFuncSetAttribute(prefill_gemm_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, pf_smem<2>()));
-        AF_CUDA_TRY(cudaFuncSetAttribute(prefill_gemm_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, pf_smem<4>()));
+        AF_CUDA_TRY(cudaFuncSetAttribute(prefill_gemm_kernel<kPfStages>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         pf_smem<kPfStages>()));
         g_pf.dev = dev;
         g_pf.xp = nullptr;  // buffers of another device are not reused (they leak with the process)
         g_pf.xp_bytes = 0;
@@ -434,10 +454,8 @@ cudaError_t prefill_gemm_launch(float* y, const uint8_t* w, int type, const floa
     prefill_pack_x_kernel<<<(unsigned)((items + 255) / 256), 256, 0, st>>>(x, g_pf.xexp, g_pf.xp, cols, T,
                                                                             ntile * kPfN);
     const dim3 grid((rows + kPfM - 1) / kPfM, ntile);
-    if ((int)(grid.x * grid.y) > num_sms())
-        prefill_gemm_kernel<2><<<grid, kPfThreads, pf_smem<2>(), st>>>(y, w, type, g_pf.xp, g_pf.xexp, rows, cols, T);
-    else
-        prefill_gemm_kernel<4><<<grid, kPfThreads, pf_smem<4>(), st>>>(y, w, type, g_pf.xp, g_pf.xexp, rows, cols, T);
+    prefill_gemm_kernel<kPfStages><<<grid, kPfThreads, pf_smem<kPfStages>(), st>>>(y, w, type, g_pf.xp, g_pf.xexp, rows,
+                                                                                 cols, T);
     return cudaGetLastError();
 }
 
