@@ -596,11 +596,18 @@ __global__ void __launch_bounds__(kGemvThreads, 1) step_kernel(const __grid_cons
             // of the grid (the tags arrive only after every rank's producing
             // phase, and everything else it reads is older)
             const bool xin = kind == PH_GEMV && ph.x.k_in >= 0;
+            // the phase's parameters and fragment range do not depend on the
+            // previous phase: fetch them before waiting for it
+            int vbeg = 0, vend = 0;
+            if (kind == PH_GEMV) {
+                copy_params(gp, &ph.g, offsetof(GemvParams, vrange));
+                vbeg = __ldg(ph.g.vrange + blockIdx.x);
+                vend = __ldg(ph.g.vrange + blockIdx.x + 1);
+            }
             if (i > 0 && !xin && !grid_wait(sp.bar, (unsigned)i * grid, abort)) break;
             if (kind == PH_EMBED) {
                 embed_phase(sp, tok);
             } else {
-                copy_params(gp, &ph.g, offsetof(GemvParams, vrange));
                 if (ph.x.k_out >= 0) {  // row-parallel partial sums, sent to every rank
                     if (threadIdx.x == 0) {
                         const unsigned long long q = xseq(ph.x.k_out);
@@ -611,7 +618,6 @@ __global__ void __launch_bounds__(kGemvThreads, 1) step_kernel(const __grid_cons
                     }
                     bar_consumers();
                 }
-                const int vbeg = ph.g.vrange[blockIdx.x], vend = ph.g.vrange[blockIdx.x + 1];
                 float s_in = 1.f;
                 if (xin) {
                     if (!xchg_input(sp, ph.x, xseq(ph.x.k_in), uni, gp->eps, abort, red)) break;
