@@ -38,6 +38,17 @@ def test_gemv_rejects_bad_arguments_without_touching_a_device():
     assert lib.af_gemv_f32(None, None, 3, None, 4, 256, None) != 0    # unsupported type
 
 
+def test_prefill_gemm_rejects_bad_arguments_without_touching_a_device():
+    lib = _lib.load()
+    assert lib.af_prefill_gemm_f32(None, None, 12, None, 16, 100, 4, None) != 0   # cols % 256
+    assert b"256" in lib.af_last_error()
+    assert lib.af_prefill_gemm_f32(None, None, 3, None, 16, 256, 4, None) != 0    # unsupported type
+    assert lib.af_prefill_gemm_f32(None, None, 12, None, 16, 256, -1, None) != 0  # negative token count
+    assert lib.af_prefill_gemm_f32(None, C.c_void_p(8), 12, None, 16, 256, 4, None) != 0  # misaligned weights
+    assert b"aligned" in lib.af_last_error()
+    assert lib.af_prefill_gemm_f32(None, None, 12, None, 0, 256, 4, None) == 0    # nothing to do
+
+
 def test_gguf_config_reader(tmp_path):
     from llm_core_b200 import gguf
     from llm_core_b200.engine import read_config
