@@ -210,6 +210,17 @@ cudaError_t af_engine_step(af_engine* e, int32_t token, int32_t pos, float* h_lo
  * greedy id as in af_engine_step. */
 cudaError_t af_engine_prefill(af_engine* e, const int32_t* h_tokens, int n, int32_t pos0,
                               float* h_logits, int32_t* h_next);
+
+/* Same contract as af_engine_prefill, computed as one batched prompt pass:
+ * tokens 0 .. n-2 through every layer as rows of the tcgen05 prefill GEMM
+ * (af_prefill_gemm_f32), row kernels for norms / bias / SwiGLU / residuals,
+ * attention per token in position order; the last token through the decode
+ * step (its logits and the next token).  The reference's batched prompt pass
+ * is llama_forward_batch (src/models/llama_model.cpp:1339-1462).  Numerics
+ * differ from the per-token path by the GEMM's f16 rounding (~2e-4 relative).
+ * Tensor-parallel engines fall back to af_engine_prefill. */
+cudaError_t af_engine_prefill_batched(af_engine* e, const int32_t* h_tokens, int n, int32_t pos0,
+                                      float* h_logits, int32_t* h_next);
 /* Device-fed greedy decode: n_steps graph launches, each feeding its argmax to
  * the next; ids written to h_out (may be NULL).  No host round trip per step. */
 cudaError_t af_engine_decode_greedy(af_engine* e, int32_t first_token, int32_t pos0, int n_steps,

@@ -87,6 +87,7 @@ def load() -> C.CDLL:
         "af_engine_finalize": (i, [vp]),
         "af_engine_step": (i, [vp, C.c_int32, C.c_int32, fp, ip]),
         "af_engine_prefill": (i, [vp, ip, i, C.c_int32, fp, ip]),
+        "af_engine_prefill_batched": (i, [vp, ip, i, C.c_int32, fp, ip]),
         "af_engine_decode_greedy": (i, [vp, C.c_int32, C.c_int32, i, ip]),
         "af_engine_generate": (i, [vp, ip, i, i, ip, C.POINTER(C.c_int)]),
         "af_engine_hidden": (i, [vp, fp]),

@@ -976,6 +976,113 @@ cudaError_t af_engine_prefill(af_engine* e, const int32_t* h_tokens, int n, int3
     return cudaSuccess;
 }
 
+// Batched prompt pass (one GPU): tokens 0 .. n-2 go through every layer as
+// T = n-1 rows at once (llama_forward_batch, src/models/llama_model.cpp:1339-1462):
+// the linear layers on the tcgen05 prefill GEMM, norms / bias / SwiGLU /
+// residuals as row kernels, attention per token in position order (the
+// decode attention kernel, which applies RoPE and Q/K norms and stores the
+// token's K/V row before attending over positions <= its own, so the cache
+// fills causally).  The last token then runs the decode step, which produces
+// its logits and the next token exactly as af_engine_prefill does.
+cudaError_t af_engine_prefill_batched(af_engine* e, const int32_t* h_tokens, int n, int32_t pos0, float* h_logits,
+                                      int32_t* h_next) {
+    AF_CUDA_TRY(check_ready(e));
+    if (n <= 0 || pos0 < 0 || pos0 + n > e->cfg.n_ctx) return fail("af_engine_prefill_batched: positions outside the context");
+    for (int i = 0; i < n; ++i)
+        if (h_tokens[i] < 0 || h_tokens[i] >= e->cfg.vocab)
+            return fail("af_engine_prefill_batched: token id outside the vocabulary");
+    const auto& c = e->cfg;
+    const int T = n - 1;
+    if (T == 0 || e->tp != 1) return af_engine_prefill(e, h_tokens, n, pos0, h_logits, h_next);
+    const int E = c.n_embd, QD = e->Hl * e->hd, KD = e->KVl * e->hd, F = e->Fl;
+    std::vector<void*> bufs;
+    auto take = [&](size_t bytes) {
+        void* p = nullptr;
+        if (cudaMalloc(&p, bytes ? bytes : 16) != cudaSuccess) return static_cast<void*>(nullptr);
+        bufs.push_back(p);
+        return p;
+    };
+    float* x = static_cast<float*>(take((size_t)T * E * 4));
+    float* xn = static_cast<float*>(take((size_t)T * E * 4));
+    float* tmp = static_cast<float*>(take((size_t)T * E * 4));
+    float* q = static_cast<float*>(take((size_t)T * QD * 4));
+    float* k = static_cast<float*>(take((size_t)T * KD * 4));
+    float* v = static_cast<float*>(take((size_t)T * KD * 4));
+    float* att = static_cast<float*>(take((size_t)T * QD * 4));
+    float* g = static_cast<float*>(take((size_t)T * F * 4));
+    float* u = static_cast<float*>(take((size_t)T * F * 4));
+    int* d_tp = static_cast<int*>(take((size_t)2 * T * 4));  // tokens, then positions
+    auto release = [&]() {
+        for (void* p : bufs) cudaFree(p);
+    };
+    for (void* p : bufs)
+        if (!p) {
+            release();
+            return fail("af_engine_prefill_batched: out of device memory for the prompt rows",
+                        cudaErrorMemoryAllocation);
+        }
+    cudaError_t err = cudaSuccess;
+    auto run = [&]() -> cudaError_t {
+        std::vector<int32_t> tp((size_t)2 * T);
+        for (int t = 0; t < T; ++t) {
+            tp[t] = h_tokens[t];
+            tp[T + t] = pos0 + t;
+        }
+        ENG_TRY(cudaMemcpyAsync(d_tp, tp.data(), tp.size() * 4, cudaMemcpyHostToDevice, e->stream));
+        ENG_TRY(prompt_embed_launch(x, e->tok_embd.w, e->tok_embd.type, E, e->tok_embd.stride, d_tp, T, e->stream));
+        for (int l = 0; l < c.n_layer; ++l) {
+            const LayerW& L = e->layers[l];
+            ENG_TRY(rows_rmsnorm_launch(xn, x, L.attn_norm, E, T, c.eps, e->stream));
+            ENG_TRY(prefill_gemm_launch(q, L.wq.w, L.wq.type, xn, QD, E, T, e->stream));
+            ENG_TRY(prefill_gemm_launch(k, L.wk.w, L.wk.type, xn, KD, E, T, e->stream));
+            ENG_TRY(prefill_gemm_launch(v, L.wv.w, L.wv.type, xn, KD, E, T, e->stream));
+            if (L.bq) ENG_TRY(rows_bias_launch(q, L.bq, QD, T, e->stream));
+            if (L.bk) ENG_TRY(rows_bias_launch(k, L.bk, KD, T, e->stream));
+            if (L.bv) ENG_TRY(rows_bias_launch(v, L.bv, KD, T, e->stream));
+            const size_t lsz = (size_t)c.n_ctx * KD;
+            for (int t = 0; t < T; ++t) {
+                AttnParams a = {};
+                a.q = q + (size_t)t * QD;
+                a.k = k + (size_t)t * KD;
+                a.v = v + (size_t)t * KD;
+                a.kc = e->kcache + (size_t)l * lsz;
+                a.vc = e->vcache + (size_t)l * lsz;
+                a.out = att + (size_t)t * QD;
+                a.cos_t = e->cos_t;
+                a.sin_t = e->sin_t;
+                a.q_norm = L.q_norm;
+                a.k_norm = L.k_norm;
+                a.part = e->apart;
+                a.counter = e->acount;
+                a.pos = d_tp + T + t;
+                a.n_heads = e->Hl;
+                a.n_kv_heads = e->KVl;
+                a.head_dim = e->hd;
+                a.n_ctx = c.n_ctx;
+                a.nsplit = e->nsplit;
+                a.qk_norm_order = c.qk_norm_order;
+                a.eps = c.eps;
+                a.scale = 1.f / std::sqrt((float)e->hd);
+                ENG_TRY(attention_launch(a, e->stream, false));
+            }
+            ENG_TRY(prefill_gemm_launch(tmp, L.wo.w, L.wo.type, att, E, QD, T, e->stream));
+            ENG_TRY(rows_add_launch(x, tmp, (long long)T * E, e->stream));
+            ENG_TRY(rows_rmsnorm_launch(xn, x, L.ffn_norm, E, T, c.eps, e->stream));
+            ENG_TRY(prefill_gemm_launch(g, L.wg.w, L.wg.type, xn, F, E, T, e->stream));
+            ENG_TRY(prefill_gemm_launch(u, L.wu.w, L.wu.type, xn, F, E, T, e->stream));
+            ENG_TRY(rows_swiglu_launch(g, u, (long long)T * F, e->stream));
+            ENG_TRY(prefill_gemm_launch(tmp, L.wd.w, L.wd.type, g, E, F, T, e->stream));
+            ENG_TRY(rows_add_launch(x, tmp, (long long)T * E, e->stream));
+        }
+        ENG_TRY(cudaStreamSynchronize(e->stream));
+        return cudaSuccess;
+    };
+    err = run();
+    release();
+    if (err != cudaSuccess) return err;
+    return af_engine_prefill(e, h_tokens + T, 1, pos0 + T, h_logits, h_next);
+}
+
 cudaError_t af_engine_decode_greedy(af_engine* e, int32_t first_token, int32_t pos0, int n_steps, int32_t* h_out) {
     AF_CUDA_TRY(check_ready(e));
     if (n_steps < 0 || pos0 < 0 || pos0 + n_steps > e->cfg.n_ctx) return fail("af_engine_decode_greedy: context overflow");

@@ -61,6 +61,17 @@ cudaError_t embed_launch(float* x, const uint8_t* W, int type, int cols, int row
                          unsigned long long* argmax, uint8_t* xq, const float* xq_norm_w, cudaStream_t st,
                          bool pdl);
 
+// Prefill (af_prefill.cu): the tcgen05 dequant-GEMM Y[T][rows] = X[T][cols]·Wᵀ
+// and the row kernels of the batched prompt pass.
+cudaError_t prefill_gemm_launch(float* y, const uint8_t* w, int type, const float* x, int rows, int cols, int T,
+                                cudaStream_t st);
+cudaError_t prompt_embed_launch(float* x, const uint8_t* W, int type, int cols, int row_stride, const int* tokens,
+                                int T, cudaStream_t st);
+cudaError_t rows_rmsnorm_launch(float* y, const float* x, const float* w, int n, int T, float eps, cudaStream_t st);
+cudaError_t rows_bias_launch(float* y, const float* b, int n, int T, cudaStream_t st);
+cudaError_t rows_swiglu_launch(float* g, const float* u, long long count, cudaStream_t st);
+cudaError_t rows_add_launch(float* x, const float* y, long long count, cudaStream_t st);
+
 // Decode attention (af_attention.cu).
 struct AttnParams {
     const float* q;        // [Hl*hd] projected (biased) queries

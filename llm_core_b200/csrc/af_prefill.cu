@@ -408,6 +408,55 @@ __global__ void prefill_pack_x_kernel(const float* __restrict__ X, const int* __
     *reinterpret_cast<uint4*>(Xp + ((size_t)(n / kPfN) * nst + s) * kPfPlane + c8 * (kPfN * 16) + (n % kPfN) * 16) = o;
 }
 
+// ---- row kernels of the batched prompt pass (one token per row)
+
+// x[t] = dequantised embedding row of token tokens[t] (emb_lookup,
+// src/models/llama_model.cpp:882-934).
+__global__ void prompt_embed_kernel(float* __restrict__ x, const uint8_t* __restrict__ W, int type, int cols,
+                                    int row_stride, const int* __restrict__ tokens) {
+    const int t = blockIdx.y;
+    const int v = blockIdx.x * blockDim.x + threadIdx.x;
+    if (v < cols) x[(size_t)t * cols + v] = embed_value(W, type, cols / 256, row_stride, tokens[t], v);
+}
+
+// y[t] = w ⊙ x[t] · 1/sqrt(Σx²/n + eps) (rms_norm_out, src/models/llama_model.cpp:393-419);
+// one block per row, warp sums added in a fixed order.
+__global__ void rows_rmsnorm_kernel(float* __restrict__ y, const float* __restrict__ x, const float* __restrict__ w,
+                                    int n, float eps) {
+    __shared__ float red[32];
+    const float* xr = x + (size_t)blockIdx.x * n;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) ss += xr[i] * xr[i];
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+    for (int k = 0; k < (int)(blockDim.x >> 5); ++k) tot += red[k];
+    const float inv = 1.f / sqrtf(tot / (float)n + eps);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) y[(size_t)blockIdx.x * n + i] = w[i] * (xr[i] * inv);
+}
+
+// y[t][i] += b[i] (add_bias, src/models/llama_model.cpp:1082-1092).
+__global__ void rows_bias_kernel(float* __restrict__ y, const float* __restrict__ b, int n, long long count) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < count) y[i] += b[i % n];
+}
+
+// g = silu(g) · u (swiglu, src/models/llama_model.cpp:319-368).
+__global__ void rows_swiglu_kernel(float* __restrict__ g, const float* __restrict__ u, long long count) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < count) {
+        const float v = g[i];
+        g[i] = (v / (1.f + expf(-v))) * u[i];
+    }
+}
+
+// x += y (residual adds, src/models/llama_model.cpp:1277, 1324).
+__global__ void rows_add_kernel(float* __restrict__ x, const float* __restrict__ y, long long count) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < count) x[i] += y[i];
+}
+
 // Staging buffers of X, grown on demand (cudaMalloc: not during stream capture).
 struct PrefillScratch {
     std::mutex mu;
@@ -456,6 +505,33 @@ cudaError_t prefill_gemm_launch(float* y, const uint8_t* w, int type, const floa
     const dim3 grid((rows + kPfM - 1) / kPfM, ntile);
     prefill_gemm_kernel<kPfStages><<<grid, kPfThreads, pf_smem<kPfStages>(), st>>>(y, w, type, g_pf.xp, g_pf.xexp, rows,
                                                                                  cols, T);
+    return cudaGetLastError();
+}
+
+cudaError_t prompt_embed_launch(float* x, const uint8_t* W, int type, int cols, int row_stride, const int* tokens,
+                                int T, cudaStream_t st) {
+    prompt_embed_kernel<<<dim3((cols + 255) / 256, T), 256, 0, st>>>(x, W, type, cols, row_stride, tokens);
+    return cudaGetLastError();
+}
+
+cudaError_t rows_rmsnorm_launch(float* y, const float* x, const float* w, int n, int T, float eps, cudaStream_t st) {
+    rows_rmsnorm_kernel<<<T, 256, 0, st>>>(y, x, w, n, eps);
+    return cudaGetLastError();
+}
+
+cudaError_t rows_bias_launch(float* y, const float* b, int n, int T, cudaStream_t st) {
+    const long long count = (long long)n * T;
+    rows_bias_kernel<<<(unsigned)((count + 255) / 256), 256, 0, st>>>(y, b, n, count);
+    return cudaGetLastError();
+}
+
+cudaError_t rows_swiglu_launch(float* g, const float* u, long long count, cudaStream_t st) {
+    rows_swiglu_kernel<<<(unsigned)((count + 255) / 256), 256, 0, st>>>(g, u, count);
+    return cudaGetLastError();
+}
+
+cudaError_t rows_add_launch(float* x, const float* y, long long count, cudaStream_t st) {
+    rows_add_kernel<<<(unsigned)((count + 255) / 256), 256, 0, st>>>(x, y, count);
     return cudaGetLastError();
 }
 

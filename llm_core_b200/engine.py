@@ -125,13 +125,16 @@ class LlamaCudaModel:
                                       C.byref(nxt)), "af_engine_step")
         return nxt.value, lg
 
-    def prefill(self, tokens, pos0: int = 0, want_logits: bool = True):
+    def prefill(self, tokens, pos0: int = 0, want_logits: bool = True, batched: bool = False):
+        """Feed a prompt; batched=True runs it as one batched pass on the
+        tensor cores (af_engine_prefill_batched) instead of token by token."""
         t = np.ascontiguousarray(tokens, dtype=np.int32)
         lg = np.zeros(self.cfg.vocab, np.float32) if want_logits else None
         nxt = C.c_int32()
-        check(self.lib.af_engine_prefill(self.h, t.ctypes.data_as(C.POINTER(C.c_int32)), t.size, pos0,
-                                         lg.ctypes.data_as(C.POINTER(C.c_float)) if want_logits else None,
-                                         C.byref(nxt)), "af_engine_prefill")
+        fn = self.lib.af_engine_prefill_batched if batched else self.lib.af_engine_prefill
+        check(fn(self.h, t.ctypes.data_as(C.POINTER(C.c_int32)), t.size, pos0,
+                 lg.ctypes.data_as(C.POINTER(C.c_float)) if want_logits else None,
+                 C.byref(nxt)), "af_engine_prefill")
         return nxt.value, lg
 
     def decode_greedy(self, first_token: int, pos0: int, n_steps: int) -> np.ndarray:
