@@ -134,11 +134,13 @@ def test_tinyllama_logits_and_greedy_agreement(gpu):
 def test_batched_prefill_matches_token_prefill(gpu, preset, seed):
     """The batched prompt pass (tcgen05 prefill GEMM, row kernels, per-token
     attention) against the per-token path, which the fixture tests pin to the
-    reference: last-position logits within the logits bar, and the first
-    layer's K/V cache rows (the layer fed by the embedding alone) within it
-    too.  Deeper layers' rows are reported, not bounded: the llama presets
-    stay within 5e-4, the qwen2 preset (q/k/v bias, tied embeddings) differs
-    by 2.7e-3 (K) and 9.5e-3 (V) at layer 1 — an open item."""
+    reference: last-position logits and the first layer's K/V cache rows
+    within the logits bar; deeper layers' rows within twice what f16 rounding
+    of the linear layers' operands alone predicts (a float64 emulation of the
+    same forward, tests/f16_emulation.py).  On the random-init qwen2 preset
+    that prediction is ~1e-2 at layer 1 (near-hard attention amplifies the
+    rounding); on the llama presets it stays below 6e-4."""
+    from f16_emulation import kv_rounding_deviation
     from llm_core_b200.engine import read_config
     path = model_path(preset, seed)
     cfg = read_config(path)
@@ -153,7 +155,10 @@ def test_batched_prefill_matches_token_prefill(gpu, preset, seed):
     n = len(prompt)
     for which_v in (False, True):
         assert rel_l2(b.kv(0, which_v, n), a.kv(0, which_v, n)) < LOGITS_TOL, which_v
+    predicted = kv_rounding_deviation(path, prompt[:-1], cfg.n_layer)
     for layer in range(1, cfg.n_layer):
-        print(preset, layer, [round(rel_l2(b.kv(layer, w, n), a.kv(layer, w, n)), 5) for w in (False, True)])
+        for w, which_v in enumerate((False, True)):
+            dev = rel_l2(b.kv(layer, which_v, n), a.kv(layer, which_v, n))
+            assert dev < 2 * predicted[layer][w] + 1e-4, (layer, which_v, dev, predicted[layer][w])
     a.close()
     b.close()
