@@ -11,8 +11,9 @@
  *      (src/backend/cuda/cuda_kernels.hpp:8-19) plus the Q6_K GEMV it lacks.
  *   2. The decode engine — the GPU-resident replacement of
  *      llama_cuda_generate (include/axonforge/models/llama_cuda.hpp:25-28):
- *      weights uploaded byte-for-byte, fp32 KV cache on the device, one CUDA
- *      graph per decode step, optional tensor parallelism over NCCL.
+ *      weights uploaded byte-for-byte, fp32 KV cache on the device, one
+ *      persistent kernel per decode step (captured in a CUDA graph), device
+ *      sampling, optional tensor parallelism over NVLink peer memory.
  *
  * Weight layout on the device ("packed"): the GGUF super-blocks, byte for byte,
  * permuted once at upload by af_weight_pack so that every pipeline stage of the
@@ -152,6 +153,33 @@ cudaError_t af_attention_decode_f32_noalloc(float* d_out, const float* d_q, cons
                                             int head_dim, int n_ctx, int qk_norm_order, float eps,
                                             int nsplit, cudaStream_t stream);
 
+/* Sampling parameters of the reference's LlamaConfig
+ * (include/axonforge/models/llama.hpp:17-35): temperature <= 0 is greedy;
+ * top_k <= 0 (or >= vocab) keeps every token; top_p >= 1 disables the
+ * nucleus cut; rep_penalty == 1 disables the penalty. */
+typedef struct {
+    float temperature;
+    int top_k;
+    float top_p;
+    float rep_penalty;
+    int rep_last_n;
+} af_sampling;
+
+/* One sampling step on the device, one CTA: the repetition penalty over the
+ * n_window ids at d_window (applied in place to d_logits, in window order, as
+ * apply_rep_penalty does, src/models/llama_model.cpp:1586-1598), then greedy
+ * first-max at temperature <= 0, else temperature / top-k / top-p sampling
+ * with the uniform draw r in [0, 1) (sample, llama_model.cpp:1466-1498).
+ * Writes the id to *d_out.  With temperature > 0 the kept candidates must
+ * number at most 1024 (top_k in 1..1024); otherwise cudaErrorNotSupported. */
+cudaError_t af_sample_f32(float* d_logits, int vocab, const int32_t* d_window, int n_window,
+                          const af_sampling* s, float r, int32_t* d_out, cudaStream_t stream);
+
+/* n uniform draws of std::uniform_real_distribution<float>(0, 1) from
+ * std::mt19937(seed) — the reference's sampler stream (llama_model.cpp:1560,
+ * 1494-1495), computed by the host C++ library. */
+cudaError_t af_mt19937_uniform(uint32_t seed, int n, float* h_out);
+
 /* y = w ⊙ x / sqrt(mean(x²) + eps): rms_norm_f32 (cuda_kernels.hpp:8). */
 cudaError_t af_rms_norm_f32(float* d_y, const float* d_x, const float* d_w, int n, float eps,
                             cudaStream_t stream);
@@ -230,6 +258,22 @@ cudaError_t af_engine_decode_greedy(af_engine* e, int32_t first_token, int32_t p
  * EOS or the context cap.  Returns the ids in h_out, count in *n_out. */
 cudaError_t af_engine_generate(af_engine* e, const int32_t* h_prompt, int n_prompt, int max_new,
                                int32_t* h_out, int* n_out);
+/* Sample the next token from the logits of the last step / prefill (all
+ * ranks' shards): af_sample_f32 over the full vocabulary, with the penalty
+ * window h_window[0..n_window) (host ids) and the draw r.  Tensor-parallel
+ * ranks given the same arguments return the same id. */
+cudaError_t af_engine_sample(af_engine* e, const af_sampling* s, const int32_t* h_window, int n_window, float r,
+                             int32_t* h_next);
+/* llama_generate with sampling (src/models/llama_model.cpp:1502-1631): BOS
+ * prepended unless present, the prompt, then one sampling step per token
+ * with the repetition window of the last rep_last_n ids of prompt +
+ * generated, stopping at EOS (not emitted) or the context cap.  h_draws holds
+ * the uniform draws in order (the reference consumes one per sampling step at
+ * temperature > 0; e.g. af_mt19937_uniform(42, ...)); n_draws must cover
+ * max_new + 1 of them then, and may be 0 when greedy. */
+cudaError_t af_engine_generate_sampled(af_engine* e, const int32_t* h_prompt, int n_prompt, int max_new,
+                                       const af_sampling* s, const float* h_draws, int n_draws, int32_t* h_out,
+                                       int* n_out);
 /* Copy the current residual stream (n_embd floats) to the host. */
 cudaError_t af_engine_hidden(af_engine* e, float* h_out);
 /* Copy layer l's fp32 K or V cache rows [0, n_pos) (local heads) to the host. */

@@ -28,6 +28,12 @@ class ModelConfig(C.Structure):
                 ("bos_id", C.c_int), ("eos_id", C.c_int)]
 
 
+class Sampling(C.Structure):
+    """af_sampling (include/af_b200.h)."""
+    _fields_ = [("temperature", C.c_float), ("top_k", C.c_int), ("top_p", C.c_float), ("rep_penalty", C.c_float),
+                ("rep_last_n", C.c_int)]
+
+
 class GemvFusedArgs(C.Structure):
     """af_gemv_fused_args (include/af_b200.h)."""
     _fields_ = [("w", C.c_void_p * 3), ("type", C.c_int * 3), ("rows", C.c_int * 3), ("y", C.c_void_p * 3),
@@ -90,6 +96,10 @@ def load() -> C.CDLL:
         "af_engine_prefill_batched": (i, [vp, ip, i, C.c_int32, fp, ip]),
         "af_engine_decode_greedy": (i, [vp, C.c_int32, C.c_int32, i, ip]),
         "af_engine_generate": (i, [vp, ip, i, i, ip, C.POINTER(C.c_int)]),
+        "af_sample_f32": (i, [vp, i, vp, i, C.POINTER(Sampling), f, vp, vp]),
+        "af_mt19937_uniform": (i, [C.c_uint32, i, fp]),
+        "af_engine_sample": (i, [vp, C.POINTER(Sampling), ip, i, f, ip]),
+        "af_engine_generate_sampled": (i, [vp, ip, i, i, C.POINTER(Sampling), fp, i, ip, C.POINTER(C.c_int)]),
         "af_engine_hidden": (i, [vp, fp]),
         "af_engine_kv": (i, [vp, i, i, i, fp]),
         "af_engine_profile": (i, [vp, C.c_int32, C.c_int32, i, C.POINTER(C.c_double), C.POINTER(C.c_double),

@@ -24,6 +24,7 @@
 
 #include <cmath>
 #include <cstdlib>
+#include <random>
 #include <cstdio>
 #include <cstring>
 #include <map>
@@ -94,6 +95,9 @@ struct af_engine {
     unsigned long long* key = nullptr;
     int* tokpos = nullptr;  // [0] token, [1] pos
     int* hist = nullptr;
+    int* d_window = nullptr;       // repetition-penalty window of the sampler [n_ctx + 1]
+    int* d_sampled = nullptr;      // sampled id
+    float* logits_full = nullptr;  // tensor parallel: the gathered vocabulary [vocab]
     int* h_tokpos = nullptr;  // pinned host mirror
     int nsplit = 1;
 
@@ -901,6 +905,9 @@ cudaError_t af_engine_finalize(af_engine* e) {
         e->key = static_cast<unsigned long long*>(e->dalloc(8));
         e->tokpos = static_cast<int*>(e->dalloc(8));
         e->hist = static_cast<int*>(e->dalloc((size_t)(c.n_ctx + 1) * 4));
+        e->d_window = static_cast<int*>(e->dalloc((size_t)(c.n_ctx + 1) * 4));
+        e->d_sampled = static_cast<int*>(e->dalloc(16));
+        if (e->tp > 1) e->logits_full = static_cast<float*>(e->dalloc((size_t)c.vocab * 4));
         ENG_TRY(cudaMemset(e->tokpos, 0, 8));
         ENG_TRY(cudaMallocHost(&e->h_tokpos, 16));
         ENG_TRY(gemv_init());
@@ -1126,6 +1133,84 @@ cudaError_t af_engine_generate(af_engine* e, const int32_t* h_prompt, int n_prom
         h_out[n++] = id;
     }
     *n_out = n;
+    return cudaSuccess;
+}
+
+cudaError_t af_engine_sample(af_engine* e, const af_sampling* s, const int32_t* h_window, int n_window, float r,
+                             int32_t* h_next) {
+    AF_CUDA_TRY(check_ready(e));
+    if (!s || !h_next || n_window < 0 || n_window > e->cfg.n_ctx + 1 || (n_window > 0 && !h_window))
+        return fail("af_engine_sample: bad arguments");
+    std::string why;
+    if (!sample_supported(*s, e->cfg.vocab, &why)) {
+        set_last_error("af_engine_sample: " + why);
+        return cudaErrorNotSupported;
+    }
+    float* lg = e->logits;
+    if (e->tp > 1) {
+        // the full vocabulary, in rank order, on every rank
+        NCCL_TRY(ncclAllGather(e->logits, e->logits_all, e->Vmax, ncclFloat32, e->comm, e->stream));
+        int off = 0;
+        for (int rk = 0; rk < e->tp; ++rk) {
+            int lo, hi;
+            block_split(e->cfg.vocab, rk, e->tp, lo, hi);
+            ENG_TRY(cudaMemcpyAsync(e->logits_full + off, e->logits_all + (size_t)rk * e->Vmax, (size_t)(hi - lo) * 4,
+                                    cudaMemcpyDeviceToDevice, e->stream));
+            off += hi - lo;
+        }
+        lg = e->logits_full;
+    }
+    if (n_window > 0)
+        ENG_TRY(cudaMemcpyAsync(e->d_window, h_window, (size_t)n_window * 4, cudaMemcpyHostToDevice, e->stream));
+    ENG_TRY(sample_launch(lg, e->cfg.vocab, e->d_window, n_window, *s, r, e->d_sampled, e->stream));
+    ENG_TRY(cudaMemcpyAsync(e->h_tokpos + 3, e->d_sampled, 4, cudaMemcpyDeviceToHost, e->stream));
+    ENG_TRY(cudaStreamSynchronize(e->stream));
+    *h_next = e->h_tokpos[3];
+    return cudaSuccess;
+}
+
+cudaError_t af_engine_generate_sampled(af_engine* e, const int32_t* h_prompt, int n_prompt, int max_new,
+                                       const af_sampling* s, const float* h_draws, int n_draws, int32_t* h_out,
+                                       int* n_out) {
+    AF_CUDA_TRY(check_ready(e));
+    if (!s || !n_out || (max_new > 0 && !h_out)) return fail("af_engine_generate_sampled: null argument");
+    if (n_prompt <= 0) return fail("llama_generate: empty prompt");
+    const bool draws = s->temperature > 0.f;
+    if (draws && (!h_draws || n_draws < max_new + 1))
+        return fail("af_engine_generate_sampled: need max_new + 1 uniform draws at temperature > 0");
+    *n_out = 0;
+    std::vector<int32_t> ctx(h_prompt, h_prompt + n_prompt);
+    if (ctx[0] != e->cfg.bos_id) ctx.insert(ctx.begin(), e->cfg.bos_id);
+    const int np = (int)ctx.size();
+    if (np > e->cfg.n_ctx) return fail("af_engine_generate_sampled: prompt longer than the context");
+    int di = 0;
+    // penalty window: the last rep_last_n ids of prompt + generated (llama_model.cpp:1588-1592)
+    auto pick = [&](int32_t& next) -> cudaError_t {
+        const int win = s->rep_penalty != 1.0f ? std::min(std::max(s->rep_last_n, 0), (int)ctx.size()) : 0;
+        return af_engine_sample(e, s, ctx.data() + ctx.size() - win, win, draws ? h_draws[di++] : 0.f, &next);
+    };
+    AF_CUDA_TRY(af_engine_prefill(e, ctx.data(), np, 0, nullptr, nullptr));
+    int32_t next = 0;
+    AF_CUDA_TRY(pick(next));
+    int n = 0, n_past = np;
+    for (int step = 0; step < max_new; ++step) {
+        if (next == e->cfg.eos_id) break;  // EOS is not emitted
+        if (n_past >= e->cfg.n_ctx) break;
+        h_out[n++] = next;
+        AF_CUDA_TRY(af_engine_step(e, next, n_past, nullptr, nullptr));
+        ++n_past;
+        ctx.push_back(next);
+        AF_CUDA_TRY(pick(next));
+    }
+    *n_out = n;
+    return cudaSuccess;
+}
+
+cudaError_t af_mt19937_uniform(uint32_t seed, int n, float* h_out) {
+    if (n < 0 || (n > 0 && !h_out)) return fail("af_mt19937_uniform: bad arguments");
+    std::mt19937 rng(seed);
+    std::uniform_real_distribution<float> dist(0.f, 1.f);
+    for (int i = 0; i < n; ++i) h_out[i] = dist(rng);
     return cudaSuccess;
 }
 

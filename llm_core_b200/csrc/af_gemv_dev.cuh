@@ -92,48 +92,46 @@ struct Ring {
 
 // ---------------------------------------------------------------- producer
 
-// Single-thread producer state; persists across the phases of a step.  The
-// in-flight table is indexed with compile-time slots only, so it stays in
-// registers (a dynamically indexed table would live in local memory and put
-// an L1 round trip on every check of the producer's serial loop).
+// Single-thread producer state; persists across the phases of a step.
+// Ring space is accounted first-in first-out: `used` counts the bytes (with
+// the waste a wrapped placement leaves at the end of the ring) of entries
+// issued and not yet released, so making room costs O(1) per released entry.
+// The producer thread shares an SM sub-partition with two busy consumer
+// warps, so every instruction it spends per entry delays the stream.  The
+// size table is indexed with compile-time slots only (registers, not local
+// memory).
 struct Producer {
     uint32_t issued = 0, released = 0;
     int head = 0;
-    int off[kRingDesc];
+    int used = 0;
     int size[kRingDesc];
 
-    // Wait (bounded) until entry `released` has been consumed.
+    // Wait (bounded) until entry `released` has been consumed and free its bytes.
     __device__ bool release_oldest(const Ring& r, const volatile int* abort) {
         const uint32_t j = released;
         if (!mbar_wait(&r.empty[j % kRingDesc], (j / kRingDesc) & 1u, abort)) return false;
+        int s = 0;
+#pragma unroll
+        for (int d = 0; d < kRingDesc; ++d)
+            if (d == (int)(j % kRingDesc)) s = size[d];
+        used -= s;
         ++released;
         return true;
     }
 
     // Reserve `bytes` at the next placement; false on timeout or abort.
     __device__ bool reserve(const Ring& r, int bytes, int& at, const volatile int* abort) {
-        int h = head;
-        at = ring_place(h, bytes, r.bytes);
-        for (;;) {
-            const uint32_t n = issued - released;
-            if (n == 0) break;
-            bool clash = n >= (uint32_t)kRingDesc;
-#pragma unroll
-            for (int d = 0; d < kRingDesc; ++d) {
-                const bool live = ((uint32_t)(d - (int)released) & (kRingDesc - 1)) < n;
-                clash |= live && at < off[d] + size[d] && off[d] < at + bytes;
-            }
-            if (!clash) break;
+        const int waste = head + bytes > r.bytes ? r.bytes - head : 0;
+        const int need = bytes + waste;
+        while (used + need > r.bytes || issued - released >= (uint32_t)kRingDesc)
             if (!release_oldest(r, abort)) return false;
-        }
-        head = h;
+        at = waste ? 0 : head;
+        head = at + bytes;
+        used += need;
         const int slot = issued % kRingDesc;
 #pragma unroll
         for (int d = 0; d < kRingDesc; ++d)
-            if (d == slot) {
-                off[d] = at;
-                size[d] = bytes;
-            }
+            if (d == slot) size[d] = need;
         return true;
     }
 

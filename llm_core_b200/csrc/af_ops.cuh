@@ -96,6 +96,11 @@ cudaError_t attention_init();
 cudaError_t attention_launch(const AttnParams& p, cudaStream_t st, bool pdl);
 int attention_smem_bytes(const AttnParams& p);
 
+// Device sampling step (af_sample.cu).
+cudaError_t sample_launch(float* d_logits, int vocab, const int* d_window, int n_window, const af_sampling& s, float r,
+                          int* d_out, cudaStream_t st);
+bool sample_supported(const af_sampling& s, int vocab, std::string* why);
+
 // Argmax finalize: packed key -> token id, pos++ (af_attention.cu).
 cudaError_t finalize_launch(const unsigned long long* key, int* token, int* pos, int* hist, cudaStream_t st,
                             bool pdl);

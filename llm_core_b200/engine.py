@@ -3,7 +3,8 @@
 ``LlamaCudaModel`` is the decode path behind ``llama_cuda_generate``
 (include/axonforge/models/llama_cuda.hpp:25-28): it loads a GGUF (weights
 byte-for-byte to the device), and ``generate`` follows llama_generate's
-decode-loop semantics (src/models/llama_model.cpp:1562-1624).  All compute is
+decode-loop semantics (src/models/llama_model.cpp:1562-1624), greedy or
+sampled (repetition penalty, temperature / top-k / top-p on the device).  All compute is
 in libaf_b200.so; this module only moves arguments across the C ABI.
 """
 from __future__ import annotations
@@ -15,15 +16,30 @@ from typing import Callable
 import numpy as np
 
 from . import _lib
-from ._lib import ModelConfig, check
+from ._lib import ModelConfig, Sampling, check
+
+SAMPLER_SEED = 42  # std::mt19937 rng(42) (src/models/llama_model.cpp:1560)
+
+
+def mt19937_uniform(n: int, seed: int = SAMPLER_SEED) -> np.ndarray:
+    """The reference sampler's uniform draws: std::uniform_real_distribution<float>(0, 1)
+    over std::mt19937(seed), computed by the library's host C++ code."""
+    out = np.zeros(max(n, 1), np.float32)
+    check(_lib.load().af_mt19937_uniform(seed, n, out.ctypes.data_as(C.POINTER(C.c_float))), "af_mt19937_uniform")
+    return out[:n]
+
+
+def sampling_of(cfg: "LlamaConfig") -> Sampling:
+    return Sampling(cfg.temperature, cfg.top_k, cfg.top_p, cfg.rep_penalty, cfg.rep_penalty_last_n)
 
 
 @dataclass
 class LlamaConfig:
-    """LlamaConfig (include/axonforge/models/llama.hpp:17-36).  The GPU path
-    is greedy: temperature <= 0 (top-k / top-p sampling is not on this path)."""
+    """LlamaConfig (include/axonforge/models/llama.hpp:17-36), same defaults:
+    temperature 1 with top-k 40 samples; temperature <= 0 is greedy.  The
+    sampler draws from std::mt19937(42) as the reference does."""
     max_new_tokens: int = 200
-    temperature: float = 0.0
+    temperature: float = 1.0
     top_k: int = 40
     verbose: bool = False
     n_threads: int = 0
@@ -144,18 +160,35 @@ class LlamaCudaModel:
               "af_engine_decode_greedy")
         return out[:n_steps]
 
+    def sample(self, cfg: LlamaConfig, window, r: float) -> int:
+        """One sampling step from the last logits (af_engine_sample)."""
+        w = np.ascontiguousarray(window, dtype=np.int32)
+        nxt = C.c_int32()
+        s = sampling_of(cfg)
+        check(self.lib.af_engine_sample(self.h, C.byref(s), w.ctypes.data_as(C.POINTER(C.c_int32)), w.size,
+                                        float(r), C.byref(nxt)), "af_engine_sample")
+        return nxt.value
+
     def generate(self, prompt_ids, cfg: LlamaConfig | None = None) -> list[int]:
         cfg = cfg or LlamaConfig()
-        if cfg.temperature > 0:
-            raise NotImplementedError("the B200 decode path samples greedily (temperature <= 0)")
         p = np.ascontiguousarray(prompt_ids, dtype=np.int32)
         if p.size == 0:
             raise ValueError("llama_generate: empty prompt")
         out = np.zeros(max(cfg.max_new_tokens, 1), np.int32)
         n = C.c_int()
-        check(self.lib.af_engine_generate(self.h, p.ctypes.data_as(C.POINTER(C.c_int32)), p.size,
-                                          cfg.max_new_tokens, out.ctypes.data_as(C.POINTER(C.c_int32)),
-                                          C.byref(n)), "af_engine_generate")
+        if cfg.temperature <= 0 and cfg.rep_penalty == 1.0:
+            # greedy: the device-fed decode loop
+            check(self.lib.af_engine_generate(self.h, p.ctypes.data_as(C.POINTER(C.c_int32)), p.size,
+                                              cfg.max_new_tokens, out.ctypes.data_as(C.POINTER(C.c_int32)),
+                                              C.byref(n)), "af_engine_generate")
+        else:
+            draws = mt19937_uniform(cfg.max_new_tokens + 1) if cfg.temperature > 0 else np.zeros(1, np.float32)
+            s = sampling_of(cfg)
+            check(self.lib.af_engine_generate_sampled(self.h, p.ctypes.data_as(C.POINTER(C.c_int32)), p.size,
+                                                      cfg.max_new_tokens, C.byref(s),
+                                                      draws.ctypes.data_as(C.POINTER(C.c_float)), draws.size,
+                                                      out.ctypes.data_as(C.POINTER(C.c_int32)), C.byref(n)),
+                  "af_engine_generate_sampled")
         ids = out[:n.value].tolist()
         if cfg.on_token:
             for t in ids:

@@ -217,6 +217,11 @@ class RefLib:
         L.axref_time_decode.argtypes = [C.c_void_p, C.c_int, C.c_int]
         L.axref_set_n_past.argtypes = [C.c_void_p, C.c_int]
         L.axref_hidden.argtypes = [C.c_void_p, _fp]
+        _ip = C.POINTER(C.c_int32)
+        L.axref_sample.argtypes = [_fp, C.c_int, _ip, C.c_int, C.c_float, C.c_int, C.c_float, C.c_float, C.c_uint32]
+        L.axref_generate_sampled.argtypes = [C.c_void_p, _ip, C.c_int, C.c_int, C.c_float, C.c_int, C.c_float,
+                                             C.c_float, C.c_int, _ip]
+        L.axref_uniform.argtypes = [C.c_uint32, C.c_int, _fp]
         self.h = None
 
     @staticmethod
@@ -273,6 +278,30 @@ class RefLib:
         if n < 0:
             raise RuntimeError(self.lib.axref_last_error().decode())
         return out[:n].tolist(), (lg[:n] if want_logits else None)
+
+    def sample(self, logits: np.ndarray, window, rep_penalty: float, top_k: int, top_p: float,
+               temperature: float, seed: int) -> int:
+        """The reference's penalty + sample() on a copy of `logits`, rng mt19937(seed)."""
+        lg = np.ascontiguousarray(logits, dtype=np.float32)
+        w = np.ascontiguousarray(window, dtype=np.int32)
+        return self.lib.axref_sample(_f(lg), lg.size, w.ctypes.data_as(C.POINTER(C.c_int32)), w.size, rep_penalty,
+                                     top_k, top_p, temperature, seed)
+
+    def generate_sampled(self, prompt, max_new: int, temperature: float, top_k: int, top_p: float,
+                         rep_penalty: float, rep_last_n: int):
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.zeros(max(max_new, 1), np.int32)
+        n = self.lib.axref_generate_sampled(self.h, p.ctypes.data_as(C.POINTER(C.c_int32)), p.size, max_new,
+                                            temperature, top_k, top_p, rep_penalty, rep_last_n,
+                                            out.ctypes.data_as(C.POINTER(C.c_int32)))
+        if n < 0:
+            raise RuntimeError(self.lib.axref_last_error().decode())
+        return out[:n].tolist()
+
+    def uniform(self, seed: int, n: int) -> np.ndarray:
+        out = np.zeros(n, np.float32)
+        self.lib.axref_uniform(seed, n, _f(out))
+        return out
 
     def time_decode(self, first_token: int, steps: int) -> float:
         return self.lib.axref_time_decode(self.h, first_token, steps)

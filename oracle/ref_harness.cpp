@@ -230,6 +230,78 @@ double axref_time_decode(void* h, int first_token, int steps) {
     return std::chrono::duration<double>(t1 - t0).count();
 }
 
+// The reference decode loop's repetition penalty, as the apply_rep_penalty
+// lambda of llama_generate_cpu_impl states it (llama_model.cpp:1586-1598),
+// over the window ids in order.
+static void ref_rep_penalty(float* lp, int V, const int32_t* win, int n, float pen) {
+    if (pen == 1.0f) return;
+    for (int i = 0; i < n; i++) {
+        const int32_t id = win[i];
+        if (id < 0 || id >= V) continue;
+        lp[id] = lp[id] > 0.f ? lp[id] / pen : lp[id] * pen;
+    }
+}
+
+// One sampling step of the reference: the penalty over `win`, then sample()
+// (llama_model.cpp:1466-1498) with a fresh std::mt19937(seed).
+int axref_sample(const float* logits, int V, const int32_t* win, int n_win, float rep_penalty, int top_k,
+                 float top_p, float temperature, uint32_t seed) {
+    std::vector<float> lp(logits, logits + V);
+    ref_rep_penalty(lp.data(), V, win, n_win, rep_penalty);
+    std::mt19937 rng(seed);
+    return sample(lp.data(), V, top_k, top_p, temperature, rng);
+}
+
+// Sampled generation: the loop of llama_generate_cpu_impl
+// (llama_model.cpp:1562-1624) with its rng (mt19937(42)) and repetition
+// window, on this harness's state (F32 activations when opened so).
+int axref_generate_sampled(void* h, const int32_t* prompt, int n_prompt, int max_new, float temperature, int top_k,
+                           float top_p, float rep_penalty, int rep_last_n, int32_t* out) {
+    auto* m = static_cast<RefModel*>(h);
+    try {
+        std::vector<int32_t> ids(prompt, prompt + n_prompt);
+        const int32_t bos = m->engine.bos_id();
+        if (ids.empty() || ids[0] != bos) ids.insert(ids.begin(), bos);
+        auto& s = *m->state;
+        const int np = (int)ids.size();
+        if (np > 1) {
+            llama_forward_batch(ids.data(), np, 0, s);
+        } else {
+            llama_forward_token(ids[0], 0, s);
+        }
+        s.n_past = np;
+        std::mt19937 rng(42);
+        std::vector<int32_t> rep_ctx(ids.begin(), ids.end());
+        auto pick = [&]() {
+            const int win = std::min(rep_last_n, (int)rep_ctx.size());
+            ref_rep_penalty(s.logits.data(), m->vocab, rep_ctx.data() + rep_ctx.size() - win, win, rep_penalty);
+            return sample(s.logits.data(), m->vocab, top_k, top_p, temperature, rng);
+        };
+        int32_t next = pick();
+        int n = 0;
+        for (int step = 0; step < max_new; ++step) {
+            if (next == m->engine.eos_id()) break;
+            if (s.n_past >= m->n_ctx) break;
+            out[n++] = next;
+            llama_forward_token(next, s.n_past, s);
+            s.n_past++;
+            rep_ctx.push_back(next);
+            next = pick();
+        }
+        return n;
+    } catch (const std::exception& e) {
+        g_last_error = e.what();
+        return -1;
+    }
+}
+
+// n draws of std::uniform_real_distribution<float>(0, 1) from std::mt19937(seed).
+void axref_uniform(uint32_t seed, int n, float* out) {
+    std::mt19937 rng(seed);
+    std::uniform_real_distribution<float> dist(0.f, 1.f);
+    for (int i = 0; i < n; ++i) out[i] = dist(rng);
+}
+
 int axref_n_past(void* h) { return static_cast<RefModel*>(h)->state->n_past; }
 void axref_set_n_past(void* h, int n) { static_cast<RefModel*>(h)->state->n_past = n; }
 

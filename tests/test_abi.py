@@ -3,6 +3,7 @@ host-side argument checks work without a GPU."""
 import ctypes as C
 import subprocess
 
+import numpy as np
 import pytest
 
 from llm_core_b200 import _lib
@@ -61,3 +62,24 @@ def test_gguf_config_reader(tmp_path):
     bad.write_bytes(b"GGUX" + b"\0" * 64)
     with pytest.raises(_lib.AfError, match="magic"):
         read_config(str(bad))
+
+
+def test_sampler_draws_are_the_reference_stream():
+    """af_mt19937_uniform is the reference sampler's rng stream
+    (std::mt19937(42) + uniform_real_distribution<float>, llama_model.cpp:1560,
+    1494-1495): known answer for the first draws, and the compiled reference
+    when it is built."""
+    from llm_core_b200.engine import mt19937_uniform
+    from oracle import RefLib
+    d = mt19937_uniform(4, 42)
+    # first output of std::mt19937(42) is 1608637542; / 2^32 rounded to float
+    assert d[0] == np.float32(np.float32(1608637542) / np.float32(4294967296.0))
+    assert np.all((d >= 0) & (d < 1))
+    if RefLib.available():
+        np.testing.assert_array_equal(mt19937_uniform(1000, 7), RefLib().uniform(7, 1000))
+
+
+def test_sampler_rejects_bad_arguments_without_touching_a_device():
+    import ctypes as C
+    s = _lib.Sampling(1.0, 40, 0.95, 1.0, 0)
+    assert _lib.load().af_sample_f32(None, 100, None, 0, C.byref(s), 0.5, None, None) != 0
