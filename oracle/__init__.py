@@ -319,3 +319,69 @@ class RefLib:
             self.close()
         except Exception:
             pass
+
+
+REF_B200_SO = os.path.join(_HERE, "_ref", "libaxref_b200.so")
+
+
+class RefB200:
+    """The UNMODIFIED reference engine with the B200 path bound in through its
+    own plugin API (oracle/_ref/libaxref_b200.so, built by oracle/ref.mk from
+    the reference sources, integration/ and oracle/integ_harness.cpp).  Test
+    infrastructure: it shows the drop-in working from the reference's side."""
+
+    def __init__(self, path: str = REF_B200_SO):
+        if not os.path.exists(path):
+            raise FileNotFoundError(path)
+        self.lib = L = C.CDLL(path)
+        _ip = C.POINTER(C.c_int32)
+        L.axintg_last_error.restype = C.c_char_p
+        L.axintg_has_backend.argtypes = [C.c_char_p]
+        L.axintg_generate.argtypes = [C.c_char_p, C.c_char_p, _ip, C.c_int, C.c_int, C.c_float, C.c_int, C.c_float,
+                                      C.c_float, C.c_int, _ip, _ip]
+        L.axintg_matmul.argtypes = [C.c_char_p, C.c_int, C.c_void_p, C.c_int, C.c_int, _fp, C.c_int, _fp]
+        L.axintg_rms_norm.argtypes = [C.c_char_p, _fp, _fp, C.c_int, C.c_float, _fp]
+
+    @staticmethod
+    def available(path: str = REF_B200_SO) -> bool:
+        return os.path.exists(path)
+
+    def has_backend(self, name: str) -> bool:
+        return bool(self.lib.axintg_has_backend(name.encode()))
+
+    def _err(self):
+        return RuntimeError(self.lib.axintg_last_error().decode(errors="replace"))
+
+    def generate(self, model_path: str, prompt, max_new: int, backend: str = "cuda", temperature: float = 1.0,
+                 top_k: int = 40, top_p: float = 1.0, rep_penalty: float = 1.0, rep_last_n: int = 64):
+        """llama_generate(Engine::from_gguf(path, {backend}), prompt, cfg); returns
+        (ids, ids seen by cfg.on_token)."""
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.zeros(max(max_new, 1), np.int32)
+        streamed = np.full(max(max_new, 1), -1, np.int32)
+        n = self.lib.axintg_generate(model_path.encode(), backend.encode(), p.ctypes.data_as(C.POINTER(C.c_int32)),
+                                     p.size, max_new, temperature, top_k, top_p, rep_penalty, rep_last_n,
+                                     out.ctypes.data_as(C.POINTER(C.c_int32)),
+                                     streamed.ctypes.data_as(C.POINTER(C.c_int32)))
+        if n < 0:
+            raise self._err()
+        return out[:n].tolist(), streamed[:n].tolist()
+
+    def matmul(self, W: np.ndarray, ggml_type: int, x: np.ndarray, rows: int, backend: str = "cuda"):
+        """MATMUL through get_kernel(MATMUL, {type, F32})->execute on raw GGUF
+        blocks; x is [cols] or [T][cols]."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        T = x.shape[0] if x.ndim == 2 else 1
+        cols = x.shape[-1]
+        y = np.zeros((T, rows) if x.ndim == 2 else rows, np.float32)
+        if self.lib.axintg_matmul(backend.encode(), ggml_type, _b(W), rows, cols, _f(x), T, _f(y)) != 0:
+            raise self._err()
+        return y
+
+    def rms_norm(self, x: np.ndarray, w: np.ndarray, eps: float, backend: str = "cuda"):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        w = np.ascontiguousarray(w, dtype=np.float32)
+        y = np.zeros_like(x)
+        if self.lib.axintg_rms_norm(backend.encode(), _f(x), _f(w), x.size, eps, _f(y)) != 0:
+            raise self._err()
+        return y

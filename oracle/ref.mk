@@ -38,7 +38,7 @@ VNNI_OBJS  := $(foreach s,$(VNNI_SRCS),$(call obj,$(s)))
 A512_OBJS  := $(foreach s,$(A512_SRCS),$(call obj,$(s)))
 HARNESS    := $(OBJ)/ref_harness.o
 
-all: $(OUT)/libaxref.so
+all: $(OUT)/libaxref.so $(OUT)/libaxref_b200.so
 
 $(OUT)/include/axonforge/version.hpp:
 	@mkdir -p $(dir $@)
@@ -65,3 +65,31 @@ $(OUT)/libaxref.so: $(PLAIN_OBJS) $(AVX2_OBJS) $(VNNI_OBJS) $(A512_OBJS) $(HARNE
 	$(CXX) -shared -pthread -o $@ $^
 
 .PHONY: all
+
+# ---- the reference engine with the B200 path bound in (test infrastructure)
+# llama_model.cpp compiled with AXONFORGE_HAS_CUDA (its llama_generate then
+# dispatches backend "cuda" to llama_cuda_generate), the reference-side
+# binding under integration/ (the "cuda" IBackend and llama_cuda_generate, in
+# place of src/backend/cuda/* and src/models/llama_cuda_model.cpp) and
+# oracle/integ_harness.cpp, linked with llm_core_b200/libaf_b200.so.
+CUDA     ?= /usr/local/cuda
+B200_LIB := llm_core_b200/libaf_b200.so
+INTEG_FLAGS := -Iinclude -I$(CUDA)/include
+INTEG_OBJS := $(OBJ)/integ_llama_model.o $(OBJ)/integ_af_cuda_backend.o $(OBJ)/integ_af_llama_cuda.o \
+              $(OBJ)/integ_harness.o
+
+$(OBJ)/integ_llama_model.o: $(REF)/src/models/llama_model.cpp $(OUT)/include/axonforge/version.hpp
+	@mkdir -p $(OBJ)
+	$(CXX) $(CXXFLAGS) $(AVX2) -DAXONFORGE_HAS_CUDA $(INTEG_FLAGS) -c $< -o $@
+
+$(OBJ)/integ_%.o: integration/%.cpp include/af_b200.h $(OUT)/include/axonforge/version.hpp
+	@mkdir -p $(OBJ)
+	$(CXX) $(CXXFLAGS) $(INTEG_FLAGS) -c $< -o $@
+
+$(OBJ)/integ_harness.o: oracle/integ_harness.cpp $(OUT)/include/axonforge/version.hpp
+	@mkdir -p $(OBJ)
+	$(CXX) $(CXXFLAGS) $(INTEG_FLAGS) -c $< -o $@
+
+$(OUT)/libaxref_b200.so: $(PLAIN_OBJS) $(AVX2_OBJS) $(VNNI_OBJS) $(A512_OBJS) $(INTEG_OBJS) $(B200_LIB)
+	$(CXX) -shared -pthread -o $@ $(filter %.o,$^) -Lllm_core_b200 -l:libaf_b200.so -L$(CUDA)/lib64 -lcudart \
+	    -Wl,-rpath,'$$ORIGIN/../../llm_core_b200'
