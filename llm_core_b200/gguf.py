@@ -178,6 +178,7 @@ class ModelConfig:
     qkv_bias: bool = False
     tied: bool = False
     name: str = ""
+    qk_norm: bool = False  # per-head attn_q_norm / attn_k_norm weights (qwen3, hunyuan-dense)
 
     @property
     def head_dim(self) -> int:
@@ -207,6 +208,7 @@ class ModelConfig:
             theta=float(g("rope.freq_base", 10000.0)),
             qkv_bias="blk.0.attn_q.bias" in r.tensors,
             tied="output.weight" not in r.tensors,
+            qk_norm="blk.0.attn_q_norm.weight" in r.tensors,
         )
 
 
@@ -223,6 +225,11 @@ PRESETS = {
     "tiny-qwen": ModelConfig("qwen2", 2, 512, 4, 2, 768, 1000, 512, 1e-6, 1e6,
                              qkv_bias=True, tied=True, name="tiny-qwen2"),
     "small": ModelConfig("llama", 4, 1024, 8, 4, 2816, 4000, 1024, 1e-5, 1e4, name="small-llama"),
+    # Per-head Q/K RMSNorm before RoPE (qwen3) and after it (hunyuan-dense),
+    # QkNormOrder at src/models/llama_model.cpp:1520-1522.
+    "tiny-qwen3": ModelConfig("qwen3", 2, 512, 4, 2, 768, 1000, 512, 1e-6, 1e6, qk_norm=True, name="tiny-qwen3"),
+    "tiny-hunyuan": ModelConfig("hunyuan-dense", 2, 512, 8, 2, 768, 1000, 512, 1e-5, 1e4, qk_norm=True,
+                                name="tiny-hunyuan"),
 }
 
 
@@ -271,6 +278,9 @@ def model_tensor_table(cfg: ModelConfig):
             t.append((p + "attn_q.bias", GGML_F32, (E,)))
             t.append((p + "attn_k.bias", GGML_F32, (KV,)))
             t.append((p + "attn_v.bias", GGML_F32, (KV,)))
+        if cfg.qk_norm:
+            t.append((p + "attn_q_norm.weight", GGML_F32, (cfg.head_dim,)))
+            t.append((p + "attn_k_norm.weight", GGML_F32, (cfg.head_dim,)))
         t.append((p + "attn_output.weight", GGML_Q4_K, (E, E)))
         t.append((p + "ffn_norm.weight", GGML_F32, (E,)))
         t.append((p + "ffn_gate.weight", GGML_Q4_K, (E, F)))
@@ -292,6 +302,9 @@ def random_tensor(name: str, ggml_type: int, dims, seed: int) -> np.ndarray:
         return random_q6k(rng, numel // QK_K).reshape(-1)
     if name.endswith(".bias"):
         return rng.normal(0.0, 0.02, size=numel).astype(np.float32).view(np.uint8)
+    if name.endswith(("attn_q_norm.weight", "attn_k_norm.weight")):
+        # per-head norm weights away from 1 so that applying them (or not) shows
+        return rng.uniform(0.5, 1.5, size=numel).astype(np.float32).view(np.uint8)
     return np.ones(numel, dtype=np.float32).view(np.uint8)  # norm weights
 
 

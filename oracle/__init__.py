@@ -79,6 +79,7 @@ class COracle:
         L.afo_destroy.argtypes = [C.c_void_p]
         L.afo_hidden.argtypes = [C.c_void_p, _fp]
         L.afo_kv.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, _fp]
+        L.afo_attention_decode.argtypes = [_fp] * 10 + [C.c_int] * 5 + [C.c_float, _fp]
         L.afo_set_threads(int(threads or min(os.cpu_count() or 1, 32)))
         self._model = None
 
@@ -104,6 +105,26 @@ class COracle:
         s = np.zeros_like(c)
         self.lib.afo_rope_tables(_f(c), _f(s), head_dim, C.c_float(theta), n_pos)
         return c, s
+
+    def attention_decode(self, q, k, v, kc, vc, cos_row, sin_row, q_norm, k_norm, pos: int, H: int, KVH: int,
+                         qk_norm_order: int, eps: float):
+        """One token's attention (af_oracle.c afo_attention_decode, restating
+        llama_model.cpp:1236-1272): returns the output [H*hd]; kc / vc (float32
+        [n_ctx][KVH*hd], modified in place) receive the new row at pos."""
+        hd = q.size // H
+        q = np.array(q, np.float32)
+        k = np.array(k, np.float32)
+        v = np.ascontiguousarray(v, np.float32)
+        ao = np.zeros(H * hd, np.float32)
+        att = np.zeros(pos + 1, np.float32)
+        qn = np.ascontiguousarray(q_norm, np.float32) if q_norm is not None else None
+        kn = np.ascontiguousarray(k_norm, np.float32) if k_norm is not None else None
+        self.lib.afo_attention_decode(_f(ao), _f(q), _f(k), _f(v), _f(kc), _f(vc),
+                                      _f(np.ascontiguousarray(cos_row, np.float32)),
+                                      _f(np.ascontiguousarray(sin_row, np.float32)),
+                                      _f(qn) if qn is not None else _fp(), _f(kn) if kn is not None else _fp(),
+                                      pos, H, KVH, hd, qk_norm_order, C.c_float(eps), _f(att))
+        return ao
 
     # -- model
     def open_model(self, reader, n_ctx: int | None = None):

@@ -376,13 +376,62 @@ static void emb_row(float* out, const void* W, int type, int row, int cols) {
     else memcpy(out, base, (size_t)cols * 4);
 }
 
+/* One new token's attention for one layer, llama_model.cpp:1236-1272: the
+ * optional per-head Q/K RMSNorm before RoPE (qwen3, order 1) or after it
+ * (hunyuan, order 2) (:1236-1247, rms_norm_heads_inplace :421-441), half-split
+ * RoPE of q and k (apply_rope / rope_and_store_k :1046-1080), K and V stored
+ * at row pos of the fp32 caches [n_ctx][KVH*HD], then GQA attention over
+ * positions 0..pos: scores * 1/sqrt(HD), max-subtracted softmax (:445-451),
+ * weighted V sum (:1253-1272).  q and k are rotated in place; att is scratch
+ * of pos + 1 floats. */
+void afo_attention_decode(float* ao, float* q, float* k, const float* v, float* kc, float* vc, const float* cr,
+                          const float* sr, const float* q_norm, const float* k_norm, int pos, int H, int KVH,
+                          int HD, int qk_norm_order, float eps, float* att) {
+    const int KVD = KVH * HD;
+    const float scale = 1.f / sqrtf((float)HD);
+    if (qk_norm_order == 1) {
+        rms_norm_heads(q, q_norm, H, HD, eps);
+        rms_norm_heads(k, k_norm, KVH, HD, eps);
+    }
+    afo_rope(q, q, H, HD, cr, sr);
+    if (qk_norm_order == 2) {
+        afo_rope(k, k, KVH, HD, cr, sr);
+        rms_norm_heads(q, q_norm, H, HD, eps);
+        rms_norm_heads(k, k_norm, KVH, HD, eps);
+        memcpy(kc + (size_t)pos * KVD, k, (size_t)KVD * 4);
+    } else {
+        afo_rope(kc + (size_t)pos * KVD, k, KVH, HD, cr, sr);
+    }
+    memcpy(vc + (size_t)pos * KVD, v, (size_t)KVD * 4);
+    const int seq = pos + 1, group = H / KVH;
+    memset(ao, 0, (size_t)H * HD * 4);
+    for (int hh = 0; hh < H; hh++) {
+        const int kvh = hh / group;
+        const float* qh = q + hh * HD;
+        for (int t = 0; t < seq; t++) {
+            const float* kt = kc + (size_t)t * KVD + kvh * HD;
+            float s = 0.f;
+            for (int i = 0; i < HD; i++) s += qh[i] * kt[i];
+            att[t] = s * scale;
+        }
+        float mx = att[0], sum = 0.f;
+        for (int t = 1; t < seq; t++) if (att[t] > mx) mx = att[t];
+        for (int t = 0; t < seq; t++) { att[t] = expf(att[t] - mx); sum += att[t]; }
+        for (int t = 0; t < seq; t++) att[t] /= sum;
+        float* oh = ao + hh * HD;
+        for (int t = 0; t < seq; t++) {
+            const float* vt = vc + (size_t)t * KVD + kvh * HD;
+            for (int i = 0; i < HD; i++) oh[i] += att[t] * vt[i];
+        }
+    }
+}
+
 int afo_forward_token(void* h, int token, int pos, float* logits_out) {
     afo_model* m = (afo_model*)h;
     const afo_cfg* c = &m->c;
     const int E = c->n_embd, H = c->n_head, KVH = c->n_kv_head, HD = m->head_dim, FD = c->ffn;
     const int KVD = m->kv_dim;
     if (pos < 0 || pos >= c->n_ctx || token < 0 || token >= c->vocab) return -1;
-    const float scale = 1.f / sqrtf((float)HD);
     const float* cr = m->cos_t + (size_t)pos * (HD / 2);
     const float* sr = m->sin_t + (size_t)pos * (HD / 2);
     emb_row(m->x, m->tok_embd, m->tok_type, token, E);
@@ -397,43 +446,8 @@ int afo_forward_token(void* h, int token, int pos, float* logits_out) {
         add_bias(m->q, lw->bq, H * HD);
         add_bias(m->k, lw->bk, KVD);
         add_bias(m->v, lw->bv, KVD);
-        if (c->qk_norm_order == 1) {
-            rms_norm_heads(m->q, lw->q_norm, H, HD, c->eps);
-            rms_norm_heads(m->k, lw->k_norm, KVH, HD, c->eps);
-        }
-        afo_rope(m->q, m->q, H, HD, cr, sr);
-        if (c->qk_norm_order == 2) {
-            afo_rope(m->k, m->k, KVH, HD, cr, sr);
-            rms_norm_heads(m->q, lw->q_norm, H, HD, c->eps);
-            rms_norm_heads(m->k, lw->k_norm, KVH, HD, c->eps);
-            memcpy(kc + (size_t)pos * KVD, m->k, (size_t)KVD * 4);
-        } else {
-            afo_rope(kc + (size_t)pos * KVD, m->k, KVH, HD, cr, sr);
-        }
-        memcpy(vc + (size_t)pos * KVD, m->v, (size_t)KVD * 4);
-        /* GQA attention, llama_model.cpp:1253-1272: scores, max-subtracted
-         * softmax (llama_model.cpp:445-451), weighted V sum. */
-        const int seq = pos + 1, group = H / KVH;
-        memset(m->ao, 0, (size_t)E * 4);
-        for (int hh = 0; hh < H; hh++) {
-            const int kvh = hh / group;
-            const float* qh = m->q + hh * HD;
-            for (int t = 0; t < seq; t++) {
-                const float* kt = kc + (size_t)t * KVD + kvh * HD;
-                float s = 0.f;
-                for (int i = 0; i < HD; i++) s += qh[i] * kt[i];
-                m->att[t] = s * scale;
-            }
-            float mx = m->att[0], sum = 0.f;
-            for (int t = 1; t < seq; t++) if (m->att[t] > mx) mx = m->att[t];
-            for (int t = 0; t < seq; t++) { m->att[t] = expf(m->att[t] - mx); sum += m->att[t]; }
-            for (int t = 0; t < seq; t++) m->att[t] /= sum;
-            float* oh = m->ao + hh * HD;
-            for (int t = 0; t < seq; t++) {
-                const float* vt = vc + (size_t)t * KVD + kvh * HD;
-                for (int i = 0; i < HD; i++) oh[i] += m->att[t] * vt[i];
-            }
-        }
+        afo_attention_decode(m->ao, m->q, m->k, m->v, kc, vc, cr, sr, lw->q_norm, lw->k_norm, pos, H, KVH, HD,
+                             c->qk_norm_order, c->eps, m->att);
         afo_gemv(m->xb, lw->wo, lw->to, m->ao, E, E);
         for (int i = 0; i < E; i++) m->x[i] += m->xb[i];
         afo_rms_norm(m->xb, m->x, lw->ffn_norm, E, c->eps);

@@ -162,3 +162,81 @@ def test_batched_prefill_matches_token_prefill(gpu, preset, seed):
             assert dev < 2 * predicted[layer][w] + 1e-4, (layer, which_v, dev, predicted[layer][w])
     a.close()
     b.close()
+
+
+@pytest.mark.parametrize("preset", ["tiny-qwen3", "tiny-hunyuan"])
+def test_qk_norm_models_match_reference(gpu, preset):
+    """Per-head Q/K RMSNorm before RoPE (qwen3) and after it (hunyuan-dense),
+    QkNormOrder at src/models/llama_model.cpp:1520-1522, through the step
+    kernel's attention: logits and greedy tokens against the reference's
+    F32-activation forward."""
+    if not RefLib.available():
+        pytest.skip("reference library not built")
+    path = model_path(preset, 8)
+    ref = RefLib().open(path, threads=4, f32_mode=True)
+    m = LlamaCudaModel(path)
+    for p, tok in enumerate([1, 17, 400, 3, 999, 256, 77, 5]):
+        _, lg = m.step(tok, p)
+        assert rel_l2(lg, ref.forward_token(tok, p)) < 1e-3
+    prompt = [9, 8, 7, 6, 5]
+    want, _ = ref.generate_greedy(prompt, 32)
+    assert m.generate(prompt, LlamaConfig(max_new_tokens=32, temperature=0)) == want
+    ref.close()
+    m.close()
+
+
+def _teacher_forced(m, ref, prompt, steps):
+    """The reference's greedy run (tokens and the logits that chose them) and
+    this engine fed the same tokens: per-step logits rel-L2 and argmax."""
+    ref_ids, ref_lg = ref.generate_greedy(prompt, steps, want_logits=True)
+    seq = [1] + list(prompt) + ref_ids[:-1]
+    n0 = len(prompt) + 1
+    nxt, lg = m.prefill(seq[:n0], 0)
+    errs, agree = [rel_l2(lg, ref_lg[0])], [nxt == ref_ids[0]]
+    for i in range(1, len(ref_ids)):
+        nxt, lg = m.step(seq[n0 - 1 + i], n0 - 1 + i)
+        errs.append(rel_l2(lg, ref_lg[i]))
+        agree.append(nxt == ref_ids[i])
+    return np.array(errs), float(np.mean(agree))
+
+
+@pytest.mark.slow
+def test_llama2_7b_logits_and_greedy_agreement(gpu):
+    """The benchmarked workload (Llama-2-7B Q4_K_M, random-init, 128-token
+    prompt): logits within 5e-3 of the reference's F32-activation forward at
+    the last prompt position and at each of 256 greedy steps (teacher-forced
+    on the reference's tokens), top-1 agreement >= 99%."""
+    if not RefLib.available():
+        pytest.skip("reference library not built")
+    import bench
+    path = bench.model_file("llama2-7b", 0, None)
+    rng = np.random.default_rng(1234)
+    prompt = rng.integers(0, 32000, bench.PROMPT_LEN).tolist()
+    ref = RefLib().open(path, threads=max(1, min(64, os.cpu_count() or 1)), f32_mode=True)
+    m = LlamaCudaModel(path)
+    errs, agree = _teacher_forced(m, ref, prompt, 256)
+    ref.close()
+    m.close()
+    assert errs.max() < LOGITS_TOL, errs.max()
+    assert agree >= TOP1_MIN, agree
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("kv", [1024, 4096])
+def test_qwen25_3b_long_context(gpu, kv):
+    """Qwen2.5-3B (q/k/v bias, tied Q6_K vocabulary of 151936, GQA 8): prefill
+    kv - 512 uniform-random ids, then 32 greedy steps; logits within 5e-3 of the
+    reference's F32-activation forward at every step, top-1 agreement >= 99%."""
+    if not RefLib.available():
+        pytest.skip("reference library not built")
+    import bench
+    path = bench.model_file("qwen2.5-3b", 0, None)
+    rng = np.random.default_rng(kv)
+    prompt = rng.integers(0, 151936, kv - 512 - 1).tolist()
+    ref = RefLib().open(path, threads=max(1, min(64, os.cpu_count() or 1)), f32_mode=True)
+    m = LlamaCudaModel(path)
+    errs, agree = _teacher_forced(m, ref, prompt, 32)
+    ref.close()
+    m.close()
+    assert errs.max() < LOGITS_TOL, errs.max()
+    assert agree >= TOP1_MIN, agree

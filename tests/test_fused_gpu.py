@@ -174,14 +174,23 @@ def rope(x, nh, hd, c, s):
     return x.reshape(-1)
 
 
-@pytest.mark.parametrize("H,KVH,hd,pos,nsplit", [(4, 2, 64, 0, 64), (32, 4, 64, 300, 37), (32, 32, 128, 200, 10),
-                                                 (16, 2, 128, 4000, 64), (16, 2, 128, 31, 1), (8, 8, 128, 5, 3)])
-def test_attention_decode(gpu, H, KVH, hd, pos, nsplit):
+@pytest.mark.parametrize("H,KVH,hd,pos,nsplit,qk", [
+    (4, 2, 64, 0, 64, 0), (32, 4, 64, 300, 37, 0), (32, 32, 128, 200, 10, 0), (16, 2, 128, 4000, 64, 0),
+    (16, 2, 128, 31, 1, 0), (8, 8, 128, 5, 3, 0),
+    # GQA ratio 8 (the step kernel's widest group), and per-head Q/K RMSNorm
+    # before RoPE (qwen3, 1) and after it (hunyuan, 2) with real norm weights
+    (64, 8, 128, 700, 16, 0), (16, 2, 128, 130, 4, 1), (32, 4, 64, 77, 8, 2), (16, 2, 128, 2047, 32, 2),
+])
+def test_attention_decode(gpu, H, KVH, hd, pos, nsplit, qk):
+    """af_attention_decode_f32 against the oracle's restatement of the
+    reference attention block (oracle/af_oracle.c afo_attention_decode,
+    src/models/llama_model.cpp:1236-1272)."""
     import torch
-    rng = np.random.default_rng(pos + H)
+    rng = np.random.default_rng(pos + H + qk)
     n_ctx = 4096
     kvd = KVH * hd
-    c, s = COracle().rope_tables(hd, 10000.0, n_ctx)
+    orc = COracle()
+    c, s = orc.rope_tables(hd, 10000.0, n_ctx)
     kc = np.zeros((n_ctx, kvd), np.float32)
     vc = np.zeros((n_ctx, kvd), np.float32)
     kc[:pos] = rng.standard_normal((pos, kvd))
@@ -189,7 +198,10 @@ def test_attention_decode(gpu, H, KVH, hd, pos, nsplit):
     q = rng.standard_normal(H * hd).astype(np.float32)
     k = rng.standard_normal(kvd).astype(np.float32)
     v = rng.standard_normal(kvd).astype(np.float32)
+    qn = rng.uniform(0.5, 1.5, hd).astype(np.float32) if qk else None
+    kn = rng.uniform(0.5, 1.5, hd).astype(np.float32) if qk else None
     d = {n: dev(a) for n, a in dict(q=q, k=k, v=v, kc=kc, vc=vc, c=c, s=s).items()}
+    dqn, dkn = (dev(qn), dev(kn)) if qk else (None, None)
     posd = torch.tensor([pos], dtype=torch.int32, device="cuda")
     out = torch.zeros(H * hd, device="cuda")
     part = torch.zeros(H * nsplit * (hd + 2), device="cuda")
@@ -197,14 +209,17 @@ def test_attention_decode(gpu, H, KVH, hd, pos, nsplit):
     for _ in range(2):  # the counters must come back to zero
         assert gpu.af_attention_decode_f32(out.data_ptr(), d["q"].data_ptr(), d["k"].data_ptr(), d["v"].data_ptr(),
                                            d["kc"].data_ptr(), d["vc"].data_ptr(), d["c"].data_ptr(),
-                                           d["s"].data_ptr(), None, None, posd.data_ptr(), H, KVH, hd, n_ctx, 0,
+                                           d["s"].data_ptr(), dqn.data_ptr() if qk else None,
+                                           dkn.data_ptr() if qk else None, posd.data_ptr(), H, KVH, hd, n_ctx, qk,
                                            1e-5, nsplit, part.data_ptr(), cnt.data_ptr(), None) == 0
         torch.cuda.synchronize()
         assert int(cnt.abs().sum()) == 0
-    kr = rope(k, KVH, hd, c[pos], s[pos])
-    qr = rope(q, H, hd, c[pos], s[pos])
-    kc[pos], vc[pos] = kr, v
-    assert np.allclose(d["kc"].cpu().numpy()[pos], kr, atol=1e-6)
+    kc_o, vc_o = kc.copy(), vc.copy()
+    exp = orc.attention_decode(q, k, v, kc_o, vc_o, c[pos], s[pos], qn, kn, pos, H, KVH, qk, 1e-5)
+    np.testing.assert_allclose(d["kc"].cpu().numpy()[pos], kc_o[pos], atol=1e-5)
     assert np.array_equal(d["vc"].cpu().numpy()[pos], v)
-    exp = np_attention(qr, kc, vc, pos, H, KVH, hd)
     assert rel_l2(out.cpu().numpy(), exp) < 1e-5
+    # the in-file double-precision restatement agrees for the plain case
+    if qk == 0:
+        qr = rope(q, H, hd, c[pos], s[pos])
+        assert rel_l2(exp, np_attention(qr, kc_o, vc_o, pos, H, KVH, hd)) < 1e-5
