@@ -107,6 +107,8 @@ struct af_engine {
     uint8_t* xchg = nullptr;                 // this rank's exchange area (tensor parallel)
     std::vector<void*> peer_maps;            // IPC mappings of the other ranks' areas
     unsigned int* step_bar = nullptr;
+    unsigned long long* sepoch = nullptr;  // steps the step kernel has run (tags its inter-CTA words)
+    unsigned long long* tpart = nullptr;   // tagged attention split partials of the step kernel
     StepParams step{};
 
     cudaGraph_t graph = nullptr;
@@ -475,6 +477,14 @@ cudaError_t build_step(af_engine* e) {
         p.x.norm_w = norm_w;
         p.x.n = E;
     };
+    e->sepoch = static_cast<unsigned long long*>(e->dalloc(sizeof(unsigned long long)));
+    ENG_TRY(cudaMemset(e->sepoch, 0, sizeof(unsigned long long)));
+    {
+        const size_t n = (size_t)e->Hl * std::max(1, std::min(std::min(e->nsplit, e->sms / e->KVl), kStepAttnMaxSplit)) *
+                         (e->hd + 2);
+        e->tpart = static_cast<unsigned long long*>(e->dalloc(n * sizeof(unsigned long long)));
+        ENG_TRY(cudaMemset(e->tpart, 0, n * sizeof(unsigned long long)));
+    }
     std::vector<StepPhase> ph;
     StepPhase embed = {};
     embed.kind = PH_EMBED;
@@ -514,12 +524,13 @@ cudaError_t build_step(af_engine* e) {
         a.k_norm = L.k_norm;
         a.part = e->apart;
         a.counter = e->acount;
+        a.tpart = e->tpart;
         a.pos = &e->tokpos[1];
         a.n_heads = e->Hl;
         a.n_kv_heads = e->KVl;
         a.head_dim = e->hd;
         a.n_ctx = c.n_ctx;
-        a.nsplit = std::max(1, std::min(e->nsplit, e->sms / e->KVl));
+        a.nsplit = std::max(1, std::min(std::min(e->nsplit, e->sms / e->KVl), kStepAttnMaxSplit));
         a.qk_norm_order = c.qk_norm_order;
         a.eps = c.eps;
         a.scale = 1.f / std::sqrt((float)e->hd);
@@ -622,6 +633,7 @@ cudaError_t build_step(af_engine* e) {
     sp.tp = e->tp;
     sp.rank = e->rank;
     sp.n_buf = tp ? 2 * c.n_layer : 0;
+    sp.epoch = e->sepoch;
     if (tp) ENG_TRY(setup_exchange(e));
     return cudaSuccess;
 }

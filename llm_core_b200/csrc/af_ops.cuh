@@ -86,6 +86,7 @@ struct AttnParams {
     const float* k_norm;
     float* part;           // scratch [Hl][nsplit][hd + 2]
     unsigned int* counter; // scratch [KVl], zero between launches
+    unsigned long long* tpart;  // step kernel: tagged split partials [Hl][nsplit][hd + 2]
     const int* pos;        // device position of the new token
     int n_heads, n_kv_heads, head_dim, n_ctx, nsplit, qk_norm_order;
     float eps, scale;

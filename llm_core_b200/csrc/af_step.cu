@@ -5,6 +5,24 @@
 #include "af_step.cuh"
 
 namespace af {
+
+#ifdef AF_STEP_TRACE
+// Timeline of one step (debug builds only): per CTA and phase, %globaltimer
+// stamps at points of the phase (0 start, 1 input ready, 2 end, 3 producer
+// done; the attention phase also 4-7 inside its item).
+constexpr int kTracePh = 192;
+__device__ unsigned long long g_trace[148][kTracePh][8];
+__device__ __forceinline__ unsigned long long gtime() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+#define AF_TRACE(ph, k) \
+    do { if (blockIdx.x < 148 && (ph) < kTracePh) g_trace[blockIdx.x][ph][k] = gtime(); } while (0)
+#else
+#define AF_TRACE(ph, k) do { } while (0)
+#endif
+
 namespace {
 
 using namespace gdev;
@@ -215,6 +233,7 @@ __device__ void embed_phase(const StepParams& sp, int tok) {
 // head dims 4l..4l+3 in registers, so the same thread needs its K rows for
 // the scores and its V rows for P·V: no shared-memory staging of the cache.
 constexpr int kAttnPer = kStepAttnChunk / kCW;
+constexpr int kAttnMaxSplit = kStepAttnMaxSplit;
 static_assert(kStepAttnChunk % kCW == 0 && kStepAttnChunk <= 64, "chunk: whole warps, two per lane at most");
 
 // Shared scratch of one attention item (floats), inside the union area.
@@ -227,6 +246,8 @@ struct AttnSmem {
     float* mrow;  // [G]
     float* lrow;  // [G]
     float* corr;  // [G]
+    float* ml;    // [G][nsplit][2] the splits' (max, sum), staged for the merge
+    float* ob;    // [G][hd] the merged output, quantised from here
     int* last;
     __device__ explicit AttnSmem(uint8_t* base) {
         qs = reinterpret_cast<float*>(base);
@@ -237,10 +258,13 @@ struct AttnSmem {
         mrow = red + kCW * 128;
         lrow = mrow + kStepMaxG;
         corr = lrow + kStepMaxG;
-        last = reinterpret_cast<int*>(corr + kStepMaxG);
+        ml = corr + kStepMaxG;
+        ob = ml + kStepMaxG * kAttnMaxSplit * 2;
+        last = reinterpret_cast<int*>(ob + kStepMaxG * 128);
     }
 };
-static_assert((kStepMaxG * 128 + 256 + kStepMaxG * kStepAttnChunk + kCW * 128 + 3 * kStepMaxG + 4) * 4 <= kStepUnion,
+static_assert((kStepMaxG * 128 + 256 + kStepMaxG * kStepAttnChunk + kCW * 128 + 3 * kStepMaxG +
+               kStepMaxG * kAttnMaxSplit * 2 + kStepMaxG * 128 + 4) * 4 <= kStepUnion,
               "attention scratch exceeds the union area");
 
 // Per-thread K/V rows of the current chunk and the RoPE factors of the item.
@@ -322,7 +346,8 @@ __device__ __forceinline__ void attn_prefetch(const AttnParams& a, int pos, int 
 // GM: query heads per kv head held in registers (G <= GM; the instance is
 // chosen per model so that P·V accumulators cost 4·GM registers).
 template <int GM>
-__device__ __forceinline__ void attn_item(const AttnParams& a, const AttnSmem& s, int pos, int kvh, int split, int ns, AttnPre& r) {
+__device__ __forceinline__ void attn_item(const AttnParams& a, const AttnSmem& s, int pos, int kvh, int split, int ns, AttnPre& r,
+                                          int tph, uint32_t tag, volatile int* abort) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int hd = a.head_dim, half = hd / 2, Q4 = hd / 4;
     const int G = a.n_heads / a.n_kv_heads;
@@ -349,6 +374,7 @@ __device__ __forceinline__ void attn_item(const AttnParams& a, const AttnSmem& s
         s.lrow[tid] = 0.f;
     }
     bar_consumers();
+    if (tid == 0) AF_TRACE(tph, 4);
     if (a.qk_norm_order == 1) {  // qwen3: per-head norm before RoPE
         for (int h = warp; h <= G; h += kCW) {
             if (h < G && a.q_norm) rms_norm_head(s.qs + h * hd, a.q_norm, hd, a.eps);
@@ -453,71 +479,120 @@ __device__ __forceinline__ void attn_item(const AttnParams& a, const AttnSmem& s
         }
         bar_consumers();  // sc is rewritten by the next chunk
     }
-    // ---- reduce the warps, write this split's partial
+    if (tid == 0) AF_TRACE(tph, 5);
+    if (tid == 0) AF_TRACE(tph, 5);
+    // ---- reduce the warps.  Split 0 keeps its partial in shared memory; the
+    // other splits publish theirs as tagged words (tag << 32 | bits) for it
+    // and are done: no fence, counter or atomic.
+    const unsigned long long tagw = (unsigned long long)tag << 32;
 #pragma unroll
     for (int g = 0; g < GM; ++g) {
         if (g >= G) break;
         if (dl) reinterpret_cast<float4*>(s.red + warp * hd)[lane] = o[g];
         bar_consumers();
         const int h = kvh * G + g;
-        float* dst = a.part + ((size_t)h * a.nsplit + split) * (hd + 2);
+        unsigned long long* dst = a.tpart + ((size_t)h * a.nsplit + split) * (hd + 2);
         for (int d = tid; d < hd; d += kCT) {
             float acc = 0.f;
 #pragma unroll
             for (int w = 0; w < kCW; ++w) acc += s.red[w * hd + d];
-            dst[d] = acc;
-            if (d == 0) {
-                dst[hd] = s.mrow[g];
-                dst[hd + 1] = s.lrow[g];
+            if (split == 0) {
+                s.ob[g * hd + d] = acc;
+            } else {
+                st_relaxed_gpu(dst + d, tagw | __float_as_uint(acc));
+                if (d == 0) {
+                    st_relaxed_gpu(dst + hd, tagw | __float_as_uint(s.mrow[g]));
+                    st_relaxed_gpu(dst + hd + 1, tagw | __float_as_uint(s.lrow[g]));
+                }
             }
         }
         bar_consumers();
     }
-    // ---- the last split of this kv head merges (exp(m_s − M) rescaling)
-    __threadfence();
-    bar_consumers();
-    if (tid == 0) *s.last = atomicAdd(&a.counter[kvh], 1u) == (unsigned)(ns - 1) ? 1 : 0;
-    bar_consumers();
-    if (!*s.last) return;
-    __threadfence();
-    for (int idx = tid; idx < G * hd; idx += kCT) {
-        const int g = idx / hd, dd = idx % hd;
-        const int h = kvh * G + g;
-        const float* base = a.part + (size_t)h * a.nsplit * (hd + 2);
-        float M = -INFINITY;
-        for (int q = 0; q < ns; ++q) M = fmaxf(M, __ldcg(base + q * (hd + 2) + hd));
-        float L = 0.f, O = 0.f;
-        for (int q = 0; q < ns; ++q) {
-            const float ms = __ldcg(base + q * (hd + 2) + hd);
-            if (ms == -INFINITY) continue;
-            const float w = expf(ms - M);
-            L += __ldcg(base + q * (hd + 2) + hd + 1) * w;
-            O += __ldcg(base + q * (hd + 2) + dd) * w;
+    if (split != 0) return;
+    // ---- split 0 merges the splits (exp(m_s − M) rescaling): the other
+    // splits' (max, sum) staged in shared memory, then each output value
+    // loads its splits' partials together; a word whose tag is not this
+    // phase's yet is re-polled (bounded).  The output goes to global memory
+    // and stays in shared memory, from where it is quantised.
+    if (ns > 1) {
+        auto poll = [&](const unsigned long long* p) {
+            unsigned long long w = ld_relaxed_gpu(p);
+            uint32_t it = 0;
+            while ((w & ~0xFFFFFFFFull) != tagw && ++it < kGridSpinLimit && !*abort) w = ld_relaxed_gpu(p);
+            if (it >= kGridSpinLimit) set_err(kErrMbarTimeout);
+            return __uint_as_float((uint32_t)w);
+        };
+        for (int i = tid; i < G * ns; i += kCT) {
+            const int g = i / ns, q = i - g * ns;
+            if (q == 0) {
+                s.ml[2 * i] = s.mrow[g];
+                s.ml[2 * i + 1] = s.lrow[g];
+            } else {
+                const unsigned long long* b = a.tpart + ((size_t)(kvh * G + g) * a.nsplit + q) * (hd + 2);
+                s.ml[2 * i] = poll(b + hd);
+                s.ml[2 * i + 1] = poll(b + hd + 1);
+            }
         }
-        a.out[(size_t)h * hd + dd] = O / L;
+        bar_consumers();
+        constexpr int kBatch = 8;  // partial loads in flight per output value
+        for (int idx = tid; idx < G * hd; idx += kCT) {
+            const int g = idx / hd, dd = idx - g * hd;
+            const unsigned long long* base = a.tpart + (size_t)(kvh * G + g) * a.nsplit * (hd + 2) + dd;
+            const float* mlg = s.ml + 2 * g * ns;
+            float M = -INFINITY;
+            for (int q = 0; q < ns; ++q) M = fmaxf(M, mlg[2 * q]);
+            float L = 0.f, O = 0.f;
+            for (int q0 = 0; q0 < ns; q0 += kBatch) {
+                unsigned long long ov[kBatch];
+#pragma unroll
+                for (int j = 0; j < kBatch; ++j)
+                    ov[j] = q0 + j > 0 && q0 + j < ns ? ld_relaxed_gpu(base + (size_t)(q0 + j) * (hd + 2)) : 0ull;
+#pragma unroll
+                for (int j = 0; j < kBatch; ++j) {
+                    const int q = q0 + j;
+                    if (q >= ns || mlg[2 * q] == -INFINITY) continue;
+                    float oq;
+                    if (q == 0) {
+                        oq = s.ob[idx];
+                    } else if ((ov[j] & ~0xFFFFFFFFull) == tagw) {
+                        oq = __uint_as_float((uint32_t)ov[j]);
+                    } else {
+                        oq = poll(base + (size_t)q * (hd + 2));
+                    }
+                    const float w = expf(mlg[2 * q] - M);
+                    L += mlg[2 * q + 1] * w;
+                    O += oq * w;
+                }
+            }
+            s.ob[idx] = O / L;
+        }
+    } else {
+        for (int idx = tid; idx < G * hd; idx += kCT) s.ob[idx] /= s.lrow[idx / hd];
     }
-    if (tid == 0) a.counter[kvh] = 0u;
+    bar_consumers();
+    for (int idx = tid; idx < G * hd; idx += kCT) a.out[(size_t)kvh * G * hd + idx] = s.ob[idx];
     if (a.xq_out) {
         // quantise this kv head's G*hd outputs (32-value groups) for the O GEMV
-        __threadfence();
-        bar_consumers();
         const int g0 = kvh * G * hd / 32, ng = G * hd / 32;
-        for (int k = warp; k < ng; k += kCW) xq_quantize_group(a.xq_out, a.out, nullptr, a.n_heads * hd, g0 + k);
+        for (int k = warp; k < ng; k += kCW)
+            xq_store32(a.xq_out, s.ob[32 * k + lane], nullptr, a.n_heads * hd, 32 * (g0 + k) + lane);
     }
+    if (tid == 0) AF_TRACE(tph, 7);
 }
 
 // The whole attention phase of one layer for this CTA: the prefetch of what
 // does not depend on the QKV phase, the grid wait, then the CTA's items.
 template <int GM>
 __device__ __forceinline__ bool attn_phase(const AttnParams& a, const AttnSmem& s, int pos, unsigned* bar,
-                                           unsigned target, volatile int* abort) {
+                                           unsigned target, volatile int* abort, int tph, uint32_t tag) {
     const int ns = attn_splits(a, pos);
     const int items = a.n_kv_heads * ns;
     for (int item = blockIdx.x; item < items; item += gridDim.x) attn_prefetch(a, pos, item / ns, item % ns, ns);
     if (!grid_wait(bar, target, abort)) return false;
+    if (threadIdx.x == 0) AF_TRACE(tph, 0);
     for (int item = blockIdx.x; item < items; item += gridDim.x) {
         AttnPre r;
-        attn_item<GM>(a, s, pos, item / ns, item % ns, ns, r);
+        attn_item<GM>(a, s, pos, item / ns, item % ns, ns, r, tph, tag, abort);
         bar_consumers();
     }
     return true;
@@ -564,6 +639,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) step_kernel(const __grid_cons
                 pr.drain(ring);
                 return;
             }
+            AF_TRACE(i, 3);
         }
         return;
     }
@@ -571,7 +647,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) step_kernel(const __grid_cons
     // ---- consumers: the phases, separated by grid-wide arrivals
     const int pos = __ldcg(sp.pos);
     const int tok = __ldcg(sp.token);
-    const unsigned long long epoch = sp.n_buf > 0 ? __ldcg(sp.epoch) : 0ull;
+    const unsigned long long epoch = __ldcg(sp.epoch);
     // sequence number of partial-sum exchange k of this step
     auto xseq = [&](int k) { return epoch * (unsigned long long)sp.n_buf + (unsigned long long)k; };
     uint32_t consumed = 0;
@@ -585,11 +661,13 @@ __global__ void __launch_bounds__(kGemvThreads, 1) step_kernel(const __grid_cons
             const int G = ap->n_heads / ap->n_kv_heads;
             const AttnSmem s(uni);
             const unsigned target = (unsigned)i * grid;
+            // tag of this phase's split partials: unique per step and phase, never 0
+            const uint32_t atag = (uint32_t)(epoch * (unsigned long long)sp.nph + (unsigned long long)i + 1ull);
             bool ok;
-            if (G == 1) ok = attn_phase<1>(*ap, s, pos, sp.bar, target, abort);
-            else if (G == 2) ok = attn_phase<2>(*ap, s, pos, sp.bar, target, abort);
-            else if (G <= 4) ok = attn_phase<4>(*ap, s, pos, sp.bar, target, abort);
-            else ok = attn_phase<kStepMaxG>(*ap, s, pos, sp.bar, target, abort);
+            if (G == 1) ok = attn_phase<1>(*ap, s, pos, sp.bar, target, abort, i, atag);
+            else if (G == 2) ok = attn_phase<2>(*ap, s, pos, sp.bar, target, abort, i, atag);
+            else if (G <= 4) ok = attn_phase<4>(*ap, s, pos, sp.bar, target, abort, i, atag);
+            else ok = attn_phase<kStepMaxG>(*ap, s, pos, sp.bar, target, abort, i, atag);
             if (!ok) break;
         } else {
             // a GEMV fed by an exchange waits for the tagged partials instead
@@ -605,6 +683,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) step_kernel(const __grid_cons
                 vend = __ldg(ph.g.vrange + blockIdx.x + 1);
             }
             if (i > 0 && !xin && !grid_wait(sp.bar, (unsigned)i * grid, abort)) break;
+            if (threadIdx.x == 0) AF_TRACE(i, 0);
             if (kind == PH_EMBED) {
                 embed_phase(sp, tok);
             } else {
@@ -626,6 +705,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) step_kernel(const __grid_cons
                 } else {
                     input_prologue(*gp, uni, red);
                 }
+                if (threadIdx.x == 0) AF_TRACE(i, 1);
                 if (!consume(*gp, vbeg, vend, ring, consumed, head, uni, s_in, smem)) {
                     *abort = 1;
                     break;
@@ -634,6 +714,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) step_kernel(const __grid_cons
         }
         // arrive: every store of this phase by this CTA happens before the count
         bar_consumers();
+        if (threadIdx.x == 0) AF_TRACE(i, 2);
         if (threadIdx.x == 0) grid_arrive(sp.bar);
     }
     // CTA 0 turns the step's argmax into the next token once every CTA has
@@ -668,7 +749,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) step_kernel(const __grid_cons
                 k = kr > k ? kr : k;
             }
         }
-        if (sp.n_buf > 0) *sp.epoch = epoch + 1ull;
+        *sp.epoch = epoch + 1ull;
         int id = (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
         if (k == 0ull || id < 0 || id >= sp.vocab) {  // no finite logit reached the argmax
             set_err(kErrBadToken);
@@ -708,3 +789,9 @@ cudaError_t step_launch(const StepParams& sp, cudaStream_t st) {
 }
 
 }  // namespace af
+
+#ifdef AF_STEP_TRACE
+extern "C" cudaError_t af_debug_step_trace(void* h_out, size_t bytes) {
+    return cudaMemcpyFromSymbol(h_out, af::g_trace, bytes);
+}
+#endif

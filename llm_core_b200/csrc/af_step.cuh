@@ -34,6 +34,7 @@ constexpr int kStepMaxRanks = kGemvMaxRanks;
 
 constexpr int kStepMaxG = 8;            // query heads per kv head
 constexpr int kStepAttnChunk = 64;      // KV positions per attention chunk
+constexpr int kStepAttnMaxSplit = 128;  // splits per kv head the attention merge stages in shared memory
 constexpr int kStepHdr = kGemvSmemHdr;  // mbarriers, flags, phase parameter copies, reduction scratch
 constexpr int kStepUnion = 40 * 1024;   // XQ input of a GEMV phase / attention scratch
 constexpr int kStepSmem = 227 * 1024;
