@@ -1,4 +1,4 @@
-"""bs=1 greedy decode throughput of Llama-2-7B Q4_K_M on B200 (BASELINE config 3).
+"""bs=1 greedy decode throughput of Llama-2-7B Q4_K_M on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
@@ -309,7 +309,7 @@ def run_b200(args):
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "q4_k/q6_k weights; u8 x s8 -> s32 tensor-core dots (exact), f32 scales and accumulation",
         "data": "synthetic (seeded random-init GGUF; uniform-random prompt ids)",
-        "config": {"workload": f"{cfg.name} Q4_K_M bs=1 greedy decode (BASELINE config 3)",
+        "config": {"workload": f"{cfg.name} Q4_K_M bs=1 greedy decode",
                    "model": cfg.name, "global_batch": 1, "seq_len": PROMPT_LEN,
                    "context": f"{PROMPT_LEN + 1 + args.warmup}..{PROMPT_LEN + 1 + args.warmup + args.steps}",
                    "parallelism": f"tp{world}" if world > 1 else "single",
@@ -336,9 +336,11 @@ def run_b200(args):
 
 
 def run_gemv_sweep(args):
-    """Standalone dequant-GEMV sweep (BASELINE config 0 shapes and the config 4
-    M x K grid, batch 1): one JSON line per shape, device-timed with CUDA
-    events; weight copies rotate so every launch streams from HBM (> L2)."""
+    """Standalone dequant-GEMV sweep (the TinyLlama layer shapes and the Llama-2-7B
+    M x K grid) at batch 1 (af_gemv_f32) and batch B > 1 (B vectors against
+    one pass over the weights, af_gemv_batched_f32): one JSON
+    line per shape and batch, device-timed with CUDA events; weight copies
+    rotate so every launch streams from HBM (> L2)."""
     import torch
     from llm_core_b200 import _lib, gguf
     lib = _lib.load()
@@ -348,9 +350,10 @@ def run_gemv_sweep(args):
     if args.shapes:
         shapes = [tuple(int(v) for v in s.split("x")) for s in args.shapes.split(",")]
     types = [gguf.GGML_Q4_K, gguf.GGML_Q6_K] if args.types == "both" else [int(args.types)]
+    batches = [int(b) for b in args.batches.split(",")]
     rng = np.random.default_rng(0)
     for t in types:
-        for (m, k) in shapes:
+        for (m, k), B in [(sh, b) for sh in shapes for b in batches]:
             gen = gguf.random_q4k if t == gguf.GGML_Q4_K else gguf.random_q6k
             host = gen(rng, m * k // 256).reshape(-1)
             nbytes = lib.af_weight_bytes(t, m, k)
@@ -361,24 +364,42 @@ def run_gemv_sweep(args):
                 w = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
                 assert lib.af_weight_pack(w.data_ptr(), src.data_ptr(), t, m, k, None) == 0
                 ws.append(w)
-            x = torch.randn(k, device="cuda")
-            y = torch.empty(m, device="cuda")
+            x = torch.randn(B, k, device="cuda")
+            y = torch.empty(B, m, device="cuda")
             st = torch.cuda.current_stream().cuda_stream
+
+            def launch(w):
+                if B == 1:
+                    return lib.af_gemv_f32(y.data_ptr(), w.data_ptr(), t, x.data_ptr(), m, k, st)
+                return lib.af_gemv_batched_f32(y.data_ptr(), w.data_ptr(), t, x.data_ptr(), m, k, B, st)
             for i in range(3):
-                assert lib.af_gemv_f32(y.data_ptr(), ws[i % copies].data_ptr(), t, x.data_ptr(), m, k, st) == 0
+                assert launch(ws[i % copies]) == 0
             n = max(args.steps, copies)
+            # the n launches replayed as one CUDA graph, so that the host's
+            # launch rate does not bound the device time of small shapes
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(side):
+                st = side.cuda_stream
+                with torch.cuda.graph(g, stream=side):
+                    for i in range(n):
+                        launch(ws[i % copies])
+            torch.cuda.synchronize()
+            g.replay()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             torch.cuda.synchronize()
             e0.record()
-            for i in range(n):
-                lib.af_gemv_f32(y.data_ptr(), ws[i % copies].data_ptr(), t, x.data_ptr(), m, k, st)
+            g.replay()
             e1.record()
             torch.cuda.synchronize()
             us = e0.elapsed_time(e1) * 1000 / n
-            alg = m * k // 256 * (144 if t == gguf.GGML_Q4_K else 210) + 4 * (k + m)
+            del g
+            alg = m * k // 256 * (144 if t == gguf.GGML_Q4_K else 210) + 4 * B * (k + m)
             gbs = alg / (us * 1e-6) / 1e9
-            print(json.dumps({"kernel": "gemv_kernel", "type": "Q4_K" if t == 12 else "Q6_K", "M": m, "K": k,
-                              "batch": 1, "us": round(us, 2), "bytes": alg, "GBps": round(gbs, 1),
+            print(json.dumps({"kernel": "gemv_kernel" if B == 1 else "bgemv_kernel",
+                              "type": "Q4_K" if t == 12 else "Q6_K", "M": m, "K": k,
+                              "batch": B, "us": round(us, 2), "bytes": alg, "GBps": round(gbs, 1),
                               "frac": round(gbs / peak, 4), "peak": f"{peak} ({kind})", "copies": copies}))
             del ws, src
             torch.cuda.empty_cache()
@@ -387,7 +408,7 @@ def run_gemv_sweep(args):
 
 def run_prefill_sweep(args):
     """Prefill dequant-GEMM (tcgen05) at the Llama-2-7B linear-layer shapes for
-    a 512-token prompt (BASELINE config 4): one JSON line per shape,
+    a 512-token prompt: one JSON line per shape,
     device-timed with CUDA events (the per-call staging of X included).
     `tflops` counts the algorithmic 2·M·K·T."""
     import torch
@@ -443,6 +464,7 @@ def main():
     ap.add_argument("--prefill-sweep", action="store_true", help="prefill GEMM at the 7B shapes, 512 tokens")
     ap.add_argument("--shapes", default="", help="sweep shapes, e.g. 4096x4096,32000x4096")
     ap.add_argument("--types", default="both", help="12 (Q4_K), 14 (Q6_K) or both")
+    ap.add_argument("--batches", default="1", help="GEMV sweep batch sizes, e.g. 1,4,16")
     args = ap.parse_args()
     if args.gemv_sweep:
         return run_gemv_sweep(args)

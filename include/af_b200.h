@@ -78,15 +78,25 @@ cudaError_t af_gemv_f32(float* d_y, const void* d_w, int ggml_type, const float*
                         int cols, cudaStream_t stream);
 
 /* Prefill dequant-GEMM: y[n_tokens][rows] = x[n_tokens][cols] · Wᵀ with W
- * packed (af_weight_pack) and f32 x, on the tcgen05 tensor cores (W
- * dequantised to bf16 in shared memory, x split into bf16 hi + lo, f32
- * accumulation in tensor memory; ~1e-3 relative error from the bf16 weights).
+ * packed (af_weight_pack) and f32 x, on the tcgen05 tensor cores: W
+ * dequantised to f16 in shared memory, each token of x scaled by a power of
+ * two (undone exactly in the epilogue) and rounded to f16, f32 accumulation in
+ * tensor memory (~2e-4 relative error).
  * The linear layers of the reference's batched prompt pass llama_forward_batch
  * (src/models/llama_model.cpp:1339-1462), whose Q4_K × Q8_0 GEMM is
  * gemm_q4k_q8_avx2_range (src/backend/cpu_x86/kernels/gemv_q4k_q8_avx2.cpp:257-346).
  * cols % 256 == 0; x and W 16-byte aligned. */
 cudaError_t af_prefill_gemm_f32(float* d_y, const void* d_w, int ggml_type, const float* d_x, int rows,
                                 int cols, int n_tokens, cudaStream_t stream);
+
+/* Batched dequant GEMV: y[n][rows] = W · x[n] for 1 <= n_vec <= 32 vectors
+ * x[n_vec][cols] against one pass over the packed weights (the reference's
+ * many-token Q8 GEMM, gemm_q4k_q8_avx2_range,
+ * src/backend/cpu_x86/kernels/gemv_q4k_q8_avx2.cpp:257-346).  Inputs are
+ * quantised per 32 values to the single-vector GEMV's 16-bit grid; integer
+ * dots per sub-block, scales in f32.  Same arguments as af_prefill_gemm_f32. */
+cudaError_t af_gemv_batched_f32(float* d_y, const void* d_w, int ggml_type, const float* d_x, int rows,
+                                int cols, int n_vec, cudaStream_t stream);
 
 /* The fused GEMV the decode step is built from: up to three matrices sharing
  * one input (e.g. attn_q/attn_k/attn_v), an optional residual add into the

@@ -75,6 +75,7 @@ def load() -> C.CDLL:
         "af_weight_unpack": (i, [vp, vp, i, i, i, vp]),
         "af_gemv_f32": (i, [vp, vp, i, vp, i, i, vp]),
         "af_prefill_gemm_f32": (i, [vp, vp, i, vp, i, i, i, vp]),
+        "af_gemv_batched_f32": (i, [vp, vp, i, vp, i, i, i, vp]),
         "af_rms_norm_f32": (i, [vp, vp, vp, i, f, vp]),
         "af_gemv_fused": (i, [C.POINTER(GemvFusedArgs), vp]),
         "af_attention_decode_f32": (i, [vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i, i, i, i, i, f, i, vp, vp,

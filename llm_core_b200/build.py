@@ -12,7 +12,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libaf_b200.so")
-SOURCES = ["af_gemv.cu", "af_ops.cu", "af_attention.cu", "af_step.cu", "af_prefill.cu", "af_sample.cu", "af_engine.cu",
+SOURCES = ["af_gemv.cu", "af_ops.cu", "af_attention.cu", "af_step.cu", "af_prefill.cu", "af_bgemv.cu", "af_sample.cu", "af_engine.cu",
            "af_gguf.cpp"]
 HEADERS = ["af_common.cuh", "af_gemv.cuh", "af_gemv_dev.cuh", "af_ops.cuh", "af_step.cuh", "af_gguf.h"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")

@@ -10,6 +10,7 @@
 // (o, running max, sum) and the last CTA of a kv head merges the partials with
 // the usual exp(m_s − M) rescaling.  Cache layout is the reference's:
 // [n_ctx][n_kv_heads * head_dim] per layer, fp32.
+#include <cuda.h>
 #include <mutex>
 #include <string>
 
@@ -335,17 +336,42 @@ struct NoAllocScratch {
 
 static __device__ __align__(256) NoAllocScratch g_attn_scratch;
 
-// Device addresses of g_attn_scratch, looked up once per device.
+// Device addresses of g_attn_scratch, looked up once per device and context:
+// a reset primary context reloads the module, so the address is looked up
+// again when the current context is not the one it was taken in.
 constexpr int kMaxDevices = 64;
-NoAllocScratch* g_scratch_ptr[kMaxDevices] = {};
+struct ScratchAddr {
+    CUcontext ctx = nullptr;
+    NoAllocScratch* ptr = nullptr;
+};
+ScratchAddr g_scratch_addr[kMaxDevices];
 std::mutex g_scratch_mu;
 
 cudaError_t scratch_for_current_device(NoAllocScratch** out) {
     int dev = 0;
     AF_CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    AF_CUDA_TRY(cudaSetDevice(dev));  // makes the device's primary context current
+    // the driver's cuCtxGetCurrent through the runtime (the library does not link libcuda)
+    using CtxGetCurrent = CUresult (*)(CUcontext*);
+    static CtxGetCurrent get_ctx = nullptr;
+    if (!get_ctx) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) != cudaSuccess || !fn) {
+            set_last_error("af_attention_decode_f32_noalloc: cuCtxGetCurrent unavailable");
+            return cudaErrorInitializationError;
+        }
+        get_ctx = reinterpret_cast<CtxGetCurrent>(fn);
+    }
+    CUcontext ctx = nullptr;
+    if (get_ctx(&ctx) != CUDA_SUCCESS || !ctx) {
+        set_last_error("af_attention_decode_f32_noalloc: no current CUDA context");
+        return cudaErrorInitializationError;
+    }
     std::lock_guard<std::mutex> lock(g_scratch_mu);
-    if (!g_scratch_ptr[dev]) {
+    ScratchAddr& a = g_scratch_addr[dev];
+    if (!a.ptr || a.ctx != ctx) {
         void* p = nullptr;
         const cudaError_t r = cudaGetSymbolAddress(&p, g_attn_scratch);
         if (r != cudaSuccess) {
@@ -353,9 +379,10 @@ cudaError_t scratch_for_current_device(NoAllocScratch** out) {
                            cudaGetErrorString(r));
             return r;
         }
-        g_scratch_ptr[dev] = static_cast<NoAllocScratch*>(p);
+        a.ptr = static_cast<NoAllocScratch*>(p);
+        a.ctx = ctx;
     }
-    *out = g_scratch_ptr[dev];
+    *out = a.ptr;
     return cudaSuccess;
 }
 

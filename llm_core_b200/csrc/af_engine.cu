@@ -24,6 +24,8 @@
 
 #include <cmath>
 #include <cstdlib>
+#include <thread>
+#include <chrono>
 #include <random>
 #include <cstdio>
 #include <cstring>
@@ -99,6 +101,10 @@ struct af_engine {
     int* d_sampled = nullptr;      // sampled id
     float* logits_full = nullptr;  // tensor parallel: the gathered vocabulary [vocab]
     int* h_tokpos = nullptr;  // pinned host mirror
+    int* h_pin = nullptr;     // pinned prompt staging of af_engine_prefill (grown on demand)
+    size_t h_pin_n = 0;
+    void* pf_ws = nullptr;    // device rows of af_engine_prefill_batched (grown on demand)
+    size_t pf_ws_bytes = 0;
     int nsplit = 1;
 
     // persistent step kernel (single GPU): phase table in device memory
@@ -137,9 +143,16 @@ cudaError_t fail(const std::string& msg, cudaError_t code = cudaErrorInvalidValu
         if (e_ != cudaSuccess) return fail(std::string(#x) + ": " + cudaGetErrorString(e_), e_); \
     } while (0)
 
+// The communicator is non-blocking (see af_engine_create): a call may return
+// ncclInProgress until NCCL has enqueued it; wait for that (bounded).
+inline ncclResult_t nccl_settle(ncclComm_t comm, ncclResult_t r) {
+    for (int i = 0; r == ncclInProgress && comm && i < 10000000; ++i)
+        if (ncclCommGetAsyncError(comm, &r) != ncclSuccess) return ncclSystemError;
+    return r;
+}
 #define NCCL_TRY(x)                                                                         \
     do {                                                                                    \
-        ncclResult_t r_ = (x);                                                              \
+        ncclResult_t r_ = nccl_settle(e->comm, (x));                                        \
         if (r_ != ncclSuccess) return fail(std::string(#x) + ": " + ncclGetErrorString(r_), cudaErrorUnknown); \
     } while (0)
 
@@ -663,7 +676,8 @@ extern "C" {
 cudaError_t af_nccl_unique_id(void* h_id) {
     if (!h_id) return fail("af_nccl_unique_id: null");
     ncclUniqueId id;
-    NCCL_TRY(ncclGetUniqueId(&id));
+    const ncclResult_t r = ncclGetUniqueId(&id);
+    if (r != ncclSuccess) return fail(std::string("ncclGetUniqueId: ") + ncclGetErrorString(r), cudaErrorUnknown);
     std::memcpy(h_id, &id, sizeof(id));
     return cudaSuccess;
 }
@@ -707,7 +721,36 @@ cudaError_t af_engine_create(const af_model_config* cfg, int device, int tp_rank
         if (!nccl_id) return fail("af_engine_create: tp_size > 1 needs an ncclUniqueId");
         ncclUniqueId id;
         std::memcpy(&id, nccl_id, sizeof(id));
-        NCCL_TRY(ncclCommInitRank(&e->comm, tp_size, id, tp_rank));
+        // non-blocking init with a host-side limit: a rank that never joins
+        // ends this call with an error instead of a hang (AF_NCCL_INIT_TIMEOUT_S,
+        // default 300 s), and the half-made communicator is aborted
+        ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+        cfg.blocking = 0;
+        ncclResult_t r = ncclCommInitRankConfig(&e->comm, tp_size, id, tp_rank, &cfg);
+        const char* tv = std::getenv("AF_NCCL_INIT_TIMEOUT_S");
+        const double limit = tv ? std::atof(tv) : 300.0;
+        const auto t0 = std::chrono::steady_clock::now();
+        while (r == ncclInProgress || (r == ncclSuccess && e->comm)) {
+            ncclResult_t st = ncclInProgress;
+            if (ncclCommGetAsyncError(e->comm, &st) != ncclSuccess) st = ncclSystemError;
+            if (st != ncclInProgress) {
+                r = st;
+                break;
+            }
+            if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > limit) {
+                ncclCommAbort(e->comm);
+                e->comm = nullptr;
+                return fail("af_engine_create: NCCL init did not complete within AF_NCCL_INIT_TIMEOUT_S (a rank "
+                            "did not join)", cudaErrorTimeout);
+            }
+            std::this_thread::sleep_for(std::chrono::milliseconds(1));
+        }
+        if (r != ncclSuccess) {
+            if (e->comm) ncclCommAbort(e->comm);
+            e->comm = nullptr;
+            return fail(std::string("af_engine_create: ncclCommInitRankConfig: ") + ncclGetErrorString(r),
+                        cudaErrorUnknown);
+        }
     }
     *out = e.release();
     return cudaSuccess;
@@ -721,6 +764,8 @@ cudaError_t af_engine_destroy(af_engine* e) {
     for (void* p : e->peer_maps) cudaIpcCloseMemHandle(p);
     for (void* p : e->allocs) cudaFree(p);
     if (e->h_tokpos) cudaFreeHost(e->h_tokpos);
+    if (e->h_pin) cudaFreeHost(e->h_pin);
+    if (e->pf_ws) cudaFree(e->pf_ws);
     if (e->comm) ncclCommDestroy(e->comm);
     if (e->stream) cudaStreamDestroy(e->stream);
     delete e;
@@ -978,8 +1023,15 @@ cudaError_t af_engine_prefill(af_engine* e, const int32_t* h_tokens, int n, int3
     for (int i = 0; i < n; ++i)
         if (h_tokens[i] < 0 || h_tokens[i] >= e->cfg.vocab) return fail("af_engine_prefill: token id outside the vocabulary");
     // Each token has its own pinned slot, so the async copies need no host sync.
-    int* pin = nullptr;
-    ENG_TRY(cudaMallocHost(&pin, (size_t)(n + 1) * 4));
+    if (e->h_pin_n < (size_t)n + 1) {
+        // the previous prefill's copies have completed (it synchronised)
+        if (e->h_pin) cudaFreeHost(e->h_pin);
+        e->h_pin = nullptr;
+        e->h_pin_n = 0;
+        ENG_TRY(cudaMallocHost(&e->h_pin, (size_t)(n + 1) * 4));
+        e->h_pin_n = (size_t)n + 1;
+    }
+    int* pin = e->h_pin;
     std::memcpy(pin, h_tokens, (size_t)n * 4);
     pin[n] = pos0;
     ENG_TRY(cudaMemcpyAsync(&e->tokpos[1], &pin[n], 4, cudaMemcpyHostToDevice, e->stream));
@@ -990,7 +1042,6 @@ cudaError_t af_engine_prefill(af_engine* e, const int32_t* h_tokens, int n, int3
     ENG_TRY(cudaMemcpyAsync(e->h_tokpos + 2, e->tokpos, 4, cudaMemcpyDeviceToHost, e->stream));
     if (h_logits) AF_CUDA_TRY(gather_logits(e, h_logits));
     ENG_TRY(cudaStreamSynchronize(e->stream));
-    cudaFreeHost(pin);
     if (h_next) *h_next = e->h_tokpos[2];
     return cudaSuccess;
 }
@@ -1014,11 +1065,24 @@ cudaError_t af_engine_prefill_batched(af_engine* e, const int32_t* h_tokens, int
     const int T = n - 1;
     if (T == 0 || e->tp != 1) return af_engine_prefill(e, h_tokens, n, pos0, h_logits, h_next);
     const int E = c.n_embd, QD = e->Hl * e->hd, KD = e->KVl * e->hd, F = e->Fl;
-    std::vector<void*> bufs;
+    // one workspace for the prompt rows, kept by the engine and grown on demand
+    auto al = [](size_t b) { return (b + 255) & ~(size_t)255; };
+    const size_t need = 3 * al((size_t)T * E * 4) + 2 * al((size_t)T * QD * 4) + 2 * al((size_t)T * KD * 4) +
+                        2 * al((size_t)T * F * 4) + al((size_t)2 * T * 4);
+    if (e->pf_ws_bytes < need) {
+        ENG_TRY(cudaStreamSynchronize(e->stream));
+        if (e->pf_ws) cudaFree(e->pf_ws);
+        e->pf_ws = nullptr;
+        e->pf_ws_bytes = 0;
+        if (cudaMalloc(&e->pf_ws, need) != cudaSuccess)
+            return fail("af_engine_prefill_batched: out of device memory for the prompt rows",
+                        cudaErrorMemoryAllocation);
+        e->pf_ws_bytes = need;
+    }
+    size_t ws_off = 0;
     auto take = [&](size_t bytes) {
-        void* p = nullptr;
-        if (cudaMalloc(&p, bytes ? bytes : 16) != cudaSuccess) return static_cast<void*>(nullptr);
-        bufs.push_back(p);
+        void* p = static_cast<uint8_t*>(e->pf_ws) + ws_off;
+        ws_off += al(bytes);
         return p;
     };
     float* x = static_cast<float*>(take((size_t)T * E * 4));
@@ -1031,15 +1095,6 @@ cudaError_t af_engine_prefill_batched(af_engine* e, const int32_t* h_tokens, int
     float* g = static_cast<float*>(take((size_t)T * F * 4));
     float* u = static_cast<float*>(take((size_t)T * F * 4));
     int* d_tp = static_cast<int*>(take((size_t)2 * T * 4));  // tokens, then positions
-    auto release = [&]() {
-        for (void* p : bufs) cudaFree(p);
-    };
-    for (void* p : bufs)
-        if (!p) {
-            release();
-            return fail("af_engine_prefill_batched: out of device memory for the prompt rows",
-                        cudaErrorMemoryAllocation);
-        }
     cudaError_t err = cudaSuccess;
     auto run = [&]() -> cudaError_t {
         std::vector<int32_t> tp((size_t)2 * T);
@@ -1097,7 +1152,6 @@ cudaError_t af_engine_prefill_batched(af_engine* e, const int32_t* h_tokens, int
         return cudaSuccess;
     };
     err = run();
-    release();
     if (err != cudaSuccess) return err;
     return af_engine_prefill(e, h_tokens + T, 1, pos0 + T, h_logits, h_next);
 }

@@ -121,11 +121,14 @@ struct Producer {
 
     // Reserve `bytes` at the next placement; false on timeout or abort.
     __device__ bool reserve(const Ring& r, int bytes, int& at, const volatile int* abort) {
-        const int waste = head + bytes > r.bytes ? r.bytes - head : 0;
+        // the placement rule of ring_place: wrap to 0 when the entry does not
+        // fit after head (head may sit exactly at the end: waste 0, still wrap)
+        const bool wrap = head + bytes > r.bytes;
+        const int waste = wrap ? r.bytes - head : 0;
         const int need = bytes + waste;
         while (used + need > r.bytes || issued - released >= (uint32_t)kRingDesc)
             if (!release_oldest(r, abort)) return false;
-        at = waste ? 0 : head;
+        at = wrap ? 0 : head;
         head = at + bytes;
         used += need;
         const int slot = issued % kRingDesc;

@@ -8,7 +8,7 @@ exact block sizes of ``gguf_tensor_nbytes`` (include/axonforge/dtype.hpp:136-155
 not ``numel * element_size`` (the reference's ``Tensor::nbytes`` bug).
 
 The writer produces the random-init Q4_K_M checkpoints the benchmark configs
-name: Q4_K everywhere except Q6_K for ``attn_v``, the
+name (the benchmark workloads): Q4_K everywhere except Q6_K for ``attn_v``, the
 even-indexed ``ffn_down`` layers and ``output`` (or the tied ``token_embd``).
 Bit fields are seeded and uniform: 4-bit quants 0-15, 6-bit scales/mins 0-63,
 ``d``/``dmin`` uniform in [1e-4, 1e-3] rounded to f16; Q6_K int8 scales 0-63.
@@ -213,12 +213,12 @@ class ModelConfig:
 
 
 PRESETS = {
-    # TinyLlama-1.1B.
+    # TinyLlama-1.1B Q4_K_M workload.
     "tinyllama": ModelConfig("llama", 22, 2048, 32, 4, 5632, 32000, 2048, 1e-5, 1e4, name="tinyllama-1.1b"),
-    # Qwen2.5-3B (q/k/v bias, tied Q6_K vocab).
+    # Qwen2.5-3B Q4_K_M workload (q/k/v bias, tied Q6_K vocab).
     "qwen2.5-3b": ModelConfig("qwen2", 36, 2048, 16, 2, 11008, 151936, 32768, 1e-6, 1e6,
                               qkv_bias=True, tied=True, name="qwen2.5-3b"),
-    # Llama-2-7B.
+    # Llama-2-7B Q4_K_M workload (the headline bs=1 decode).
     "llama2-7b": ModelConfig("llama", 32, 4096, 32, 32, 11008, 32000, 4096, 1e-5, 1e4, name="llama-2-7b"),
     # Small shapes for CPU tests (same code paths; K multiples of 256).
     "tiny": ModelConfig("llama", 2, 256, 4, 2, 512, 512, 256, 1e-5, 1e4, name="tiny-llama"),

@@ -41,9 +41,12 @@ def build_oracle() -> str:
     return ORACLE_SO
 
 
-def build_ref(ref_root: str = "/root/reference") -> str | None:
+def build_ref(ref_root: str | None = None) -> str | None:
     """Compile oracle/_ref/libaxref.so from the reference sources when they are
-    present (only in the build container); returns the path or None."""
+    present (only in the build container): AXONFORGE_SRC, else a `reference`
+    directory beside the repository; returns the path or None."""
+    if ref_root is None:
+        ref_root = os.environ.get("AXONFORGE_SRC") or os.path.join(os.path.dirname(os.path.dirname(_HERE)), "reference")
     if os.path.isdir(os.path.join(ref_root, "src")):
         repo = os.path.dirname(_HERE)
         subprocess.check_call(["make", "-s", "-j8", "-f", os.path.join("oracle", "ref.mk"),

@@ -8,7 +8,7 @@
 # used: the only file CMake would generate, include/axonforge/version.hpp, is
 # written here as a four-macro stand-in (its template is
 # include/axonforge/version.hpp.in).
-REF      ?= /root/reference
+REF      ?= ../reference
 OUT      := oracle/_ref
 OBJ      := $(OUT)/obj
 CXX      ?= g++

@@ -101,7 +101,7 @@ def _ref_or_oracle(path):
 
 @pytest.mark.slow
 def test_tinyllama_logits_and_greedy_agreement(gpu):
-    """BASELINE config 1: TinyLlama-1.1B random-init, 32-token prompt, 256 greedy steps."""
+    """TinyLlama-1.1B random-init, 32-token prompt, 256 greedy steps."""
     path = model_path("tinyllama", 0)
     rng = np.random.default_rng(1)
     prompt = rng.integers(0, 32000, 32).tolist()

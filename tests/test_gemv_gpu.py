@@ -49,7 +49,7 @@ def test_gemv_matches_reference_fixture(gpu, fx):
     assert err < GEMV_TOL and err < TIGHT, err
 
 
-# TinyLlama shapes, seeded Q4_K blocks, x ~ N(0,1)
+# TinyLlama layer shapes, seeded Q4_K blocks, x ~ N(0,1)
 CONFIG0 = [(2048, 2048), (256, 2048), (5632, 2048), (2048, 5632)]
 
 

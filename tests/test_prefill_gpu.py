@@ -42,7 +42,9 @@ def oracle_rows(W, t, X, rows):
 
 @pytest.mark.parametrize("t", [gguf.GGML_Q4_K, gguf.GGML_Q6_K])
 @pytest.mark.parametrize("rows,cols,T", [(128, 256, 128), (256, 2048, 64), (300, 768, 130), (37, 512, 1),
-                                         (1024, 4096, 200), (4096, 512, 1200)])
+                                         (1024, 4096, 200), (4096, 512, 1200),
+                                         # the batched-GEMV sizes of the sweep: 4 and 16 vectors
+                                         (2048, 4096, 4), (4096, 2048, 16)])
 def test_prefill_gemm_matches_oracle(gpu, t, rows, cols, T):
     """(4096, 512, 1200) is a grid of 320 CTAs: the two-CTAs-per-SM variant;
     the others run one CTA per SM with four stages."""

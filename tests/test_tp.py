@@ -102,3 +102,28 @@ def test_tp_matches_single_gpu(world):
     assert int(z["first"]) == nxt
     agree = np.mean(z["ids"] == ids)
     assert agree >= 0.9, agree
+
+
+@pytest.mark.gpu
+def test_rank_that_never_joins_ends_nccl_init_with_an_error(gpu, tmp_path):
+    """Failure detection on the host: rank 0 of a 2-rank engine whose peer
+    never calls af_engine_create gets an error from af_engine_create once
+    AF_NCCL_INIT_TIMEOUT_S passes (non-blocking init, then ncclCommAbort),
+    instead of hanging.  Nothing runs on the GPU but NCCL's setup."""
+    code = (
+        "import sys; sys.path.insert(0, %r)\n"
+        "from llm_core_b200 import gguf\n"
+        "from llm_core_b200.engine import LlamaCudaModel, nccl_unique_id, read_config\n"
+        "from llm_core_b200._lib import AfError\n"
+        "import time\n"
+        "t = time.time()\n"
+        "try:\n"
+        "    LlamaCudaModel(config=read_config(%r), tp_rank=0, tp_size=2, nccl_id=nccl_unique_id())\n"
+        "    print('JOINED')\n"
+        "except AfError as e:\n"
+        "    print('ERR', round(time.time() - t, 1), e)\n"
+    ) % (ROOT, model_path("small", 3))
+    env = dict(os.environ, AF_NCCL_INIT_TIMEOUT_S="4", NCCL_NVLS_ENABLE="0")
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=120, env=env)
+    assert "ERR" in r.stdout, r.stdout + r.stderr
+    assert "did not join" in r.stdout
