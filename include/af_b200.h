@@ -77,6 +77,15 @@ cudaError_t af_weight_unpack(void* d_dst, const void* d_src, int ggml_type, int 
 cudaError_t af_gemv_f32(float* d_y, const void* d_w, int ggml_type, const float* d_x, int rows,
                         int cols, cudaStream_t stream);
 
+/* The same GEMV with x quantised to the reference's Q8_0 blocks first
+ * (quantize_q8_avx2, src/backend/cpu_x86/kernels/quant_q8_avx2.cpp:33-84:
+ * d = amax/127, q = round-half-even(x·127/amax) per 32 values): the
+ * production decode GEMV gemv_wt_q8 (src/models/llama_model.cpp:767-831) with
+ * its integer dots and min correction (gemv_q4k_r8_avx2.cpp:209-220,
+ * gemv_q6k_q8_avx2.cpp:103).  cols % 256 == 0, cols <= 12288. */
+cudaError_t af_gemv_q8_f32(float* d_y, const void* d_w, int ggml_type, const float* d_x, int rows,
+                           int cols, cudaStream_t stream);
+
 /* Prefill dequant-GEMM: y[n_tokens][rows] = x[n_tokens][cols] · Wᵀ with W
  * packed (af_weight_pack) and f32 x, on the tcgen05 tensor cores: W
  * dequantised to f16 in shared memory, each token of x scaled by a power of
@@ -85,7 +94,9 @@ cudaError_t af_gemv_f32(float* d_y, const void* d_w, int ggml_type, const float*
  * The linear layers of the reference's batched prompt pass llama_forward_batch
  * (src/models/llama_model.cpp:1339-1462), whose Q4_K × Q8_0 GEMM is
  * gemm_q4k_q8_avx2_range (src/backend/cpu_x86/kernels/gemv_q4k_q8_avx2.cpp:257-346).
- * cols % 256 == 0; x and W 16-byte aligned. */
+ * cols % 256 == 0; x and W 16-byte aligned.  n_tokens <= 32 runs the
+ * batched GEMV instead (af_gemv_batched_f32: one weight pass, exact integer
+ * dots), which is faster at that size. */
 cudaError_t af_prefill_gemm_f32(float* d_y, const void* d_w, int ggml_type, const float* d_x, int rows,
                                 int cols, int n_tokens, cudaStream_t stream);
 
@@ -93,8 +104,9 @@ cudaError_t af_prefill_gemm_f32(float* d_y, const void* d_w, int ggml_type, cons
  * x[n_vec][cols] against one pass over the packed weights (the reference's
  * many-token Q8 GEMM, gemm_q4k_q8_avx2_range,
  * src/backend/cpu_x86/kernels/gemv_q4k_q8_avx2.cpp:257-346).  Inputs are
- * quantised per 32 values to the single-vector GEMV's 16-bit grid; integer
- * dots per sub-block, scales in f32.  Same arguments as af_prefill_gemm_f32. */
+ * quantised per token and 256 values to a 16-bit grid (~1e-5 relative);
+ * integer dots and sub-block scales, f32 per super-block.  Deterministic.
+ * Same arguments as af_prefill_gemm_f32. */
 cudaError_t af_gemv_batched_f32(float* d_y, const void* d_w, int ggml_type, const float* d_x, int rows,
                                 int cols, int n_vec, cudaStream_t stream);
 
@@ -236,6 +248,13 @@ cudaError_t af_engine_load_tensor(af_engine* e, const char* name, int ggml_type,
 /* Parse a GGUF file (mmap) and load every tensor; fills *cfg_out if non-NULL. */
 cudaError_t af_gguf_read_config(const char* path, int max_context_len, af_model_config* cfg_out);
 cudaError_t af_engine_load_gguf(af_engine* e, const char* path);
+/* Activation format of the decode step, before af_engine_finalize: 0 (the
+ * default) quantises every GEMV input to a 16-bit grid per 32 values (the
+ * F32-activation reference within ~1e-5); 1 quantises them to Q8_0 blocks as
+ * the reference's production path does (kQ8Quant before each gemv_wt_q8,
+ * src/models/llama_model.cpp:1227,1275,1281,1322,1331).  The batched prompt
+ * pass (af_engine_prefill_batched) keeps its own f16 GEMM numerics. */
+cudaError_t af_engine_set_q8_activations(af_engine* e, int on);
 /* Allocate activations/KV, check every required tensor, capture the step graph. */
 cudaError_t af_engine_finalize(af_engine* e);
 

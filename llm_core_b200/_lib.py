@@ -74,6 +74,7 @@ def load() -> C.CDLL:
         "af_weight_pack": (i, [vp, vp, i, i, i, vp]),
         "af_weight_unpack": (i, [vp, vp, i, i, i, vp]),
         "af_gemv_f32": (i, [vp, vp, i, vp, i, i, vp]),
+        "af_gemv_q8_f32": (i, [vp, vp, i, vp, i, i, vp]),
         "af_prefill_gemm_f32": (i, [vp, vp, i, vp, i, i, i, vp]),
         "af_gemv_batched_f32": (i, [vp, vp, i, vp, i, i, i, vp]),
         "af_rms_norm_f32": (i, [vp, vp, vp, i, f, vp]),
@@ -92,6 +93,7 @@ def load() -> C.CDLL:
         "af_gguf_read_config": (i, [C.c_char_p, i, C.POINTER(ModelConfig)]),
         "af_engine_load_gguf": (i, [vp, C.c_char_p]),
         "af_engine_finalize": (i, [vp]),
+        "af_engine_set_q8_activations": (i, [vp, i]),
         "af_engine_step": (i, [vp, C.c_int32, C.c_int32, fp, ip]),
         "af_engine_prefill": (i, [vp, ip, i, C.c_int32, fp, ip]),
         "af_engine_prefill_batched": (i, [vp, ip, i, C.c_int32, fp, ip]),

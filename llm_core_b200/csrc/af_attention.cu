@@ -250,7 +250,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
         __syncthreads();
         const int g0 = kvh * G * hd / 32, ng = G * hd / 32;  // 32-value warp groups
         for (int k = warp; k < ng; k += kAttnThreads / 32)
-            xq_quantize_group(p.xq_out, p.out, nullptr, p.n_heads * hd, g0 + k);
+            xq_quantize_group(p.xq_out, p.out, nullptr, p.n_heads * hd, g0 + k, p.q8 != 0);
     }
 }
 

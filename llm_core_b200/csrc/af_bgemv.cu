@@ -14,24 +14,26 @@
 // by up to 8 tokens at a time with mma.sync (u8 weights × s8 inputs → s32):
 //
 //  * Tokens are the MMA's N dimension.  The inputs are quantised per token
-//    and 32 values to the same 16-bit grid as the single-vector GEMV,
-//    x ≈ xs·(256·hi + lo), and the two int8 planes are two MMAs, so every
-//    accumulator is an exact integer dot Σ q·hi, Σ q·lo of one row, one
-//    token and one 32-value sub-block (Q4_K) or 16-value group (Q6_K, one
-//    m16n8k16 per group) — the granularity at which the block scales apply:
-//    w = d·sc·q − dmin·m (Q4_K), w = d·sc·(q − 32) (Q6_K), in f32.
+//    and super-block to a 16-bit grid, x ≈ xs·(256·hi + lo), and the two int8
+//    planes are two MMAs, so every accumulator is an exact integer dot
+//    Σ q·hi, Σ q·lo of one row, one token and one 32-value sub-block (Q4_K)
+//    or 16-value group (Q6_K, one m16n8k16 per group).  The sub-block scales
+//    (6-bit Q4_K, int8 Q6_K) are applied in integer arithmetic and summed
+//    over the super-block, the min / offset term from per-sub-block input
+//    sums Σ(256·hi + lo); f32 only once per super-block:
+//    w = d·sc·q − dmin·m (Q4_K), w = d·sc·(q − 32) (Q6_K).
 //  * The packed layout (af_gemv.cuh) already holds each lane's A fragment
 //    in one 16-byte word per 64 values; the input layout "XB" below is
 //    arranged the same way: a lane's B words of one sub-block are one
-//    16-byte load, its two tokens' scales another.
-//  * CTA work: a contiguous range of 16-row tiles (one CTA per SM), taken in
-//    groups of at most 8 tiles.  A ring entry is (group, S super-blocks):
-//    the group's weights for those super-blocks plus the inputs of all B
-//    tokens for them (the inputs are re-read from L2 once per group, never
-//    per tile).  Warp w owns tile w % nt of the group and a part of the
-//    entry's super-blocks / sub-blocks, accumulating in registers across the
-//    whole K; at the end of a group the warps of a tile are added in a fixed
-//    order through shared memory (deterministic) and stored token-major.
+//    16-byte load.
+//  * Work: 8-tile groups (128 rows, one tile per consumer warp) × K
+//    super-blocks, as (group, super-block) pairs split evenly over the grid
+//    (one or two CTAs per SM).  A CTA streams its pairs as ring entries of
+//    up to two super-blocks: the group's weights plus the inputs of all
+//    tokens for them.  A group whose K range spans several CTAs is split-K:
+//    each CTA writes its slice, and the last slice to arrive (an atomic
+//    count, no waiting) adds all slices in slice order — the result does
+//    not depend on the arrival order.
 //  Every wait is bounded (kSpinLimit); a timeout records kErrMbarTimeout.
 #include <algorithm>
 #include <cstdlib>

@@ -120,6 +120,7 @@ struct af_engine {
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t gexec = nullptr;
     bool finalized = false;
+    int q8 = 0;  // activations as Q8_0 blocks (af_engine_set_q8_activations)
     int kernels_per_step = 0;
 
     void* dalloc(size_t bytes) {
@@ -195,6 +196,7 @@ GemvParams base_params(const af_engine* e, int K) {
     GemvParams p = {};
     p.K = K;
     p.eps = e->cfg.eps;
+    p.q8 = e->q8;
     return p;
 }
 
@@ -252,7 +254,7 @@ cudaError_t enqueue_step(af_engine* e, Prof* prof = nullptr) {
         return cudaSuccess;
     }
     ENG_TRY(embed_launch(e->x[0], e->tok_embd.w, e->tok_embd.type, E, e->tok_embd.stride, &e->tokpos[0], e->key,
-                         xq ? e->xq_a : nullptr, e->layers[0].attn_norm, e->stream, e->pdl));
+                         xq ? e->xq_a : nullptr, e->layers[0].attn_norm, e->stream, e->pdl, e->q8 != 0));
     ++nk;
     AF_MARK(AF_PROF_EMBED, (double)e->tok_embd.stride + E * 4.0);
     bool pending = false;  // TP: ypart holds an un-added partial sum
@@ -308,6 +310,7 @@ cudaError_t enqueue_step(af_engine* e, Prof* prof = nullptr) {
             a.eps = c.eps;
             a.scale = 1.f / std::sqrt((float)e->hd);
             a.xq_out = xq ? e->xq_o : nullptr;
+            a.q8 = e->q8;
             ENG_TRY(attention_launch(a, e->stream, e->pdl));
             ++nk;
             if (prof) {
@@ -514,7 +517,8 @@ cudaError_t build_step(af_engine* e) {
         q.g.seg[2] = seg_of(L.wv, e->v, L.bv);
         q.g.nseg = 3;
         q.g.xq = e->xq_a;
-        q.g.xq_norm = 1;
+        // layer 0 in Q8 mode: the embedding phase stores the normalised input
+        q.g.xq_norm = (l == 0 && e->q8 && step_q8_exact_embed(E)) ? 0 : 1;
         q.g.epi = EPI_STORE;
         if (tp && l > 0) xin(q, 2 * l - 1, L.attn_norm);
         gemv_configure(q.g, e->sms);
@@ -548,6 +552,7 @@ cudaError_t build_step(af_engine* e) {
         a.eps = c.eps;
         a.scale = 1.f / std::sqrt((float)e->hd);
         a.xq_out = e->xq_o;
+        a.q8 = e->q8;
         ph.push_back(at);
 
         StepPhase o = {};
@@ -638,6 +643,8 @@ cudaError_t build_step(af_engine* e) {
     sp.x = e->x[0];
     sp.xq = e->xq_a;
     sp.xq_norm_w = e->layers[0].attn_norm;
+    sp.q8 = e->q8;
+    sp.eps = c.eps;
     sp.key = e->key;
     sp.token = &e->tokpos[0];
     sp.pos = &e->tokpos[1];
@@ -886,6 +893,13 @@ cudaError_t af_engine_load_gguf(af_engine* e, const char* path) {
     } catch (const std::exception& ex) {
         return fail(ex.what());
     }
+}
+
+cudaError_t af_engine_set_q8_activations(af_engine* e, int on) {
+    if (!e) return fail("af_engine_set_q8_activations: null engine");
+    if (e->finalized) return fail("af_engine_set_q8_activations: engine already finalized");
+    e->q8 = on ? 1 : 0;
+    return cudaSuccess;
 }
 
 cudaError_t af_engine_finalize(af_engine* e) {

@@ -12,11 +12,11 @@ namespace {
 
 using namespace gdev;
 
-__global__ void xq_quantize_kernel(uint8_t* xq, const float* x, const float* norm_w, int K) {
+__global__ void xq_quantize_kernel(uint8_t* xq, const float* x, const float* norm_w, int K, int q8) {
     pdl_launch_dependents();
     pdl_wait();
     const int g = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
-    if (g < (K + 31) / 32) xq_quantize_group(xq, x, norm_w, K, g);
+    if (g < (K + 31) / 32) xq_quantize_group(xq, x, norm_w, K, g, q8 != 0);
 }
 
 __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_constant__ GemvParams p) {
@@ -118,7 +118,8 @@ cudaError_t gemv_launch(const GemvParams& p, cudaStream_t stream, bool pdl) {
     return cudaLaunchKernelEx(&cfg, gemv_kernel, p);
 }
 
-cudaError_t xq_quantize_launch(uint8_t* xq, const float* x, const float* norm_w, int K, cudaStream_t st, bool pdl) {
+cudaError_t xq_quantize_launch(uint8_t* xq, const float* x, const float* norm_w, int K, cudaStream_t st, bool pdl,
+                               bool q8) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(((K + 31) / 32 + 3) / 4);
     cfg.blockDim = dim3(128);
@@ -128,7 +129,7 @@ cudaError_t xq_quantize_launch(uint8_t* xq, const float* x, const float* norm_w,
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, xq_quantize_kernel, xq, x, norm_w, K);
+    return cudaLaunchKernelEx(&cfg, xq_quantize_kernel, xq, x, norm_w, K, q8 ? 1 : 0);
 }
 
 }  // namespace af

@@ -119,6 +119,9 @@ struct GemvParams {
     unsigned long long* xsend[kGemvMaxRanks];
     int xsend_n;
     uint32_t xtag;
+    // quantise inputs as Q8_0 blocks (the reference's production activation
+    // format) instead of the 16-bit grid
+    int q8;
     int ring_bytes;        // weight ring in shared memory (multiple of 16)
     int grid;
     int vrange[kGemvMaxGrid + 1];  // CTA i owns fragments [vrange[i], vrange[i+1])
@@ -157,7 +160,8 @@ cudaError_t gemv_launch(const GemvParams& p, cudaStream_t stream, bool pdl);
 
 // Quantise an f32 vector (RMSNorm weights applied when norm_w is set) into XQ
 // form, for inputs no producing kernel writes.
-cudaError_t xq_quantize_launch(uint8_t* xq, const float* x, const float* norm_w, int K, cudaStream_t st, bool pdl);
+cudaError_t xq_quantize_launch(uint8_t* xq, const float* x, const float* norm_w, int K, cudaStream_t st, bool pdl,
+                               bool q8 = false);
 
 // Quantise value v (this lane's; the warp's 32 lanes hold one 32-value group,
 // indices idx = 32·g + lane) into the XQ buffer, with the lane's RMSNorm
@@ -166,19 +170,34 @@ cudaError_t xq_quantize_launch(uint8_t* xq, const float* x, const float* norm_w,
 // past the vector pass any v; they store nothing).  The 16-bit split matches
 // the consumers' integer form: q = rint(v·32639/amax), hi = (q + 128) >> 8,
 // lo = q − 256·hi.  Inline: it runs in the epilogues of the hot loops.
-__device__ __forceinline__ void xq_store32w(uint8_t* xq, float v, float wgt, bool norm, int K, int idx) {
+// With q8, the group is quantised as the reference's Q8_0 block instead
+// (quantize_q8_avx2, src/backend/cpu_x86/kernels/quant_q8_avx2.cpp:33-84):
+// d = amax/127, q = round-half-even(a · 127/amax), stored as hi = 0, lo = q,
+// xs = d, and the group sum d·Σq (the min correction of the Q8 dot,
+// gemv_q4k_r8_avx2.cpp:209-220).
+__device__ __forceinline__ void xq_store32w(uint8_t* xq, float v, float wgt, bool norm, int K, int idx,
+                                            bool q8 = false) {
     const int lane = threadIdx.x & 31;
     const bool in = idx >= 0 && idx < K;
     if (!in) v = 0.f;
     const float a = v * wgt;
     const float amax = warp_max(fabsf(a));
-    const float inv = amax > 0.f ? 32639.f / amax : 0.f;
-    const int q = max(-32639, min(32639, __float2int_rn(a * inv)));
-    const int hi = (q + 128) >> 8, lo = q - 256 * hi;
+    int q, hi, lo;
+    if (q8) {
+        const float id = amax > 0.f ? 127.f / amax : 0.f;
+        q = max(-127, min(127, __float2int_rn(a * id)));
+        hi = 0;
+        lo = q;
+    } else {
+        const float inv = amax > 0.f ? 32639.f / amax : 0.f;
+        q = max(-32639, min(32639, __float2int_rn(a * inv)));
+        hi = (q + 128) >> 8;
+        lo = q - 256 * hi;
+    }
     int is = q;
 #pragma unroll
     for (int o = 1; o < 16; o <<= 1) is += __shfl_xor_sync(0xffffffffu, is, o);  // per 16
-    const float fs = warp_sum(a);
+    const float fs = q8 ? (amax / 127.f) * (float)(is + __shfl_xor_sync(0xffffffffu, is, 16)) : warp_sum(a);
     const float ss = norm ? warp_sum(v * v) : 0.f;
     if (!in) return;
     uint8_t* sb = xq + (idx >> 8) * kXqSb;
@@ -187,23 +206,25 @@ __device__ __forceinline__ void xq_store32w(uint8_t* xq, float v, float wgt, boo
     sb[256 + ko] = (uint8_t)(lo & 0xFF);
     if ((lane & 15) == 0) reinterpret_cast<int*>(sb + kXqI16)[ko >> 4] = is;
     if (lane == 0) {
-        reinterpret_cast<float*>(sb + kXqXs)[ko >> 5] = amax / 32639.f;
+        reinterpret_cast<float*>(sb + kXqXs)[ko >> 5] = q8 ? amax / 127.f : amax / 32639.f;
         reinterpret_cast<float*>(sb + kXqS32)[ko >> 5] = fs;
         if (norm) reinterpret_cast<float*>(xq + xq_bytes(K))[idx >> 5] = ss;
     }
 }
 
 // Same, loading the weight from norm_w (nullptr: no norm).
-__device__ __forceinline__ void xq_store32(uint8_t* xq, float v, const float* norm_w, int K, int idx) {
+__device__ __forceinline__ void xq_store32(uint8_t* xq, float v, const float* norm_w, int K, int idx,
+                                           bool q8 = false) {
     const bool in = idx >= 0 && idx < K;
-    xq_store32w(xq, v, norm_w && in ? __ldg(norm_w + idx) : 1.f, norm_w != nullptr, K, idx);
+    xq_store32w(xq, v, norm_w && in ? __ldg(norm_w + idx) : 1.f, norm_w != nullptr, K, idx, q8);
 }
 
 // One warp quantises values [32·g, 32·g + 32) of src (global f32, written by
 // other CTAs: read through L2).
-__device__ __forceinline__ void xq_quantize_group(uint8_t* xq, const float* src, const float* norm_w, int K, int g) {
+__device__ __forceinline__ void xq_quantize_group(uint8_t* xq, const float* src, const float* norm_w, int K, int g,
+                                                  bool q8 = false) {
     const int idx = 32 * g + (threadIdx.x & 31);
-    xq_store32(xq, idx < K ? __ldcg(src + idx) : 0.f, norm_w, K, idx);
+    xq_store32(xq, idx < K ? __ldcg(src + idx) : 0.f, norm_w, K, idx, q8);
 }
 
 }  // namespace af

@@ -340,7 +340,7 @@ __device__ __forceinline__ float2 q6_unit(const uint8_t* u, const XQ6& x, int la
 // of shared scratch.
 template <int NIT, bool NORM>
 __device__ __forceinline__ void quantise_f4(float4 (&a)[NIT], const float4 (&w)[NORM ? NIT : 1], int nvec, float eps,
-                                            uint8_t* xqs, float* red) {
+                                            uint8_t* xqs, float* red, bool q8 = false) {
     static_assert(kCT % 8 == 0, "8 consecutive threads own one 32-value group");
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
@@ -372,16 +372,18 @@ __device__ __forceinline__ void quantise_f4(float4 (&a)[NIT], const float4 (&w)[
         amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
         amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
         amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));  // 8 threads = 32 values
-        // 16-bit grid of ±32639 so that hi = (q + 128) >> 8 stays within int8.
-        const float inv = amax > 0.f ? 32639.f / amax : 0.f;
+        // 16-bit grid of ±32639 so that hi = (q + 128) >> 8 stays within int8;
+        // q8: the Q8_0 block of the reference (see xq_store32w)
+        const float inv = amax > 0.f ? (q8 ? 127.f : 32639.f) / amax : 0.f;
+        const int qmax = q8 ? 127 : 32639;
         const float av[4] = {a[j].x, a[j].y, a[j].z, a[j].w};
         uint32_t hw = 0, lw = 0;
         int is = 0;
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             int q = __float2int_rn(av[e] * inv);
-            q = max(-32639, min(32639, q));
-            const int hi = (q + 128) >> 8;
+            q = max(-qmax, min(qmax, q));
+            const int hi = q8 ? 0 : (q + 128) >> 8;
             const int lo = q - hi * 256;
             hw |= (uint32_t)(hi & 0xFF) << (8 * e);
             lw |= (uint32_t)(lo & 0xFF) << (8 * e);
@@ -393,6 +395,7 @@ __device__ __forceinline__ void quantise_f4(float4 (&a)[NIT], const float4 (&w)[
         fs += __shfl_xor_sync(0xffffffffu, fs, 1);
         fs += __shfl_xor_sync(0xffffffffu, fs, 2);
         fs += __shfl_xor_sync(0xffffffffu, fs, 4);
+        if (q8) fs = (amax / 127.f) * (float)(is + __shfl_xor_sync(0xffffffffu, is, 4));
         if (v < nvec) {
             uint8_t* sb = xqs + (v >> 6) * kXqSb;
             const int ko = (4 * v) & 255;
@@ -400,7 +403,7 @@ __device__ __forceinline__ void quantise_f4(float4 (&a)[NIT], const float4 (&w)[
             *reinterpret_cast<uint32_t*>(sb + 256 + ko) = lw;
             if ((tid & 3) == 0) reinterpret_cast<int*>(sb + kXqI16)[ko >> 4] = is;
             if ((tid & 7) == 0) {
-                reinterpret_cast<float*>(sb + kXqXs)[ko >> 5] = amax / 32639.f;
+                reinterpret_cast<float*>(sb + kXqXs)[ko >> 5] = amax / (q8 ? 127.f : 32639.f);
                 reinterpret_cast<float*>(sb + kXqS32)[ko >> 5] = fs;
             }
         }
@@ -437,7 +440,7 @@ __device__ __forceinline__ void input_prologue_t(const GemvParams& p, uint8_t* x
             if (v < nvec) reinterpret_cast<float4*>(p.x_store)[v] = a[j];
         }
     }
-    quantise_f4<NIT, NORM>(a, w, nvec, p.eps, xqs, red);
+    quantise_f4<NIT, NORM>(a, w, nvec, p.eps, xqs, red, p.q8 != 0);
 }
 
 // Quantise the f32 input of p into the shared XQ layout (all consumer warps;
@@ -622,7 +625,8 @@ __device__ __forceinline__ bool consume(const GemvParams& p, int vbeg, int vend,
                 }
             }
             // the fragment's 32 rows are one 32-value group of q_out
-            if (p.q_out) xq_store32w(p.q_out, out, qw, p.q_norm_w != nullptr, p.seg[0].rows, evalid ? erow : -1);
+            if (p.q_out)
+                xq_store32w(p.q_out, out, qw, p.q_norm_w != nullptr, p.seg[0].rows, evalid ? erow : -1, p.q8 != 0);
         }
     }
     if (p.epi == EPI_ARGMAX) {

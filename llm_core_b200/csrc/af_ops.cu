@@ -138,7 +138,7 @@ cudaError_t weight_pack(void* d_dst, const void* d_src, int type, int rows, int 
 // key for the step (this is the step's first kernel).
 __global__ void embed_kernel(float* __restrict__ x, const uint8_t* __restrict__ W, int type, int cols,
                              int row_stride, const int* __restrict__ token, unsigned long long* argmax,
-                             uint8_t* xq, const float* xq_norm_w) {
+                             uint8_t* xq, const float* xq_norm_w, int q8) {
     pdl_launch_dependents();
     pdl_wait();
     if (argmax && blockIdx.x == 0 && threadIdx.x == 0) *argmax = 0ull;
@@ -151,13 +151,13 @@ __global__ void embed_kernel(float* __restrict__ x, const uint8_t* __restrict__ 
         __threadfence();
         __syncthreads();
         const int g = (blockIdx.x * blockDim.x) / 32 + (threadIdx.x >> 5);
-        if (g < cols / 32) xq_quantize_group(xq, x, xq_norm_w, cols, g);
+        if (g < cols / 32) xq_quantize_group(xq, x, xq_norm_w, cols, g, q8 != 0);
     }
 }
 
 cudaError_t embed_launch(float* x, const uint8_t* W, int type, int cols, int row_stride, const int* token,
                          unsigned long long* argmax, uint8_t* xq, const float* xq_norm_w, cudaStream_t st,
-                         bool pdl) {
+                         bool pdl, bool q8) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((cols + 255) / 256);
     cfg.blockDim = dim3(256);
@@ -167,7 +167,8 @@ cudaError_t embed_launch(float* x, const uint8_t* W, int type, int cols, int row
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, embed_kernel, x, W, type, cols, row_stride, token, argmax, xq, xq_norm_w);
+    return cudaLaunchKernelEx(&cfg, embed_kernel, x, W, type, cols, row_stride, token, argmax, xq, xq_norm_w,
+                              q8 ? 1 : 0);
 }
 
 // -------------------------------------------------- reference CUDA op set
@@ -276,6 +277,34 @@ cudaError_t af_gemv_f32(float* d_y, const void* d_w, int ggml_type, const float*
     p.K = cols;
     p.x = d_x;
     p.epi = EPI_STORE;
+    gemv_configure(p, gemv_grid());
+    AF_CUDA_TRY(gemv_init());
+    return gemv_launch(p, stream, false);
+}
+
+cudaError_t af_gemv_q8_f32(float* d_y, const void* d_w, int ggml_type, const float* d_x, int rows, int cols,
+                           cudaStream_t stream) {
+    if ((ggml_type != AF_GGML_Q4_K && ggml_type != AF_GGML_Q6_K) || cols <= 0 || cols % 256 || rows < 0 ||
+        cols > kGemvMaxK) {
+        set_last_error("af_gemv_q8_f32: need Q4_K/Q6_K weights, cols % 256 == 0, cols <= 12288");
+        return cudaErrorInvalidValue;
+    }
+    if ((reinterpret_cast<uintptr_t>(d_w) & 15) || (reinterpret_cast<uintptr_t>(d_x) & 15)) {
+        set_last_error("af_gemv_q8_f32: weights and x must be 16-byte aligned");
+        return cudaErrorInvalidValue;
+    }
+    if (rows == 0) return cudaSuccess;
+    GemvParams p = {};
+    p.seg[0].w = static_cast<const uint8_t*>(d_w);
+    p.seg[0].y = d_y;
+    p.seg[0].type = ggml_type;
+    p.seg[0].rows = rows;
+    p.seg[0].row_stride = dev_row_stride(ggml_type, cols);
+    p.nseg = 1;
+    p.K = cols;
+    p.x = d_x;
+    p.epi = EPI_STORE;
+    p.q8 = 1;
     gemv_configure(p, gemv_grid());
     AF_CUDA_TRY(gemv_init());
     return gemv_launch(p, stream, false);

@@ -59,10 +59,14 @@ __device__ __forceinline__ float embed_value(const uint8_t* __restrict__ W, int 
 cudaError_t weight_pack(void* d_dst, const void* d_src, int type, int rows, int cols, bool unpack, cudaStream_t st);
 cudaError_t embed_launch(float* x, const uint8_t* W, int type, int cols, int row_stride, const int* token,
                          unsigned long long* argmax, uint8_t* xq, const float* xq_norm_w, cudaStream_t st,
-                         bool pdl);
+                         bool pdl, bool q8 = false);
 
 // Prefill (af_prefill.cu): the tcgen05 dequant-GEMM Y[T][rows] = X[T][cols]·Wᵀ
 // and the row kernels of the batched prompt pass.
+// Batched dequant GEMV (af_bgemv.cu): y[B][rows] for 1 <= B <= 32 vectors.
+cudaError_t bgemv_launch(float* y, const uint8_t* w, int type, const float* x, int rows, int cols, int B,
+                         cudaStream_t st);
+bool bgemv_supported(int n_vec);
 cudaError_t prefill_gemm_launch(float* y, const uint8_t* w, int type, const float* x, int rows, int cols, int T,
                                 cudaStream_t st);
 cudaError_t prompt_embed_launch(float* x, const uint8_t* W, int type, int cols, int row_stride, const int* tokens,
@@ -91,6 +95,7 @@ struct AttnParams {
     int n_heads, n_kv_heads, head_dim, n_ctx, nsplit, qk_norm_order;
     float eps, scale;
     uint8_t* xq_out;       // optional: quantised copy of `out` for the next GEMV
+    int q8;                // xq_out as Q8_0 blocks (see xq_store32w)
 };
 
 cudaError_t attention_init();

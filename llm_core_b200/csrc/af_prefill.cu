@@ -466,6 +466,9 @@ PrefillScratch g_pf;
 
 cudaError_t prefill_gemm_launch(float* y, const uint8_t* w, int type, const float* x, int rows, int cols, int T,
                                 cudaStream_t st) {
+    // a few tokens stream the weights once through the batched GEMV instead
+    // (faster below ~32 tokens, and exact integer dots)
+    if (bgemv_supported(T)) return bgemv_launch(y, w, type, x, rows, cols, T, st);
     int dev = 0;
     AF_CUDA_TRY(cudaGetDevice(&dev));
     std::lock_guard<std::mutex> lock(g_pf.mu);

@@ -180,7 +180,7 @@ __device__ bool xchg_input_t(const StepParams& sp, const XchgParams& x, unsigned
         if (!kEarlyW)
             w[j] = v < nvec ? __ldg(reinterpret_cast<const float4*>(x.norm_w) + v) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    quantise_f4<NIT, true>(a, w, nvec, eps, xqs, red);
+    quantise_f4<NIT, true>(a, w, nvec, eps, xqs, red, sp.q8 != 0);
     bar_consumers();
     return true;
 }
@@ -210,7 +210,7 @@ __device__ __forceinline__ void copy_params(void* dst, const void* src, int byte
 
 // x = dequant(row token of the embedding) and its quantised, attn_norm-
 // weighted form for the first QKV GEMV: one warp per 32 values.
-__device__ void embed_phase(const StepParams& sp, int tok) {
+__device__ void embed_phase(const StepParams& sp, int tok, float* row, float* red) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (blockIdx.x == 0 && threadIdx.x == 0) *sp.key = 0ull;  // argmax of this step starts empty
     if (tok < 0 || tok >= sp.vocab) {  // never index outside the table
@@ -218,11 +218,38 @@ __device__ void embed_phase(const StepParams& sp, int tok) {
         tok = 0;
     }
     const int nb = sp.n_embd / 256, ng = sp.n_embd / 32;
+    if (sp.q8 && sp.xq && step_q8_exact_embed(sp.n_embd)) {
+        // Q8_0 input of layer 0, exactly as the reference forms it:
+        // rms_norm_out (src/models/llama_model.cpp:396-419) sums x² in 8
+        // interleaved FMA chains added in lane order, then xn = w·(x·inv_rms)
+        // is quantised; every CTA computes inv_rms itself (one row, cheap)
+        const int E = sp.n_embd;
+        for (int v = threadIdx.x; v < E; v += kCT) row[v] = embed_value(sp.tok_w, sp.tok_type, nb, sp.tok_stride, tok, v);
+        bar_consumers();
+        if (warp == 0) {
+            float acc = 0.f;
+            if (lane < 8)
+                for (int i = lane; i < E; i += 8) acc = fmaf(row[i], row[i], acc);
+            float ss = 0.f;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) ss += __shfl_sync(0xffffffffu, acc, k);
+            if (lane == 0) red[0] = 1.f / sqrtf(ss / (float)E + sp.eps);
+        }
+        bar_consumers();
+        const float inv = red[0];
+        for (int g = blockIdx.x * kCW + warp; g < ng; g += gridDim.x * kCW) {
+            const int v = 32 * g + lane;
+            const float a = row[v];
+            sp.x[v] = a;
+            xq_store32w(sp.xq, __ldg(sp.xq_norm_w + v) * (a * inv), 1.f, false, E, v, true);
+        }
+        return;
+    }
     for (int g = blockIdx.x * kCW + warp; g < ng; g += gridDim.x * kCW) {
         const int v = 32 * g + lane;
         const float a = embed_value(sp.tok_w, sp.tok_type, nb, sp.tok_stride, tok, v);
         sp.x[v] = a;
-        if (sp.xq) xq_store32(sp.xq, a, sp.xq_norm_w, sp.n_embd, v);
+        if (sp.xq) xq_store32(sp.xq, a, sp.xq_norm_w, sp.n_embd, v, sp.q8 != 0);
     }
 }
 
@@ -575,7 +602,7 @@ __device__ __forceinline__ void attn_item(const AttnParams& a, const AttnSmem& s
         // quantise this kv head's G*hd outputs (32-value groups) for the O GEMV
         const int g0 = kvh * G * hd / 32, ng = G * hd / 32;
         for (int k = warp; k < ng; k += kCW)
-            xq_store32(a.xq_out, s.ob[32 * k + lane], nullptr, a.n_heads * hd, 32 * (g0 + k) + lane);
+            xq_store32(a.xq_out, s.ob[32 * k + lane], nullptr, a.n_heads * hd, 32 * (g0 + k) + lane, a.q8 != 0);
     }
     if (tid == 0) AF_TRACE(tph, 7);
 }
@@ -685,7 +712,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) step_kernel(const __grid_cons
             if (i > 0 && !xin && !grid_wait(sp.bar, (unsigned)i * grid, abort)) break;
             if (threadIdx.x == 0) AF_TRACE(i, 0);
             if (kind == PH_EMBED) {
-                embed_phase(sp, tok);
+                embed_phase(sp, tok, reinterpret_cast<float*>(uni), red);
             } else {
                 if (ph.x.k_out >= 0) {  // row-parallel partial sums, sent to every rank
                     if (threadIdx.x == 0) {

@@ -37,6 +37,13 @@ constexpr int kStepAttnChunk = 64;      // KV positions per attention chunk
 constexpr int kStepAttnMaxSplit = 128;  // splits per kv head the attention merge stages in shared memory
 constexpr int kStepHdr = kGemvSmemHdr;  // mbarriers, flags, phase parameter copies, reduction scratch
 constexpr int kStepUnion = 40 * 1024;   // XQ input of a GEMV phase / attention scratch
+
+// With Q8_0 activations the embedding phase normalises the first layer's
+// input itself, in the reference's summation order (its embedding values are
+// a discrete grid, where the Q8 rounding of x·127/amax often sits exactly on
+// a tie, so the normalised values must be bit-identical); it stages the row
+// in the union area, so n_embd·4 bytes must fit there.
+__host__ __device__ inline bool step_q8_exact_embed(int n_embd) { return n_embd * 4 <= kStepUnion; }
 constexpr int kStepSmem = 227 * 1024;
 
 // Tensor-parallel exchanges (the outputs of the row-parallel O and down
@@ -74,6 +81,8 @@ struct StepParams {
     float* x;
     uint8_t* xq;
     const float* xq_norm_w;
+    int q8;                          // activations as Q8_0 blocks (see xq_store32w)
+    float eps;                       // RMSNorm epsilon (the Q8 embedding path normalises itself)
     // finalize
     unsigned long long* key;
     int* token;

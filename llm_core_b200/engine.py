@@ -106,7 +106,7 @@ class LlamaCudaModel:
 
     def __init__(self, path: str | None = None, *, config: ModelConfig | None = None, device: int = 0,
                  tp_rank: int = 0, tp_size: int = 1, nccl_id: bytes | None = None,
-                 max_context_len: int = 4096, tensors=None):
+                 max_context_len: int = 4096, tensors=None, q8_activations: bool = False):
         self.lib = _lib.load()
         if config is None:
             if path is None:
@@ -124,6 +124,8 @@ class LlamaCudaModel:
                 self.load_tensor(name, ggml_type, dims, data)
         elif path is not None:
             check(self.lib.af_engine_load_gguf(self.h, path.encode()), "af_engine_load_gguf")
+        if q8_activations:
+            check(self.lib.af_engine_set_q8_activations(self.h, 1), "af_engine_set_q8_activations")
         check(self.lib.af_engine_finalize(self.h), "af_engine_finalize")
 
     def load_tensor(self, name: str, ggml_type: int, dims, data: np.ndarray):
