@@ -39,6 +39,13 @@ sys.path.insert(0, ROOT)
 PROMPT_LEN = 128
 SEED = 0
 
+# DRAM bytes (read + write) of one step_kernel launch, measured by ncu on the
+# full workload (dram__bytes_read.sum + dram__bytes_write.sum, one pass; launch
+# 132 of `python bench.py --steps 3 --warmup 3 --no-cpu-baseline`, context
+# 132, single B200): 4.22 GB read + 5.77 MB written, 1.003x the algorithmic
+# bytes.  Reported as roofline.traffic for that workload only.
+STEP_KERNEL_DRAM_BYTES = {("llama2-7b", 1): 4_225_770_000}
+
 
 def env_int(k, d):
     try:
@@ -141,21 +148,64 @@ def open_ref(path: str, threads: int):
         return RefLib().open(path, threads=threads, f32_mode=False, max_ctx=4096)
 
 
-def cpu_baseline_sample(path: str, steps: int, threads: int) -> dict | None:
-    """The reference CPU decode (production Q8_0 path), `steps` tokens from position 0."""
+def bench_prompt(vocab: int):
+    """The 128-token uniform-random prompt both arms decode after (BOS first)."""
+    rng = np.random.default_rng(1234)
+    return [1] + rng.integers(0, vocab, PROMPT_LEN).tolist()
+
+
+def host_cpu() -> dict:
+    """The host CPU the CPU numbers ran on: model name and the affinity mask."""
+    model = "unknown"
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if ln.startswith("model name"):
+                model = ln.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    try:
+        aff = sorted(os.sched_getaffinity(0))
+    except AttributeError:
+        aff = list(range(os.cpu_count() or 1))
+    # compress the mask into ranges, e.g. "0-63"
+    parts, i = [], 0
+    while i < len(aff):
+        j = i
+        while j + 1 < len(aff) and aff[j + 1] == aff[j] + 1:
+            j += 1
+        parts.append(f"{aff[i]}-{aff[j]}" if j > i else f"{aff[i]}")
+        i = j + 1
+    return {"cpu_model": model, "affinity": ",".join(parts), "threads": len(aff)}
+
+
+def ref_decode_after_prompt(path: str, threads: int, vocab: int, warmup: int, steps: int):
+    """The reference's own CPU path on the b200 arm's workload: prefill the
+    same 128-token prompt (llama_forward_batch), `warmup` untimed decode
+    steps, then `steps` timed ones — context PROMPT_LEN+1+warmup .. +steps.
+    Returns (seconds, first timed position)."""
+    prompt = bench_prompt(vocab)
+    ref = open_ref(path, threads)
+    lg = ref.forward_batch(prompt, 0)
+    tok = int(np.argmax(lg))
+    ref.time_decode(tok, warmup)
+    p0 = len(prompt) + warmup
+    secs = ref.time_decode(tok, steps)
+    ref.close()
+    return secs, p0
+
+
+def cpu_baseline_sample(path: str, steps: int, threads: int, vocab: int, warmup: int) -> dict | None:
+    """The reference CPU decode (production Q8_0 path) after the bench prompt."""
     from oracle import RefLib
     if not RefLib.available():
         return None
-    ref = open_ref(path, threads)
-    ref.set_n_past(0)
-    ref.time_decode(1, 2)  # warm the r8 weight cache / page in
-    ref.set_n_past(0)
-    secs = ref.time_decode(1, steps)
-    ref.close()
+    secs, p0 = ref_decode_after_prompt(path, threads, vocab, warmup, steps)
     return {"value": steps / secs, "unit": "tok/s", "cores": threads, "kind": "reference",
+            **host_cpu(),
             "sample": f"{steps} decode steps of the reference's own CPU path (Q8_0 activations, r8 repack, "
-                      f"oracle/_ref built from the unmodified sources) at context 1..{steps}, "
-                      f"{threads} threads, random-init Llama-2-7B Q4_K_M"}
+                      f"oracle/_ref built from the unmodified sources) at context {p0}..{p0 + steps} after "
+                      f"the same 128-token prompt, {threads} threads, random-init Llama-2-7B Q4_K_M"}
 
 
 def run_reference(args):
@@ -170,24 +220,25 @@ def run_reference(args):
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libaxref.so was not built "
                           "(reference sources absent when the repo was built)"}))
         return 0
-    ref = open_ref(path, threads)
-    ref.set_n_past(0)
-    ref.time_decode(1, max(1, args.warmup))
-    # each timed step: one reference decode token (context grows from W)
-    secs = ref.time_decode(1, args.steps)
-    ref.close()
-    val = args.steps / secs
     cfg = gguf.PRESETS[args.model]
+    # the b200 arm's workload: the same prompt, then W untimed and K timed
+    # decode tokens over the same context positions
+    secs, p0 = ref_decode_after_prompt(path, threads, cfg.vocab, args.warmup, args.steps)
+    val = args.steps / secs
     line = {
         "impl": "reference", "metric": "bs=1 decode tok/s", "value": round(val, 3), "unit": "tok/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(1000 * secs / args.steps, 3), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "q8_0-int8 dot + f32", "data": "synthetic (seeded random-init GGUF)",
-        "config": {"workload": f"{cfg.name} Q4_K_M bs=1 greedy decode", "global_batch": 1,
-                   "seq_len": PROMPT_LEN, "parallelism": "cpu threads"},
+        "config": {"workload": f"{cfg.name} Q4_K_M bs=1 greedy decode",
+                   "model": cfg.name, "global_batch": 1, "seq_len": PROMPT_LEN,
+                   "context": f"{p0}..{p0 + args.steps}",
+                   "parallelism": "cpu threads",
+                   "l2": "inputs larger than L2 (4.07 GB weights per step)"},
         "cpu_baseline": {"value": round(val, 3), "unit": "tok/s", "cores": threads, "kind": "reference",
-                         "sample": f"{args.steps} decode steps at context {args.warmup}..{args.warmup + args.steps} "
-                                   "(production Q8_0 path, all host threads)"},
+                         **host_cpu(),
+                         "sample": f"{args.steps} decode steps at context {p0}..{p0 + args.steps} after the "
+                                   "128-token prompt (production Q8_0 path, all host threads)"},
         "e2e": {"value": round(val, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line))
@@ -217,8 +268,7 @@ def run_b200(args):
     m = LlamaCudaModel(path, device=local, tp_rank=rank, tp_size=world, nccl_id=nid)
     t_load = time.time() - t_load
     cfg = gguf.PRESETS[args.model]
-    rng = np.random.default_rng(1234)
-    prompt = [1] + rng.integers(0, cfg.vocab, PROMPT_LEN).tolist()
+    prompt = bench_prompt(cfg.vocab)
     nxt, _ = m.prefill(prompt, 0, want_logits=False)
     pos = len(prompt)
     stream = torch.cuda.ExternalStream(m.stream)
@@ -292,17 +342,11 @@ def run_b200(args):
     achieved = kb / (k_us / 1e6) / 1e9 if k_us > 0 else 0.0
     if rank != 0:
         return 0
-    traffic = None
-    tp_file = os.path.join(ROOT, "profiles", "dram_traffic_per_launch.json")
-    if os.path.exists(tp_file):
-        try:
-            traffic = json.load(open(tp_file)).get(args.model, {}).get(str(world))
-        except Exception:
-            traffic = None
+    traffic = STEP_KERNEL_DRAM_BYTES.get((args.model, world)) if m.kernels_per_step == 1 else None
     threads = os.cpu_count() or 1
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline_sample(path, args.cpu_steps, threads)
+        cpu = cpu_baseline_sample(path, args.cpu_steps, threads, cfg.vocab, 2)
     line = {
         "metric": "bs=1 decode tok/s", "value": round(value, 2), "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
