@@ -492,7 +492,36 @@ def run_prefill_sweep(args):
                           "frac": round(tf / peak, 4), "peak": f"{peak} ({kind}, bf16 burst; f16 operands run at the same rate)"}))
         del w, src, x, y
         torch.cuda.empty_cache()
+    if not args.shapes:
+        run_prompt_pass(args, peak, kind)
     return 0
+
+
+def run_prompt_pass(args, peak, kind):
+    """The whole batched prompt pass of the 7B model (af_engine_prefill_batched:
+    prefill GEMMs, row kernels, one causal-attention launch per layer, the
+    last token through the decode step) on a 512-token prompt: time to first
+    token, and the same prompt fed token by token for comparison.  Host wall
+    clock around the synchronous calls, after one untimed pass each."""
+    from llm_core_b200 import gguf
+    from llm_core_b200.engine import LlamaCudaModel
+    cfg = gguf.PRESETS[args.model]
+    path = model_file(args.model, 0, None)
+    m = LlamaCudaModel(path)
+    rng = np.random.default_rng(7)
+    T = 512
+    prompt = [1] + rng.integers(0, cfg.vocab, T - 1).tolist()
+    res = {}
+    for batched in (True, False):
+        m.prefill(prompt, 0, want_logits=False, batched=batched)
+        t0 = time.perf_counter()
+        m.prefill(prompt, 0, want_logits=False, batched=batched)
+        res[batched] = time.perf_counter() - t0
+    m.close()
+    print(json.dumps({"kernel": "prompt pass (af_engine_prefill_batched)", "model": cfg.name, "tokens": T,
+                      "ttft_ms": round(1000 * res[True], 2), "prefill_tok_s": round(T / res[True], 1),
+                      "token_by_token_ms": round(1000 * res[False], 2),
+                      "speedup_vs_token_by_token": round(res[False] / res[True], 2)}))
 
 
 def main():

@@ -77,6 +77,17 @@ cudaError_t af_weight_unpack(void* d_dst, const void* d_src, int ggml_type, int 
 cudaError_t af_gemv_f32(float* d_y, const void* d_w, int ggml_type, const float* d_x, int rows,
                         int cols, cudaStream_t stream);
 
+/* The reference CUDA backend's GEMV entry with its exact arguments:
+ * q4km_gemv_f32(y, w, x, rows, cols, row_bytes, stream)
+ * (src/backend/cuda/cuda_kernels.hpp:13-19, called for MATMUL by
+ * cuda_backend.cu:98-111), w = raw GGUF Q4_K_M rows on the device.  Each call
+ * repacks w into a shared device buffer and runs af_gemv_f32; callers that
+ * keep a matrix resident pack it once with af_weight_pack instead (the
+ * engine and the "cuda" IBackend do).  row_bytes must be cols/256*144 (GGUF
+ * rows are contiguous). */
+cudaError_t af_q4km_gemv_f32(float* d_y, const uint8_t* d_w, const float* d_x, int rows, int cols,
+                             size_t row_bytes, cudaStream_t stream);
+
 /* The same GEMV with x quantised to the reference's Q8_0 blocks first
  * (quantize_q8_avx2, src/backend/cpu_x86/kernels/quant_q8_avx2.cpp:33-84:
  * d = amax/127, q = round-half-even(x·127/amax) per 32 values): the

@@ -75,6 +75,7 @@ def load() -> C.CDLL:
         "af_weight_unpack": (i, [vp, vp, i, i, i, vp]),
         "af_gemv_f32": (i, [vp, vp, i, vp, i, i, vp]),
         "af_gemv_q8_f32": (i, [vp, vp, i, vp, i, i, vp]),
+        "af_q4km_gemv_f32": (i, [vp, vp, vp, i, i, C.c_size_t, vp]),
         "af_prefill_gemm_f32": (i, [vp, vp, i, vp, i, i, i, vp]),
         "af_gemv_batched_f32": (i, [vp, vp, i, vp, i, i, i, vp]),
         "af_rms_norm_f32": (i, [vp, vp, vp, i, f, vp]),

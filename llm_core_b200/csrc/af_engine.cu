@@ -1128,7 +1128,13 @@ cudaError_t af_engine_prefill_batched(af_engine* e, const int32_t* h_tokens, int
             if (L.bk) ENG_TRY(rows_bias_launch(k, L.bk, KD, T, e->stream));
             if (L.bv) ENG_TRY(rows_bias_launch(v, L.bv, KD, T, e->stream));
             const size_t lsz = (size_t)c.n_ctx * KD;
-            for (int t = 0; t < T; ++t) {
+            if (prompt_attention_supported(e->hd)) {
+                // all T tokens at once: RoPE / Q-K norms, the KV rows, causal attention
+                ENG_TRY(prompt_attention_launch(q, k, v, e->kcache + (size_t)l * lsz, e->vcache + (size_t)l * lsz, att,
+                                                e->cos_t, e->sin_t, L.q_norm, L.k_norm, T, pos0, e->Hl, e->KVl, e->hd,
+                                                c.qk_norm_order, c.eps, e->stream));
+            }
+            for (int t = 0; t < T && !prompt_attention_supported(e->hd); ++t) {
                 AttnParams a = {};
                 a.q = q + (size_t)t * QD;
                 a.k = k + (size_t)t * KD;

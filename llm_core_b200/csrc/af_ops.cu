@@ -2,6 +2,7 @@
 // regroup, embedding-row dequant, and the reference CUDA backend's op set
 // (RMSNorm, SiLU, Mul, RoPE; src/backend/cuda/cuda_kernels.hpp:8-19).
 #include <cstdlib>
+#include <mutex>
 #include <string>
 
 #include "af_gemv.cuh"
@@ -280,6 +281,47 @@ cudaError_t af_gemv_f32(float* d_y, const void* d_w, int ggml_type, const float*
     gemv_configure(p, gemv_grid());
     AF_CUDA_TRY(gemv_init());
     return gemv_launch(p, stream, false);
+}
+
+// Packed copy of the last raw matrix af_q4km_gemv_f32 was given, grown on
+// demand (cudaMalloc: not during stream capture; calls on one device share it).
+namespace {
+std::mutex g_raw_mu;
+int g_raw_dev = -1;
+void* g_raw_packed = nullptr;
+size_t g_raw_bytes = 0;
+}  // namespace
+
+cudaError_t af_q4km_gemv_f32(float* d_y, const uint8_t* d_w, const float* d_x, int rows, int cols, size_t row_bytes,
+                             cudaStream_t stream) {
+    if (cols <= 0 || cols % 256 || rows < 0 || cols > kGemvMaxK ||
+        row_bytes != (size_t)dev_row_stride(AF_GGML_Q4_K, cols)) {
+        set_last_error("af_q4km_gemv_f32: need cols % 256 == 0, cols <= 12288 and row_bytes == cols/256*144");
+        return cudaErrorInvalidValue;
+    }
+    if ((reinterpret_cast<uintptr_t>(d_w) & 15) || (reinterpret_cast<uintptr_t>(d_x) & 15)) {
+        set_last_error("af_q4km_gemv_f32: weights and x must be 16-byte aligned");
+        return cudaErrorInvalidValue;
+    }
+    if (rows == 0) return cudaSuccess;
+    int dev = 0;
+    AF_CUDA_TRY(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lock(g_raw_mu);
+    const size_t need = packed_bytes(AF_GGML_Q4_K, rows, cols);
+    if (g_raw_dev != dev) {
+        g_raw_dev = dev;
+        g_raw_packed = nullptr;  // a buffer of another device is not reused (it leaks with the process)
+        g_raw_bytes = 0;
+    }
+    if (g_raw_bytes < need) {
+        if (g_raw_packed) AF_CUDA_TRY(cudaFree(g_raw_packed));
+        g_raw_packed = nullptr;
+        g_raw_bytes = 0;
+        AF_CUDA_TRY(cudaMalloc(&g_raw_packed, need));
+        g_raw_bytes = need;
+    }
+    AF_CUDA_TRY(weight_pack(g_raw_packed, d_w, AF_GGML_Q4_K, rows, cols, false, stream));
+    return af_gemv_f32(d_y, g_raw_packed, AF_GGML_Q4_K, d_x, rows, cols, stream);
 }
 
 cudaError_t af_gemv_q8_f32(float* d_y, const void* d_w, int ggml_type, const float* d_x, int rows, int cols,

@@ -69,6 +69,13 @@ cudaError_t bgemv_launch(float* y, const uint8_t* w, int type, const float* x, i
 bool bgemv_supported(int n_vec);
 cudaError_t prefill_gemm_launch(float* y, const uint8_t* w, int type, const float* x, int rows, int cols, int T,
                                 cudaStream_t st);
+// Batched prompt attention (af_prefill.cu): per-head norms + RoPE of q/k,
+// K/V rows stored at positions pos0.., then causal attention of the T tokens
+// (head_dim 64 or 128).
+bool prompt_attention_supported(int hd);
+cudaError_t prompt_attention_launch(float* q, const float* k, const float* v, float* kc, float* vc, float* out,
+                                   const float* cos_t, const float* sin_t, const float* q_norm, const float* k_norm,
+                                   int T, int pos0, int H, int KV, int hd, int qk_order, float eps, cudaStream_t st);
 cudaError_t prompt_embed_launch(float* x, const uint8_t* W, int type, int cols, int row_stride, const int* tokens,
                                 int T, cudaStream_t st);
 cudaError_t rows_rmsnorm_launch(float* y, const float* x, const float* w, int n, int T, float eps, cudaStream_t st);

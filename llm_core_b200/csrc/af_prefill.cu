@@ -40,6 +40,7 @@
 //  issuing, and still frees its tensor memory.
 #include <cuda_fp16.h>
 
+#include <cmath>
 #include <cstdint>
 #include <mutex>
 
@@ -451,6 +452,157 @@ __global__ void rows_add_kernel(float* __restrict__ x, const float* __restrict__
     if (i < count) x[i] += y[i];
 }
 
+// ---- causal attention of the batched prompt pass
+
+// Per (token, head row): the Q/K head norm (qwen3 before RoPE, hunyuan after
+// it), half-split RoPE at the token's position, and for the K/V heads the
+// store of the rotated k and the v row into the layer's cache — the RoPE and
+// KV-fill loop of llama_forward_batch (src/models/llama_model.cpp:1387-1408).
+// Block (t, r): rows r < H are q heads (rotated in place), r >= H kv heads.
+__global__ void prompt_rope_kernel(float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
+                                   float* __restrict__ kc, float* __restrict__ vc, const float* __restrict__ cos_t,
+                                   const float* __restrict__ sin_t, const float* __restrict__ q_norm,
+                                   const float* __restrict__ k_norm, int pos0, int H, int KV, int hd, int qk_order,
+                                   float eps) {
+    __shared__ float row[256];
+    __shared__ float red[32];
+    const int t = blockIdx.x, r = blockIdx.y, tid = threadIdx.x;
+    const int pos = pos0 + t, half = hd / 2, KD = KV * hd;
+    const bool isq = r < H;
+    const int kvh = r - H;
+    const float* src = isq ? q + ((size_t)t * H + r) * hd : k + (size_t)t * KD + (size_t)kvh * hd;
+    const float* nw = isq ? q_norm : k_norm;
+    for (int i = tid; i < hd; i += blockDim.x) row[i] = src[i];
+    __syncthreads();
+    // per-head RMSNorm of hd values (rms_norm_avx2 per head): x = w·(x·s)
+    auto head_norm = [&]() {
+        float ss = 0.f;
+        for (int i = tid; i < hd; i += blockDim.x) ss += row[i] * row[i];
+        ss = warp_sum(ss);
+        if ((tid & 31) == 0) red[tid >> 5] = ss;
+        __syncthreads();
+        float tot = 0.f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) tot += red[w];
+        const float sc = 1.f / sqrtf(tot / (float)hd + eps);
+        __syncthreads();
+        for (int i = tid; i < hd; i += blockDim.x) row[i] = nw[i] * (row[i] * sc);
+        __syncthreads();
+    };
+    if (qk_order == 1 && nw) head_norm();
+    for (int i = tid; i < half; i += blockDim.x) {
+        const float c = cos_t[(size_t)pos * half + i], sn = sin_t[(size_t)pos * half + i];
+        const float x0 = row[i], x1 = row[i + half];
+        row[i] = x0 * c - x1 * sn;
+        row[i + half] = x0 * sn + x1 * c;
+    }
+    __syncthreads();
+    if (qk_order == 2 && nw) head_norm();
+    if (isq) {
+        float* dst = q + ((size_t)t * H + r) * hd;
+        for (int i = tid; i < hd; i += blockDim.x) dst[i] = row[i];
+    } else {
+        float* kd = kc + (size_t)pos * KD + (size_t)kvh * hd;
+        float* vd = vc + (size_t)pos * KD + (size_t)kvh * hd;
+        const float* vs = v + (size_t)t * KD + (size_t)kvh * hd;
+        for (int i = tid; i < hd; i += blockDim.x) {
+            kd[i] = row[i];
+            vd[i] = vs[i];
+        }
+    }
+}
+
+constexpr int kPaQ = 16;       // queries per block
+constexpr int kPaK = 32;       // key positions per tile
+constexpr int kPaThreads = 128;
+
+// Causal attention of T prompt tokens at positions pos0 .. pos0+T-1 for one
+// query head and a block of kPaQ tokens: token t attends to cache positions
+// 0 .. pos0+t (the reference's per-token loop, llama_model.cpp:1410-1425:
+// scores q·k·scale, softmax, Σ p·v), here as an online softmax over tiles of
+// kPaK positions (fp32 throughout).  Thread (i = tid / 8, g = tid % 8) holds
+// the 4 scores of query i at positions g, g+8, g+16, g+24 of a tile and the
+// output values [g·HD/8, (g+1)·HD/8) of query i.
+template <int HD>
+__global__ void __launch_bounds__(kPaThreads) prompt_attn_kernel(const float* __restrict__ q, const float* __restrict__ kc,
+                                                               const float* __restrict__ vc, float* __restrict__ out,
+                                                               int T, int pos0, int H, int KV, float scale) {
+    constexpr int DPT = HD / 8;
+    __shared__ float Qs[kPaQ][HD];
+    __shared__ float Ks[kPaK][HD + 1];
+    __shared__ float Vs[kPaK][HD];
+    __shared__ float Ps[kPaQ][kPaK];
+    const int h = blockIdx.x, qb = blockIdx.y, tid = threadIdx.x;
+    const int G = H / KV, kvh = h / G, KD = KV * HD;
+    const int i = tid >> 3, g = tid & 7;
+    const int t0 = qb * kPaQ;
+    const int nq = min(kPaQ, T - t0);
+    for (int x = tid; x < kPaQ * HD; x += kPaThreads) {
+        const int qi = x / HD, d = x % HD;
+        Qs[qi][d] = qi < nq ? q[((size_t)(t0 + qi) * H + h) * HD + d] : 0.f;
+    }
+    const int my_pos = pos0 + t0 + min(i, nq - 1);  // last position query i attends to
+    const int last = pos0 + t0 + nq - 1;            // the block's last position
+    float o[DPT];
+#pragma unroll
+    for (int e = 0; e < DPT; ++e) o[e] = 0.f;
+    float m = -INFINITY, l = 0.f;
+    for (int p0 = 0; p0 <= last; p0 += kPaK) {
+        __syncthreads();
+        for (int x = tid; x < kPaK * HD; x += kPaThreads) {
+            const int j = x / HD, d = x % HD, p = p0 + j;
+            const bool in = p <= last;
+            Ks[j][d] = in ? kc[(size_t)p * KD + (size_t)kvh * HD + d] : 0.f;
+            Vs[j][d] = in ? vc[(size_t)p * KD + (size_t)kvh * HD + d] : 0.f;
+        }
+        __syncthreads();
+        float sc[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) sc[r] = 0.f;
+        for (int d = 0; d < HD; ++d) {
+            const float qv = Qs[i][d];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) sc[r] = fmaf(qv, Ks[g + 8 * r][d], sc[r]);
+        }
+        float tmax = -INFINITY;
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const int p = p0 + g + 8 * r;
+            sc[r] = p <= my_pos ? sc[r] * scale : -INFINITY;
+            tmax = fmaxf(tmax, sc[r]);
+        }
+        // the 8 lanes of query i are consecutive: reduce among them
+#pragma unroll
+        for (int off = 1; off < 8; off <<= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, off));
+        const float mn = fmaxf(m, tmax);
+        const float corr = m == -INFINITY ? 0.f : expf(m - mn);
+        float ps = 0.f;
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const float pv = sc[r] == -INFINITY ? 0.f : expf(sc[r] - mn);
+            Ps[i][g + 8 * r] = pv;
+            ps += pv;
+        }
+#pragma unroll
+        for (int off = 1; off < 8; off <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
+        l = l * corr + ps;
+        m = mn;
+        __syncwarp();
+#pragma unroll
+        for (int e = 0; e < DPT; ++e) o[e] *= corr;
+        for (int j = 0; j < kPaK; ++j) {
+            const float pj = Ps[i][j];
+#pragma unroll
+            for (int e = 0; e < DPT; ++e) o[e] = fmaf(pj, Vs[j][g * DPT + e], o[e]);
+        }
+    }
+    if (i < nq) {
+        const float inv = 1.f / l;
+        float* dst = out + ((size_t)(t0 + i) * H + h) * HD + g * DPT;
+#pragma unroll
+        for (int e = 0; e < DPT; ++e) dst[e] = o[e] * inv;
+    }
+}
+
 // Staging buffers of X, grown on demand (cudaMalloc: not during stream capture).
 struct PrefillScratch {
     std::mutex mu;
@@ -502,6 +654,22 @@ cudaError_t prefill_gemm_launch(float* y, const uint8_t* w, int type, const floa
     const dim3 grid((rows + kPfM - 1) / kPfM, ntile);
     prefill_gemm_kernel<kPfStages><<<grid, kPfThreads, pf_smem<kPfStages>(), st>>>(y, w, type, g_pf.xp, g_pf.xexp, rows,
                                                                                  cols, T);
+    return cudaGetLastError();
+}
+
+bool prompt_attention_supported(int hd) { return hd == 64 || hd == 128; }
+
+cudaError_t prompt_attention_launch(float* q, const float* k, const float* v, float* kc, float* vc, float* out,
+                                   const float* cos_t, const float* sin_t, const float* q_norm, const float* k_norm,
+                                   int T, int pos0, int H, int KV, int hd, int qk_order, float eps, cudaStream_t st) {
+    if (!prompt_attention_supported(hd)) return cudaErrorNotSupported;
+    prompt_rope_kernel<<<dim3(T, H + KV), 128, 0, st>>>(q, k, v, kc, vc, cos_t, sin_t, q_norm, k_norm, pos0, H, KV, hd,
+                                                       qk_order, eps);
+    AF_CUDA_TRY(cudaGetLastError());
+    const dim3 grid(H, (T + kPaQ - 1) / kPaQ);
+    const float scale = 1.f / std::sqrt((float)hd);
+    if (hd == 64) prompt_attn_kernel<64><<<grid, kPaThreads, 0, st>>>(q, kc, vc, out, T, pos0, H, KV, scale);
+    else prompt_attn_kernel<128><<<grid, kPaThreads, 0, st>>>(q, kc, vc, out, T, pos0, H, KV, scale);
     return cudaGetLastError();
 }
 

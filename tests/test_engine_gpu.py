@@ -240,3 +240,44 @@ def test_qwen25_3b_long_context(gpu, kv):
     m.close()
     assert errs.max() < LOGITS_TOL, errs.max()
     assert agree >= TOP1_MIN, agree
+
+
+@pytest.mark.parametrize("preset,seed,pos0,n", [("tiny", 2, 0, 97), ("tiny-qwen", 6, 0, 60), ("small", 7, 0, 130),
+                                               ("tiny-qwen3", 9, 0, 50), ("tiny", 3, 20, 70)])
+def test_batched_prefill_matches_reference_forward_batch(gpu, preset, seed, pos0, n):
+    """The batched prompt pass (prefill GEMMs + one causal-attention launch per
+    layer) against the reference's own batched pass llama_forward_batch
+    (src/models/llama_model.cpp:1339-1462, F32-activation mode): logits of the
+    last prompt position within the logits bar, then 16 greedy tokens equal.
+    pos0 > 0 continues a context whose first tokens went token by token on
+    both sides."""
+    if not RefLib.available():
+        pytest.skip("reference library not built")
+    from llm_core_b200.engine import read_config
+    path = model_path(preset, seed)
+    cfg = read_config(path)
+    rng = np.random.default_rng(500 + seed)
+    head = [1] + rng.integers(0, cfg.vocab, pos0 - 1).tolist() if pos0 else []
+    prompt = rng.integers(0, cfg.vocab, n).tolist() if pos0 else [1] + rng.integers(0, cfg.vocab, n - 1).tolist()
+    ref = RefLib().open(path, threads=4, f32_mode=True)
+    for p, tok in enumerate(head):
+        ref.forward_token(tok, p)
+    want = ref.forward_batch(prompt, pos0)
+    m = LlamaCudaModel(path)
+    for p, tok in enumerate(head):
+        m.step(tok, p)
+    nxt, got = m.prefill(prompt, pos0, batched=True)
+    assert rel_l2(got, want) < LOGITS_TOL, rel_l2(got, want)
+    assert nxt == int(np.argmax(want))
+    # greedy continuation: both sides decode 16 tokens token by token
+    ids, p, tok = [], pos0 + n, nxt
+    rids, rtok = [], int(np.argmax(want))
+    ref.set_n_past(pos0 + n)
+    for i in range(16):
+        ids.append(tok)
+        rids.append(rtok)
+        tok, _ = m.step(tok, p + i)
+        rtok = int(np.argmax(ref.forward_token(rtok, p + i)))
+    ref.close()
+    m.close()
+    assert ids == rids

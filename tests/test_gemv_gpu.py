@@ -131,3 +131,23 @@ def test_reference_op_set(gpu):
     qh = q.reshape(4, 64)
     exp = np.concatenate([qh[:, :32] * c[17] - qh[:, 32:] * s[17], qh[:, :32] * s[17] + qh[:, 32:] * c[17]], 1)
     np.testing.assert_allclose(qd.cpu().numpy().reshape(4, 64), exp, rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("rows,cols", [(2048, 2048), (1000, 4096), (37, 512)])
+def test_q4km_gemv_on_raw_gguf_rows(gpu, rows, cols):
+    """af_q4km_gemv_f32 takes the reference backend's arguments — raw GGUF
+    Q4_K_M rows and row_bytes (cuda_kernels.hpp:13-19) — and matches the
+    oracle's F32 GEMV; a row_bytes that is not the GGUF row size is refused."""
+    import torch
+    rng = np.random.default_rng(rows + cols)
+    W = gguf.random_q4k(rng, rows * cols // 256).reshape(-1)
+    x = rng.standard_normal(cols).astype(np.float32)
+    wd, xd = dev(W), dev(x)
+    y = torch.full((rows,), float("nan"), dtype=torch.float32, device="cuda")
+    rb = cols // 256 * 144
+    assert gpu.af_q4km_gemv_f32(y.data_ptr(), wd.data_ptr(), xd.data_ptr(), rows, cols, rb, None) == 0
+    got = y.cpu().numpy()
+    want = COracle().gemv(W, gguf.GGML_Q4_K, x, rows)
+    assert rel_l2(got, want) < GEMV_TOL and rel_l2(got, want) < 1e-4
+    assert gpu.af_q4km_gemv_f32(y.data_ptr(), wd.data_ptr(), xd.data_ptr(), rows, cols, rb + 16, None) != 0
+    assert b"row_bytes" in gpu.af_last_error()
