@@ -521,24 +521,27 @@ constexpr int kPaThreads = 128;
 // scores q·k·scale, softmax, Σ p·v), here as an online softmax over tiles of
 // kPaK positions (fp32 throughout).  Thread (i = tid / 8, g = tid % 8) holds
 // the 4 scores of query i at positions g, g+8, g+16, g+24 of a tile and the
-// output values [g·HD/8, (g+1)·HD/8) of query i.
+// output columns 32c + 4g .. 32c + 4g + 3 (c = 0 .. HD/32 - 1) of query i.
 template <int HD>
 __global__ void __launch_bounds__(kPaThreads) prompt_attn_kernel(const float* __restrict__ q, const float* __restrict__ kc,
                                                                const float* __restrict__ vc, float* __restrict__ out,
                                                                int T, int pos0, int H, int KV, float scale) {
     constexpr int DPT = HD / 8;
-    __shared__ float Qs[kPaQ][HD];
-    __shared__ float Ks[kPaK][HD + 1];
-    __shared__ float Vs[kPaK][HD];
+    constexpr int KP = HD + 4;  // padded K rows: the 8 key rows a warp reads at once sit in distinct banks
+    __shared__ __align__(16) float Qs[kPaQ][HD];
+    __shared__ __align__(16) float Ks[kPaK][KP];
+    __shared__ __align__(16) float Vs[kPaK][HD];
     __shared__ float Ps[kPaQ][kPaK];
     const int h = blockIdx.x, qb = blockIdx.y, tid = threadIdx.x;
     const int G = H / KV, kvh = h / G, KD = KV * HD;
     const int i = tid >> 3, g = tid & 7;
     const int t0 = qb * kPaQ;
     const int nq = min(kPaQ, T - t0);
-    for (int x = tid; x < kPaQ * HD; x += kPaThreads) {
-        const int qi = x / HD, d = x % HD;
-        Qs[qi][d] = qi < nq ? q[((size_t)(t0 + qi) * H + h) * HD + d] : 0.f;
+    for (int x = tid; x < kPaQ * HD / 4; x += kPaThreads) {
+        const int qi = x / (HD / 4), d = 4 * (x % (HD / 4));
+        *reinterpret_cast<float4*>(&Qs[qi][d]) =
+            qi < nq ? *reinterpret_cast<const float4*>(q + ((size_t)(t0 + qi) * H + h) * HD + d)
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     const int my_pos = pos0 + t0 + min(i, nq - 1);  // last position query i attends to
     const int last = pos0 + t0 + nq - 1;            // the block's last position
@@ -548,20 +551,29 @@ __global__ void __launch_bounds__(kPaThreads) prompt_attn_kernel(const float* __
     float m = -INFINITY, l = 0.f;
     for (int p0 = 0; p0 <= last; p0 += kPaK) {
         __syncthreads();
-        for (int x = tid; x < kPaK * HD; x += kPaThreads) {
-            const int j = x / HD, d = x % HD, p = p0 + j;
+        for (int x = tid; x < kPaK * HD / 4; x += kPaThreads) {
+            const int j = x / (HD / 4), d = 4 * (x % (HD / 4)), p = p0 + j;
             const bool in = p <= last;
-            Ks[j][d] = in ? kc[(size_t)p * KD + (size_t)kvh * HD + d] : 0.f;
-            Vs[j][d] = in ? vc[(size_t)p * KD + (size_t)kvh * HD + d] : 0.f;
+            const size_t off = (size_t)p * KD + (size_t)kvh * HD + d;
+            const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+            *reinterpret_cast<float4*>(&Ks[j][d]) = in ? *reinterpret_cast<const float4*>(kc + off) : z;
+            *reinterpret_cast<float4*>(&Vs[j][d]) = in ? *reinterpret_cast<const float4*>(vc + off) : z;
         }
         __syncthreads();
         float sc[4];
 #pragma unroll
         for (int r = 0; r < 4; ++r) sc[r] = 0.f;
-        for (int d = 0; d < HD; ++d) {
-            const float qv = Qs[i][d];
+#pragma unroll 4
+        for (int d = 0; d < HD; d += 4) {
+            const float4 qv = *reinterpret_cast<const float4*>(&Qs[i][d]);
 #pragma unroll
-            for (int r = 0; r < 4; ++r) sc[r] = fmaf(qv, Ks[g + 8 * r][d], sc[r]);
+            for (int r = 0; r < 4; ++r) {
+                const float4 kv = *reinterpret_cast<const float4*>(&Ks[g + 8 * r][d]);
+                sc[r] = fmaf(qv.x, kv.x, sc[r]);
+                sc[r] = fmaf(qv.y, kv.y, sc[r]);
+                sc[r] = fmaf(qv.z, kv.z, sc[r]);
+                sc[r] = fmaf(qv.w, kv.w, sc[r]);
+            }
         }
         float tmax = -INFINITY;
 #pragma unroll
@@ -592,14 +604,23 @@ __global__ void __launch_bounds__(kPaThreads) prompt_attn_kernel(const float* __
         for (int j = 0; j < kPaK; ++j) {
             const float pj = Ps[i][j];
 #pragma unroll
-            for (int e = 0; e < DPT; ++e) o[e] = fmaf(pj, Vs[j][g * DPT + e], o[e]);
+            for (int e = 0; e < DPT; e += 4) {
+                // columns 32·(e/4) + 4g .. +3: the 8 lanes of a query read one 128-byte row span
+                const float4 vv = *reinterpret_cast<const float4*>(&Vs[j][8 * e + 4 * g]);
+                o[e] = fmaf(pj, vv.x, o[e]);
+                o[e + 1] = fmaf(pj, vv.y, o[e + 1]);
+                o[e + 2] = fmaf(pj, vv.z, o[e + 2]);
+                o[e + 3] = fmaf(pj, vv.w, o[e + 3]);
+            }
         }
     }
     if (i < nq) {
         const float inv = 1.f / l;
-        float* dst = out + ((size_t)(t0 + i) * H + h) * HD + g * DPT;
+        float* dst = out + ((size_t)(t0 + i) * H + h) * HD;
 #pragma unroll
-        for (int e = 0; e < DPT; ++e) dst[e] = o[e] * inv;
+        for (int e = 0; e < DPT; e += 4)
+            *reinterpret_cast<float4*>(dst + 8 * e + 4 * g) =
+                make_float4(o[e] * inv, o[e + 1] * inv, o[e + 2] * inv, o[e + 3] * inv);
     }
 }
 
