@@ -143,12 +143,31 @@ cudaError_t fail(const std::string& msg, cudaError_t code = cudaErrorInvalidValu
         cudaError_t e_ = (x);                                                               \
         if (e_ != cudaSuccess) return fail(std::string(#x) + ": " + cudaGetErrorString(e_), e_); \
     } while (0)
+// A call of this file's own functions, which set their message themselves.
+#define ENG_CALL(x)                       \
+    do {                                  \
+        cudaError_t e_ = (x);             \
+        if (e_ != cudaSuccess) return e_; \
+    } while (0)
+
+// Host-side limit of every wait on NCCL (AF_NCCL_INIT_TIMEOUT_S, default 300 s).
+inline double nccl_limit_s() {
+    const char* tv = std::getenv("AF_NCCL_INIT_TIMEOUT_S");
+    return tv ? std::atof(tv) : 300.0;
+}
 
 // The communicator is non-blocking (see af_engine_create): a call may return
-// ncclInProgress until NCCL has enqueued it; wait for that (bounded).
+// ncclInProgress until NCCL has enqueued it (the first collective also sets up
+// its connections, which can take a while); wait for that, bounded in time.
 inline ncclResult_t nccl_settle(ncclComm_t comm, ncclResult_t r) {
-    for (int i = 0; r == ncclInProgress && comm && i < 10000000; ++i)
+    const auto t0 = std::chrono::steady_clock::now();
+    while (r == ncclInProgress && comm) {
         if (ncclCommGetAsyncError(comm, &r) != ncclSuccess) return ncclSystemError;
+        if (r != ncclInProgress) break;
+        if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > nccl_limit_s())
+            return ncclInProgress;
+        std::this_thread::yield();
+    }
     return r;
 }
 #define NCCL_TRY(x)                                                                         \
@@ -486,12 +505,31 @@ cudaError_t build_step(af_engine* e) {
     auto none = [](StepPhase& p) { p.x.k_out = p.x.k_in = -1; };
     // exchange k: input of the next normalised GEMV (norm weights norm_w);
     // the residual ping-pongs x[k % 2] -> x[(k + 1) % 2]
+    std::vector<StepPhase> ph;
+    // AF_TP_XRED=0: the consuming GEMV reads every rank's partials itself
+    // (no separate phase); default: a reduction phase before it (StepPhase)
+    const bool xred = [] {
+        const char* v = std::getenv("AF_TP_XRED");
+        return !(v && v[0] == '0');
+    }();
     auto xin = [&](StepPhase& p, int k, const float* norm_w) {
-        p.x.k_in = k;
-        p.x.resid_in = e->x[k & 1];
-        p.x.resid_out = e->x[(k + 1) & 1];
-        p.x.norm_w = norm_w;
-        p.x.n = E;
+        XchgParams x = {};
+        x.k_out = -1;
+        x.k_in = k;
+        x.resid_in = e->x[k & 1];
+        x.resid_out = e->x[(k + 1) & 1];
+        x.norm_w = norm_w;
+        x.n = E;
+        if (xred) {
+            StepPhase r = {};
+            r.kind = PH_XRED;
+            r.x = x;
+            r.x.xq = const_cast<uint8_t*>(p.g.xq);  // the consuming GEMV copies the quantised sum
+            ph.push_back(r);
+        } else {
+            x.k_out = p.x.k_out;
+            p.x = x;
+        }
     };
     e->sepoch = static_cast<unsigned long long*>(e->dalloc(sizeof(unsigned long long)));
     ENG_TRY(cudaMemset(e->sepoch, 0, sizeof(unsigned long long)));
@@ -501,7 +539,6 @@ cudaError_t build_step(af_engine* e) {
         e->tpart = static_cast<unsigned long long*>(e->dalloc(n * sizeof(unsigned long long)));
         ENG_TRY(cudaMemset(e->tpart, 0, n * sizeof(unsigned long long)));
     }
-    std::vector<StepPhase> ph;
     StepPhase embed = {};
     embed.kind = PH_EMBED;
     none(embed);
@@ -654,7 +691,7 @@ cudaError_t build_step(af_engine* e) {
     sp.rank = e->rank;
     sp.n_buf = tp ? 2 * c.n_layer : 0;
     sp.epoch = e->sepoch;
-    if (tp) ENG_TRY(setup_exchange(e));
+    if (tp) ENG_CALL(setup_exchange(e));
     return cudaSuccess;
 }
 
@@ -734,8 +771,7 @@ cudaError_t af_engine_create(const af_model_config* cfg, int device, int tp_rank
         ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
         cfg.blocking = 0;
         ncclResult_t r = ncclCommInitRankConfig(&e->comm, tp_size, id, tp_rank, &cfg);
-        const char* tv = std::getenv("AF_NCCL_INIT_TIMEOUT_S");
-        const double limit = tv ? std::atof(tv) : 300.0;
+        const double limit = nccl_limit_s();
         const auto t0 = std::chrono::steady_clock::now();
         while (r == ncclInProgress || (r == ncclSuccess && e->comm)) {
             ncclResult_t st = ncclInProgress;
@@ -988,7 +1024,7 @@ cudaError_t af_engine_finalize(af_engine* e) {
         e->use_step = (!sv || std::atoi(sv) != 0) && e->tp <= kStepMaxRanks && c.n_embd % 32 == 0 &&
                       (e->tp == 1 || c.n_embd <= 8192) &&
                       step_supported(e->Hl, e->KVl, e->hd, c.n_embd, e->Fl);
-        if (e->use_step) ENG_TRY(build_step(e));
+        if (e->use_step) ENG_CALL(build_step(e));
         ENG_TRY(cudaDeviceSynchronize());
         // Capture one step into a graph.
         ENG_TRY(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));

@@ -185,6 +185,50 @@ __device__ bool xchg_input_t(const StepParams& sp, const XchgParams& x, unsigned
     return true;
 }
 
+// PH_XRED: reduce exchange `seq` one 32-value group per warp (group
+// w·grid + CTA, spread over the CTAs), store the new residual and quantise
+// the RMSNorm-weighted sum into x.xq.  False on a timeout or an abort.
+__device__ bool xred_phase(const StepParams& sp, const XchgParams& x, unsigned long long seq, volatile int* flags) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t tag = (uint32_t)(seq + 1ull);
+    const unsigned long long* area = sp.xrecv[sp.rank] + (size_t)(seq & 1ull) * kStepMaxRanks * x.n;
+    const int ng = x.n / 32;
+    bool ok = true;
+    for (int g = warp * (int)gridDim.x + (int)blockIdx.x; g < ng && ok; g += kCW * (int)gridDim.x) {
+        const int v = 32 * g + lane;
+        float a = __ldcg(x.resid_in + v);
+        unsigned long long w[kStepMaxRanks];
+#pragma unroll
+        for (int r = 0; r < kStepMaxRanks; ++r)
+            if (r < sp.tp) w[r] = ld_relaxed_sys(area + (size_t)r * x.n + v);
+        for (uint32_t it = 0;; ++it) {
+            bool all = true;
+#pragma unroll
+            for (int r = 0; r < kStepMaxRanks; ++r)
+                if (r < sp.tp) all &= (uint32_t)(w[r] >> 32) == tag;
+            if (__all_sync(0xffffffffu, all)) break;
+            if (it >= kGridSpinLimit || ((it & 15u) == 15u && flags[0])) {
+                ok = false;
+                break;
+            }
+#pragma unroll
+            for (int r = 0; r < kStepMaxRanks; ++r)
+                if (r < sp.tp && (uint32_t)(w[r] >> 32) != tag) w[r] = ld_relaxed_sys(area + (size_t)r * x.n + v);
+        }
+        if (!ok) break;
+#pragma unroll
+        for (int r = 0; r < kStepMaxRanks; ++r)
+            if (r < sp.tp) a += __uint_as_float((uint32_t)w[r]);
+        x.resid_out[v] = a;
+        xq_store32(x.xq, a, x.norm_w, x.n, v, sp.q8 != 0);
+    }
+    if (!ok) {
+        if (!flags[0]) set_err(kErrMbarTimeout);
+        flags[0] = 1;
+    }
+    return ok;
+}
+
 __device__ bool xchg_input(const StepParams& sp, const XchgParams& x, unsigned long long seq, uint8_t* xqs,
                            float eps, volatile int* flags, float* red) {
     switch ((x.n / 4 + kCT - 1) / kCT) {
@@ -700,7 +744,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) step_kernel(const __grid_cons
             // a GEMV fed by an exchange waits for the tagged partials instead
             // of the grid (the tags arrive only after every rank's producing
             // phase, and everything else it reads is older)
-            const bool xin = kind == PH_GEMV && ph.x.k_in >= 0;
+            const bool xin = (kind == PH_GEMV && ph.x.k_in >= 0) || kind == PH_XRED;
             // the phase's parameters and fragment range do not depend on the
             // previous phase: fetch them before waiting for it
             int vbeg = 0, vend = 0;
@@ -713,6 +757,11 @@ __global__ void __launch_bounds__(kGemvThreads, 1) step_kernel(const __grid_cons
             if (threadIdx.x == 0) AF_TRACE(i, 0);
             if (kind == PH_EMBED) {
                 embed_phase(sp, tok, reinterpret_cast<float*>(uni), red);
+            } else if (kind == PH_XRED) {
+                if (!xred_phase(sp, ph.x, xseq(ph.x.k_in), abort)) {
+                    *abort = 1;
+                    break;
+                }
             } else {
                 if (ph.x.k_out >= 0) {  // row-parallel partial sums, sent to every rank
                     if (threadIdx.x == 0) {

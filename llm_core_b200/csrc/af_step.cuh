@@ -28,7 +28,7 @@
 
 namespace af {
 
-enum StepPhaseKind : int { PH_EMBED = 0, PH_GEMV = 1, PH_ATTN = 2 };
+enum StepPhaseKind : int { PH_EMBED = 0, PH_GEMV = 1, PH_ATTN = 2, PH_XRED = 3 };
 
 constexpr int kStepMaxRanks = kGemvMaxRanks;
 
@@ -62,13 +62,22 @@ struct XchgParams {
     float* resid_out;      // after it (CTA g % grid writes group g)
     const float* norm_w;   // RMSNorm weights of the consuming GEMV
     int n;                 // values (n_embd)
+    uint8_t* xq;           // PH_XRED: the quantised sum (XQ layout) for the consuming GEMV
 };
 
+// Two ways to consume an exchange: (1) the GEMV itself (k_in on a PH_GEMV):
+// every CTA reads every rank's partials for the whole vector; (2) a PH_XRED
+// phase before the GEMV: each 32-value group is reduced by one warp of one
+// CTA (the ranks' tagged partials added in rank order to the residual),
+// stored to resid_out and quantised (RMSNorm-weighted, with its Σx²) into
+// x.xq; the GEMV then waits for the grid and copies the quantised vector like
+// a single-GPU phase.  (2) reads n·tp words per rank instead of per CTA, for
+// one more grid arrival.
 struct StepPhase {
     int kind;
     GemvParams g;  // PH_GEMV
     AttnParams a;  // PH_ATTN (nsplit = splits per kv head)
-    XchgParams x;  // PH_GEMV: tensor-parallel exchanges
+    XchgParams x;  // PH_GEMV / PH_XRED: tensor-parallel exchanges
 };
 
 struct StepParams {

@@ -225,6 +225,9 @@ PRESETS = {
     "tiny-qwen": ModelConfig("qwen2", 2, 512, 4, 2, 768, 1000, 512, 1e-6, 1e6,
                              qkv_bias=True, tied=True, name="tiny-qwen2"),
     "small": ModelConfig("llama", 4, 1024, 8, 4, 2816, 4000, 1024, 1e-5, 1e4, name="small-llama"),
+    # splits over 8 tensor-parallel ranks (8 kv heads, n_embd = 8 super-blocks;
+    # ffn_down's 22 super-blocks split unevenly)
+    "tp8": ModelConfig("llama", 3, 2048, 16, 8, 5632, 4000, 1024, 1e-5, 1e4, name="tp8-llama"),
     # Per-head Q/K RMSNorm before RoPE (qwen3) and after it (hunyuan-dense),
     # QkNormOrder at src/models/llama_model.cpp:1520-1522.
     "tiny-qwen3": ModelConfig("qwen3", 2, 512, 4, 2, 768, 1000, 512, 1e-6, 1e6, qk_norm=True, name="tiny-qwen3"),

@@ -18,7 +18,7 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 from llm_core_b200.engine import LlamaCudaModel, nccl_unique_id  # noqa: E402
 
 PROMPT = [1, 17, 999, 4, 250, 3000, 12, 7]
-STEPS = 24
+STEPS = 48
 
 
 def main(path: str, out: str) -> int:
