@@ -304,11 +304,12 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         const int mt = m0 / kPackTile + un;
         for (int j = 0; j < nst; ++j) {
             const int slot = j % kPfS, sb = j >> 2, rs = sb % kPfRawSlots, c = j & 3;
-            // the stage's X tile has landed (so its A slot is free: the loader
-            // copied it only after the MMAs that read the slot completed), and
-            // at a super-block's first stage, its raw units
+            // the stage's A slot is free once the MMAs that last read it have
+            // completed (the same signal the loader waits for before the X
+            // copy, so building overlaps the copy instead of following it),
+            // and at a super-block's first stage its raw units have landed
             if ((c == 0 && !mbar_wait(&raw_full[rs], (uint32_t)(sb / kPfRawSlots) & 1u, flag)) ||
-                !mbar_wait(&full_b[slot], (uint32_t)(j / kPfS) & 1u, flag)) {
+                (j >= kPfS && !mbar_wait(&empty[slot], (uint32_t)((j / kPfS) - 1) & 1u, flag))) {
                 *flag = 1;
                 break;
             }
