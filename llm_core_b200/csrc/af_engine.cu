@@ -682,6 +682,7 @@ cudaError_t build_step(af_engine* e) {
     sp.xq_norm_w = e->layers[0].attn_norm;
     sp.q8 = e->q8;
     sp.eps = c.eps;
+    sp.attn_dist = std::max(1, std::min(std::min(e->nsplit, e->sms / e->KVl), kStepAttnMaxSplit)) > kStepAttnDistMerge ? 1 : 0;
     sp.key = e->key;
     sp.token = &e->tokpos[0];
     sp.pos = &e->tokpos[1];

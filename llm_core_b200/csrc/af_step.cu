@@ -408,6 +408,81 @@ __device__ __forceinline__ void attn_prefetch(const AttnParams& a, int pos, int 
     }
 }
 
+constexpr int kAttnDistMerge = kStepAttnDistMerge;
+
+// The spread merge of kv head kvh's ns split partials (every split published
+// its un-normalised (o, max, sum) as tagged words): split `split` merges the
+// 32-value output groups split, split + ns, ... of the head's G·hd outputs.
+// For a group: the splits' (max, sum) of its head are polled into shared
+// memory, M = max; warp w adds the splits q ≡ w (mod 8) for the group's 32
+// dims (lane = dim; all its loads in flight, words whose tag is not this
+// phase's re-polled, bounded), then warp 0 adds the 8 warps in order,
+// normalises, stores and quantises the group for the O GEMV.
+__device__ __forceinline__ void attn_merge_spread(const AttnParams& a, const AttnSmem& s, int kvh, int split, int ns,
+                                               int G, int hd, unsigned long long tagw, volatile int* abort) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    auto poll = [&](const unsigned long long* p, unsigned long long w) {
+        uint32_t it = 0;
+        while ((w & ~0xFFFFFFFFull) != tagw && ++it < kGridSpinLimit && !*abort) w = ld_relaxed_gpu(p);
+        if (it >= kGridSpinLimit) set_err(kErrMbarTimeout);
+        return __uint_as_float((uint32_t)w);
+    };
+    constexpr int kPer = kAttnMaxSplit / kCW;  // splits per warp at most
+    const int ngr = G * hd / 32;
+    const int g0 = kvh * G * hd / 32;
+    for (int gi = split; gi < ngr; gi += ns) {
+        const int g = gi * 32 / hd, d0 = gi * 32 - g * hd;
+        const unsigned long long* hb = a.tpart + (size_t)(kvh * G + g) * a.nsplit * (hd + 2);
+        for (int q = tid; q < ns; q += kCT) {
+            const unsigned long long* p = hb + (size_t)q * (hd + 2) + hd;
+            s.ml[2 * q] = poll(p, ld_relaxed_gpu(p));
+            s.ml[2 * q + 1] = poll(p + 1, ld_relaxed_gpu(p + 1));
+        }
+        bar_consumers();
+        if (warp == 0) {
+            float m = -INFINITY;
+            for (int q = lane; q < ns; q += 32) m = fmaxf(m, s.ml[2 * q]);
+            m = warp_max(m);
+            if (lane == 0) s.corr[0] = m;
+        }
+        bar_consumers();
+        const float M = s.corr[0];
+        unsigned long long ov[kPer];
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+            const int q = warp + kCW * k;
+            ov[k] = q < ns ? ld_relaxed_gpu(hb + (size_t)q * (hd + 2) + d0 + lane) : 0ull;
+        }
+        float O = 0.f, L = 0.f;
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+            const int q = warp + kCW * k;
+            if (q >= ns) break;
+            const float mq = s.ml[2 * q];
+            if (mq == -INFINITY) continue;
+            const float oq = poll(hb + (size_t)q * (hd + 2) + d0 + lane, ov[k]);
+            const float w = expf(mq - M);
+            L += s.ml[2 * q + 1] * w;
+            O += oq * w;
+        }
+        s.red[warp * 32 + lane] = O;
+        if (lane == 0) s.lrow[warp] = L;
+        bar_consumers();
+        if (warp == 0) {
+            float Ot = 0.f, Lt = 0.f;
+#pragma unroll
+            for (int w = 0; w < kCW; ++w) {
+                Ot += s.red[w * 32 + lane];
+                Lt += s.lrow[w];
+            }
+            const float out = Ot / Lt;
+            a.out[(size_t)kvh * G * hd + (size_t)gi * 32 + lane] = out;
+            if (a.xq_out) xq_store32(a.xq_out, out, nullptr, a.n_heads * hd, 32 * (g0 + gi) + lane, a.q8 != 0);
+        }
+        bar_consumers();
+    }
+}
+
 // One (kv head, split) item: llama_forward_token's attention
 // (src/models/llama_model.cpp:1236-1272) for the G query heads of kv head kvh
 // over positions [t0, t1), as an online softmax over chunks; the
@@ -416,7 +491,7 @@ __device__ __forceinline__ void attn_prefetch(const AttnParams& a, int pos, int 
 // `r` holds the prefetched first chunk and RoPE factors.
 // GM: query heads per kv head held in registers (G <= GM; the instance is
 // chosen per model so that P·V accumulators cost 4·GM registers).
-template <int GM>
+template <int GM, bool DIST>
 __device__ __forceinline__ void attn_item(const AttnParams& a, const AttnSmem& s, int pos, int kvh, int split, int ns, AttnPre& r,
                                           int tph, uint32_t tag, volatile int* abort) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -556,6 +631,10 @@ __device__ __forceinline__ void attn_item(const AttnParams& a, const AttnSmem& s
     // other splits publish theirs as tagged words (tag << 32 | bits) for it
     // and are done: no fence, counter or atomic.
     const unsigned long long tagw = (unsigned long long)tag << 32;
+    // many splits (long context, few kv heads): every split publishes and the
+    // merge is spread over the splits, one 32-value output group each, instead
+    // of split 0 reading all of them
+    const bool dist = DIST && ns > kAttnDistMerge;
 #pragma unroll
     for (int g = 0; g < GM; ++g) {
         if (g >= G) break;
@@ -567,7 +646,7 @@ __device__ __forceinline__ void attn_item(const AttnParams& a, const AttnSmem& s
             float acc = 0.f;
 #pragma unroll
             for (int w = 0; w < kCW; ++w) acc += s.red[w * hd + d];
-            if (split == 0) {
+            if (split == 0 && !dist) {
                 s.ob[g * hd + d] = acc;
             } else {
                 st_relaxed_gpu(dst + d, tagw | __float_as_uint(acc));
@@ -578,6 +657,11 @@ __device__ __forceinline__ void attn_item(const AttnParams& a, const AttnSmem& s
             }
         }
         bar_consumers();
+    }
+    if (dist) {
+        attn_merge_spread(a, s, kvh, split, ns, G, hd, tagw, abort);
+        if (tid == 0) AF_TRACE(tph, 7);
+        return;
     }
     if (split != 0) return;
     // ---- split 0 merges the splits (exp(m_s − M) rescaling): the other
@@ -653,7 +737,7 @@ __device__ __forceinline__ void attn_item(const AttnParams& a, const AttnSmem& s
 
 // The whole attention phase of one layer for this CTA: the prefetch of what
 // does not depend on the QKV phase, the grid wait, then the CTA's items.
-template <int GM>
+template <int GM, bool DIST>
 __device__ __forceinline__ bool attn_phase(const AttnParams& a, const AttnSmem& s, int pos, unsigned* bar,
                                            unsigned target, volatile int* abort, int tph, uint32_t tag) {
     const int ns = attn_splits(a, pos);
@@ -663,7 +747,7 @@ __device__ __forceinline__ bool attn_phase(const AttnParams& a, const AttnSmem& 
     if (threadIdx.x == 0) AF_TRACE(tph, 0);
     for (int item = blockIdx.x; item < items; item += gridDim.x) {
         AttnPre r;
-        attn_item<GM>(a, s, pos, item / ns, item % ns, ns, r, tph, tag, abort);
+        attn_item<GM, DIST>(a, s, pos, item / ns, item % ns, ns, r, tph, tag, abort);
         bar_consumers();
     }
     return true;
@@ -671,6 +755,10 @@ __device__ __forceinline__ bool attn_phase(const AttnParams& a, const AttnSmem& 
 
 // ------------------------------------------------------------------ kernel
 
+// DIST: the instance whose attention can spread the merge of more than
+// kAttnDistMerge splits (engines whose kv heads allow that many splits); the
+// other instance carries no code for it.
+template <bool DIST>
 __global__ void __launch_bounds__(kGemvThreads, 1) step_kernel(const __grid_constant__ StepParams sp) {
     extern __shared__ __align__(128) uint8_t smem[];
     Ring ring;
@@ -735,10 +823,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) step_kernel(const __grid_cons
             // tag of this phase's split partials: unique per step and phase, never 0
             const uint32_t atag = (uint32_t)(epoch * (unsigned long long)sp.nph + (unsigned long long)i + 1ull);
             bool ok;
-            if (G == 1) ok = attn_phase<1>(*ap, s, pos, sp.bar, target, abort, i, atag);
-            else if (G == 2) ok = attn_phase<2>(*ap, s, pos, sp.bar, target, abort, i, atag);
-            else if (G <= 4) ok = attn_phase<4>(*ap, s, pos, sp.bar, target, abort, i, atag);
-            else ok = attn_phase<kStepMaxG>(*ap, s, pos, sp.bar, target, abort, i, atag);
+            if (G == 1) ok = attn_phase<1, DIST>(*ap, s, pos, sp.bar, target, abort, i, atag);
+            else if (G == 2) ok = attn_phase<2, DIST>(*ap, s, pos, sp.bar, target, abort, i, atag);
+            else if (G <= 4) ok = attn_phase<4, DIST>(*ap, s, pos, sp.bar, target, abort, i, atag);
+            else ok = attn_phase<kStepMaxG, DIST>(*ap, s, pos, sp.bar, target, abort, i, atag);
             if (!ok) break;
         } else {
             // a GEMV fed by an exchange waits for the tagged partials instead
@@ -846,7 +934,8 @@ bool step_supported(int n_heads, int n_kv_heads, int head_dim, int n_embd, int f
 }
 
 cudaError_t step_init() {
-    return cudaFuncSetAttribute(step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kStepSmem);
+    AF_CUDA_TRY(cudaFuncSetAttribute(step_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStepSmem));
+    return cudaFuncSetAttribute(step_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStepSmem);
 }
 
 cudaError_t step_launch(const StepParams& sp, cudaStream_t st) {
@@ -861,7 +950,8 @@ cudaError_t step_launch(const StepParams& sp, cudaStream_t st) {
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, step_kernel, sp);
+    if (sp.attn_dist) return cudaLaunchKernelEx(&cfg, step_kernel<true>, sp);
+    return cudaLaunchKernelEx(&cfg, step_kernel<false>, sp);
 }
 
 }  // namespace af

@@ -35,6 +35,7 @@ constexpr int kStepMaxRanks = kGemvMaxRanks;
 constexpr int kStepMaxG = 8;            // query heads per kv head
 constexpr int kStepAttnChunk = 64;      // KV positions per attention chunk
 constexpr int kStepAttnMaxSplit = 128;  // splits per kv head the attention merge stages in shared memory
+constexpr int kStepAttnDistMerge = 8;   // splits above which the merge is spread over the splits
 constexpr int kStepHdr = kGemvSmemHdr;  // mbarriers, flags, phase parameter copies, reduction scratch
 constexpr int kStepUnion = 40 * 1024;   // XQ input of a GEMV phase / attention scratch
 
@@ -92,6 +93,7 @@ struct StepParams {
     const float* xq_norm_w;
     int q8;                          // activations as Q8_0 blocks (see xq_store32w)
     float eps;                       // RMSNorm epsilon (the Q8 embedding path normalises itself)
+    int attn_dist;                   // attention splits per kv head can exceed kAttnDistMerge
     // finalize
     unsigned long long* key;
     int* token;

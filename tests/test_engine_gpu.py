@@ -281,3 +281,30 @@ def test_batched_prefill_matches_reference_forward_batch(gpu, preset, seed, pos0
     ref.close()
     m.close()
     assert ids == rids
+
+
+@pytest.mark.parametrize("preset,n", [("small", 900), ("tp8", 1000)])
+def test_long_context_decode_matches_reference(gpu, preset, n):
+    """Decode at a context where the step kernel's attention uses many splits
+    per kv head (more than 8: the merge is spread over the splits): logits
+    of 8 steps after an n-token prompt against the reference's F32 forward.
+    Both presets hold 1024 positions."""
+    if not RefLib.available():
+        pytest.skip("reference library not built")
+    from llm_core_b200.engine import read_config
+    path = model_path(preset, 13)
+    cfg = read_config(path)
+    assert n + 8 <= cfg.n_ctx
+    rng = np.random.default_rng(n)
+    prompt = [1] + rng.integers(0, cfg.vocab, n - 1).tolist()
+    ref = RefLib().open(path, threads=4, f32_mode=True)
+    ref.forward_batch(prompt, 0)
+    m = LlamaCudaModel(path)
+    m.prefill(prompt, 0, want_logits=False)
+    toks = rng.integers(0, cfg.vocab, 8).tolist()
+    for i, tok in enumerate(toks):
+        _, lg = m.step(tok, n + i)
+        want = ref.forward_token(tok, n + i)
+        assert rel_l2(lg, want) < LOGITS_TOL, (i, rel_l2(lg, want))
+    ref.close()
+    m.close()
