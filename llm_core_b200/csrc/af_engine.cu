@@ -687,7 +687,15 @@ cudaError_t build_step(af_engine* e) {
     sp.token = &e->tokpos[0];
     sp.pos = &e->tokpos[1];
     sp.hist = e->hist;
-    sp.ring_bytes = kStepSmem - kStepHdr - kStepUnion;
+    // union area: the largest quantised GEMV input, the attention scratch and,
+    // with Q8 activations, the staged embedding row; the rest is weight ring
+    {
+        int ub = std::max(kStepAttnScratch, std::max(xq_norm_bytes(E), xq_norm_bytes(e->Fl)));
+        if (e->q8 && step_q8_exact_embed(E)) ub = std::max(ub, E * 4);
+        ub = (ub + 127) & ~127;
+        sp.union_bytes = std::min(ub, kStepUnion);
+    }
+    sp.ring_bytes = (kStepSmem - kStepHdr - sp.union_bytes) & ~15;
     sp.tp = e->tp;
     sp.rank = e->rank;
     sp.n_buf = tp ? 2 * c.n_layer : 0;

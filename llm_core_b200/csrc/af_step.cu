@@ -334,9 +334,7 @@ struct AttnSmem {
         last = reinterpret_cast<int*>(ob + kStepMaxG * 128);
     }
 };
-static_assert((kStepMaxG * 128 + 256 + kStepMaxG * kStepAttnChunk + kCW * 128 + 3 * kStepMaxG +
-               kStepMaxG * kAttnMaxSplit * 2 + kStepMaxG * 128 + 4) * 4 <= kStepUnion,
-              "attention scratch exceeds the union area");
+static_assert(kCW == 8 && kAttnMaxSplit == kStepAttnMaxSplit, "kStepAttnScratch counts 8 warps");
 
 // Per-thread K/V rows of the current chunk and the RoPE factors of the item.
 struct AttnPre {
@@ -769,7 +767,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) step_kernel(const __grid_cons
     float* red = reinterpret_cast<float*>(smem + kParamOff + 448);  // 16 floats
     AttnParams* ap = reinterpret_cast<AttnParams*>(smem + kParamOff + 512);
     uint8_t* uni = smem + kStepHdr;
-    ring.buf = uni + kStepUnion;
+    ring.buf = uni + sp.union_bytes;
     ring.bytes = sp.ring_bytes;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 

@@ -37,7 +37,14 @@ constexpr int kStepAttnChunk = 64;      // KV positions per attention chunk
 constexpr int kStepAttnMaxSplit = 128;  // splits per kv head the attention merge stages in shared memory
 constexpr int kStepAttnDistMerge = 8;   // splits above which the merge is spread over the splits
 constexpr int kStepHdr = kGemvSmemHdr;  // mbarriers, flags, phase parameter copies, reduction scratch
-constexpr int kStepUnion = 40 * 1024;   // XQ input of a GEMV phase / attention scratch
+constexpr int kStepUnion = 40 * 1024;   // XQ input of a GEMV phase / attention scratch, at most
+// Attention scratch in the union area (AttnSmem, af_step.cu): q of the
+// kv head's query heads, k, v, scores, the warps' P·V partials, per-head
+// (max, sum, correction), the splits' (max, sum) and the merged output.
+constexpr int kStepAttnScratch =
+    (kStepMaxG * 128 + 256 + kStepMaxG * kStepAttnChunk + 8 * 128 + 3 * kStepMaxG + kStepMaxG * kStepAttnMaxSplit * 2 +
+     kStepMaxG * 128 + 4) * 4;
+static_assert(kStepAttnScratch <= kStepUnion, "attention scratch exceeds the union area");
 
 // With Q8_0 activations the embedding phase normalises the first layer's
 // input itself, in the reference's summation order (its embedding values are
@@ -94,6 +101,7 @@ struct StepParams {
     int q8;                          // activations as Q8_0 blocks (see xq_store32w)
     float eps;                       // RMSNorm epsilon (the Q8 embedding path normalises itself)
     int attn_dist;                   // attention splits per kv head can exceed kAttnDistMerge
+    int union_bytes;                 // the union area this engine needs (the rest of shared memory is ring)
     // finalize
     unsigned long long* key;
     int* token;
