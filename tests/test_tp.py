@@ -161,3 +161,25 @@ def test_rank_that_never_joins_ends_nccl_init_with_an_error(gpu, tmp_path):
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=120, env=env)
     assert "ERR" in r.stdout, r.stdout + r.stderr
     assert "did not join" in r.stdout
+
+
+def test_tp_shards_of_the_eight_way_preset():
+    """The preset the TP parity runs use splits over 2, 4 and 8 ranks with
+    every head, kv head, FFN super-block and vocabulary row owned exactly
+    once (ffn_down's 22 super-blocks unevenly at 4 and 8)."""
+    from llm_core_b200 import gguf
+    from llm_core_b200._lib import ModelConfig
+    from llm_core_b200.engine import tp_shard
+    p = gguf.PRESETS["tp8"]
+    c = ModelConfig()
+    c.n_layer, c.n_embd, c.n_head, c.n_kv_head, c.ffn, c.vocab = p.n_layer, p.n_embd, p.n_head, p.n_kv_head, p.ffn, p.vocab
+    for world in (2, 4, 8):
+        sh = [tp_shard(c, r, world) for r in range(world)]
+        assert sh[0].h0 == 0 and sh[-1].h1 == p.n_head
+        assert sh[0].kv0 == 0 and sh[-1].kv1 == p.n_kv_head
+        assert sh[0].f0 == 0 and sh[-1].f1 == p.ffn
+        assert sh[0].v0 == 0 and sh[-1].v1 == p.vocab
+        for a, b in zip(sh, sh[1:]):
+            assert a.h1 == b.h0 and a.kv1 == b.kv0 and a.f1 == b.f0 and a.v1 == b.v0
+        blocks = [(s.f1 - s.f0) // 256 for s in sh]
+        assert sum(blocks) == p.ffn // 256 and max(blocks) - min(blocks) <= 1
