@@ -93,6 +93,21 @@ class COracle:
         self.lib.afo_gemv(_f(y), W.ctypes.data_as(C.c_void_p), ggml_type, _f(x), rows, x.size)
         return y
 
+    def quantize_q8(self, x: np.ndarray):
+        """(d[k/32], q[k] int8): the Q8_0 blocks of x."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        d = np.zeros(x.size // 32, np.float32)
+        q = np.zeros(x.size, np.int8)
+        self.lib.afo_quantize_q8(_f(d), q.ctypes.data_as(C.c_void_p), _f(x), x.size)
+        return d, q
+
+    def gemv_q8(self, W: np.ndarray, ggml_type: int, x: np.ndarray, rows: int) -> np.ndarray:
+        """The production (Q8_0-input) GEMV."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        y = np.zeros(rows, np.float32)
+        self.lib.afo_gemv_q8(_f(y), W.ctypes.data_as(C.c_void_p), ggml_type, _f(x), rows, x.size)
+        return y
+
     def dequant_rows(self, W: np.ndarray, ggml_type: int, rows: int, cols: int) -> np.ndarray:
         from llm_core_b200.gguf import row_bytes
         out = np.zeros((rows, cols), np.float32)
@@ -258,6 +273,14 @@ class RefLib:
         name = {12: "axref_gemv_q4k_f32", 14: "axref_gemv_q6k_f32"}[ggml_type] + ("_scalar" if scalar else "")
         getattr(self.lib, name)(_f(y), _b(W), _f(x), rows, x.size)
         return y
+
+    def quantize_q8(self, x: np.ndarray):
+        """The reference's own Q8_0 quantiser: (d[k/32], q[k] int8)."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        d = np.zeros(x.size // 32, np.float32)
+        q = np.zeros(x.size, np.int8)
+        self.lib.axref_quantize_q8(_f(x), x.size, _f(d), q.ctypes.data_as(C.c_void_p))
+        return d, q
 
     def gemv_q8(self, W: np.ndarray, ggml_type: int, x: np.ndarray, rows: int, threads: int = 1):
         x = np.ascontiguousarray(x, dtype=np.float32)

@@ -244,6 +244,109 @@ void afo_gemv(float* y, const void* W, int type, const float* x, int rows, int c
     for (int t = 1; t < nt; t++) pthread_join(th[t], NULL);
 }
 
+/* F32 -> Q8_0 blocks (32 int8 + f32 d): quantize_q8_avx2,
+ * src/backend/cpu_x86/kernels/quant_q8_avx2.cpp:33-84.  d = amax/127;
+ * q = x·(127/amax) rounded to nearest, ties to even (the default rounding of
+ * _mm256_cvtps_epi32, here lrintf), saturated to int8 like the packs. */
+void afo_quantize_q8(float* d_out, int8_t* q_out, const float* x, int k) {
+    for (int i = 0; i < k / 32; i++) {
+        const float* s = x + (size_t)32 * i;
+        float amax = 0.f;
+        for (int j = 0; j < 32; j++) {
+            const float a = fabsf(s[j]);
+            if (a > amax) amax = a;
+        }
+        const float id = amax > 0.f ? 127.f / amax : 0.f;
+        d_out[i] = amax / 127.f;
+        for (int j = 0; j < 32; j++) {
+            long v = lrintf(s[j] * id);
+            q_out[(size_t)32 * i + j] = (int8_t)(v > 127 ? 127 : (v < -128 ? -128 : v));
+        }
+    }
+}
+
+/* Q4_K row · Q8_0 input, the production decode GEMV's arithmetic
+ * (gemv_q4k_r8_avx2.cpp:196-220): per 32-value sub-block j with Q8 block
+ * scale dq, (d·sc_j·dq)·Σ q·q8 − (dmin·m_j·dq)·Σ q8, integer sums exact. */
+static float q4k_q8_dot_row(const uint8_t* row, const float* xd, const int8_t* xq, int cols) {
+    float acc = 0.f;
+    for (int b = 0; b < cols / QK_K; b++) {
+        const uint8_t* block = row + (size_t)b * Q4K_BYTES;
+        uint16_t db, mb;
+        memcpy(&db, block, 2);
+        memcpy(&mb, block + 2, 2);
+        const float d = afo_f16_to_f32(db), dmin = afo_f16_to_f32(mb);
+        const uint8_t* qs = block + 16;
+        for (int chunk = 0; chunk < 4; chunk++) {
+            for (int half = 0; half < 2; half++) {
+                const int j = 2 * chunk + half, blk = 8 * b + j;
+                uint8_t sc, m;
+                q4k_get_scale_min(j, block + 4, &sc, &m);
+                const int8_t* q8 = xq + (size_t)32 * blk;
+                int dot = 0, sum = 0;
+                for (int l = 0; l < 32; l++) {
+                    const int q = half ? (qs[32 * chunk + l] >> 4) : (qs[32 * chunk + l] & 0xF);
+                    dot += q * q8[l];
+                    sum += q8[l];
+                }
+                acc += (d * sc * xd[blk]) * (float)dot;
+                acc -= (dmin * m * xd[blk]) * (float)sum;
+            }
+        }
+    }
+    return acc;
+}
+
+/* Q6_K row · Q8_0 input: gemv_q6k_q8_avx2.cpp:103 — per 16-value group g,
+ * d·sc_g·dq·(Σ q6·q8 − 32·Σ q8), q6 the unsigned 6-bit value. */
+static float q6k_q8_dot_row(const uint8_t* row, const float* xd, const int8_t* xq, int cols) {
+    float acc = 0.f;
+    for (int b = 0; b < cols / QK_K; b++) {
+        const uint8_t* block = row + (size_t)b * Q6K_BYTES;
+        uint16_t db;
+        memcpy(&db, block + 208, 2);
+        const float d = afo_f16_to_f32(db);
+        const int8_t* sc = (const int8_t*)(block + 192);
+        int q6[QK_K];
+        for (int n = 0; n < 2; n++) {
+            const uint8_t* ql = block + 64 * n;
+            const uint8_t* qh = block + 128 + 32 * n;
+            for (int l = 0; l < 32; l++) {
+                q6[128 * n + l] = (ql[l] & 0x0F) | (((qh[l] >> 0) & 3) << 4);
+                q6[128 * n + l + 32] = (ql[l + 32] & 0x0F) | (((qh[l] >> 2) & 3) << 4);
+                q6[128 * n + l + 64] = (ql[l] >> 4) | (((qh[l] >> 4) & 3) << 4);
+                q6[128 * n + l + 96] = (ql[l + 32] >> 4) | (((qh[l] >> 6) & 3) << 4);
+            }
+        }
+        for (int g = 0; g < 16; g++) {
+            const int blk = 8 * b + g / 2;
+            const int8_t* q8 = xq + (size_t)QK_K * b + 16 * g;
+            int dot = 0, sum = 0;
+            for (int l = 0; l < 16; l++) {
+                dot += q6[16 * g + l] * q8[l];
+                sum += q8[l];
+            }
+            acc += (d * sc[g] * xd[blk]) * (float)(dot - 32 * sum);
+        }
+    }
+    return acc;
+}
+
+/* y = W · Q8_0(x): the reference's production decode GEMV gemv_wt_q8
+ * (src/models/llama_model.cpp:767-831) with x quantised as above. */
+void afo_gemv_q8(float* y, const void* W, int type, const float* x, int rows, int cols) {
+    const size_t rb = row_bytes_of(type, cols);
+    float* xd = (float*)malloc(sizeof(float) * (size_t)(cols / 32));
+    int8_t* xq = (int8_t*)malloc((size_t)cols);
+    afo_quantize_q8(xd, xq, x, cols);
+    for (int r = 0; r < rows; r++) {
+        const uint8_t* row = (const uint8_t*)W + (size_t)r * rb;
+        y[r] = type == GGML_Q6_K ? q6k_q8_dot_row(row, xd, xq, cols) : q4k_q8_dot_row(row, xd, xq, cols);
+    }
+    free(xd);
+    free(xq);
+}
+
 /* RMSNorm with separate output: rms_norm_out, llama_model.cpp:393-419. */
 void afo_rms_norm(float* dst, const float* src, const float* w, int n, float eps) {
     float ss = 0.f;

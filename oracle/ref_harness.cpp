@@ -76,6 +76,17 @@ void axref_gemv_q6k_f32_scalar(float* y, const uint8_t* W, const float* x, int r
 // Production GEMV (Q8_0 activations) exactly as gemv_wt_q8 runs it
 // (llama_model.cpp:767-831), with an r8 repack when rows % 8 == 0.
 // dtype: 12 = Q4_K, 14 = Q6_K (ggml type ids).
+// The reference's own F32 -> Q8_0 quantiser (the kQ8Quant the production
+// decode uses), unpacked into d[k/32] and q[k].
+void axref_quantize_q8(const float* x, int k, float* d, int8_t* q) {
+    std::vector<block_q8_0> blocks((size_t)(k / 32));
+    kQ8Quant(blocks.data(), x, k);
+    for (int i = 0; i < k / 32; ++i) {
+        d[i] = blocks[i].d;
+        std::memcpy(q + (size_t)32 * i, blocks[i].qs, 32);
+    }
+}
+
 void axref_gemv_q8_production(float* y, const uint8_t* W, int ggml_type, const float* x,
                               int rows, int cols, int n_threads) {
     WT wt;

@@ -125,3 +125,44 @@ def test_reference_prompt_paths(preset, seed):
     assert np.array_equal(run(True, True), tok)
     dev = float(np.linalg.norm(run(False, True) - tok) / np.linalg.norm(tok))
     assert dev < 2e-2, dev
+
+
+@pytest.mark.skipif(not RefLib.available(), reason="oracle/_ref not built here")
+def test_oracle_q8_quantiser_is_the_reference_quantiser(orc):
+    """The oracle's Q8_0 quantiser against the reference's own (the kQ8Quant
+    of the production decode): bit-identical d and q, including values that
+    sit exactly on a rounding tie (x·127/amax = k + 0.5, rounded to even)."""
+    rng = np.random.default_rng(77)
+    ref = RefLib()
+    x = (rng.standard_normal(4096) * np.repeat(10.0 ** rng.uniform(-6, 4, 128), 32)).astype(np.float32)
+    ties = np.zeros(256, np.float32)
+    for b in range(8):  # amax = 127 in every block, then exact half-integers
+        blk = ties[32 * b: 32 * b + 32]
+        blk[0] = 127.0
+        blk[1:] = (np.arange(31) - 15) + 0.5
+    x = np.concatenate([x, ties, np.zeros(32, np.float32)])
+    d0, q0 = orc.quantize_q8(x)
+    d1, q1 = ref.quantize_q8(x)
+    np.testing.assert_array_equal(d0.view(np.uint32), d1.view(np.uint32))
+    np.testing.assert_array_equal(q0, q1)
+    # ties go to even: 0.5 -> 0, 1.5 -> 2, -0.5 -> -0, -1.5 -> -2
+    t = q0[4096:4096 + 32]
+    assert t[16] == 0 and t[17] == 2 and t[15] == 0 and t[14] == -2
+
+
+@pytest.mark.skipif(not RefLib.available(), reason="oracle/_ref not built here")
+@pytest.mark.parametrize("t,rows,cols", [(gguf.GGML_Q4_K, 256, 2048), (gguf.GGML_Q4_K, 100, 4096),
+                                         (gguf.GGML_Q6_K, 128, 2048), (gguf.GGML_Q6_K, 64, 11008)])
+def test_oracle_q8_gemv_matches_reference_production_gemv(orc, t, rows, cols):
+    """The oracle's restatement of the production Q8_0-input GEMV against the
+    reference's own (8-row repacked Q4_K kernel when rows % 8 == 0, else the
+    4-row kernel; the Q6_K Q8 kernel): same integer dots, float order differs."""
+    rng = np.random.default_rng(rows + cols + t)
+    gen = gguf.random_q4k if t == gguf.GGML_Q4_K else gguf.random_q6k
+    W = gen(rng, rows * cols // 256).reshape(-1)
+    x = rng.standard_normal(cols).astype(np.float32)
+    got = orc.gemv_q8(W, t, x, rows)
+    want = RefLib().gemv_q8(W, t, x, rows)
+    assert rel_l2(got, want) < 1e-5, rel_l2(got, want)
+    # and it is the Q8 arithmetic: the F32 GEMV is farther away
+    assert rel_l2(orc.gemv(W, t, x, rows), want) > 10 * rel_l2(got, want)
