@@ -101,6 +101,14 @@ class COracle:
         self.lib.afo_quantize_q8(_f(d), q.ctypes.data_as(C.c_void_p), _f(x), x.size)
         return d, q
 
+    def sample(self, logits: np.ndarray, window, rep_penalty: float, top_k: int, top_p: float,
+               temperature: float, r: float) -> int:
+        """Penalty + sample() on a copy of `logits` with the uniform draw r."""
+        lg = np.array(logits, dtype=np.float32)
+        w = np.ascontiguousarray(window, dtype=np.int32)
+        return self.lib.afo_sample(_f(lg), lg.size, w.ctypes.data_as(C.c_void_p), w.size, C.c_float(rep_penalty),
+                                   top_k, C.c_float(top_p), C.c_float(temperature), C.c_float(r))
+
     def gemv_q8(self, W: np.ndarray, ggml_type: int, x: np.ndarray, rows: int) -> np.ndarray:
         """The production (Q8_0-input) GEMV."""
         x = np.ascontiguousarray(x, dtype=np.float32)

@@ -347,6 +347,84 @@ void afo_gemv_q8(float* y, const void* W, int type, const float* x, int rows, in
     free(xq);
 }
 
+/* One sampling step on `lg` (modified in place): the repetition penalty of
+ * llama_generate's decode loop (llama_model.cpp:1586-1598: for each window id
+ * in order, v/pen if v > 0 else v·pen), then sample() (llama_model.cpp:
+ * 1466-1498): greedy first maximum at temperature <= 0; otherwise the k
+ * largest of lg/T in descending order (ties: lower index first), p_i =
+ * exp(s_i − s_0) normalised in order, the nucleus cut at the first cumulative
+ * p >= top_p and renormalised, and the first i whose cumulative p exceeds r
+ * (r: the uniform draw of the reference's rng). */
+typedef struct {
+    float v;
+    int i;
+} afo_scored;
+
+static int scored_desc(const void* a, const void* b) {
+    const afo_scored* x = (const afo_scored*)a;
+    const afo_scored* y = (const afo_scored*)b;
+    if (x->v != y->v) return x->v > y->v ? -1 : 1;
+    return x->i - y->i;
+}
+
+int afo_sample(float* lg, int V, const int32_t* win, int n_win, float pen, int top_k, float top_p, float temp,
+               float r) {
+    if (pen != 1.0f)
+        for (int i = 0; i < n_win; i++) {
+            const int id = win[i];
+            if (id < 0 || id >= V) continue;
+            lg[id] = lg[id] > 0.f ? lg[id] / pen : lg[id] * pen;
+        }
+    if (temp <= 0.f) {
+        int best = 0;
+        for (int i = 1; i < V; i++)
+            if (lg[i] > lg[best]) best = i;
+        return best;
+    }
+    int k = (top_k > 0 && top_k < V) ? top_k : V;
+    afo_scored* sc = (afo_scored*)malloc(sizeof(afo_scored) * (size_t)V);
+    for (int i = 0; i < V; i++) {
+        sc[i].v = lg[i] / temp;
+        sc[i].i = i;
+    }
+    qsort(sc, (size_t)V, sizeof(afo_scored), scored_desc);
+    float* p = (float*)malloc(sizeof(float) * (size_t)k);
+    const float mx = sc[0].v;
+    float sum = 0.f;
+    for (int i = 0; i < k; i++) {
+        p[i] = expf(sc[i].v - mx);
+        sum += p[i];
+    }
+    for (int i = 0; i < k; i++) p[i] /= sum;
+    if (top_p < 1.0f) {
+        float cum = 0.f;
+        int cut = k;
+        for (int i = 0; i < k; i++) {
+            cum += p[i];
+            if (cum >= top_p) {
+                cut = i + 1;
+                break;
+            }
+        }
+        sum = 0.f;
+        for (int i = 0; i < cut; i++) sum += p[i];
+        for (int i = 0; i < cut; i++) p[i] /= sum;
+        k = cut;
+    }
+    float cum = 0.f;
+    int pick = sc[k - 1].i;
+    for (int i = 0; i < k; i++) {
+        cum += p[i];
+        if (r < cum) {
+            pick = sc[i].i;
+            break;
+        }
+    }
+    free(p);
+    free(sc);
+    return pick;
+}
+
 /* RMSNorm with separate output: rms_norm_out, llama_model.cpp:393-419. */
 void afo_rms_norm(float* dst, const float* src, const float* w, int n, float eps) {
     float ss = 0.f;

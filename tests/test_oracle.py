@@ -166,3 +166,20 @@ def test_oracle_q8_gemv_matches_reference_production_gemv(orc, t, rows, cols):
     assert rel_l2(got, want) < 1e-5, rel_l2(got, want)
     # and it is the Q8 arithmetic: the F32 GEMV is farther away
     assert rel_l2(orc.gemv(W, t, x, rows), want) > 10 * rel_l2(got, want)
+
+
+@pytest.mark.skipif(not RefLib.available(), reason="oracle/_ref not built here")
+@pytest.mark.parametrize("V,T,k,p,pen,nw", [(32000, 0.0, 40, 1.0, 1.3, 64), (32000, 1.0, 40, 0.95, 1.0, 0),
+                                            (32000, 0.7, 40, 1.0, 1.1, 64), (151936, 1.0, 40, 0.95, 1.2, 16),
+                                            (1000, 2.0, 999, 0.5, 1.0, 0), (5000, 0.8, 0, 0.9, 1.0, 0)])
+def test_oracle_sampler_matches_reference(orc, V, T, k, p, pen, nw):
+    """The oracle's restatement of the penalty + sample() against the
+    reference's own, same logits and the reference rng's draw."""
+    ref = RefLib()
+    rng = np.random.default_rng(V + nw + int(10 * T))
+    for trial in range(16):
+        logits = (rng.standard_normal(V) * 3.0).astype(np.float32)
+        window = rng.integers(0, V, nw).astype(np.int32)
+        seed = 500 + trial
+        r = float(ref.uniform(seed, 1)[0])
+        assert orc.sample(logits, window, pen, k, p, T, r) == ref.sample(logits, window, pen, k, p, T, seed), trial
