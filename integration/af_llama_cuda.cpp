@@ -18,6 +18,7 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <random>
 #include <stdexcept>
 #include <string>
@@ -124,6 +125,11 @@ std::vector<int32_t> llama_cuda_generate(const Engine& engine, std::vector<int32
         dm.owner = nullptr;
         check(af_engine_create(&c, /*device*/ 0, /*tp_rank*/ 0, /*tp_size*/ 1, nullptr, &dm.e), "af_engine_create");
         upload_model(dm.e, engine, c.n_layer);
+        // AF_Q8_ACTIVATIONS=1: the reference CPU path's production activation
+        // format (Q8_0 before every GEMV) instead of the default 16-bit grid,
+        // which tracks the F32-activation forward
+        if (const char* q8 = std::getenv("AF_Q8_ACTIVATIONS"); q8 && q8[0] == '1')
+            check(af_engine_set_q8_activations(dm.e, 1), "af_engine_set_q8_activations");
         check(af_engine_finalize(dm.e), "af_engine_finalize");
         dm.owner = &engine;
         dm.n_ctx = c.n_ctx;
