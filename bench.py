@@ -186,6 +186,14 @@ def host_cpu() -> dict:
     return {"cpu_model": model, "affinity": ",".join(parts), "threads": len(aff)}
 
 
+def host_threads() -> int:
+    """Host threads this process may run on (its affinity mask, not the machine's count)."""
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
 def ref_decode_after_prompt(path: str, threads: int, vocab: int, warmup: int, steps: int):
     """The reference's own CPU path on the b200 arm's workload: prefill the
     same 128-token prompt (llama_forward_batch), `warmup` untimed decode
@@ -221,7 +229,7 @@ def run_reference(args):
         return 0
     from llm_core_b200 import gguf
     path = model_file(args.model, 0, None)
-    threads = os.cpu_count() or 1
+    threads = host_threads()
     from oracle import RefLib
     if not RefLib.available():
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libaxref.so was not built "
@@ -352,7 +360,7 @@ def run_b200(args):
     if rank != 0:
         return 0
     traffic = STEP_KERNEL_DRAM_BYTES.get((args.model, world)) if m.kernels_per_step == 1 else None
-    threads = os.cpu_count() or 1
+    threads = host_threads()
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_sample(path, args.cpu_steps, threads, cfg.vocab, 2)
