@@ -186,6 +186,15 @@ def host_cpu() -> dict:
     return {"cpu_model": model, "affinity": ",".join(parts), "threads": len(aff)}
 
 
+L2_BYTES = 126 * 1024 * 1024
+
+
+def l2_note(weight_bytes: int, scope: str) -> str:
+    """The config's L2 statement: the weights streamed per step against the 126 MB L2."""
+    gb = (f"{weight_bytes / 1e9:.2f} GB" if weight_bytes >= 1e9 else f"{weight_bytes / 1e6:.1f} MB") + f" weights per step{scope}"
+    return f"inputs larger than L2 ({gb})" if weight_bytes > L2_BYTES else f"weights fit in L2 ({gb})"
+
+
 def host_threads() -> int:
     """Host threads this process may run on (its affinity mask, not the machine's count)."""
     try:
@@ -249,7 +258,7 @@ def run_reference(args):
                    "model": cfg.name, "global_batch": 1, "seq_len": PROMPT_LEN,
                    "context": f"{p0}..{p0 + args.steps}",
                    "parallelism": "cpu threads",
-                   "l2": "inputs larger than L2 (4.07 GB weights per step)"},
+                   "l2": l2_note(gguf.model_weight_bytes(cfg), "")},
         "cpu_baseline": {"value": round(val, 3), "unit": "tok/s", "cores": threads, "kind": "reference",
                          **host_cpu(),
                          "sample": f"{args.steps} decode steps at context {p0}..{p0 + args.steps} after the "
@@ -374,7 +383,7 @@ def run_b200(args):
                    "model": cfg.name, "global_batch": 1, "seq_len": PROMPT_LEN,
                    "context": f"{PROMPT_LEN + 1 + args.warmup}..{PROMPT_LEN + 1 + args.warmup + args.steps}",
                    "parallelism": f"tp{world}" if world > 1 else "single",
-                   "l2": "inputs larger than L2 (4.07 GB weights per step)"},
+                   "l2": l2_note(wb, " per rank")},
         "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic, "kernel": kname,
