@@ -1107,12 +1107,13 @@ cudaError_t af_engine_prefill(af_engine* e, const int32_t* h_tokens, int n, int3
 
 // Batched prompt pass (one GPU): tokens 0 .. n-2 go through every layer as
 // T = n-1 rows at once (llama_forward_batch, src/models/llama_model.cpp:1339-1462):
-// the linear layers on the tcgen05 prefill GEMM, norms / bias / SwiGLU /
-// residuals as row kernels, attention per token in position order (the
-// decode attention kernel, which applies RoPE and Q/K norms and stores the
-// token's K/V row before attending over positions <= its own, so the cache
-// fills causally).  The last token then runs the decode step, which produces
-// its logits and the next token exactly as af_engine_prefill does.
+// the linear layers on the tcgen05 prefill GEMM (the batched GEMV below 33
+// rows), norms / bias / SwiGLU / residuals as row kernels, and per layer one
+// RoPE / K-V store launch plus one causal-attention launch over all T rows
+// (head dims 64 and 128; other head dims run the decode attention kernel per
+// token in position order, which stores each token's K/V row before attending
+// over positions <= its own).  The last token then runs the decode step, which
+// produces its logits and the next token exactly as af_engine_prefill does.
 cudaError_t af_engine_prefill_batched(af_engine* e, const int32_t* h_tokens, int n, int32_t pos0, float* h_logits,
                                       int32_t* h_next) {
     AF_CUDA_TRY(check_ready(e));
