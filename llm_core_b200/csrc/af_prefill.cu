@@ -273,6 +273,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     *flag = 1;
                     break;
                 }
+                // the staged X is the previous launch's output (programmatic
+                // dependent launch: everything before this overlaps it)
+                if (j == 0) pdl_wait();
                 mbar_arrive_expect_tx(&full_b[slot], (uint32_t)kPfPlane);
                 bulk_g2s(stbase + slot * kPfStage + kPfPlane, Xp + ((size_t)nt * nst + j) * kPfPlane, kPfPlane,
                          &full_b[slot], pol_x);
@@ -333,6 +336,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         }
         // epilogue: warps 0-3 own TMEM lanes 32·warp .. 32·warp + 31
         if (warp < 4) {
+            pdl_wait();  // xexp and the Y rows belong to earlier launches
             if (!*flag && !mbar_wait(accf, 0u, flag)) *flag = 1;
             tc_fence_after();
             if (!*flag) {
@@ -365,6 +369,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 // Per-token power-of-two exponent e with max|x|·2^e in [2^14, 2^15) (0 for
 // an all-zero row): one warp per token.
 __global__ void prefill_xexp_kernel(const float* __restrict__ X, int* __restrict__ xexp, int cols, int T) {
+    pdl_launch_dependents();  // the X packing may start launching
     const int n = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (n >= T) return;
     float m = 0.f;
@@ -388,6 +393,8 @@ __global__ void prefill_xexp_kernel(const float* __restrict__ X, int* __restrict
 // K-major no-swizzle layout of one MMA B operand stage; tokens ≥ T are zero.
 __global__ void prefill_pack_x_kernel(const float* __restrict__ X, const int* __restrict__ xexp, uint8_t* __restrict__ Xp,
                                       int cols, int T, int ntok) {
+    pdl_launch_dependents();  // the GEMM's set-up and first weight copies overlap the packing
+    pdl_wait();               // xexp from the previous launch
     const int kc = cols / 8;
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (long long)ntok * kc) return;
@@ -671,12 +678,25 @@ cudaError_t prefill_gemm_launch(float* y, const uint8_t* w, int type, const floa
     }
     prefill_xexp_kernel<<<(T + 7) / 8, 256, 0, st>>>(x, g_pf.xexp, cols, T);
     const long long items = (long long)ntile * kPfN * (cols / 8);
-    prefill_pack_x_kernel<<<(unsigned)((items + 255) / 256), 256, 0, st>>>(x, g_pf.xexp, g_pf.xp, cols, T,
-                                                                            ntile * kPfN);
-    const dim3 grid((rows + kPfM - 1) / kPfM, ntile);
-    prefill_gemm_kernel<kPfStages><<<grid, kPfThreads, pf_smem<kPfStages>(), st>>>(y, w, type, g_pf.xp, g_pf.xexp, rows,
-                                                                                 cols, T);
-    return cudaGetLastError();
+    AF_CUDA_TRY(cudaGetLastError());
+    // the packing and the GEMM start under programmatic dependent launch:
+    // each waits (griddepcontrol.wait) before it reads its predecessor's output
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((items + 255) / 256));
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    AF_CUDA_TRY(cudaLaunchKernelEx(&cfg, prefill_pack_x_kernel, x, (const int*)g_pf.xexp, g_pf.xp, cols, T,
+                                   ntile * kPfN));
+    cfg.gridDim = dim3((rows + kPfM - 1) / kPfM, ntile);
+    cfg.blockDim = dim3(kPfThreads);
+    cfg.dynamicSmemBytes = pf_smem<kPfStages>();
+    return cudaLaunchKernelEx(&cfg, prefill_gemm_kernel<kPfStages>, y, w, type, (const uint8_t*)g_pf.xp,
+                              (const int*)g_pf.xexp, rows, cols, T);
 }
 
 bool prompt_attention_supported(int hd) { return hd == 64 || hd == 128; }
