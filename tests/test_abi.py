@@ -39,6 +39,27 @@ def test_gemv_rejects_bad_arguments_without_touching_a_device():
     assert lib.af_gemv_f32(None, None, 3, None, 4, 256, None) != 0    # unsupported type
 
 
+def test_other_gemv_entries_reject_bad_arguments_without_touching_a_device():
+    lib = _lib.load()
+    # the reference backend's raw-GGUF entry: row_bytes must be the dense Q4_K row
+    assert lib.af_q4km_gemv_f32(None, None, None, 4, 256, 150, None) != 0
+    assert b"row_bytes" in lib.af_last_error()
+    assert lib.af_q4km_gemv_f32(None, None, None, 4, 100, 144, None) != 0          # cols % 256
+    assert lib.af_q4km_gemv_f32(None, C.c_void_p(8), None, 4, 256, 144, None) != 0  # misaligned weights
+    assert b"aligned" in lib.af_last_error()
+    assert lib.af_q4km_gemv_f32(None, None, None, 0, 256, 144, None) == 0           # nothing to do
+    # Q8_0-input GEMV
+    assert lib.af_gemv_q8_f32(None, None, 3, None, 4, 256, None) != 0               # unsupported type
+    assert lib.af_gemv_q8_f32(None, None, 12, None, 4, 12288 + 256, None) != 0      # K above the limit
+    assert lib.af_gemv_q8_f32(None, None, 14, None, 0, 256, None) == 0
+    # batched GEMV: 1..32 vectors
+    assert lib.af_gemv_batched_f32(None, None, 12, None, 4, 256, 0, None) != 0
+    assert lib.af_gemv_batched_f32(None, None, 12, None, 4, 256, 33, None) != 0
+    assert b"n_vec" in lib.af_last_error()
+    assert lib.af_gemv_batched_f32(None, None, 12, None, 4, 200, 4, None) != 0      # cols % 256
+    assert lib.af_gemv_batched_f32(None, None, 12, None, 0, 256, 4, None) == 0
+
+
 def test_prefill_gemm_rejects_bad_arguments_without_touching_a_device():
     lib = _lib.load()
     assert lib.af_prefill_gemm_f32(None, None, 12, None, 16, 100, 4, None) != 0   # cols % 256
