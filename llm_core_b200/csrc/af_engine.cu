@@ -926,6 +926,7 @@ cudaError_t af_gguf_read_config(const char* path, int max_context_len, af_model_
 }
 
 cudaError_t af_engine_load_gguf(af_engine* e, const char* path) {
+    if (!e || !path) return fail("af_engine_load_gguf: null argument");
     try {
         GgufFile g;
         g.open(path);

@@ -104,3 +104,22 @@ def test_sampler_rejects_bad_arguments_without_touching_a_device():
     import ctypes as C
     s = _lib.Sampling(1.0, 40, 0.95, 1.0, 0)
     assert _lib.load().af_sample_f32(None, 100, None, 0, C.byref(s), 0.5, None, None) != 0
+
+
+def test_engine_entries_reject_a_null_engine_without_touching_a_device():
+    lib = _lib.load()
+    i1 = (C.c_int32 * 1)()
+    n = C.c_int(0)
+    assert lib.af_engine_destroy(None) == 0
+    assert lib.af_engine_load_gguf(None, b"x.gguf") != 0 and b"null" in lib.af_last_error()
+    assert lib.af_engine_set_q8_activations(None, 1) != 0
+    assert lib.af_engine_finalize(None) != 0
+    for call in (lambda: lib.af_engine_step(None, 0, 0, None, i1),
+                 lambda: lib.af_engine_prefill(None, i1, 1, 0, None, i1),
+                 lambda: lib.af_engine_prefill_batched(None, i1, 1, 0, None, i1),
+                 lambda: lib.af_engine_decode_greedy(None, 0, 0, 1, i1),
+                 lambda: lib.af_engine_generate(None, i1, 1, 1, i1, C.byref(n)),
+                 lambda: lib.af_engine_hidden(None, None),
+                 lambda: lib.af_engine_kv(None, 0, 0, 1, None)):
+        assert call() != 0
+        assert b"not finalized" in lib.af_last_error()
